@@ -1,0 +1,95 @@
+// Launchers for the tcgen05 GEMM (plain store epilogue, optional SiLU).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "gemm.h"
+#include "gemm_tc.cuh"
+#include "tma_desc.h"
+
+namespace es {
+
+static CUtensorMapDataType tma_dtype(int dtype) {
+  return dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb) {
+  const CUtensorMapDataType dt = tma_dtype(g.dtype);
+  const uint64_t a_d0 = g.a_mn ? g.M : g.K;
+  const uint64_t a_d1 = g.a_mn ? g.K : g.M;
+  const uint64_t a_bs = g.batch > 1 ? g.a_batch_stride : g.lda * a_d1;
+  *ma = make_tmap_3d(g.A, dt, 2, a_d0, a_d1, g.batch, g.lda, a_bs, 64, g.a_mn ? 64 : kBM);
+  const uint64_t b_d0 = g.b_mn ? g.N : g.K;
+  const uint64_t b_d1 = g.b_mn ? g.K : g.N;
+  const uint64_t b_bs = g.batch > 1 ? g.b_batch_stride : g.ldb * b_d1;
+  *mb = make_tmap_3d(g.B, dt, 2, b_d0, b_d1, g.batch, g.ldb, b_bs, 64, g.b_mn ? 64 : kBN);
+}
+
+GemmShape make_shape(const GemmArgs& g) {
+  GemmShape s;
+  s.M = g.M;
+  s.N = g.N;
+  s.K = g.K;
+  s.batch = g.batch;
+  s.num_m = (g.M + kBM - 1) / kBM;
+  s.num_n = (g.N + kBN - 1) / kBN;
+  s.num_kb = (g.K + kBK - 1) / kBK;
+  s.a_mn = g.a_mn;
+  s.b_mn = g.b_mn;
+  s.in_bf16 = g.dtype == kDtypeBF16 ? 1 : 0;
+  s.group_m = 16;
+  s.err = g.err;
+  return s;
+}
+
+const char* check_gemm_args(const GemmArgs& g) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0 || g.batch <= 0) return "empty GEMM";
+  if ((reinterpret_cast<uintptr_t>(g.A) & 15) || (reinterpret_cast<uintptr_t>(g.B) & 15))
+    return "operand base not 16-byte aligned";
+  if ((g.lda * 2) % 16 || (g.ldb * 2) % 16) return "operand row stride not a multiple of 16 bytes";
+  if (g.batch > 1 && (((g.a_batch_stride * 2) % 16) || ((g.b_batch_stride * 2) % 16)))
+    return "operand batch stride not a multiple of 16 bytes";
+  return nullptr;
+}
+
+template <typename OutT>
+static int launch_store(const GemmArgs& g, cudaStream_t stream) {
+  CUtensorMap ma, mb;
+  make_operand_maps(g, &ma, &mb);
+  GemmShape s = make_shape(g);
+  StoreEpilogue<OutT> epi;
+  epi.C = reinterpret_cast<OutT*>(g.C);
+  epi.ldc = g.ldc;
+  epi.batch_stride = g.c_batch_stride;
+  epi.act = g.act;
+  const int esz = sizeof(OutT);
+  epi.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * esz) % 16 == 0) &&
+               (g.batch == 1 || (g.c_batch_stride * esz) % 16 == 0);
+  auto kernel = gemm_tc_kernel<StoreEpilogue<OutT>>;
+  static unsigned long long attr_set = 0;  // one bit per device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> dev & 1ull)) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    attr_set |= 1ull << dev;
+  }
+  const int tiles = s.num_m * s.num_n * s.batch;
+  const int grid = tiles < g.num_sms ? tiles : g.num_sms;
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, s, epi);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
+  if (check_gemm_args(g)) return -1;
+  switch (g.out_dtype) {
+    case kDtypeBF16:
+      return launch_store<__nv_bfloat16>(g, stream);
+    case kDtypeF16:
+      return launch_store<__half>(g, stream);
+    case kDtypeF32:
+      return launch_store<float>(g, stream);
+    default:
+      return -1;
+  }
+}
+
+}  // namespace es

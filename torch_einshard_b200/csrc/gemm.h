@@ -1,0 +1,38 @@
+// Plain C++ interface of the native GEMM family (no torch types), shared by the
+// torch bindings and the fused compute+collective kernels.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace es {
+
+enum Dtype : int { kDtypeBF16 = 0, kDtypeF16 = 1, kDtypeF32 = 2 };
+
+// C[b] = act(A[b] @ B[b]) with A: [batch, M, K], B: [batch, K, N], C: [batch, M, N] row-major.
+// a_mn = 0: A is K-contiguous, lda = elements between consecutive m rows.
+// a_mn = 1: A is M-contiguous, lda = elements between consecutive k rows.
+// b_mn = 0: B is K-contiguous, ldb = elements between consecutive n columns.
+// b_mn = 1: B is N-contiguous, ldb = elements between consecutive k rows.
+struct GemmArgs {
+  const void* A = nullptr;
+  const void* B = nullptr;
+  void* C = nullptr;
+  int dtype = kDtypeBF16;
+  int out_dtype = kDtypeBF16;
+  int batch = 1, M = 0, N = 0, K = 0;
+  int a_mn = 0;
+  long long lda = 0, a_batch_stride = 0;
+  int b_mn = 0;
+  long long ldb = 0, b_batch_stride = 0;
+  long long ldc = 0, c_batch_stride = 0;
+  int act = 0;
+  int* err = nullptr;
+  int num_sms = 148;
+};
+
+const char* check_gemm_args(const GemmArgs& g);
+int gemm_launch(const GemmArgs& g, cudaStream_t stream);
+
+}  // namespace es

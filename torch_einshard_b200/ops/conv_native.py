@@ -1,0 +1,17 @@
+"""Native implicit-GEMM convolution for ``einconv`` (tcgen05, NHWC, no im2col).
+
+``try_conv`` returns ``None`` when the call is outside the native envelope
+(not CUDA bf16/fp16, not 2-D, dilation != 1, channel counts the TMA boxes
+cannot address) and ``einconv`` then uses ``torch.nn.functional``.
+"""
+
+__all__ = ["try_conv"]
+
+
+def try_conv(x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation):
+    from . import _native
+    mod = _native.module()
+    if mod is None or not hasattr(mod, "conv2d_implicit") or not x.is_cuda:
+        return None
+    from .conv_impl import conv2d_nhwc
+    return conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation)

@@ -1,0 +1,19 @@
+"""Native Stockham FFT along one axis for CUDA complex tensors.
+
+``try_fft`` returns ``None`` when the native kernels do not cover the call
+(not CUDA complex64, length not a supported power of two) and the caller then
+uses ``torch.fft``.
+"""
+
+__all__ = ["try_fft"]
+
+
+def try_fft(x, dim, inverse):
+    from . import _native
+    if not x.is_cuda:
+        return None
+    mod = _native.module()
+    if mod is None or not hasattr(mod, "fft_c2c"):
+        return None
+    from .fft_impl import fft_c2c
+    return fft_c2c(mod, x, dim, inverse)

@@ -1,0 +1,90 @@
+"""Native batched GEMM with autograd: ``matmul(A[B,M,K], B[B,K,N]) -> [B,M,N]``.
+
+Forward and both backward products run on the tcgen05 kernel
+(``csrc/gemm_tc.cuh``).  Transposed operands are passed as strided views: the
+kernel reads either operand K-major or MN-major, so ``dA = dC @ B^T`` and
+``dB = A^T @ dC`` need no transpose copies.  Operands whose strides the TMA
+engine cannot address (row stride not a multiple of 16 bytes, unaligned base)
+are first copied into a padded buffer.
+"""
+
+import torch
+
+from . import _native
+
+__all__ = ["eligible", "matmul", "native_bmm"]
+
+_NATIVE_DTYPES = (torch.bfloat16, torch.float16)
+_ACTS = {None: 0, "silu": 1}
+_OUT_CODE = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+
+
+def eligible(x, y) -> bool:
+    """True when the contraction of ``x`` and ``y`` should run natively."""
+    if not (x.is_cuda and y.is_cuda) or x.dtype != y.dtype or x.dtype not in _NATIVE_DTYPES:
+        return False
+    if _native.available():
+        return True
+    if _native.allow_fallback():
+        return False
+    _native.require()  # raises: native extension missing on a CUDA machine
+    return False
+
+
+def _tma_ready(t: torch.Tensor, contiguous_dim: int) -> bool:
+    other = 2 if contiguous_dim == 1 else 1
+    if t.stride(contiguous_dim) != 1 and t.size(contiguous_dim) > 1:
+        return False
+    if t.data_ptr() % 16:
+        return False
+    row = t.stride(other) if t.size(other) > 1 else t.size(contiguous_dim)
+    if (row * t.element_size()) % 16:
+        return False
+    if t.size(0) > 1 and (t.stride(0) * t.element_size()) % 16:
+        return False
+    return True
+
+
+def _padded_copy(t: torch.Tensor) -> torch.Tensor:
+    """Contiguous copy whose last-dim row pitch is padded to 16 bytes."""
+    b, r, c = t.shape
+    align = 16 // t.element_size()
+    pitch = -(-c // align) * align
+    buf = t.new_zeros((b, r, pitch))
+    buf[:, :, :c].copy_(t)
+    return buf[:, :, :c]
+
+
+def _prepare(t: torch.Tensor) -> torch.Tensor:
+    # either the last dim (row-major) or the middle dim (column-major) must be contiguous
+    if _tma_ready(t, 2) or _tma_ready(t, 1):
+        return t
+    t = t.contiguous()
+    return t if _tma_ready(t, 2) else _padded_copy(t)
+
+
+def native_bmm(a: torch.Tensor, b: torch.Tensor, out_dtype=None, act=None) -> torch.Tensor:
+    mod = _native.require()
+    a, b = _prepare(a), _prepare(b)
+    out_dtype = a.dtype if out_dtype is None else out_dtype
+    return mod.gemm(a, b, _OUT_CODE[out_dtype], _ACTS[act], _native.error_word(a.device))
+
+
+class _NativeMatmul(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, a, b):
+        ctx.save_for_backward(a, b)
+        return native_bmm(a, b)
+
+    @staticmethod
+    def backward(ctx, grad):
+        a, b = ctx.saved_tensors
+        grad_a = native_bmm(grad, b.transpose(1, 2)) if ctx.needs_input_grad[0] else None
+        grad_b = native_bmm(a.transpose(1, 2), grad) if ctx.needs_input_grad[1] else None
+        return grad_a, grad_b
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    if a.requires_grad or b.requires_grad:
+        return _NativeMatmul.apply(a, b)
+    return native_bmm(a, b)
