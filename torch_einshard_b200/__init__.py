@@ -18,6 +18,7 @@ from .ops.halo import einhalo, einwindow
 from .ops.roll import einroll
 from .parallel.executor import distributed_1d
 from .parallel.mesh import CompoundDeviceMesh, wrap_mesh
+from .parallel.setup import setup_native_comm
 from .params import (
     NativeGradReductionHandle,
     ParameterGradComm,

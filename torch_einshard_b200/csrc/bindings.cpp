@@ -3,9 +3,14 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <atomic>
+
 #include "gemm.h"
 
 namespace {
+
+// Number of native kernel launches issued through these bindings (all devices).
+std::atomic<long long> g_launches{0};
 
 int dtype_code(at::ScalarType t) {
   switch (t) {
@@ -77,6 +82,7 @@ void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t
   TORCH_CHECK(why == nullptr, "einshard native gemm: ", why ? why : "");
   const int rc = es::gemm_launch(g, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "einshard native gemm: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
 at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, int64_t out_dtype, int64_t act, const at::Tensor& err) {
@@ -96,4 +102,5 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "einshard sm_100a native kernels";
   m.def("gemm", &gemm, "C = act(A @ B), tcgen05 GEMM (A [B,M,K], B [B,K,N])");
   m.def("gemm_out", &gemm_out, "gemm into a preallocated row-major output");
+  m.def("launch_count", []() { return g_launches.load(); }, "native kernel launches so far");
 }

@@ -1,0 +1,49 @@
+"""Tensor-parallel MLP written with einshard formulas (the flagship benchmark model).
+
+    h   = einshard("b n c, h/tp c -> b n h/tp", x, w1)        column parallel
+    a   = silu(h)
+    y_p = einshard("b n h/tp, c h/tp -> b n c // tp", a, w2)  row parallel, partial sums
+    y   = einshard("b n c // tp -> b n c", y_p)                all-reduce over tp
+
+The column-parallel step plans ``identity_forward_allreduce_backward`` on x
+(its gradient is all-reduced in backward) and the row-parallel step ends with
+an all-reduce; on the native path both the forward all-reduce and the
+backward input-gradient all-reduce are fused into the GEMM that produces them.
+"""
+
+import torch
+import torch.nn.functional as F
+
+from ..api import einshard
+
+__all__ = ["TPMLP", "tp_mlp_flops"]
+
+
+class TPMLP(torch.nn.Module):
+    def __init__(self, c, h, mesh, *, tp_dim="tp", dtype=torch.bfloat16, device=None, std=0.02, seed=0):
+        super().__init__()
+        tp = mesh[tp_dim].size() if hasattr(mesh[tp_dim], "size") else 1
+        if h % tp:
+            raise ValueError(f"hidden size {h} is not divisible by tp={tp}")
+        self.mesh, self.tp_dim, self.tp = mesh, tp_dim, tp
+        local = h // tp
+        gen = torch.Generator(device="cpu").manual_seed(seed)
+        rank = mesh[tp_dim].get_local_rank() if hasattr(mesh[tp_dim], "get_local_rank") else 0
+        # every rank draws the full weights from the same seed and keeps its shard
+        full1 = torch.empty(h, c, dtype=torch.float32).normal_(0.0, std, generator=gen)
+        full2 = torch.empty(c, h, dtype=torch.float32).normal_(0.0, std, generator=gen)
+        self.w1 = torch.nn.Parameter(full1[rank * local:(rank + 1) * local].to(device=device, dtype=dtype))
+        self.w2 = torch.nn.Parameter(full2[:, rank * local:(rank + 1) * local].contiguous().to(device=device, dtype=dtype))
+
+    def forward(self, x):
+        t = self.tp_dim
+        h = einshard(f"b n c, h/{t} c -> b n h/{t}", x, self.w1, mesh=self.mesh)
+        a = F.silu(h)
+        y = einshard(f"b n h/{t}, c h/{t} -> b n c // {t}", a, self.w2, mesh=self.mesh)
+        return einshard(f"b n c // {t} -> b n c", y, mesh=self.mesh)
+
+
+def tp_mlp_flops(b, n, c, h, *, backward=True):
+    """Whole-job FLOPs of one step (2 GEMMs forward, 4 more in backward)."""
+    gemm = 2.0 * b * n * c * h
+    return gemm * (6 if backward else 2)

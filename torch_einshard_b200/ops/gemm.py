@@ -80,7 +80,14 @@ class _NativeMatmul(torch.autograd.Function):
     def backward(ctx, grad):
         a, b = ctx.saved_tensors
         grad_a = native_bmm(grad, b.transpose(1, 2)) if ctx.needs_input_grad[0] else None
-        grad_b = native_bmm(a.transpose(1, 2), grad) if ctx.needs_input_grad[1] else None
+        grad_b = None
+        if ctx.needs_input_grad[1]:
+            if b.stride(1) == 1 and b.size(1) > 1:
+                # b is a transposed view (e.g. a [out, in] weight): produce its gradient
+                # directly in that memory order, (dC^T A)^T, so no copy is needed later
+                grad_b = native_bmm(grad.transpose(1, 2), a).transpose(1, 2)
+            else:
+                grad_b = native_bmm(a.transpose(1, 2), grad)
         return grad_a, grad_b
 
 
