@@ -1,0 +1,75 @@
+"""Fused GEMM + NVLink all-reduce and the TP-MLP path on 2+ GPUs."""
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+    pytest.skip("needs 2 or more CUDA devices", allow_module_level=True)
+
+from gpu_harness import run_gpus  # noqa: E402
+
+
+def _fused(rank, world):
+    import torch.distributed as dist
+    from torch.distributed.device_mesh import init_device_mesh
+
+    import torch_einshard_b200 as es
+    from torch_einshard_b200.ops import _native, gemm
+    from torch_einshard_b200.ops.fused_native import gemm_allreduce
+    from torch_einshard_b200.parallel import native_comm
+    from torch_einshard_b200.models.tp_mlp import TPMLP
+
+    mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
+    assert es.setup_native_comm(mesh)
+    group = mesh["tp"].get_group()
+    comm = native_comm.communicator_for(group)
+
+    # raw fused kernel: ragged shapes, repeated calls (epochs), both operand layouts
+    for (m, n, k) in [(256, 512, 128), (300, 700, 136), (1024, 2048, 512)]:
+        for _ in range(2):
+            a = torch.randn(1, m, k, device="cuda", dtype=torch.bfloat16) * (rank + 1)
+            b = torch.randn(1, n, k, device="cuda", dtype=torch.bfloat16).transpose(1, 2)
+            got = gemm_allreduce(comm, a, b)
+            want = gemm.native_bmm(a, b).float()
+            dist.all_reduce(want, group=group)
+            scale = want.abs().max().item() + 1
+            err = (got.float() - want).abs().max().item()
+            assert err < 3e-2 * scale, (m, n, k, err, scale)
+    torch.cuda.synchronize()
+    _native.check_errors()
+
+    # TP-MLP through the public API: fused native path vs the NCCL-only path
+    torch.manual_seed(0)
+    model = TPMLP(512, 2048, mesh, device="cuda")
+    x = torch.randn(2, 256, 512, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = model(x)
+    assert [s.name for s in es.last_plan()] == ["rank_local_einsum", "allreduce_forward_identity_backward"]
+    dy = torch.randn_like(y)
+    y.backward(dy)
+    got = (y.detach().float(), x.grad.float(), model.w1.grad.float(), model.w2.grad.float())
+
+    native_comm.disable()
+    x2 = x.detach().clone().requires_grad_(True)
+    model.w1.grad = model.w2.grad = None
+    y2 = model(x2)
+    y2.backward(dy)
+    want = (y2.detach().float(), x2.grad.float(), model.w1.grad.float(), model.w2.grad.float())
+    native_comm._state["enabled"] = True
+    for g, w in zip(got, want):
+        scale = w.abs().max().item() + 1e-3
+        assert (g - w).abs().max().item() < 3e-2 * scale
+    torch.cuda.synchronize()
+    _native.check_errors()
+
+
+def test_fused_gemm_allreduce_2gpu():
+    run_gpus(_fused, 2)
+
+
+def test_fused_gemm_allreduce_all_gpus():
+    n = torch.cuda.device_count()
+    if n < 4:
+        pytest.skip("needs 4+ GPUs")
+    run_gpus(_fused, min(n, 8))

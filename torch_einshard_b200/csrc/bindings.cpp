@@ -5,7 +5,12 @@
 
 #include <atomic>
 
+#include "comm.h"
 #include "gemm.h"
+#include "gemm_ar.h"
+
+#include <memory>
+#include <vector>
 
 namespace {
 
@@ -51,7 +56,17 @@ void operand_layout(const at::Tensor& t, bool is_a, int& mn, long long& ld, long
   bstride = t.stride(0);
 }
 
+es::GemmArgs gemm_args(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t act, const at::Tensor& err);
+
 void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t act, const at::Tensor& err) {
+  const c10::cuda::CUDAGuard guard(a.device());
+  es::GemmArgs g = gemm_args(a, b, out, act, err);
+  const int rc = es::gemm_launch(g, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard native gemm: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+es::GemmArgs gemm_args(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t act, const at::Tensor& err) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "einshard native gemm: CUDA tensors required");
   TORCH_CHECK(a.dim() == 3 && b.dim() == 3 && out.dim() == 3, "einshard native gemm: 3-D operands required");
   TORCH_CHECK(a.scalar_type() == b.scalar_type(), "einshard native gemm: operand dtypes differ");
@@ -59,7 +74,6 @@ void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t
   TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == a.size(1) && out.size(2) == b.size(2),
               "einshard native gemm: output shape mismatch");
   TORCH_CHECK(out.stride(2) == 1, "einshard native gemm: output must be row-major");
-  const c10::cuda::CUDAGuard guard(a.device());
   es::GemmArgs g;
   g.A = a.data_ptr();
   g.B = b.data_ptr();
@@ -80,9 +94,7 @@ void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t
   g.num_sms = num_sms(a.get_device());
   const char* why = es::check_gemm_args(g);
   TORCH_CHECK(why == nullptr, "einshard native gemm: ", why ? why : "");
-  const int rc = es::gemm_launch(g, at::cuda::getCurrentCUDAStream());
-  TORCH_CHECK(rc == 0, "einshard native gemm: launch failed (", rc, ")");
-  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return g;
 }
 
 at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, int64_t out_dtype, int64_t act, const at::Tensor& err) {
@@ -96,11 +108,180 @@ void gemm_out(const at::Tensor& a, const at::Tensor& b, at::Tensor out, int64_t 
   run_gemm(a, b, out, act, err);
 }
 
+
+// ------------------------------------------------------------------ communicators
+
+struct HostComm {
+  int rank = 0, size = 1, device = 0;
+  void* local = nullptr;
+  std::vector<void*> bases;  // per rank: flags base (peer-mapped for peers)
+  size_t data_bytes = 0;
+  int epoch = 0;
+  uint32_t bar = 0;
+  uint32_t arrive = 0;
+  bool open = false;
+};
+
+std::vector<std::unique_ptr<HostComm>> g_comms;
+
+HostComm& comm_ref(int64_t id) {
+  TORCH_CHECK(id >= 0 && id < (int64_t)g_comms.size() && g_comms[id], "einshard comm: bad communicator id");
+  return *g_comms[id];
+}
+
+py::tuple comm_create(int64_t data_bytes, int64_t device) {
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
+  auto hc = std::make_unique<HostComm>();
+  char handle[64];
+  hc->local = es::comm_alloc(static_cast<size_t>(data_bytes), handle);
+  TORCH_CHECK(hc->local != nullptr, "einshard comm: cudaMalloc/IPC handle failed");
+  hc->data_bytes = static_cast<size_t>(data_bytes);
+  hc->device = static_cast<int>(device);
+  g_comms.push_back(std::move(hc));
+  return py::make_tuple(static_cast<int64_t>(g_comms.size() - 1), py::bytes(handle, 64));
+}
+
+void comm_connect(int64_t id, int64_t rank, std::vector<std::string> handles) {
+  HostComm& hc = comm_ref(id);
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(hc.device));
+  TORCH_CHECK((int)handles.size() <= es::kMaxRanks, "einshard comm: at most 8 ranks");
+  hc.rank = static_cast<int>(rank);
+  hc.size = static_cast<int>(handles.size());
+  hc.bases.assign(hc.size, nullptr);
+  for (int p = 0; p < hc.size; ++p) {
+    if (p == hc.rank) {
+      hc.bases[p] = hc.local;
+      continue;
+    }
+    TORCH_CHECK(handles[p].size() == 64, "einshard comm: bad IPC handle");
+    hc.bases[p] = es::comm_open_peer(handles[p].data());
+    TORCH_CHECK(hc.bases[p] != nullptr, "einshard comm: cudaIpcOpenMemHandle failed for rank ", p);
+  }
+  hc.open = true;
+}
+
+void comm_destroy(int64_t id) {
+  HostComm& hc = comm_ref(id);
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(hc.device));
+  cudaDeviceSynchronize();
+  for (int p = 0; p < hc.size; ++p)
+    if (p != hc.rank) es::comm_close_peer(hc.bases[p]);
+  es::comm_free(hc.local);
+  g_comms[id].reset();
+}
+
+es::CommDev make_dev(HostComm& hc, const at::Tensor& err, int nblocks, int nbarriers) {
+  es::CommDev d;
+  d.rank = hc.rank;
+  d.size = hc.size;
+  for (int p = 0; p < es::kMaxRanks; ++p) {
+    d.flags[p] = p < hc.size ? reinterpret_cast<uint64_t>(hc.bases[p]) : 0;
+    d.data[p] = p < hc.size ? reinterpret_cast<uint64_t>(hc.bases[p]) + es::kFlagBytes : 0;
+  }
+  d.epoch = ++hc.epoch;
+  d.bar_base = hc.bar;
+  d.arrive_base = 0;
+  d.err = err.data_ptr<int>();
+  hc.bar += static_cast<uint32_t>(nblocks * nbarriers);
+  return d;
+}
+
+int es_dtype(const at::Tensor& t) {
+  return t.scalar_type() == at::kBFloat16 ? 0 : t.scalar_type() == at::kHalf ? 1 : 2;
+}
+
+void comm_all_reduce(int64_t id, at::Tensor buf, double scale, int64_t nblocks, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open && buf.is_cuda() && buf.is_contiguous(), "einshard comm all_reduce: bad arguments");
+  TORCH_CHECK(buf.scalar_type() == at::kBFloat16 || buf.scalar_type() == at::kHalf || buf.scalar_type() == at::kFloat,
+              "einshard comm all_reduce: dtype");
+  const int64_t bytes = buf.numel() * buf.element_size();
+  const int64_t per = (bytes / 16 + hc.size - 1) / hc.size * 16;
+  TORCH_CHECK(bytes % 16 == 0 && (size_t)(bytes + per) <= hc.data_bytes, "einshard comm all_reduce: size");
+  const c10::cuda::CUDAGuard guard(buf.device());
+  es::CommDev d = make_dev(hc, err, static_cast<int>(nblocks), 3);
+  const int rc = es::comm_all_reduce(d, buf.data_ptr(), buf.numel(), es_dtype(buf), static_cast<float>(scale),
+                                     static_cast<int>(nblocks), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard comm all_reduce: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// boxes: list of (src_rank, (d0,d1,d2,d3), src_off, dst_off, (s0,s1,s2), (t0,t1,t2)) in bytes for offsets/strides
+void comm_copy(int64_t id, at::Tensor src, int64_t stage_bytes, at::Tensor dst, py::list boxes, int64_t esize,
+               bool reduce, bool accumulate, double scale, bool sequential, int64_t nblocks, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open, "einshard comm: not connected");
+  TORCH_CHECK((size_t)stage_bytes <= hc.data_bytes, "einshard comm copy: staging exceeds buffer");
+  TORCH_CHECK((int)py::len(boxes) <= es::kMaxBoxes, "einshard comm copy: too many boxes");
+  es::CopyPlan plan;
+  memset(&plan, 0, sizeof(plan));
+  plan.nbox = static_cast<int>(py::len(boxes));
+  plan.esize = static_cast<int>(esize);
+  plan.dtype = es_dtype(dst);
+  plan.accumulate = accumulate ? 1 : 0;
+  plan.scale = static_cast<float>(scale);
+  plan.sequential = sequential ? 1 : 0;
+  for (int i = 0; i < plan.nbox; ++i) {
+    py::tuple b = boxes[i].cast<py::tuple>();
+    es::CopyBox& x = plan.box[i];
+    x.src_rank = b[0].cast<int>();
+    py::tuple dims = b[1].cast<py::tuple>();
+    for (int k = 0; k < 4; ++k) x.dims[k] = dims[k].cast<int>();
+    x.src_off = b[2].cast<long long>();
+    x.dst_off = b[3].cast<long long>();
+    py::tuple ss = b[4].cast<py::tuple>();
+    py::tuple ds = b[5].cast<py::tuple>();
+    for (int k = 0; k < 3; ++k) {
+      x.sstr[k] = ss[k].cast<long long>();
+      x.dstr[k] = ds[k].cast<long long>();
+    }
+    x.sstr[3] = x.dstr[3] = esize;
+  }
+  const c10::cuda::CUDAGuard guard(dst.device());
+  const int nbar = 2 + (sequential ? plan.nbox : 0);
+  es::CommDev d = make_dev(hc, err, static_cast<int>(nblocks), nbar);
+  const void* sp = stage_bytes > 0 ? src.data_ptr() : nullptr;
+  const int rc = reduce ? es::comm_stage_and_reduce(d, sp, stage_bytes, 0, dst.data_ptr(), plan, static_cast<int>(nblocks),
+                                                    at::cuda::getCurrentCUDAStream())
+                        : es::comm_stage_and_copy(d, sp, stage_bytes, 0, dst.data_ptr(), plan, static_cast<int>(nblocks),
+                                                  at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard comm copy: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// out = all-reduce over the communicator's ranks of (a @ b); one fused kernel.
+void gemm_allreduce(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open, "einshard fused gemm+allreduce: communicator not connected");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && a.size(0) == 1, "einshard fused gemm+allreduce: bf16, batch 1");
+  const c10::cuda::CUDAGuard guard(a.device());
+  es::GemmArgs g = gemm_args(a, b, out, 0, err);
+  const long long tiles = (long long)((g.M + 127) / 128) * ((g.N + 255) / 256);
+  TORCH_CHECK(tiles * 128 * 256 * 2 <= (long long)hc.data_bytes && tiles <= es::kMaxTiles,
+              "einshard fused gemm+allreduce: output too large for the symmetric buffer");
+  const int grid = es::gemm_allreduce_grid(g);
+  es::CommDev d = make_dev(hc, err, 0, 0);
+  d.arrive_base = hc.arrive;
+  hc.arrive += static_cast<uint32_t>(grid);
+  const int rc = es::gemm_allreduce_launch(g, d, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard fused gemm+allreduce: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+int64_t comm_data_bytes(int64_t id) { return static_cast<int64_t>(comm_ref(id).data_bytes); }
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "einshard sm_100a native kernels";
   m.def("gemm", &gemm, "C = act(A @ B), tcgen05 GEMM (A [B,M,K], B [B,K,N])");
   m.def("gemm_out", &gemm_out, "gemm into a preallocated row-major output");
+  m.def("comm_create", &comm_create, "allocate a symmetric buffer; returns (id, ipc handle)");
+  m.def("comm_connect", &comm_connect, "map every rank's buffer");
+  m.def("comm_destroy", &comm_destroy, "unmap and free");
+  m.def("comm_all_reduce", &comm_all_reduce, "two-shot NVLink all-reduce in place");
+  m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)");
+  m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
+  m.def("comm_data_bytes", &comm_data_bytes, "data capacity of a communicator");
   m.def("launch_count", []() { return g_launches.load(); }, "native kernel launches so far");
 }

@@ -33,6 +33,7 @@ struct GemmArgs {
 };
 
 const char* check_gemm_args(const GemmArgs& g);
+void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb);
 int gemm_launch(const GemmArgs& g, cudaStream_t stream);
 
 }  // namespace es

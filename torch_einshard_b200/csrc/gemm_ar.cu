@@ -1,0 +1,269 @@
+// GEMM fused with an all-reduce of its output over NVLink (one cooperative kernel).
+//
+//   C = sum over ranks of (A_r @ B_r)      every rank gets the full C
+//
+// The tcgen05 mainloop of gemm_tc.cuh computes this rank's partial tile into
+// TMEM.  Tile t is owned by rank t % P:
+//   * non-owners store their bf16 partial tile into their own symmetric buffer
+//     (chunk-interleaved so that a warp's NVLink reads are contiguous) and set
+//     partial[t] = epoch in their flag region;
+//   * the owner waits for partial[t] of every peer, sums the peers' partials with
+//     its own fp32 accumulator read straight from TMEM, writes C's tile locally
+//     and a reduced copy into its buffer, then sets reduced[t] = epoch;
+//   * non-owners keep tile t in a small queue and, between later tiles (and at
+//     the end), copy the owner's reduced tile into their own C.
+// Only reads cross NVLink; every rank writes only its own memory.  The epoch
+// protocol of comm.h makes buffer reuse across calls safe; every wait is bounded.
+#include <cuda_bf16.h>
+
+#include "comm.h"
+#include "gemm.h"
+#include "gemm_tc.cuh"
+#include "gemm_ar.h"
+
+namespace es {
+
+GemmShape make_shape(const GemmArgs& g);
+
+constexpr int kTileBytes = kBM * kBN * 2;  // bf16 partial / reduced tile
+constexpr int kQueue = 8;                  // pending pulls per CTA
+// epilogue scratch slots in SharedState::epi
+constexpr int kQHead = 0, kQTail = 1, kDecision = 2, kAbortEpi = 3, kQBase = 8;
+
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+struct ArEpilogue {
+  CommDev c;
+  __nv_bfloat16* C;
+  long long ldc;
+  int vec_ok;  // C rows 16-byte aligned
+  int* sm;     // SharedState::epi
+
+  __device__ __forceinline__ int* flag(int rank, int slot) const { return reinterpret_cast<int*>(c.flags[rank]) + slot; }
+  __device__ __forceinline__ uint8_t* tile_buf(int rank, int t) const {
+    return reinterpret_cast<uint8_t*>(c.data[rank]) + static_cast<size_t>(t) * kTileBytes;
+  }
+
+  __device__ void setup(SharedState* st, const GemmShape&) {
+    sm = st->epi;
+    // peers must be done reading our buffer from the previous operation
+    if (threadIdx.x == 64) {
+      for (int p = 0; p < c.size; ++p) {
+        if (p == c.rank) continue;
+        if (!wait_flag_geq(flag(p, kFlagDone), c.epoch - 1, c.err, kErrWaitPeerFlag)) {
+          sm[kAbortEpi] = 1;
+          break;
+        }
+      }
+    }
+  }
+
+  // copy the reduced tile t (owner o) into this rank's C
+  __device__ void pull_tile(int t, const GemmShape& s, int row_in_tile) {
+    const TileCoord tc = tile_coord(s, t);
+    const int row = tc.m0 + row_in_tile;
+    const uint8_t* src = tile_buf(t % c.size, t);
+    if (row >= s.M) return;
+    __nv_bfloat16* crow = C + static_cast<long long>(row) * ldc;
+#pragma unroll 8
+    for (int j = 0; j < kBN / 8; ++j) {
+      const int col = tc.n0 + j * 8;
+      if (col >= s.N) break;
+      const uint4 v = *reinterpret_cast<const uint4*>(src + (static_cast<size_t>(j) * kBM + row_in_tile) * 16);
+      if (col + 8 <= s.N && vec_ok) {
+        *reinterpret_cast<uint4*>(crow + col) = v;
+      } else {
+        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
+        for (int k = 0; k < 8 && col + k < s.N; ++k) crow[col + k] = h[k];
+      }
+    }
+  }
+
+  // Service the pull queue.  blocking: wait (bounded) for the oldest entry.
+  // Returns false when the kernel must abort.
+  __device__ bool service(const GemmShape& s, int e, bool blocking, int max_items) {
+    for (int done = 0; done < max_items; ++done) {
+      if (e == 0) {
+        int decision = -1;
+        if (sm[kQHead] != sm[kQTail]) {
+          const int t = sm[kQBase + (sm[kQHead] % kQueue)];
+          const int* f = flag(t % c.size, kFlagTile0 + kMaxTiles + t);
+          bool ready = ld_acquire_sys(f) >= c.epoch;
+          if (!ready && blocking) {
+            ready = wait_flag_geq(f, c.epoch, c.err, kErrWaitPeerFlag);
+            if (!ready) sm[kAbortEpi] = 1;
+          }
+          if (ready) decision = t;
+        }
+        sm[kDecision] = decision;
+      }
+      epi_bar();
+      const int t = sm[kDecision];
+      if (sm[kAbortEpi]) return false;
+      if (t < 0) return true;
+      pull_tile(t, s, e);
+      epi_bar();
+      if (e == 0) ++sm[kQHead];
+    }
+    return true;
+  }
+
+  __device__ bool tile(const EpiTile& et, const GemmShape& s, volatile int* abort_flag) {
+    const int e = et.row;  // epilogue thread index == tile row
+    const int t = et.t;
+    if (sm[kAbortEpi]) return false;
+    const bool mine = (t % c.size) == c.rank;
+    uint8_t* my_buf = tile_buf(c.rank, t);
+    if (!mine) {
+#pragma unroll 1
+      for (int chunk = 0; chunk < kBN / 32; ++chunk) {
+        uint32_t r[32];
+        tmem_ld32(et.tmem + chunk * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const uint4 v = make_uint4(pack_bf16(__uint_as_float(r[8 * k + 0]), __uint_as_float(r[8 * k + 1])),
+                                     pack_bf16(__uint_as_float(r[8 * k + 2]), __uint_as_float(r[8 * k + 3])),
+                                     pack_bf16(__uint_as_float(r[8 * k + 4]), __uint_as_float(r[8 * k + 5])),
+                                     pack_bf16(__uint_as_float(r[8 * k + 6]), __uint_as_float(r[8 * k + 7])));
+          *reinterpret_cast<uint4*>(my_buf + (static_cast<size_t>(chunk * 4 + k) * kBM + e) * 16) = v;
+        }
+      }
+      epi_bar();
+      if (e == 0) {
+        fence_acq_rel_sys();
+        st_release_sys(flag(c.rank, kFlagTile0 + t), c.epoch);
+        // queue the pull of the reduced tile; make room first if the queue is full
+        sm[kQBase + (sm[kQTail] % kQueue)] = t;
+        ++sm[kQTail];
+      }
+      epi_bar();
+      const bool full = (sm[kQTail] - sm[kQHead]) >= kQueue;
+      return service(s, e, full, full ? 1 : 2);
+    }
+    // owner: gather every peer's partial of tile t
+    if (e == 0) {
+      for (int p = 0; p < c.size; ++p) {
+        if (p == c.rank) continue;
+        if (!wait_flag_geq(flag(p, kFlagTile0 + t), c.epoch, c.err, kErrWaitPeerFlag)) {
+          sm[kAbortEpi] = 1;
+          *abort_flag = 1;
+          break;
+        }
+      }
+    }
+    epi_bar();
+    if (sm[kAbortEpi]) return false;
+    const int row = et.c.m0 + e;
+    __nv_bfloat16* crow = C + static_cast<long long>(row) * ldc;
+#pragma unroll 1
+    for (int chunk = 0; chunk < kBN / 32; ++chunk) {
+      uint32_t r[32];
+      tmem_ld32(et.tmem + chunk * 32, r);
+      tmem_ld_wait();
+      float acc[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(r[i]);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 v[kMaxRanks - 1];
+        const size_t off = (static_cast<size_t>(chunk * 4 + q) * kBM + e) * 16;
+#pragma unroll
+        for (int k = 1; k < kMaxRanks; ++k)
+          if (k < c.size) v[k - 1] = *reinterpret_cast<const uint4*>(tile_buf((c.rank + k) % c.size, t) + off);
+#pragma unroll
+        for (int k = 1; k < kMaxRanks; ++k) {
+          if (k >= c.size) break;
+          const uint32_t w[4] = {v[k - 1].x, v[k - 1].y, v[k - 1].z, v[k - 1].w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+            acc[8 * q + 2 * j] += f.x;
+            acc[8 * q + 2 * j + 1] += f.y;
+          }
+        }
+      }
+      uint4 o[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        o[q] = make_uint4(pack_bf16(acc[8 * q + 0], acc[8 * q + 1]), pack_bf16(acc[8 * q + 2], acc[8 * q + 3]),
+                          pack_bf16(acc[8 * q + 4], acc[8 * q + 5]), pack_bf16(acc[8 * q + 6], acc[8 * q + 7]));
+        *reinterpret_cast<uint4*>(my_buf + (static_cast<size_t>(chunk * 4 + q) * kBM + e) * 16) = o[q];
+      }
+      const int col0 = et.c.n0 + chunk * 32;
+      if (row < s.M && col0 < s.N) {
+        if (col0 + 32 <= s.N && vec_ok) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(crow + col0 + 8 * q) = o[q];
+        } else {
+          for (int q = 0; q < 4; ++q) {
+            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&o[q]);
+            for (int k = 0; k < 8 && col0 + 8 * q + k < s.N; ++k) crow[col0 + 8 * q + k] = h[k];
+          }
+        }
+      }
+    }
+    epi_bar();
+    if (e == 0) {
+      fence_acq_rel_sys();
+      st_release_sys(flag(c.rank, kFlagTile0 + kMaxTiles + t), c.epoch);
+    }
+    return service(s, e, false, 2);
+  }
+
+  __device__ void finish(const GemmShape& s, volatile int* abort_flag) {
+    const int e = threadIdx.x - 64;
+    bool ok = !sm[kAbortEpi] && !*abort_flag;
+    if (ok) {
+      while (true) {
+        epi_bar();
+        if (sm[kQHead] == sm[kQTail]) break;
+        if (!service(s, e, true, 1)) {
+          ok = false;
+          break;
+        }
+      }
+    }
+    epi_bar();
+    if (e == 0) {
+      // the last CTA of this rank to finish publishes done = epoch
+      int* arrive = flag(c.rank, kFlagArrive);
+      fence_acq_rel_sys();
+      const int prev = atomicAdd(arrive, 1);
+      if (prev + 1 - static_cast<int>(c.arrive_base) == static_cast<int>(gridDim.x) && ok) {
+        fence_acq_rel_sys();
+        st_release_sys(flag(c.rank, kFlagDone), c.epoch);
+      }
+    }
+  }
+};
+
+int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t stream) {
+  if (check_gemm_args(g)) return -1;
+  if (g.out_dtype != kDtypeBF16 || g.batch != 1) return -2;
+  CUtensorMap ma, mb;
+  make_operand_maps(g, &ma, &mb);
+  GemmShape s = make_shape(g);
+  const int tiles = s.num_m * s.num_n;
+  if (tiles > kMaxTiles) return -3;
+  ArEpilogue epi;
+  epi.c = comm;
+  epi.C = reinterpret_cast<__nv_bfloat16*>(g.C);
+  epi.ldc = g.ldc;
+  epi.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && (g.ldc % 8 == 0);
+  epi.sm = nullptr;
+  auto kernel = gemm_tc_kernel<ArEpilogue>;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> dev & 1ull)) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    attr_set |= 1ull << dev;
+  }
+  const int grid = tiles < g.num_sms ? tiles : g.num_sms;
+  void* args[] = {&ma, &mb, &s, &epi};
+  return static_cast<int>(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kernel), dim3(grid),
+                                                      dim3(kThreads), args, kSmemBytes, stream));
+}
+
+}  // namespace es

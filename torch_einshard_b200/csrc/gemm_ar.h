@@ -1,0 +1,18 @@
+// GEMM fused with an NVLink all-reduce of its output (see gemm_ar.cu).
+#pragma once
+
+#include "comm.h"
+#include "gemm.h"
+
+namespace es {
+
+// Number of CTAs the fused kernel launches for this problem (the completion
+// counter of the communicator advances by this much).
+inline int gemm_allreduce_grid(const GemmArgs& g) {
+  const int tiles = ((g.M + 127) / 128) * ((g.N + 255) / 256);
+  return tiles < g.num_sms ? tiles : g.num_sms;
+}
+
+int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t stream);
+
+}  // namespace es

@@ -77,11 +77,13 @@ struct SharedState {
   uint32_t tmem_base;
   int abort_flag;
   int consumed;  // k-iterations consumed by the MMA warp (for the producer's drain)
+  int epi[32];   // scratch for the epilogue policy (its own queues and flags)
 };
 
 // Context handed to the epilogue policy for one tile.
 struct EpiTile {
   TileCoord c;
+  int t;          // linear tile index
   uint32_t tmem;  // TMEM address of this thread's lane quadrant and accumulator buffer
   int row;        // this thread's tile row (0..127)
   int q;          // lane quadrant of this warp
@@ -114,6 +116,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(&st->drain, 1);
     st->abort_flag = 0;
     st->consumed = 0;
+    for (int i = 0; i < 32; ++i) st->epi[i] = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
@@ -229,6 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       EpiTile et;
       et.c = tile_coord(shp, t);
+      et.t = t;
       et.tmem = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * kBN;
       et.row = q * 32 + lane;
       et.q = q;
@@ -237,7 +241,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&st->tempty[acc]);
-      if (!ok) break;
+      if (!ok) {
+        *abort_flag = 1;
+        break;
+      }
     }
     epi.finish(shp, abort_flag);
   }

@@ -20,8 +20,14 @@ __all__ = ["TPMLP", "tp_mlp_flops"]
 
 
 class TPMLP(torch.nn.Module):
-    def __init__(self, c, h, mesh, *, tp_dim="tp", dtype=torch.bfloat16, device=None, std=0.02, seed=0):
+    def __init__(self, c, h, mesh, *, tp_dim="tp", dtype=torch.bfloat16, device=None, std=0.02, seed=0,
+                 single_formula=True):
         super().__init__()
+        # single_formula: write the row-parallel step as one formula
+        # ("b n h/tp, c h/tp -> b n c"), whose plan is the same local contraction
+        # followed by the same all-reduce as the two-call chain below, so the
+        # executor can run both as one fused kernel.
+        self.single_formula = single_formula
         tp = mesh[tp_dim].size() if hasattr(mesh[tp_dim], "size") else 1
         if h % tp:
             raise ValueError(f"hidden size {h} is not divisible by tp={tp}")
@@ -39,6 +45,8 @@ class TPMLP(torch.nn.Module):
         t = self.tp_dim
         h = einshard(f"b n c, h/{t} c -> b n h/{t}", x, self.w1, mesh=self.mesh)
         a = F.silu(h)
+        if self.single_formula:
+            return einshard(f"b n h/{t}, c h/{t} -> b n c", a, self.w2, mesh=self.mesh)
         y = einshard(f"b n h/{t}, c h/{t} -> b n c // {t}", a, self.w2, mesh=self.mesh)
         return einshard(f"b n c // {t} -> b n c", y, mesh=self.mesh)
 

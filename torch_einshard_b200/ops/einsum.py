@@ -110,6 +110,15 @@ def _letters(spec, table, name_only, allow_missing=True):
     return out
 
 
+def equation_for(shard, name_only=False):
+    """The einsum equation (letters) the local contraction of ``shard`` uses."""
+    table = {}
+    lhs = _letters(shard[0], table, name_only)
+    if shard[1] is not None:
+        lhs += "," + _letters(shard[1], table, name_only)
+    return f"{lhs}->{_letters(shard[2], table, name_only, allow_missing=False)}"
+
+
 def einsum(shard, *xs, name_only=False, sizes=None):
     """Run the local contraction described by ``shard`` on ``xs``."""
     binary = shard[1] is not None

@@ -136,7 +136,7 @@ class _HaloExchange(torch.autograd.Function):
         from ..parallel import native_comm
         comm = native_comm.communicator_for(group) if x.is_cuda else None
         if comm is not None:
-            out = comm.halo_gather(x.contiguous(), dim, table, length)
+            out = comm.halo_gather(x.contiguous(), dim, table, length, shapes)
             if out is not None:
                 return out
         out = _resized(x, dim, length)

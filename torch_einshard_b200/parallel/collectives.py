@@ -316,7 +316,7 @@ def roll_sharded(input, group, dim, shift, shapes):
     table = roll_intervals(shapes, shift)
     comm = _native(group, input)
     if comm is not None:
-        out = comm.interval_exchange(input, dim, table, input.shape)
+        out = comm.interval_exchange(input, dim, table, shapes)
         if out is not None:
             return out
     output = torch.empty_like(input)
