@@ -11,6 +11,15 @@ if not torch.cuda.is_available():
 from torch_einshard_b200.ops import _native, gemm  # noqa: E402
 
 
+@pytest.fixture(params=[0, 1], ids=["1sm", "2sm"], autouse=True)
+def kernel_variant(request):
+    """Run every case on both the 1-SM and the 2-SM (CTA pair) kernel."""
+    mod = _native.require()
+    mod.set_gemm_pair_mode(request.param)
+    yield request.param
+    mod.set_gemm_pair_mode(-1)
+
+
 def _operand(shape_rows, shape_cols, batch, dtype, transposed):
     """[batch, rows, cols] view; transposed=True stores it column-major."""
     if transposed:

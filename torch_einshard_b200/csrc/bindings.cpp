@@ -16,6 +16,9 @@ namespace {
 
 // Number of native kernel launches issued through these bindings (all devices).
 std::atomic<long long> g_launches{0};
+// -1: heuristic; 0/1: force the 1-SM / 2-SM GEMM kernel (tests, tuning)
+int g_pair_mode = -1;
+int g_group_m = 0;  // raster group override (0: kernel default)
 
 int dtype_code(at::ScalarType t) {
   switch (t) {
@@ -92,6 +95,8 @@ es::GemmArgs gemm_args(const at::Tensor& a, const at::Tensor& b, at::Tensor& out
   g.act = static_cast<int>(act);
   g.err = err.data_ptr<int>();
   g.num_sms = num_sms(a.get_device());
+  g.pair = g_pair_mode;
+  g.group_m = g_group_m;
   const char* why = es::check_gemm_args(g);
   TORCH_CHECK(why == nullptr, "einshard native gemm: ", why ? why : "");
   return g;
@@ -283,5 +288,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)");
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
   m.def("comm_data_bytes", &comm_data_bytes, "data capacity of a communicator");
+  m.def("set_gemm_pair_mode", [](int64_t m) { g_pair_mode = static_cast<int>(m); },
+        "-1 heuristic, 0 force 1-SM, 1 force 2-SM GEMM kernel");
+  m.def("set_gemm_group_m", [](int64_t v) { g_group_m = static_cast<int>(v); }, "raster group height (0 default)");
   m.def("launch_count", []() { return g_launches.load(); }, "native kernel launches so far");
 }

@@ -4,6 +4,7 @@
 
 #include "gemm.h"
 #include "gemm_tc.cuh"
+#include "gemm_tc2.cuh"
 #include "tma_desc.h"
 
 namespace es {
@@ -12,7 +13,14 @@ static CUtensorMapDataType tma_dtype(int dtype) {
   return dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb) {
+bool use_pair_kernel(const GemmArgs& g) {
+  if (g.pair >= 0) return g.pair == 1;
+  // Measured on B200: the 1-SM kernel is faster on long power-capped runs of
+  // the large TP shapes, the 2-SM kernel on short ones; default to 1-SM.
+  return false;
+}
+
+void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb, bool pair) {
   const CUtensorMapDataType dt = tma_dtype(g.dtype);
   const uint64_t a_d0 = g.a_mn ? g.M : g.K;
   const uint64_t a_d1 = g.a_mn ? g.K : g.M;
@@ -21,7 +29,7 @@ void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb) {
   const uint64_t b_d0 = g.b_mn ? g.N : g.K;
   const uint64_t b_d1 = g.b_mn ? g.K : g.N;
   const uint64_t b_bs = g.batch > 1 ? g.b_batch_stride : g.ldb * b_d1;
-  *mb = make_tmap_3d(g.B, dt, 2, b_d0, b_d1, g.batch, g.ldb, b_bs, 64, g.b_mn ? 64 : kBN);
+  *mb = make_tmap_3d(g.B, dt, 2, b_d0, b_d1, g.batch, g.ldb, b_bs, 64, g.b_mn ? 64 : (pair ? kBN / 2 : kBN));
 }
 
 GemmShape make_shape(const GemmArgs& g) {
@@ -36,7 +44,8 @@ GemmShape make_shape(const GemmArgs& g) {
   s.a_mn = g.a_mn;
   s.b_mn = g.b_mn;
   s.in_bf16 = g.dtype == kDtypeBF16 ? 1 : 0;
-  s.group_m = 16;
+  s.group_m = g.group_m > 0 ? g.group_m : 16;
+  s.pair = 0;
   s.err = g.err;
   return s;
 }
@@ -51,11 +60,51 @@ const char* check_gemm_args(const GemmArgs& g) {
   return nullptr;
 }
 
+GemmShape make_shape_pair(const GemmArgs& g) {
+  GemmShape s = make_shape(g);
+  s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
+  s.group_m = g.group_m > 0 ? g.group_m : 8;
+  s.pair = 1;
+  return s;
+}
+
+// Launch a 2-SM kernel instantiation on clusters of two CTAs.
+template <class Epi>
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShape& s, const Epi& epi, int num_sms,
+                cudaStream_t stream) {
+  auto kernel = gemm_tc2_kernel<Epi>;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> dev & 1ull)) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2Bytes);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+    attr_set |= 1ull << dev;
+  }
+  const int pairs = s.num_m * s.num_n * s.batch;
+  int clusters = num_sms / 2;
+  if (pairs < clusters) clusters = pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem2Bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, s, epi));
+}
+
 template <typename OutT>
 static int launch_store(const GemmArgs& g, cudaStream_t stream) {
+  const bool pair = use_pair_kernel(g);
   CUtensorMap ma, mb;
-  make_operand_maps(g, &ma, &mb);
-  GemmShape s = make_shape(g);
+  make_operand_maps(g, &ma, &mb, pair);
+  GemmShape s = pair ? make_shape_pair(g) : make_shape(g);
   StoreEpilogue<OutT> epi;
   epi.C = reinterpret_cast<OutT*>(g.C);
   epi.ldc = g.ldc;
@@ -64,6 +113,7 @@ static int launch_store(const GemmArgs& g, cudaStream_t stream) {
   const int esz = sizeof(OutT);
   epi.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * esz) % 16 == 0) &&
                (g.batch == 1 || (g.c_batch_stride * esz) % 16 == 0);
+  if (pair) return launch_pair(ma, mb, s, epi, g.num_sms, stream);
   auto kernel = gemm_tc_kernel<StoreEpilogue<OutT>>;
   static unsigned long long attr_set = 0;  // one bit per device
   int dev = 0;

@@ -30,10 +30,13 @@ struct GemmArgs {
   int act = 0;
   int* err = nullptr;
   int num_sms = 148;
+  int pair = -1;     // -1: choose; 0: 1-SM kernel; 1: 2-SM (CTA pair) kernel
+  int group_m = 0;   // raster group height in M tiles (0: default)
 };
 
 const char* check_gemm_args(const GemmArgs& g);
-void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb);
+void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb, bool pair = false);
+bool use_pair_kernel(const GemmArgs& g);
 int gemm_launch(const GemmArgs& g, cudaStream_t stream);
 
 }  // namespace es

@@ -47,6 +47,7 @@ struct GemmShape {
   int a_mn, b_mn;  // operand majorness in global memory
   int in_bf16;
   int group_m;     // raster group height (M tiles) for L2 reuse
+  int pair;        // 1: 2-SM kernel; tile t is half (t & 1) of 256-row pair tile t >> 1
   int* err;
 };
 
@@ -55,6 +56,11 @@ struct TileCoord {
 };
 
 __device__ __forceinline__ TileCoord tile_coord(const GemmShape& s, int t) {
+  int half = 0;
+  if (s.pair) {
+    half = t & 1;
+    t >>= 1;
+  }
   const int per_batch = s.num_m * s.num_n;
   const int b = t / per_batch;
   const int r = t - b * per_batch;
@@ -65,7 +71,7 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmShape& s, int t) {
   const int in_group = r - g * per_group;
   const int mb = first_m + in_group % gm;
   const int nb = in_group / gm;
-  return {b, mb * kBM, nb * kBN};
+  return {b, mb * (s.pair ? 2 * kBM : kBM) + half * kBM, nb * kBN};
 }
 
 struct SharedState {
