@@ -217,7 +217,7 @@ def main():
     ms = timed(step, args.steps)
     clocks = sampler.stop() if sampler else None
     launches = native_launches(es) - launches0
-    flops = 6.0 * b * n * c * h
+    flops = 12.0 * b * n * c * h  # 2 forward GEMMs + 4 backward GEMMs of 2*b*n*c*h each
     value = flops * args.steps / (ms / 1e3) / 1e12
 
     # ---------------------------------------------------------------- end to end
