@@ -6,6 +6,7 @@
 #include <atomic>
 
 #include "comm.h"
+#include "fft.h"
 #include "gemm.h"
 #include "gemm_ar.h"
 
@@ -273,6 +274,123 @@ void gemm_allreduce(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Te
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+
+// ------------------------------------------------------------------ FFT
+
+const float2* f2(const at::Tensor& t) { return reinterpret_cast<const float2*>(t.data_ptr()); }
+float2* f2m(at::Tensor& t) { return reinterpret_cast<float2*>(t.data_ptr()); }
+
+void check_twiddles(const at::Tensor& tw, int64_t n, const at::Tensor& like) {
+  TORCH_CHECK(tw.is_cuda() && tw.scalar_type() == at::kComplexFloat && tw.is_contiguous() && tw.numel() == n &&
+                  tw.get_device() == like.get_device(),
+              "einshard fft: twiddle table must be a contiguous complex64 CUDA tensor of length n");
+}
+
+// out = scale * DFT_dim(in) (unnormalised inverse when `inverse`); in and out
+// are contiguous complex64 tensors of the same shape (out may alias in).
+void fft_c2c(const at::Tensor& in, at::Tensor out, int64_t dim, bool inverse, const at::Tensor& tw, double scale) {
+  TORCH_CHECK(in.is_cuda() && in.scalar_type() == at::kComplexFloat && in.is_contiguous(),
+              "einshard fft: contiguous complex64 CUDA input required");
+  TORCH_CHECK(out.sizes() == in.sizes() && out.scalar_type() == at::kComplexFloat && out.is_contiguous() &&
+                  out.get_device() == in.get_device(),
+              "einshard fft: output must match the input");
+  TORCH_CHECK(dim >= 0 && dim < in.dim(), "einshard fft: bad dim");
+  const int64_t n = in.size(dim);
+  TORCH_CHECK(es::fft_supported(n), "einshard fft: length ", n, " is not a supported power of two");
+  check_twiddles(tw, n, in);
+  long long outer = 1, inner = 1;
+  for (int64_t d = 0; d < dim; ++d) outer *= in.size(d);
+  for (int64_t d = dim + 1; d < in.dim(); ++d) inner *= in.size(d);
+  if (outer * inner == 0) return;
+  const c10::cuda::CUDAGuard guard(in.device());
+  es::FftLines f;
+  f.in = f2(in);
+  f.out = f2m(out);
+  f.n = n;
+  f.outer = outer;
+  f.inner = inner;
+  f.in_os = f.out_os = n * inner;
+  f.in_ps = f.out_ps = inner;
+  f.in_is = f.out_is = 1;
+  f.tw = f2(tw);
+  f.scale = static_cast<float>(scale);
+  f.inverse = inverse ? 1 : 0;
+  const int rc = es::fft_lines(f, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard fft: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+es::CommDev peek_dev(HostComm& hc, const at::Tensor& err) {
+  es::CommDev d;
+  d.rank = hc.rank;
+  d.size = hc.size;
+  for (int p = 0; p < es::kMaxRanks; ++p) {
+    d.flags[p] = p < hc.size ? reinterpret_cast<uint64_t>(hc.bases[p]) : 0;
+    d.data[p] = p < hc.size ? reinterpret_cast<uint64_t>(hc.bases[p]) + es::kFlagBytes : 0;
+  }
+  d.epoch = hc.epoch;
+  d.bar_base = hc.bar;
+  d.arrive_base = hc.arrive;
+  d.err = err.data_ptr<int>();
+  return d;
+}
+
+// The first `nbytes` of this rank's symmetric data region as a uint8 tensor.
+// Writes into it must follow comm_acquire (peers may still read the previous op).
+at::Tensor comm_region(int64_t id, int64_t nbytes) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open && nbytes >= 0 && (size_t)nbytes <= hc.data_bytes, "einshard comm region: size");
+  void* p = static_cast<char*>(hc.local) + es::kFlagBytes;
+  return torch::from_blob(p, {nbytes}, at::TensorOptions().dtype(at::kByte).device(at::kCUDA, hc.device));
+}
+
+// Stream-ordered wait until every peer finished reading this rank's region for
+// the last op on the communicator.
+void comm_acquire(int64_t id, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open, "einshard comm: not connected");
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(hc.device));
+  es::CommDev d = peek_dev(hc, err);
+  const int rc = es::comm_wait_peers(d, es::kFlagDone, hc.epoch, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard comm acquire: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// Slab transpose fused with the FFT along the exchanged axis (fft.h FftSlab).
+void fft_slab(int64_t id, at::Tensor out, int64_t n, int64_t A, int64_t B, int64_t C, int64_t D, int64_t Dl,
+              int64_t doff, int64_t mode, const at::Tensor& tw, double scale, bool inverse, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open, "einshard fft slab: communicator not connected");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kComplexFloat && out.is_contiguous(),
+              "einshard fft slab: contiguous complex64 output required");
+  TORCH_CHECK(es::fft_supported(n) && n % hc.size == 0 && D % hc.size == 0 && Dl * hc.size == D,
+              "einshard fft slab: unsupported sizes");
+  TORCH_CHECK(out.numel() == A * B * C * Dl * n, "einshard fft slab: output size");
+  TORCH_CHECK((size_t)(A * B * C * D * (n / hc.size)) * 8 <= hc.data_bytes, "einshard fft slab: region too small");
+  check_twiddles(tw, n, out);
+  const c10::cuda::CUDAGuard guard(out.device());
+  es::FftSlab f;
+  f.out = f2m(out);
+  f.n = n;
+  f.A = A;
+  f.B = B;
+  f.C = C;
+  f.D = D;
+  f.Dl = Dl;
+  f.doff = doff;
+  f.mode = static_cast<int>(mode);
+  f.tw = f2(tw);
+  f.scale = static_cast<float>(scale);
+  f.inverse = inverse ? 1 : 0;
+  es::CommDev d = make_dev(hc, err, 0, 0);
+  const long long lines = A * B * C * Dl;
+  d.arrive_base = hc.arrive;
+  hc.arrive += static_cast<uint32_t>(es::fft_grid(n, lines));
+  const int rc = es::fft_slab(d, f, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard fft slab: launch failed (", rc, ")");
+  g_launches.fetch_add(2, std::memory_order_relaxed);
+}
+
 int64_t comm_data_bytes(int64_t id) { return static_cast<int64_t>(comm_ref(id).data_bytes); }
 
 }  // namespace
@@ -287,6 +405,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_all_reduce", &comm_all_reduce, "two-shot NVLink all-reduce in place");
   m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)");
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
+  m.def("fft_c2c", &fft_c2c, "complex64 FFT along one dim (powers of two up to 1024)");
+  m.def("comm_region", &comm_region, "this rank's symmetric data region as a uint8 tensor");
+  m.def("comm_acquire", &comm_acquire, "wait until peers finished reading this rank's region");
+  m.def("fft_slab", &fft_slab, "slab transpose fused with the FFT along the exchanged axis");
   m.def("comm_data_bytes", &comm_data_bytes, "data capacity of a communicator");
   m.def("set_gemm_pair_mode", [](int64_t m) { g_pair_mode = static_cast<int>(m); },
         "-1 heuristic, 0 force 1-SM, 1 force 2-SM GEMM kernel");

@@ -96,15 +96,25 @@ def _group(mesh, dim):
 
 # ----------------------------------------------------------------- local transforms
 
-def _local_fft(x, dim, inverse):
-    """Unnormalised DFT along ``dim`` (inverse without the 1/n)."""
+def _local_fft(x, dim, inverse, scale=1.0):
+    """``scale`` times the unnormalised DFT along ``dim`` (inverse without the 1/n).
+    The native kernel folds the scale into its stores."""
     from . import fft_native
-    out = fft_native.try_fft(x, dim, inverse)
+    out = fft_native.try_fft(x, dim, inverse, scale)
     if out is not None:
         return out
-    if inverse:
-        return torch.fft.ifft(x, dim=dim, norm="forward")
-    return torch.fft.fft(x, dim=dim)
+    out = torch.fft.ifft(x, dim=dim, norm="forward") if inverse else torch.fft.fft(x, dim=dim)
+    return out if scale == 1.0 else out * scale
+
+
+def _norm_scale(*, n, inverse, norm):
+    if norm == "ortho":
+        return 1.0 / math.sqrt(n)
+    if norm in (None, "backward"):
+        return 1.0 / n if inverse else 1.0
+    if norm == "forward":
+        return 1.0 if inverse else 1.0 / n
+    raise ValueError(f"Invalid FFT norm {norm!r}")
 
 
 def _normalize(x, *, n, inverse, norm):
@@ -296,23 +306,30 @@ def _complex_plan(x, tmap, in_by, out_by, in_axes, shapes, mesh, *, require_comp
     return plan
 
 
-def _run_items(z, current, out_by, plan, *, inverse, per_axis_norm):
-    for item in plan:
+def _run_items(z, current, out_by, plan, *, inverse, per_axis_norm, last_scale=None):
+    """Runs the plan; ``last_scale`` (when given) is folded into a final local FFT.
+    Returns (z, scale_applied)."""
+    applied = False
+    for index, item in enumerate(plan):
         if item[0] == "local":
             _, source, target, dim, _ = item
-            z = _local_fft(z, dim, inverse)
+            fold = last_scale is not None and index == len(plan) - 1
+            z = _local_fft(z, dim, inverse, last_scale if fold else 1.0)
+            applied = applied or fold
             current[dim] = Axis(target)
         else:
             _, source, target, dim, _, group, split = item
             z = _dist_fft(z, group, dim, split, inverse=inverse, norm=per_axis_norm)
             current[dim] = Axis(target, out_by[target].shard_dim)
-    return z
+    return z, applied
 
 
 def _run_complex_plan(z, current, out_by, plan, *, inverse, norm):
     total = math.prod(item[4] for item in plan)
-    z = _run_items(z, current, out_by, plan, inverse=inverse, per_axis_norm="forward" if inverse else None)
-    return _normalize(z, n=total, inverse=inverse, norm=norm)
+    scale = _norm_scale(n=total, inverse=inverse, norm=norm)
+    z, applied = _run_items(z, current, out_by, plan, inverse=inverse, per_axis_norm="forward" if inverse else None,
+                            last_scale=scale)
+    return z if applied or scale == 1.0 else z * scale
 
 
 def _real_input_ok(x):
@@ -402,7 +419,7 @@ def _run_real_plan(z, current, out_by, tmap, plan, *, inverse, norm, signal_size
         z = _dist_fft(z, group, hdim, full, inverse=False, norm=None)
         z = _PrefixRepartition.apply(z, group, hdim, full, half)
         current[hdim] = Axis(half_dst, out_by[half_dst].shard_dim)
-        z = _run_items(z, current, out_by, rest_plan, inverse=False, per_axis_norm=None)
+        z, _ = _run_items(z, current, out_by, rest_plan, inverse=False, per_axis_norm=None)
         return _normalize(z, n=total, inverse=False, norm=norm)
     sizes = _signal_sizes(tmap, current, z, signal_sizes) if inverse else None
     planned = {item[1]: item[4] for item in plan}
@@ -411,7 +428,7 @@ def _run_real_plan(z, current, out_by, tmap, plan, *, inverse, norm, signal_size
     )
     per_axis = "forward" if inverse else None
     if inverse:
-        z = _run_items(z, current, out_by, plan, inverse=True, per_axis_norm=per_axis)
+        z, _ = _run_items(z, current, out_by, plan, inverse=True, per_axis_norm=per_axis)
         hdim = _dim(current, half_src)
         z = torch.fft.irfft(z, n=sizes[-1], dim=hdim, norm="forward")
         current[hdim] = Axis(half_dst)
@@ -419,7 +436,7 @@ def _run_real_plan(z, current, out_by, tmap, plan, *, inverse, norm, signal_size
         hdim = _dim(current, half_src)
         z = torch.fft.rfft(z, dim=hdim)
         current[hdim] = Axis(half_dst)
-        z = _run_items(z, current, out_by, plan, inverse=False, per_axis_norm=per_axis)
+        z, _ = _run_items(z, current, out_by, plan, inverse=False, per_axis_norm=per_axis)
     return _normalize(z, n=total, inverse=inverse, norm=norm)
 
 
@@ -481,6 +498,15 @@ def _run_slab(z, current, out_by, tmap, plan, *, inverse, norm):
             total *= plan["n_src"]
         else:
             total *= z.shape[_dim(current, s)]
+    fused = _run_slab_native(z, current, tmap, plan, inverse=inverse, scale=_norm_scale(n=total, inverse=inverse,
+                                                                                        norm=norm))
+    if fused is not None:
+        for s, t in tmap.items():
+            dim = _dim(current, s)
+            current[dim] = Axis(t)
+        dst_t = tmap[plan["dst"]]
+        current[plan["dst_dim"]] = Axis(dst_t, out_by[dst_t].shard_dim)
+        return fused
     # 1) transforms over every axis that is local on the input
     for s, t in tmap.items():
         if s == plan["src"]:
@@ -492,10 +518,29 @@ def _run_slab(z, current, out_by, tmap, plan, *, inverse, norm):
     z = alltoall_repartition(z, plan["group"], plan["src_dim"], plan["dst_dim"], plan["src_shapes"], plan["dst_shapes"])
     dst_t = tmap[plan["dst"]]
     current[plan["dst_dim"]] = Axis(dst_t, out_by[dst_t].shard_dim)
-    # 3) the remaining transform over the now-local src axis
-    z = _local_fft(z, plan["src_dim"], inverse)
+    # 3) the remaining transform over the now-local src axis, normalisation folded in
+    z = _local_fft(z, plan["src_dim"], inverse, _norm_scale(n=total, inverse=inverse, norm=norm))
     current[plan["src_dim"]] = Axis(tmap[plan["src"]])
-    return _normalize(z, n=total, inverse=inverse, norm=norm)
+    return z
+
+
+def _run_slab_native(z, current, tmap, plan, *, inverse, scale):
+    """The slab pipeline on the native kernels: local FFTs, then the all-to-all
+    fused into the loads of the FFT along the gathered axis (peer memory over
+    NVLink).  ``None`` when the native path does not cover the call."""
+    if not z.is_cuda or z.dtype != torch.complex64:
+        return None
+    P = len(plan["src_shapes"])
+    if len(set(plan["src_shapes"])) != 1 or len(set(plan["dst_shapes"])) != 1:
+        return None
+    from ..parallel import native_comm
+    from . import fft_impl
+    comm = native_comm.communicator_for(plan["group"])
+    pre = [_dim(current, s) for s in tmap if s != plan["src"]]
+    if not fft_impl.slab_eligible(z, comm, plan["src_dim"], plan["dst_dim"], P, pre, ()):
+        return None
+    return fft_impl.slab_fft(z, comm, P, dist.get_rank(plan["group"]), pre_dims=pre, gather_dim=plan["src_dim"],
+                             split_dim=plan["dst_dim"], inverse=inverse, scale=scale)
 
 
 # ------------------------------------------------------------------ diagnostics
@@ -693,7 +738,10 @@ def einfft(shard, x, axes, *, inverse=False, norm=None, mesh=None, shapes=None, 
         else:
             z = torch.fft.rfftn(z, dim=tuple(dims), norm=norm)
     else:
-        z = (torch.fft.ifftn if inverse else torch.fft.fftn)(z, dim=tuple(dims), norm=norm)
+        total = math.prod(z.shape[d] for d in dims)
+        scale = _norm_scale(n=total, inverse=inverse, norm=norm)
+        for k, d in enumerate(dims):
+            z = _local_fft(z, d, inverse, scale if k == len(dims) - 1 else 1.0)
     for s, t in tmap.items():
         dim = _dim(current, s)
         out_axis = out_by[t]

@@ -8,7 +8,7 @@ uses ``torch.fft``.
 __all__ = ["try_fft"]
 
 
-def try_fft(x, dim, inverse):
+def try_fft(x, dim, inverse, scale=1.0):
     from . import _native
     if not x.is_cuda:
         return None
@@ -16,4 +16,4 @@ def try_fft(x, dim, inverse):
     if mod is None or not hasattr(mod, "fft_c2c"):
         return None
     from .fft_impl import fft_c2c
-    return fft_c2c(mod, x, dim, inverse)
+    return fft_c2c(mod, x, dim, inverse, scale)

@@ -86,6 +86,24 @@ class Communicator:
         self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
         self.broken = False
 
+    # -- raw access for fused kernels ----------------------------------------
+    @property
+    def id(self):
+        return self.cid
+
+    @property
+    def data_bytes(self):
+        return self.capacity
+
+    def acquire(self):
+        """Stream-ordered wait until every peer finished reading this rank's
+        region for the previous op; writes into ``region()`` must follow it."""
+        self.mod.comm_acquire(self.cid, self.err)
+
+    def region(self, nbytes):
+        """This rank's symmetric data region (first ``nbytes``) as uint8."""
+        return self.mod.comm_region(self.cid, int(nbytes))
+
     # -- helpers -----------------------------------------------------------
     def _blocks(self, nbytes):
         return int(max(8, min(self.sms, nbytes // (512 * 1024) + 8)))
