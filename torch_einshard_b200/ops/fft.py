@@ -535,7 +535,7 @@ def _run_slab_native(z, current, tmap, plan, *, inverse, scale):
         return None
     from ..parallel import native_comm
     from . import fft_impl
-    comm = native_comm.communicator_for(plan["group"])
+    comm = native_comm.workspace_for(plan["group"], z.numel() * z.element_size())
     pre = [_dim(current, s) for s in tmap if s != plan["src"]]
     if not fft_impl.slab_eligible(z, comm, plan["src_dim"], plan["dst_dim"], P, pre, ()):
         return None

@@ -7,14 +7,16 @@ collective helpers ask :func:`communicator_for` and fall back to
 by :mod:`torch_einshard_b200.parallel.symmetric`.
 """
 
-__all__ = ["communicator_for", "world_communicator", "enable", "disable", "enabled"]
+__all__ = ["communicator_for", "workspace_for", "world_communicator", "enable", "disable", "enabled"]
 
-_state = {"enabled": False, "factory": None}
+_state = {"enabled": False, "factory": None, "workspace": None}
 
 
-def enable(factory):
-    """Register the factory mapping a process group to a communicator (or None)."""
+def enable(factory, workspace=None):
+    """Register the factory mapping a process group to a communicator (or None),
+    and optionally the one returning a communicator with at least n bytes."""
     _state["factory"] = factory
+    _state["workspace"] = workspace
     _state["enabled"] = True
 
 
@@ -30,6 +32,17 @@ def communicator_for(group):
     if not enabled():
         return None
     return _state["factory"](group)
+
+
+def workspace_for(group, nbytes):
+    """A communicator of ``group`` whose symmetric region holds ``nbytes``
+    (collective: every member must ask with the same size), or None."""
+    if not enabled():
+        return None
+    if _state["workspace"] is None:
+        comm = _state["factory"](group)
+        return comm if comm is not None and comm.data_bytes >= nbytes else None
+    return _state["workspace"](group, nbytes)
 
 
 def world_communicator():

@@ -29,6 +29,7 @@ __all__ = ["Communicator", "activate", "deactivate", "communicator_for_group"]
 _DEFAULT_MB = int(os.environ.get("EINSHARD_SYMM_MB", "1280"))
 _COMMS = {}
 _REJECTED = set()
+_LARGE = {}  # group key -> larger communicators created on demand (kept until deactivate)
 
 
 def _contig_strides(shape):
@@ -324,6 +325,26 @@ def communicator_for_group(group):
     return comm
 
 
+def workspace_for_group(group, nbytes):
+    """A communicator with at least ``nbytes`` of symmetric region.  The default
+    one is used when large enough; otherwise a dedicated one is created (a
+    collective call: every member asks with the same size) and kept, because
+    freeing peer-mapped memory while a peer might still read it is unsafe."""
+    comm = _COMMS.get(_group_key(group))
+    if comm is None:
+        return None
+    if comm.capacity >= nbytes:
+        return comm
+    for big in _LARGE.get(_group_key(group), []):
+        if big.capacity >= nbytes:
+            return big
+    mb = 256
+    size = ((int(nbytes) + (mb << 20) - 1) // (mb << 20)) * (mb << 20)
+    big = Communicator(group, size)
+    _LARGE.setdefault(_group_key(group), []).append(big)
+    return big
+
+
 def _mesh_groups(mesh):
     groups = [dist.group.WORLD]
     if mesh is not None:
@@ -339,7 +360,8 @@ def activate(mesh=None):
         return False
     for group in _mesh_groups(mesh):
         communicator_for_group(group)
-    native_comm.enable(lambda group: _COMMS.get(_group_key(group)) if group is not None else None)
+    native_comm.enable(lambda group: _COMMS.get(_group_key(group)) if group is not None else None,
+                       lambda group, nbytes: workspace_for_group(group, nbytes) if group is not None else None)
     _install_fusions()
     return True
 
@@ -354,10 +376,11 @@ def _install_fusions():
 
 def deactivate():
     native_comm.disable()
-    for comm in _COMMS.values():
+    for comm in list(_COMMS.values()) + [c for cs in _LARGE.values() for c in cs]:
         try:
             comm.mod.comm_destroy(comm.cid)
         except Exception:  # noqa: BLE001
             pass
     _COMMS.clear()
+    _LARGE.clear()
     _REJECTED.clear()
