@@ -1,0 +1,72 @@
+"""Implicit-GEMM conv2d (tcgen05, NHWC) against an fp32 PyTorch reference."""
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from torch_einshard_b200.ops import _native  # noqa: E402
+from torch_einshard_b200.ops.conv_impl import conv2d_native  # noqa: E402
+
+
+def _ref(x, w, bias, pad=0):
+    out = F.conv2d(x.float().permute(0, 3, 1, 2), w.float().permute(0, 3, 1, 2),
+                   None if bias is None else bias.float(), padding=pad)
+    return out.permute(0, 2, 3, 1)
+
+
+def _close(got, want, tol=2e-2):
+    scale = want.abs().max().item() + 1e-6
+    err = (got.float() - want).abs().max().item()
+    assert err <= tol * scale, (err, scale)
+
+
+@pytest.mark.parametrize("B,H,W,C,O,K", [(1, 8, 8, 64, 128, 3), (2, 17, 300, 64, 96, 3), (1, 5, 513, 128, 128, 1),
+                                         (3, 9, 40, 192, 256, 5), (1, 4, 4, 64, 8, 3)])
+def test_conv_forward(B, H, W, C, O, K):
+    torch.manual_seed(0)
+    x = torch.randn(B, H, W, C, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(O, K, K, C, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = torch.randn(O, device="cuda")
+    got = conv2d_native(x, w, bias)
+    _close(got, _ref(x, w, bias))
+    again = conv2d_native(x, w, bias)
+    assert torch.equal(got, again)
+    _native.check_errors()
+
+
+def test_conv_backward():
+    torch.manual_seed(1)
+    x = torch.randn(2, 12, 33, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(128, 3, 3, 64, device="cuda") * 0.05).to(torch.bfloat16).requires_grad_(True)
+    bias = torch.randn(128, device="cuda", requires_grad=True)
+    y = conv2d_native(x, w, bias)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().float().requires_grad_(True)
+    br = bias.detach().clone().requires_grad_(True)
+    _ref(xr, wr, br).backward(g.float())
+    _close(x.grad, xr.grad)
+    _close(w.grad, wr.grad)
+    _close(bias.grad, br.grad, tol=1e-3)
+    _native.check_errors()
+
+
+def test_einconv_local_uses_native(monkeypatch):
+    import torch_einshard_b200 as es
+    from torch_einshard_b200.ops import conv_impl
+    calls = []
+    real = conv_impl._run
+    monkeypatch.setattr(conv_impl, "_run", lambda *a, **k: calls.append(1) or real(*a, **k))
+    torch.manual_seed(2)
+    x = torch.randn(2, 16, 40, 64, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(3, 3, 64, 128, device="cuda") * 0.05).to(torch.bfloat16)
+    y = es.einconv("b h w c, kh kw c o -> b h w o", x, w, {"h": "kh", "w": "kw"})
+    want = _ref(x, w.permute(3, 0, 1, 2), None, pad=1)
+    _close(y, want)
+    assert calls

@@ -1,0 +1,157 @@
+// Implicit-GEMM 2-D convolution on the tcgen05 GEMM mainloop (NHWC, bf16/fp16,
+// stride 1, dilation 1), with no im2col tensor in memory.
+//
+// The convolution is computed transposed, as one GEMM per launch:
+//   out^T[o, p] = sum_{kh, kw, c} Wt[o, (kh, kw, c)] * X[b, h + kh - ph, w + kw - pw, c]
+// with p = (b, h, w) an output pixel.  GEMM M = output channels (weights are the
+// K-major A operand [O][KH*KW*C]), N = output pixels, K = KH*KW*C.  An N tile is
+// 256 consecutive output columns w of one output row (b, h); the K loop walks
+// (kh, kw, 64-channel block), and for every step the producer issues one 4-D
+// TMA load of a [256 w x 64 c] box of the NHWC input at the shifted coordinates
+// (c0, w0 + kw - pw, h + kh - ph, b).  Coordinates left of / above / beyond
+// the tensor read zeros (TMA fill), which is the zero padding; the channel
+// coordinate is always a multiple of 64, so the 16-byte rule holds.  The
+// epilogue reads the accumulator tile (channels on TMEM lanes, pixels on
+// columns), adds the bias and writes NHWC, one coalesced 2-byte store per lane
+// per pixel (lanes are neighbouring channels).
+//
+// The same kernel computes the input gradient: dX = conv(dY, W') with
+// W'[c, kh', kw', o] = W[o, KH-1-kh', KW-1-kw', c] and padding (KH-1, KW-1).
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "conv.h"
+#include "gemm_tc.cuh"
+#include "tma_desc.h"
+
+namespace es {
+
+namespace {
+
+struct ConvLoads {
+  int C;        // input channels (multiple of 64)
+  int KW;       // kernel width
+  int Hout;     // output rows per image
+  int Wv;       // virtual output width: column tiles per row * 256
+  int ph, pw;   // input offset of output pixel (0, 0) is (-ph, -pw)
+  __device__ __forceinline__ void load(const GemmShape&, const TileCoord& c, int kb, uint8_t* a, uint8_t* b,
+                                       uint64_t* bar, const CUtensorMap* tmA, const CUtensorMap* tmB) const {
+    const int k0 = kb * kBK;
+    const int tap = k0 / C;
+    const int c0 = k0 - tap * C;
+    const int kh = tap / KW;
+    const int kw = tap - kh * KW;
+    tma_load_3d(a, tmA, bar, k0, c.m0, 0);
+    const int r = c.n0 / Wv;
+    const int w0 = c.n0 - r * Wv;
+    const int img = r / Hout;
+    const int h = r - img * Hout;
+    tma_load_4d(b, tmB, bar, c0, w0 + kw - pw, h + kh - ph, img);
+  }
+};
+
+template <typename OutT>
+struct ConvStoreEpilogue {
+  OutT* out;
+  const float* bias;  // may be null
+  int O, Wout, Wv;
+
+  __device__ __forceinline__ void setup(SharedState*, const GemmShape&) {}
+  __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
+
+  __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape&, volatile int*) {
+    const int o = et.c.m0 + et.row;
+    const bool ok = o < O;
+    const int r = et.c.n0 / Wv;
+    const int w0 = et.c.n0 - r * Wv;
+    const long long pix0 = static_cast<long long>(r) * Wout + w0;
+    const float bv = (ok && bias != nullptr) ? bias[o] : 0.0f;
+#pragma unroll 1
+    for (int chunk = 0; chunk < kBN / 32; ++chunk) {
+      const int col0 = w0 + chunk * 32;
+      if (col0 >= Wout) break;  // uniform across the warp
+      uint32_t v[32];
+      tmem_ld32(et.tmem + chunk * 32, v);
+      tmem_ld_wait();
+      if (!ok) continue;
+      OutT* dst = out + (pix0 + chunk * 32) * O + o;
+      const int valid = Wout - col0 < 32 ? Wout - col0 : 32;
+#pragma unroll
+      for (int i = 0; i < 32; ++i)
+        if (i < valid) StoreOut<OutT>::store1(dst + static_cast<long long>(i) * O, __uint_as_float(v[i]) + bv);
+    }
+    return true;
+  }
+};
+
+template <typename OutT>
+int launch(const ConvArgs& a, cudaStream_t stream) {
+  const CUtensorMapDataType dt = a.dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int K = a.KH * a.KW * a.C;
+  // A: weights [O][K] (K-major), as a 3-D map with one batch
+  const CUtensorMap ma = make_tmap_3d(a.w, dt, 2, K, a.O, 1, K, static_cast<uint64_t>(K) * a.O, kBK, kBM);
+  // B: NHWC input, dims (C, Win, Hin, B), box 64 channels x 256 columns
+  const uint64_t dims[4] = {static_cast<uint64_t>(a.C), static_cast<uint64_t>(a.Win), static_cast<uint64_t>(a.Hin),
+                            static_cast<uint64_t>(a.B)};
+  const uint64_t strides[3] = {static_cast<uint64_t>(a.C) * 2, static_cast<uint64_t>(a.Win) * a.C * 2,
+                               static_cast<uint64_t>(a.Hin) * a.Win * a.C * 2};
+  const uint32_t box[4] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kBN), 1, 1};
+  const CUtensorMap mb = make_tmap_nd(a.x, dt, 4, dims, strides, box);
+
+  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
+  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  const int Wv = (Wout + kBN - 1) / kBN * kBN;
+  GemmShape s;
+  s.M = a.O;
+  s.N = a.B * Hout * Wv;
+  s.K = K;
+  s.batch = 1;
+  s.num_m = (a.O + kBM - 1) / kBM;
+  s.num_n = s.N / kBN;
+  s.num_kb = K / kBK;
+  s.a_mn = 0;
+  s.b_mn = 0;
+  s.in_bf16 = a.dtype == kDtypeBF16 ? 1 : 0;
+  s.group_m = 16;
+  s.pair = 0;
+  s.err = a.err;
+
+  ConvLoads loads{a.C, a.KW, Hout, Wv, a.ph, a.pw};
+  ConvStoreEpilogue<OutT> epi{reinterpret_cast<OutT*>(a.out), a.bias, a.O, Wout, Wv};
+  auto kernel = gemm_tc_kernel<ConvStoreEpilogue<OutT>, ConvLoads>;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> dev & 1ull)) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    attr_set |= 1ull << dev;
+  }
+  const long long tiles = static_cast<long long>(s.num_m) * s.num_n;
+  const int grid = tiles < a.num_sms ? static_cast<int>(tiles) : a.num_sms;
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, s, epi, loads);
+  return static_cast<int>(cudaGetLastError());
+}
+
+}  // namespace
+
+const char* check_conv_args(const ConvArgs& a) {
+  if (a.B <= 0 || a.Hin <= 0 || a.Win <= 0 || a.C <= 0 || a.O <= 0 || a.KH <= 0 || a.KW <= 0)
+    return "empty convolution";
+  if (a.C % kBK) return "input channels must be a multiple of 64";
+  if (a.ph < 0 || a.pw < 0) return "negative padding";
+  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
+  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  if (Hout <= 0 || Wout <= 0) return "empty output";
+  if ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.w)) & 15) return "operands not 16-byte aligned";
+  const long long n = static_cast<long long>(a.B) * Hout * ((Wout + kBN - 1) / kBN) * kBN;
+  if (n / kBN > 0x7fffffffLL / 2) return "too many output tiles";
+  return nullptr;
+}
+
+int conv_launch(const ConvArgs& a, cudaStream_t stream) {
+  if (check_conv_args(a)) return -1;
+  return a.dtype == kDtypeBF16 ? launch<__nv_bfloat16>(a, stream) : launch<__half>(a, stream);
+}
+
+}  // namespace es

@@ -1,0 +1,25 @@
+// Implicit-GEMM 2-D convolution (conv.cu): NHWC input, weights [O][KH][KW][C].
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include "gemm.h"
+
+namespace es {
+
+struct ConvArgs {
+  const void* x = nullptr;     // [B][Hin][Win][C]
+  const void* w = nullptr;     // [O][KH][KW][C]
+  const float* bias = nullptr; // [O] or null
+  void* out = nullptr;         // [B][Hout][Wout][O], Hout = Hin + 2 ph - KH + 1
+  int dtype = kDtypeBF16;      // x, w and out share it
+  int B = 0, Hin = 0, Win = 0, C = 0, O = 0, KH = 0, KW = 0;
+  int ph = 0, pw = 0;          // zero padding on each side
+  int* err = nullptr;
+  int num_sms = 148;
+};
+
+const char* check_conv_args(const ConvArgs& a);
+int conv_launch(const ConvArgs& a, cudaStream_t stream);
+
+}  // namespace es

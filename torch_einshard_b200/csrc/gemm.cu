@@ -124,7 +124,7 @@ static int launch_store(const GemmArgs& g, cudaStream_t stream) {
   }
   const int tiles = s.num_m * s.num_n * s.batch;
   const int grid = tiles < g.num_sms ? tiles : g.num_sms;
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, s, epi);
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, s, epi, GemmLoads{});
   return static_cast<int>(cudaGetLastError());
 }
 

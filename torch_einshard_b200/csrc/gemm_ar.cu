@@ -261,7 +261,8 @@ int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t s
     attr_set |= 1ull << dev;
   }
   const int grid = tiles < g.num_sms ? tiles : g.num_sms;
-  void* args[] = {&ma, &mb, &s, &epi};
+  GemmLoads loads{};
+  void* args[] = {&ma, &mb, &s, &epi, &loads};
   return static_cast<int>(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kernel), dim3(grid),
                                                       dim3(kThreads), args, kSmemBytes, stream));
 }

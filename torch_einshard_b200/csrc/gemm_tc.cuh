@@ -96,10 +96,31 @@ struct EpiTile {
   int lane;
 };
 
-template <class Epi>
+// Operand loads of one K block for the plain GEMM: A and B tiles by TMA from
+// 3-D maps over [batch, rows, cols] (K-major: one box; MN-major: 64-wide boxes).
+struct GemmLoads {
+  __device__ __forceinline__ void load(const GemmShape& shp, const TileCoord& c, int kb, uint8_t* a, uint8_t* b,
+                                       uint64_t* bar, const CUtensorMap* tmA, const CUtensorMap* tmB) const {
+    const int k0 = kb * kBK;
+    if (!shp.a_mn) {
+      tma_load_3d(a, tmA, bar, k0, c.m0, c.b);
+    } else {
+      tma_load_3d(a, tmA, bar, c.m0, k0, c.b);
+      tma_load_3d(a + 8192, tmA, bar, c.m0 + 64, k0, c.b);
+    }
+    if (!shp.b_mn) {
+      tma_load_3d(b, tmB, bar, k0, c.n0, c.b);
+    } else {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) tma_load_3d(b + j * 8192, tmB, bar, c.n0 + 64 * j, k0, c.b);
+    }
+  }
+};
+
+template <class Epi, class Loads = GemmLoads>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmShape shp, Epi epi) {
+                   const GemmShape shp, Epi epi, const Loads loads) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -150,22 +171,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t ph = (it / kStages) & 1u;
         if (!mbar_wait(&st->empty[s], ph ^ 1u, abort_flag, shp.err, kErrWaitEmpty)) goto producer_done;
         if (lane == 0) {
-          uint8_t* a = sA + s * kABytes;
-          uint8_t* b = sB + s * kBBytes;
           mbar_arrive_expect_tx(&st->full[s], kStageBytes);
-          const int k0 = kb * kBK;
-          if (!shp.a_mn) {
-            tma_load_3d(a, &tmA, &st->full[s], k0, c.m0, c.b);
-          } else {
-            tma_load_3d(a, &tmA, &st->full[s], c.m0, k0, c.b);
-            tma_load_3d(a + 8192, &tmA, &st->full[s], c.m0 + 64, k0, c.b);
-          }
-          if (!shp.b_mn) {
-            tma_load_3d(b, &tmB, &st->full[s], k0, c.n0, c.b);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) tma_load_3d(b + j * 8192, &tmB, &st->full[s], c.n0 + 64 * j, k0, c.b);
-          }
+          loads.load(shp, c, kb, sA + s * kABytes, sB + s * kBBytes, &st->full[s], &tmA, &tmB);
         }
         __syncwarp();
       }

@@ -59,4 +59,36 @@ inline CUtensorMap make_tmap_3d(const void* base, CUtensorMapDataType dtype, int
   return map;
 }
 
+// N-D tiled map (rank 1..5).  dims/box innermost-first; strides in bytes for
+// dims 1..rank-1.  128-byte swizzle, zero fill outside the tensor.
+inline CUtensorMap make_tmap_nd(const void* base, CUtensorMapDataType dtype, int rank, const uint64_t* dims,
+                                const uint64_t* strides_bytes, const uint32_t* box,
+                                CUtensorMapSwizzle swz = CU_TENSOR_MAP_SWIZZLE_128B) {
+  CUtensorMap map;
+  cuuint64_t d[5], st[4];
+  cuuint32_t bx[5], estr[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    bx[i] = box[i];
+    estr[i] = 1;
+    if (i + 1 < rank) st[i] = strides_bytes[i];
+  }
+  auto encode = [&]() {
+    return encode_tiled_fn()(&map, dtype, rank, const_cast<void*>(base), d, st, bx, estr,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  };
+  CUresult r = encode();
+  if (r == CUDA_ERROR_INVALID_CONTEXT) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaSetDevice(dev);
+    cudaFree(nullptr);
+    r = encode();
+  }
+  if (r != CUDA_SUCCESS)
+    throw std::runtime_error("einshard: cuTensorMapEncodeTiled failed with code " + std::to_string(int(r)));
+  return map;
+}
+
 }  // namespace es

@@ -1,0 +1,83 @@
+"""Native implicit-GEMM conv2d for ``einconv`` (``_C.conv2d_implicit``).
+
+The einconv path hands this module the halo-extended input (padding 0 from
+here on), so the forward is a valid convolution.  Tensors are brought to NHWC
+(batch axes flattened), weights to [O][KH][KW][C]; the kernel reads the input
+windows straight from the NHWC tensor with shifted TMA boxes (no im2col).
+
+Backward: the input gradient runs on the same kernel as a full correlation of
+dY with the flipped, channel-transposed weights (zero padding KH-1, KW-1 done
+by the TMA zero fill); the weight gradient uses
+``torch.nn.grad.conv2d_weight`` and the bias gradient a reduction.
+"""
+
+import torch
+
+from . import _native
+
+__all__ = ["conv2d_nhwc", "conv2d_native"]
+
+
+def _run(mod, x, w, bias, ph, pw):
+    B, H, W, _ = x.shape
+    O, KH, KW, _ = w.shape
+    out = torch.empty(B, H + 2 * ph - KH + 1, W + 2 * pw - KW + 1, O, dtype=x.dtype, device=x.device)
+    b = bias if bias is not None else torch.empty(0, dtype=torch.float32, device=x.device)
+    mod.conv2d_implicit(x, w, b, out, ph, pw, _native.error_word(x.device))
+    return out
+
+
+class _Conv2dNHWC(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, w, bias):
+        ctx.save_for_backward(x, w)
+        ctx.has_bias = bias is not None
+        ctx.bias_dtype = bias.dtype if bias is not None else None
+        return _run(_native.require(), x, w, None if bias is None else bias.float().contiguous(), 0, 0)
+
+    @staticmethod
+    def backward(ctx, grad):
+        x, w = ctx.saved_tensors
+        grad = grad.contiguous()
+        gx = gw = gb = None
+        O, KH, KW, C = w.shape
+        if ctx.needs_input_grad[0]:
+            if O % 64 == 0:
+                wt = w.flip(1, 2).permute(3, 1, 2, 0).contiguous()  # [C][KH][KW][O]
+                gx = _run(_native.require(), grad, wt, None, KH - 1, KW - 1)
+            else:
+                gx = torch.nn.grad.conv2d_input(x.permute(0, 3, 1, 2).shape, w.permute(0, 3, 1, 2),
+                                                grad.permute(0, 3, 1, 2)).permute(0, 2, 3, 1)
+        if ctx.needs_input_grad[1]:
+            gw = torch.nn.grad.conv2d_weight(x.permute(0, 3, 1, 2), w.permute(0, 3, 1, 2).shape,
+                                             grad.permute(0, 3, 1, 2)).permute(0, 2, 3, 1)
+        if ctx.has_bias and ctx.needs_input_grad[2]:
+            gb = grad.float().sum(dim=(0, 1, 2)).to(ctx.bias_dtype)
+        return gx, gw, gb
+
+
+def conv2d_native(x, w, bias=None):
+    """Valid NHWC conv2d: x [B, H, W, C], w [O, KH, KW, C] -> [B, H-KH+1, W-KW+1, O]."""
+    x, w = x.contiguous(), w.contiguous()
+    if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad or (bias is not None and bias.requires_grad)):
+        return _Conv2dNHWC.apply(x, w, bias)
+    return _run(_native.require(), x, w, None if bias is None else bias.float().contiguous(), 0, 0)
+
+
+def conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation):
+    if len(spatial) != 2 or any(d != 1 for d in dilation):
+        return None
+    if x.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != x.dtype or not weight.is_cuda:
+        return None
+    C = x.shape[in_names.index(cin)]
+    if C % 64:
+        return None
+    batch = [n for n in in_names if n not in spatial and n != cin]
+    xn = x.permute([in_names.index(n) for n in batch + list(spatial) + [cin]])
+    lead = xn.shape[:len(batch)]
+    xn = xn.reshape(-1, *xn.shape[len(batch):])
+    wn = weight.permute([w_names.index(n) for n in [cout] + list(kernel) + [cin]])
+    out = conv2d_native(xn, wn, bias)
+    out = out.reshape(*lead, *out.shape[1:])
+    produced = batch + list(spatial) + [cout]
+    return out.permute([produced.index(n) for n in out_names]).contiguous()
