@@ -117,7 +117,7 @@ def main():
             if kern == "cublas":
                 fn = lambda: torch.matmul(a, b)  # noqa: E731
             else:
-                mod.set_gemm_pair_mode({"1sm": 0, "2sm": 1, "auto": -1}[kern])
+                mod.set_gemm_pair_mode({"1sm": 0, "2sm": 1, "wide": 2, "auto": -1}[kern])
                 mod.set_gemm_group_m(args.group_m)
                 fn = lambda: gemm.native_bmm(a, b)  # noqa: E731
             label = f"gemm_{name}_{kern}"

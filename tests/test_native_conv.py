@@ -70,3 +70,42 @@ def test_einconv_local_uses_native(monkeypatch):
     want = _ref(x, w.permute(3, 0, 1, 2), None, pad=1)
     _close(y, want)
     assert calls
+
+
+@pytest.mark.parametrize("pad", [1, 2])
+def test_conv_kernel_padding_forward_backward(pad):
+    torch.manual_seed(3)
+    K = 2 * pad + 1
+    x = torch.randn(2, 9, 37, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(64, K, K, 64, device="cuda") * 0.05).to(torch.bfloat16).requires_grad_(True)
+    y = conv2d_native(x, w, None, pad, pad)
+    assert y.shape == (2, 9, 37, 64)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().float().requires_grad_(True)
+    yr = _ref(xr, wr, None, pad=pad)
+    yr.backward(g.float())
+    _close(y, yr)
+    _close(x.grad, xr.grad)
+    _close(w.grad, wr.grad)
+    _native.check_errors()
+
+
+def test_einconv_pads_in_kernel_without_copy(monkeypatch):
+    """Local zero-boundary axes are padded by the kernel: no halo_tensor copy is made."""
+    import torch_einshard_b200 as es
+    from torch_einshard_b200.ops import conv as conv_mod
+    calls = []
+    real = conv_mod.halo_tensor
+
+    def spy(spec, x, halos, **kw):
+        if halos:
+            calls.append(dict(halos))
+        return real(spec, x, halos, **kw)
+    monkeypatch.setattr(conv_mod, "halo_tensor", spy)
+    x = torch.randn(2, 16, 40, 64, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(3, 3, 64, 128, device="cuda") * 0.05).to(torch.bfloat16)
+    y = es.einconv("b h w c, kh kw c o -> b h w o", x, w, {"h": "kh", "w": "kw"}, checkpoint=None)
+    _close(y, _ref(x, w.permute(3, 0, 1, 2), None, pad=1))
+    assert calls == []

@@ -11,9 +11,9 @@ if not torch.cuda.is_available():
 from torch_einshard_b200.ops import _native, gemm  # noqa: E402
 
 
-@pytest.fixture(params=[0, 1], ids=["1sm", "2sm"], autouse=True)
+@pytest.fixture(params=[0, 1, 2], ids=["1sm", "2sm", "2sm_wide"], autouse=True)
 def kernel_variant(request):
-    """Run every case on both the 1-SM and the 2-SM (CTA pair) kernel."""
+    """Run every case on the 1-SM, the 2-SM (CTA pair) and the wide 2-SM kernel."""
     mod = _native.require()
     mod.set_gemm_pair_mode(request.param)
     yield request.param
@@ -91,3 +91,24 @@ def test_gemm_autograd_matches_torch():
         scale = ref.abs().max().item() + 1.0
         assert (got.float() - ref).abs().max().item() <= 3e-2 * scale
     _native.check_errors(a.device)
+
+
+@pytest.mark.parametrize("a_t,b_t", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("m,n,k", [(1000, 128, 320), (777, 100, 64), (4096, 8, 128)])
+def test_gemm_narrow_n_runs_transposed(a_t, b_t, m, n, k):
+    """N narrower than a tile with M larger: computed as C^T = B^T A^T, stored transposed."""
+    torch.manual_seed(5)
+    a = _operand(m, k, 1, torch.bfloat16, a_t)
+    b = _operand(k, n, 1, torch.bfloat16, b_t)
+    _check(a, b)
+    _check(a, b, out_dtype=torch.float32)
+
+
+def test_gemm_narrow_n_batched_silu():
+    torch.manual_seed(6)
+    a = _operand(640, 96, 3, torch.bfloat16, False)
+    b = _operand(96, 64, 3, torch.bfloat16, True)
+    _native.reset_errors()
+    c = gemm.native_bmm(a, b, act="silu")
+    ref = torch.nn.functional.silu(torch.matmul(a.float(), b.float()))
+    assert (c.float() - ref).abs().max().item() <= 2e-2 * (ref.abs().max().item() + 1)

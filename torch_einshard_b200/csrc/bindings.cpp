@@ -6,6 +6,8 @@
 #include <atomic>
 
 #include "comm.h"
+#include "conv.h"
+#include "copy.h"
 #include "fft.h"
 #include "gemm.h"
 #include "gemm_ar.h"
@@ -391,6 +393,74 @@ void fft_slab(int64_t id, at::Tensor out, int64_t n, int64_t A, int64_t B, int64
   g_launches.fetch_add(2, std::memory_order_relaxed);
 }
 
+// ------------------------------------------------------------------ convolution
+
+// out[B, Hout, Wout, O] = conv2d(x[B, Hin, Win, C], w[O, KH, KW, C]) + bias, zero padding (ph, pw).
+void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor& bias, at::Tensor out, int64_t ph,
+                     int64_t pw, const at::Tensor& err) {
+  TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda() && x.dim() == 4 && w.dim() == 4 && out.dim() == 4,
+              "einshard conv: 4-D CUDA tensors required");
+  TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "einshard conv: contiguous NHWC required");
+  TORCH_CHECK(x.scalar_type() == w.scalar_type() && x.scalar_type() == out.scalar_type() &&
+                  (x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kHalf),
+              "einshard conv: bf16/fp16 tensors of one dtype required");
+  TORCH_CHECK(w.size(3) == x.size(3), "einshard conv: channel mismatch");
+  es::ConvArgs a;
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.out = out.data_ptr();
+  a.dtype = dtype_code(x.scalar_type());
+  a.B = x.size(0);
+  a.Hin = x.size(1);
+  a.Win = x.size(2);
+  a.C = x.size(3);
+  a.O = w.size(0);
+  a.KH = w.size(1);
+  a.KW = w.size(2);
+  a.ph = static_cast<int>(ph);
+  a.pw = static_cast<int>(pw);
+  if (bias.numel() > 0) {
+    TORCH_CHECK(bias.is_cuda() && bias.scalar_type() == at::kFloat && bias.is_contiguous() && bias.numel() == a.O,
+                "einshard conv: bias must be a contiguous float32 CUDA tensor of length O");
+    a.bias = bias.data_ptr<float>();
+  }
+  a.err = err.data_ptr<int>();
+  a.num_sms = num_sms(x.get_device());
+  const char* why = es::check_conv_args(a);
+  TORCH_CHECK(why == nullptr, "einshard conv: ", why ? why : "");
+  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
+  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  TORCH_CHECK(out.size(0) == a.B && out.size(1) == Hout && out.size(2) == Wout && out.size(3) == a.O,
+              "einshard conv: output shape");
+  const c10::cuda::CUDAGuard guard(x.device());
+  const int rc = es::conv_launch(a, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard conv: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// out (contiguous) = view (any strides, rank <= 8), one gather kernel.
+void strided_copy(const at::Tensor& view, at::Tensor out) {
+  TORCH_CHECK(view.is_cuda() && out.is_cuda() && out.is_contiguous() && out.sizes() == view.sizes() &&
+                  out.scalar_type() == view.scalar_type() && view.dim() <= es::kCopyMaxRank,
+              "einshard strided_copy: bad arguments");
+  if (view.numel() == 0) return;
+  long long size[es::kCopyMaxRank], stride[es::kCopyMaxRank];
+  for (int64_t d = 0; d < view.dim(); ++d) {
+    size[d] = view.size(d);
+    stride[d] = view.stride(d);
+  }
+  const int rank = view.dim() == 0 ? 1 : static_cast<int>(view.dim());
+  if (view.dim() == 0) {
+    size[0] = 1;
+    stride[0] = 1;
+  }
+  const c10::cuda::CUDAGuard guard(view.device());
+  const int rc = es::strided_gather(view.data_ptr(), out.data_ptr(), static_cast<int>(view.element_size()), rank, size,
+                                    stride, num_sms(view.get_device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard strided_copy: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
 int64_t comm_data_bytes(int64_t id) { return static_cast<int64_t>(comm_ref(id).data_bytes); }
 
 }  // namespace
@@ -405,6 +475,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_all_reduce", &comm_all_reduce, "two-shot NVLink all-reduce in place");
   m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)");
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
+  m.def("conv2d_implicit", &conv2d_implicit, "implicit-GEMM NHWC conv2d on tcgen05 (stride 1)");
+  m.def("strided_copy", &strided_copy, "materialise a strided view contiguously");
   m.def("fft_c2c", &fft_c2c, "complex64 FFT along one dim (powers of two up to 1024)");
   m.def("comm_region", &comm_region, "this rank's symmetric data region as a uint8 tensor");
   m.def("comm_acquire", &comm_acquire, "wait until peers finished reading this rank's region");

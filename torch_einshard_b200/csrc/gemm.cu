@@ -5,6 +5,7 @@
 #include "gemm.h"
 #include "gemm_tc.cuh"
 #include "gemm_tc2.cuh"
+#include "gemm_tc3.cuh"
 #include "tma_desc.h"
 
 namespace es {
@@ -14,7 +15,7 @@ static CUtensorMapDataType tma_dtype(int dtype) {
 }
 
 bool use_pair_kernel(const GemmArgs& g) {
-  if (g.pair >= 0) return g.pair == 1;
+  if (g.pair >= 0) return g.pair >= 1;
   // Measured on B200: the 1-SM kernel is faster on long power-capped runs of
   // the large TP shapes, the 2-SM kernel on short ones; default to 1-SM.
   return false;
@@ -99,8 +100,64 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShape& s
   return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, s, epi));
 }
 
+// C = A B computed as C^T = B^T A^T: operand roles and majorness swap, the
+// epilogue stores transposed.  Used when N is narrower than a tile and M is
+// larger, so the 256-wide N tile is not half empty.
+static GemmArgs swapped(const GemmArgs& g) {
+  GemmArgs t = g;
+  t.A = g.B;
+  t.B = g.A;
+  t.M = g.N;
+  t.N = g.M;
+  t.a_mn = g.b_mn;  // B [N][K] K-major -> A' K-major; B [K][N] -> A' MN-major
+  t.lda = g.ldb;
+  t.a_batch_stride = g.b_batch_stride;
+  t.b_mn = g.a_mn;
+  t.ldb = g.lda;
+  t.b_batch_stride = g.a_batch_stride;
+  return t;
+}
+
+static bool want_swap(const GemmArgs& g) { return g.N < kBN && g.M > g.N; }
+
+// Launch the wide 2-SM kernel (256 x 512 pair tiles) on clusters of two CTAs.
+template <class Epi>
+int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, const Epi& epi, cudaStream_t stream) {
+  GemmShape s = make_shape(g);
+  s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
+  s.num_n = (g.N + kBN3 - 1) / kBN3;
+  s.group_m = g.group_m > 0 ? g.group_m : 8;
+  s.pair = 1;
+  auto kernel = gemm_tc3_kernel<Epi>;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> dev & 1ull)) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3Bytes);
+    attr_set |= 1ull << dev;
+  }
+  const int pairs = s.num_m * s.num_n * s.batch;
+  int clusters = g.num_sms / 2;
+  if (pairs < clusters) clusters = pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kThreads3);
+  cfg.dynamicSmemBytes = kSmem3Bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, s, epi));
+}
+
 template <typename OutT>
-static int launch_store(const GemmArgs& g, cudaStream_t stream) {
+static int launch_store(const GemmArgs& g0, cudaStream_t stream) {
+  const bool trans = want_swap(g0);
+  const GemmArgs g = trans ? swapped(g0) : g0;
   const bool pair = use_pair_kernel(g);
   CUtensorMap ma, mb;
   make_operand_maps(g, &ma, &mb, pair);
@@ -110,9 +167,11 @@ static int launch_store(const GemmArgs& g, cudaStream_t stream) {
   epi.ldc = g.ldc;
   epi.batch_stride = g.c_batch_stride;
   epi.act = g.act;
+  epi.trans = trans ? 1 : 0;
   const int esz = sizeof(OutT);
   epi.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * esz) % 16 == 0) &&
                (g.batch == 1 || (g.c_batch_stride * esz) % 16 == 0);
+  if (pair && g.pair == 2) return launch_wide(ma, mb, g, epi, stream);
   if (pair) return launch_pair(ma, mb, s, epi, g.num_sms, stream);
   auto kernel = gemm_tc_kernel<StoreEpilogue<OutT>>;
   static unsigned long long attr_set = 0;  // one bit per device

@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
         const int s = it % kStages;
         const uint32_t ph = (it / kStages) & 1u;
-        if (!mbar_wait(&st->empty[s], ph ^ 1u, abort_flag, shp.err, kErrWaitEmpty)) goto producer_done;
+        if (!mbar_wait_lane0(&st->empty[s], ph ^ 1u, abort_flag, shp.err, kErrWaitEmpty)) goto producer_done;
         if (lane == 0) {
           mbar_arrive_expect_tx(&st->full[s], kStageBytes);
           loads.load(shp, c, kb, sA + s * kABytes, sB + s * kBBytes, &st->full[s], &tmA, &tmB);
@@ -200,13 +200,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++tc) {
       const uint32_t acc = tc & 1u;
       const uint32_t aph = (tc >> 1) & 1u;
-      if (!mbar_wait(&st->tempty[acc], aph ^ 1u, abort_flag, shp.err, kErrWaitTmemEmpty)) goto mma_done;
+      if (!mbar_wait_lane0(&st->tempty[acc], aph ^ 1u, abort_flag, shp.err, kErrWaitTmemEmpty)) goto mma_done;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + acc * kBN;
       for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
         const int s = it % kStages;
         const uint32_t ph = (it / kStages) & 1u;
-        if (!mbar_wait(&st->full[s], ph, abort_flag, shp.err, kErrWaitFull)) goto mma_done;
+        if (!mbar_wait_lane0(&st->full[s], ph, abort_flag, shp.err, kErrWaitFull)) goto mma_done;
         tc_fence_after();
         if (lane == 0) {
           const uint32_t a_addr = smem_u32(sA + s * kABytes);
@@ -330,6 +330,7 @@ struct StoreEpilogue {
   long long batch_stride;
   int vec_ok;
   int act;
+  int trans;  // 1: the kernel computes C^T (operands swapped); tile rows are columns of C
 
   __device__ __forceinline__ void setup(SharedState*, const GemmShape&) {}
   __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
@@ -337,6 +338,27 @@ struct StoreEpilogue {
   __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape& s, volatile int*) {
     const int row = et.c.m0 + et.row;
     const bool row_ok = row < s.M;
+    if (trans) {
+      // lanes hold neighbouring columns of C: every store is 32 consecutive elements of one C row
+      OutT* ccol = C + static_cast<long long>(et.c.b) * batch_stride + row;
+#pragma unroll 1
+      for (int chunk = 0; chunk < kBN / 32; ++chunk) {
+        const int col0 = et.c.n0 + chunk * 32;
+        if (col0 >= s.N) break;
+        uint32_t r[32];
+        tmem_ld32(et.tmem + chunk * 32, r);
+        tmem_ld_wait();
+        if (!row_ok) continue;
+        const int valid = s.N - col0 < 32 ? s.N - col0 : 32;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v = __uint_as_float(r[i]);
+          if (act == kActSilu) v = silu_f(v);
+          if (i < valid) StoreOut<OutT>::store1(ccol + static_cast<long long>(col0 + i) * ldc, v);
+        }
+      }
+      return true;
+    }
     OutT* crow = C + static_cast<long long>(et.c.b) * batch_stride + static_cast<long long>(row) * ldc;
 #pragma unroll 1
     for (int chunk = 0; chunk < kBN / 32; ++chunk) {

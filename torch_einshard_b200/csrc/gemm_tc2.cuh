@@ -102,7 +102,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
         const int s = it % kStages2;
         const uint32_t ph = (it / kStages2) & 1u;
-        if (!mbar_wait(&st->empty[s], ph ^ 1u, abort_flag, shp.err, kErrWaitEmpty)) goto producer_done;
+        if (!mbar_wait_lane0(&st->empty[s], ph ^ 1u, abort_flag, shp.err, kErrWaitEmpty)) goto producer_done;
         if (lane == 0) {
           uint8_t* a = sA + s * kA2Bytes;
           uint8_t* b = sB + s * kB2Bytes;
@@ -147,13 +147,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int p = cluster; p < pairs; p += nclusters, ++tc) {
         const uint32_t acc = tc & 1u;
         const uint32_t aph = (tc >> 1) & 1u;
-        if (!mbar_wait(&st->tempty[acc], aph ^ 1u, abort_flag, shp.err, kErrWaitTmemEmpty)) goto mma_done;
+        if (!mbar_wait_lane0(&st->tempty[acc], aph ^ 1u, abort_flag, shp.err, kErrWaitTmemEmpty)) goto mma_done;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * kBN;
         for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
           const int s = it % kStages2;
           const uint32_t ph = (it / kStages2) & 1u;
-          if (!mbar_wait(&st->full[s], ph, abort_flag, shp.err, kErrWaitFull)) goto mma_done;
+          if (!mbar_wait_lane0(&st->full[s], ph, abort_flag, shp.err, kErrWaitFull)) goto mma_done;
           tc_fence_after();
           if (lane == 0) {
             const uint32_t a_addr = smem_u32(sA + s * kA2Bytes);

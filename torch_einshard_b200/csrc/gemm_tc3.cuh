@@ -1,0 +1,243 @@
+// Wide 2-SM (CTA pair) persistent tcgen05 GEMM: 256 x 512 output tile per pair.
+//
+// Each CTA of the pair owns 128 rows x 512 columns of the tile, i.e. all 512
+// TMEM columns as one fp32 accumulator; each K=16 step issues two
+// tcgen05.mma.cta_group::2 (M=256, N=256), one per 256-column half.  Per 64-deep
+// K block every SM stages 16 KB of A (its 128 rows) and 32 KB of B (its two
+// 128-column quarters), so the L2->SM traffic per MMA cycle is 3/4 of the
+// 256 x 256 pair kernel's and 1/2 of the 1-SM 128 x 256 kernel's; no TMA
+// multicast is used (every CTA loads its own boxes).
+//
+// With the whole TMEM in one accumulator there is no second buffer: the MMA
+// warp waits for the epilogue to drain the previous tile before the first MMA
+// of the next one.  Eight epilogue warps per CTA (two per TMEM lane quadrant,
+// one per 256-column half) keep that drain short, and the producer keeps
+// filling the shared-memory stages meanwhile.
+//
+// Warps (320 threads): 0 TMA producer, 1 MMA issuer (leader CTA) + TMEM owner,
+// 2..9 epilogue.  Barriers as in gemm_tc2.cuh; tempty counts the 16 epilogue
+// warps of the pair.
+#pragma once
+
+#include "gemm_tc.cuh"
+
+namespace es {
+
+constexpr int kBN3 = 512;                          // pair tile width
+constexpr int kStages3 = 4;
+constexpr int kA3Bytes = kBM * kBK * 2;            // 16 KB: this CTA's 128 A rows
+constexpr int kB3Bytes = (kBN3 / 2) * kBK * 2;     // 32 KB: this CTA's two 128-column B quarters
+constexpr int kStage3Bytes = kA3Bytes + kB3Bytes;
+constexpr int kThreads3 = 320;
+constexpr int kEpiWarps3 = 8;
+constexpr int kSmem3Bytes = kStages3 * kStage3Bytes + 1024 + 1024;
+
+struct SharedState3 {
+  uint64_t full[kStages3];
+  uint64_t empty[kStages3];
+  uint64_t tfull;
+  uint64_t tempty;
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort_flag;
+  int consumed;
+  int epi[32];
+};
+
+// Pair tile p -> this CTA's 128-row half; columns n0 .. n0 + 511.
+__device__ __forceinline__ TileCoord tile_coord3(const GemmShape& s, int p, int rank) {
+  const int per_batch = s.num_m * s.num_n;
+  const int b = p / per_batch;
+  const int r = p - b * per_batch;
+  const int per_group = s.group_m * s.num_n;
+  const int g = r / per_group;
+  const int first_m = g * s.group_m;
+  const int gm = min(s.num_m - first_m, s.group_m);
+  const int in_group = r - g * per_group;
+  const int mb = first_m + in_group % gm;
+  const int nb = in_group / gm;
+  return {b, mb * 2 * kBM + rank * kBM, nb * kBN3};
+}
+
+template <class Epi>
+__global__ void __launch_bounds__(kThreads3, 1)
+    gemm_tc3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const GemmShape shp, Epi epi) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kStages3 * kA3Bytes;
+  SharedState3* st = reinterpret_cast<SharedState3*>(smem + kStages3 * kStage3Bytes);
+  SharedState* st_common = reinterpret_cast<SharedState*>(st);  // epilogue policies use only common fields
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pairs = shp.num_m * shp.num_n * shp.batch;
+  const int cluster = static_cast<int>(cluster_id_x());
+  const int nclusters = static_cast<int>(nclusters_x());
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages3; ++s) {
+      mbar_init(&st->full[s], 1);
+      mbar_init(&st->empty[s], 1);
+    }
+    mbar_init(&st->tfull, 1);
+    mbar_init(&st->tempty, 2 * kEpiWarps3);
+    mbar_init(&st->drain, 1);
+    st->abort_flag = 0;
+    st->consumed = 0;
+    for (int i = 0; i < 32; ++i) st->epi[i] = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(&st->tmem_base, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = st->tmem_base;
+  volatile int* abort_flag = &st->abort_flag;
+  epi.setup(st_common, shp);
+
+  const uint32_t full_leader0 = map_to_cta(&st->full[0], 0);
+  const uint32_t tempty_leader = map_to_cta(&st->tempty, 0);
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    uint32_t it = 0;
+    for (int p = cluster; p < pairs; p += nclusters) {
+      const TileCoord c = tile_coord3(shp, p, static_cast<int>(rank));
+      const int nq0 = c.n0 + static_cast<int>(rank) * (kBN / 2);  // this CTA's quarter in each 256-col half
+      for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
+        const int s = it % kStages3;
+        const uint32_t ph = (it / kStages3) & 1u;
+        if (!mbar_wait_lane0(&st->empty[s], ph ^ 1u, abort_flag, shp.err, kErrWaitEmpty)) goto producer_done;
+        if (lane == 0) {
+          uint8_t* a = sA + s * kA3Bytes;
+          uint8_t* b = sB + s * kB3Bytes;
+          const uint32_t fbar = full_leader0 + s * 8;
+          if (leader) mbar_arrive_expect_tx(&st->full[s], 2 * kStage3Bytes);
+          const int k0 = kb * kBK;
+          if (!shp.a_mn) {
+            tma_load_3d_pair(a, &tmA, fbar, k0, c.m0, c.b);
+          } else {
+            tma_load_3d_pair(a, &tmA, fbar, c.m0, k0, c.b);
+            tma_load_3d_pair(a + 8192, &tmA, fbar, c.m0 + 64, k0, c.b);
+          }
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint8_t* bh = b + h * (kB3Bytes / 2);
+            const int n = nq0 + h * kBN;
+            if (!shp.b_mn) {
+              tma_load_3d_pair(bh, &tmB, fbar, k0, n, c.b);
+            } else {
+              tma_load_3d_pair(bh, &tmB, fbar, n, k0, c.b);
+              tma_load_3d_pair(bh + 8192, &tmB, fbar, n + 64, k0, c.b);
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+  producer_done:
+    __syncwarp();
+    if (*abort_flag && leader && lane == 0) {
+      const uint32_t consumed = static_cast<uint32_t>(*reinterpret_cast<volatile int*>(&st->consumed));
+      for (uint32_t j = consumed; j < it; ++j) {
+        int dummy_abort = 0;
+        mbar_wait(&st->full[j % kStages3], (j / kStages3) & 1u, &dummy_abort, nullptr, 0);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader CTA)
+    if (leader) {
+      const uint32_t idesc = umma_idesc_f16(2 * kBM, kBN, shp.in_bf16, shp.a_mn, shp.b_mn);
+      const uint32_t a_lbo = shp.a_mn ? 8192u : 16u;
+      const uint32_t b_lbo = shp.b_mn ? 8192u : 16u;
+      const uint32_t a_kstep = shp.a_mn ? 2048u : 32u;
+      const uint32_t b_kstep = shp.b_mn ? 2048u : 32u;
+      uint32_t it = 0, tc = 0;
+      bool issued_any = false;
+      for (int p = cluster; p < pairs; p += nclusters, ++tc) {
+        if (!mbar_wait_lane0(&st->tempty, (tc & 1u) ^ 1u, abort_flag, shp.err, kErrWaitTmemEmpty)) goto mma_done;
+        tc_fence_after();
+        for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
+          const int s = it % kStages3;
+          const uint32_t ph = (it / kStages3) & 1u;
+          if (!mbar_wait_lane0(&st->full[s], ph, abort_flag, shp.err, kErrWaitFull)) goto mma_done;
+          tc_fence_after();
+          if (lane == 0) {
+            const uint32_t a_addr = smem_u32(sA + s * kA3Bytes);
+            const uint32_t b_addr = smem_u32(sB + s * kB3Bytes);
+#pragma unroll
+            for (int k = 0; k < kBK / kUmmaK; ++k) {
+              const uint64_t ad = umma_desc_sw128(a_addr + k * a_kstep, a_lbo, 1024u);
+              const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const uint64_t bd = umma_desc_sw128(b_addr + h * (kB3Bytes / 2) + k * b_kstep, b_lbo, 1024u);
+                umma_f16_pair(tmem_base + h * kBN, ad, bd, idesc, acc);
+              }
+            }
+            umma_commit_pair_mc(&st->empty[s], 0x3);
+            *reinterpret_cast<volatile int*>(&st->consumed) = static_cast<int>(it + 1);
+          }
+          issued_any = true;
+          __syncwarp();
+        }
+        if (lane == 0) umma_commit_pair_mc(&st->tfull, 0x3);
+        __syncwarp();
+      }
+    mma_done:
+      __syncwarp();
+      if (*abort_flag && issued_any && lane == 0) {
+        umma_commit_pair_mc(&st->drain, 0x1);
+        int dummy_abort = 0;
+        mbar_wait(&st->drain, 0, &dummy_abort, nullptr, 0);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs, 8 warps)
+    const int q = warp & 3;           // TMEM lane quadrant this warp may access
+    const int half = (warp - 2) >> 2;  // 256-column half of the tile
+    uint32_t tc = 0;
+    for (int p = cluster; p < pairs; p += nclusters, ++tc) {
+      if (!mbar_wait(&st->tfull, tc & 1u, abort_flag, shp.err, kErrWaitTmemFull)) break;
+      tc_fence_after();
+      EpiTile et;
+      et.t = 2 * p + static_cast<int>(rank);
+      et.c = tile_coord3(shp, p, static_cast<int>(rank));
+      et.c.n0 += half * kBN;
+      et.tmem = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + half * kBN;
+      et.row = q * 32 + lane;
+      et.q = q;
+      et.lane = lane;
+      const bool ok = et.c.n0 < shp.N ? epi.tile(et, shp, abort_flag) : true;
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader);
+      if (!ok) {
+        *abort_flag = 1;
+        break;
+      }
+    }
+    epi.finish(shp, abort_flag);
+  }
+
+  __syncthreads();
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+}  // namespace es

@@ -84,6 +84,15 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Warp-uniform wait in which only lane 0 polls the barrier (the other lanes
+// park on the shuffle), for the single-issuer producer and MMA warps.
+__device__ __forceinline__ bool mbar_wait_lane0(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                                int code) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, err, code) ? 1 : 0;
+  return __shfl_sync(0xffffffffu, ok, 0) != 0;
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
                                             int c2) {

@@ -58,6 +58,13 @@ def _conv_fn(ndim):
         raise ValueError("einconv supports 1D, 2D, and 3D convolutions") from None
 
 
+def _mesh_dim_size(mesh, dim):
+    try:
+        return mesh[dim].size()
+    except Exception:  # noqa: BLE001 - compound or unknown names: not treated as trivial
+        return 0
+
+
 def _checkpointed(function, tensors, mode, use_reentrant):
     if mode in (False, None, "none"):
         return function(*tensors)
@@ -166,12 +173,28 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
     conv_out = batch + [cout] + spatial
     out_perm = [conv_out.index(n) for n in out_names]
 
+    from . import conv_native
+    # Local spatial axes with a zero boundary are padded by the native kernel itself
+    # (TMA zero fill), so no padded copy of the input is made for them.
+    kernel_pads = {}
+    if conv_native.kernel_padding_ok(x, weight, x.shape[in_names.index(cin)], spatial, dilation) and \
+            boundary == "constant" and fill == 0:
+        for name in spatial:
+            left, right = normalize_halo(halos[name])
+            axis = in_axes[in_names.index(name)]
+            # an axis sharded over a one-rank mesh dim has no neighbours: its halo is the zero boundary
+            alone = not axis.local() and mesh is not None and _mesh_dim_size(mesh, axis.shard_dim) == 1
+            if (axis.local() or alone) and left == right:
+                kernel_pads[name] = left
+    other_halos = {n: h for n, h in halos.items() if n not in kernel_pads}
+
     def run_conv(xa, wa, ba=None):
-        from . import conv_native
         native = conv_native.try_conv(xa, wa, ba, in_names, w_names, out_names, spatial, kernel, cin, cout,
-                                      dilation)
+                                      dilation, kernel_pads)
         if native is not None:
             return native
+        if kernel_pads:
+            xa = halo_tensor(in_spec, xa, kernel_pads, mesh=mesh, shapes=shapes, boundary=boundary, fill=fill)
         xc = xa.permute(x_perm).contiguous()
         lead = xc.shape[:len(batch)]
         xc = xc.reshape((-1, xc.shape[len(batch)], *xc.shape[len(batch) + 1:]))
@@ -182,7 +205,7 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
 
     def run_full(xa, wa, *maybe_bias):
         ba = maybe_bias[0] if maybe_bias else None
-        haloed = halo_tensor(in_spec, xa, halos, mesh=mesh, shapes=shapes, boundary=boundary, fill=fill)
+        haloed = halo_tensor(in_spec, xa, other_halos, mesh=mesh, shapes=shapes, boundary=boundary, fill=fill)
         if checkpoint == "conv":
             args = (haloed, wa) if ba is None else (haloed, wa, ba)
             return _checkpointed(lambda *a: run_conv(*a), args, "conv", use_reentrant)

@@ -29,11 +29,12 @@ def _run(mod, x, w, bias, ph, pw):
 
 class _Conv2dNHWC(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, w, bias):
+    def forward(ctx, x, w, bias, ph, pw):
         ctx.save_for_backward(x, w)
+        ctx.pad = (ph, pw)
         ctx.has_bias = bias is not None
         ctx.bias_dtype = bias.dtype if bias is not None else None
-        return _run(_native.require(), x, w, None if bias is None else bias.float().contiguous(), 0, 0)
+        return _run(_native.require(), x, w, None if bias is None else bias.float().contiguous(), ph, pw)
 
     @staticmethod
     def backward(ctx, grad):
@@ -41,43 +42,49 @@ class _Conv2dNHWC(torch.autograd.Function):
         grad = grad.contiguous()
         gx = gw = gb = None
         O, KH, KW, C = w.shape
+        ph, pw = ctx.pad
         if ctx.needs_input_grad[0]:
             if O % 64 == 0:
+                # full correlation with the flipped, channel-transposed kernel, cropped by the padding
                 wt = w.flip(1, 2).permute(3, 1, 2, 0).contiguous()  # [C][KH][KW][O]
-                gx = _run(_native.require(), grad, wt, None, KH - 1, KW - 1)
+                gx = _run(_native.require(), grad, wt, None, KH - 1 - ph, KW - 1 - pw)
             else:
                 gx = torch.nn.grad.conv2d_input(x.permute(0, 3, 1, 2).shape, w.permute(0, 3, 1, 2),
-                                                grad.permute(0, 3, 1, 2)).permute(0, 2, 3, 1)
+                                                grad.permute(0, 3, 1, 2), padding=(ph, pw)).permute(0, 2, 3, 1)
         if ctx.needs_input_grad[1]:
             gw = torch.nn.grad.conv2d_weight(x.permute(0, 3, 1, 2), w.permute(0, 3, 1, 2).shape,
-                                             grad.permute(0, 3, 1, 2)).permute(0, 2, 3, 1)
+                                             grad.permute(0, 3, 1, 2), padding=(ph, pw)).permute(0, 2, 3, 1)
         if ctx.has_bias and ctx.needs_input_grad[2]:
             gb = grad.float().sum(dim=(0, 1, 2)).to(ctx.bias_dtype)
-        return gx, gw, gb
+        return gx, gw, gb, None, None
 
 
-def conv2d_native(x, w, bias=None):
-    """Valid NHWC conv2d: x [B, H, W, C], w [O, KH, KW, C] -> [B, H-KH+1, W-KW+1, O]."""
+def supported(x, w_dtype, cin_size, ndim, dilation):
+    return (x.is_cuda and ndim == 2 and all(d == 1 for d in dilation) and x.dtype in (torch.bfloat16, torch.float16)
+            and w_dtype == x.dtype and cin_size % 64 == 0)
+
+
+def conv2d_native(x, w, bias=None, ph=0, pw=0):
+    """NHWC conv2d with zero padding (ph, pw): x [B, H, W, C], w [O, KH, KW, C] ->
+    [B, H + 2 ph - KH + 1, W + 2 pw - KW + 1, O]."""
     x, w = x.contiguous(), w.contiguous()
     if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad or (bias is not None and bias.requires_grad)):
-        return _Conv2dNHWC.apply(x, w, bias)
-    return _run(_native.require(), x, w, None if bias is None else bias.float().contiguous(), 0, 0)
+        return _Conv2dNHWC.apply(x, w, bias, ph, pw)
+    return _run(_native.require(), x, w, None if bias is None else bias.float().contiguous(), ph, pw)
 
 
-def conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation):
-    if len(spatial) != 2 or any(d != 1 for d in dilation):
+def conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation,
+                pads=None):
+    """``pads``: {spatial name: symmetric zero padding done by the kernel (TMA zero fill)}."""
+    if not weight.is_cuda or not supported(x, weight.dtype, x.shape[in_names.index(cin)], len(spatial), dilation):
         return None
-    if x.dtype not in (torch.bfloat16, torch.float16) or weight.dtype != x.dtype or not weight.is_cuda:
-        return None
-    C = x.shape[in_names.index(cin)]
-    if C % 64:
-        return None
+    pads = pads or {}
     batch = [n for n in in_names if n not in spatial and n != cin]
     xn = x.permute([in_names.index(n) for n in batch + list(spatial) + [cin]])
     lead = xn.shape[:len(batch)]
     xn = xn.reshape(-1, *xn.shape[len(batch):])
     wn = weight.permute([w_names.index(n) for n in [cout] + list(kernel) + [cin]])
-    out = conv2d_native(xn, wn, bias)
+    out = conv2d_native(xn, wn, bias, pads.get(spatial[0], 0), pads.get(spatial[1], 0))
     out = out.reshape(*lead, *out.shape[1:])
     produced = batch + list(spatial) + [cout]
     return out.permute([produced.index(n) for n in out_names]).contiguous()

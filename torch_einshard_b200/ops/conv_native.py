@@ -8,10 +8,21 @@ cannot address) and ``einconv`` then uses ``torch.nn.functional``.
 __all__ = ["try_conv"]
 
 
-def try_conv(x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation):
+def try_conv(x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation, pads=None):
     from . import _native
     mod = _native.module()
     if mod is None or not hasattr(mod, "conv2d_implicit") or not x.is_cuda:
         return None
     from .conv_impl import conv2d_nhwc
-    return conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation)
+    return conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation,
+                       pads)
+
+
+def kernel_padding_ok(x, weight, cin_size, spatial, dilation):
+    """True when the native kernel would run and can zero-pad by itself."""
+    from . import _native
+    mod = _native.module()
+    if mod is None or not hasattr(mod, "conv2d_implicit") or not x.is_cuda:
+        return False
+    from .conv_impl import supported
+    return supported(x, weight.dtype, cin_size, len(spatial), dilation)

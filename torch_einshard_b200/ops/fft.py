@@ -158,7 +158,7 @@ def _exchange_blocks(z, group, send_block, out_shape, recv_view):
     return out
 
 
-def _four_step_fft(x, group, dim, *, inverse, norm):
+def _distributed_fft_1d_no_autograd(x, group, dim, *, inverse, norm):
     """Distributed 1-D FFT along a sharded axis with equal shards, local size % P == 0."""
     P, r = dist.get_world_size(group), dist.get_rank(group)
     L = x.shape[dim]
@@ -199,12 +199,12 @@ class _DistributedFFT1D(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, group, dim, shapes, inverse, norm):
         ctx.args = (group, dim, inverse, norm)
-        return _four_step_fft(x, group, dim, inverse=inverse, norm=norm)
+        return _distributed_fft_1d_no_autograd(x, group, dim, inverse=inverse, norm=norm)
 
     @staticmethod
     def backward(ctx, grad):
         group, dim, inverse, norm = ctx.args
-        out = _four_step_fft(grad, group, dim, inverse=not inverse, norm=_adjoint_norm(inverse, norm))
+        out = _distributed_fft_1d_no_autograd(grad, group, dim, inverse=not inverse, norm=_adjoint_norm(inverse, norm))
         return out, None, None, None, None, None
 
 
