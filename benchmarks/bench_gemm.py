@@ -104,6 +104,7 @@ def main():
     p.add_argument("--shapes", default="cube_nt,cube_nn,cube_tt")
     p.add_argument("--kernels", default="cublas,1sm,2sm")
     p.add_argument("--group-m", type=int, default=0)
+    p.add_argument("--split", type=int, default=0, help="wide kernel: cluster split mode 0/1/2")
     args = p.parse_args()
     device = torch.device(args.device)
     from torch_einshard_b200.ops import _native, gemm
@@ -119,6 +120,7 @@ def main():
             else:
                 mod.set_gemm_pair_mode({"1sm": 0, "2sm": 1, "wide": 2, "auto": -1}[kern])
                 mod.set_gemm_group_m(args.group_m)
+                mod.set_gemm_split(args.split)
                 fn = lambda: gemm.native_bmm(a, b)  # noqa: E731
             label = f"gemm_{name}_{kern}"
             if args.mode == "burst":
@@ -135,6 +137,7 @@ def main():
                               "M": m, "N": n, "K": k, "a_mn": a_mn, "b_mn": b_mn, "kernel": kern})
         mod.set_gemm_pair_mode(-1)
         mod.set_gemm_group_m(0)
+        mod.set_gemm_split(0)
         del a, b
         torch.cuda.empty_cache()
     _native.check_errors()

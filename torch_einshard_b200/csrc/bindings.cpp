@@ -22,6 +22,8 @@ std::atomic<long long> g_launches{0};
 // -1: heuristic; 0/1: force the 1-SM / 2-SM GEMM kernel (tests, tuning)
 int g_pair_mode = -1;
 int g_group_m = 0;  // raster group override (0: kernel default)
+int g_split = 0;    // wide-kernel cluster split mode (tuning)
+unsigned long long* g_prof = nullptr;  // wide-kernel wait counters (tuning), device pointer or null
 
 int dtype_code(at::ScalarType t) {
   switch (t) {
@@ -100,6 +102,8 @@ es::GemmArgs gemm_args(const at::Tensor& a, const at::Tensor& b, at::Tensor& out
   g.num_sms = num_sms(a.get_device());
   g.pair = g_pair_mode;
   g.group_m = g_group_m;
+  g.split = g_split;
+  g.prof = g_prof;
   const char* why = es::check_gemm_args(g);
   TORCH_CHECK(why == nullptr, "einshard native gemm: ", why ? why : "");
   return g;
@@ -438,6 +442,15 @@ void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+void wait_probe(const at::Tensor& flag, int64_t target, int64_t timeout_ns, at::Tensor result, const at::Tensor& err) {
+  TORCH_CHECK(flag.is_cuda() && flag.scalar_type() == at::kInt && result.is_cuda() && result.scalar_type() == at::kInt,
+              "einshard wait_probe: int32 CUDA tensors required");
+  const c10::cuda::CUDAGuard guard(flag.device());
+  const int rc = es::wait_probe(flag.data_ptr<int>(), static_cast<int>(target), err.data_ptr<int>(), timeout_ns,
+                                result.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard wait_probe: launch failed (", rc, ")");
+}
+
 // out (contiguous) = view (any strides, rank <= 8), one gather kernel.
 void strided_copy(const at::Tensor& view, at::Tensor out) {
   TORCH_CHECK(view.is_cuda() && out.is_cuda() && out.is_contiguous() && out.sizes() == view.sizes() &&
@@ -476,6 +489,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)");
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
   m.def("conv2d_implicit", &conv2d_implicit, "implicit-GEMM NHWC conv2d on tcgen05 (stride 1)");
+  m.def("wait_probe", &wait_probe, "bounded wait on a flag (tests the timeout path)");
   m.def("strided_copy", &strided_copy, "materialise a strided view contiguously");
   m.def("fft_c2c", &fft_c2c, "complex64 FFT along one dim (powers of two up to 1024)");
   m.def("comm_region", &comm_region, "this rank's symmetric data region as a uint8 tensor");
@@ -485,5 +499,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_gemm_pair_mode", [](int64_t m) { g_pair_mode = static_cast<int>(m); },
         "-1 heuristic, 0 force 1-SM, 1 force 2-SM GEMM kernel");
   m.def("set_gemm_group_m", [](int64_t v) { g_group_m = static_cast<int>(v); }, "raster group height (0 default)");
+  m.def("set_gemm_split", [](int64_t v) { g_split = static_cast<int>(v); }, "wide-kernel cluster split (0/1/2)");
+  m.def("set_gemm_profile", [](const at::Tensor& t) {
+        g_prof = t.numel() >= 3 ? reinterpret_cast<unsigned long long*>(t.data_ptr()) : nullptr;
+      }, "int64 CUDA tensor of >= 3 wait-cycle counters for the wide GEMM (empty tensor: off)");
   m.def("launch_count", []() { return g_launches.load(); }, "native kernel launches so far");
 }

@@ -115,7 +115,9 @@ int launch(const ConvArgs& a, cudaStream_t stream) {
   s.in_bf16 = a.dtype == kDtypeBF16 ? 1 : 0;
   s.group_m = 16;
   s.pair = 0;
+  s.split = 0;
   s.err = a.err;
+  s.prof = nullptr;
 
   ConvLoads loads{a.C, a.KW, Hout, Wv, a.ph, a.pw};
   ConvStoreEpilogue<OutT> epi{reinterpret_cast<OutT*>(a.out), a.bias, a.O, Wout, Wv};

@@ -8,6 +8,7 @@
 #include <stdint.h>
 
 #include "copy.h"
+#include "ptx.cuh"
 
 namespace es {
 
@@ -167,6 +168,20 @@ int strided_gather(const void* src, void* dst, int esize, int rank, const long l
   } else {
     return -1;
   }
+  return static_cast<int>(cudaGetLastError());
+}
+
+// ------------------------------------------------------------------ bounded-wait probe
+
+namespace {
+__global__ void wait_probe_kernel(const int* flag, int target, int* err, long long timeout_ns, int* result) {
+  if (threadIdx.x != 0) return;
+  result[0] = wait_flag_geq_for(flag, target, err, kErrWaitPeerFlag, static_cast<uint64_t>(timeout_ns)) ? 1 : 0;
+}
+}  // namespace
+
+int wait_probe(const int* flag, int target, int* err, long long timeout_ns, int* result, cudaStream_t stream) {
+  wait_probe_kernel<<<1, 32, 0, stream>>>(flag, target, err, timeout_ns, result);
   return static_cast<int>(cudaGetLastError());
 }
 

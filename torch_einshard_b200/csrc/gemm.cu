@@ -14,12 +14,18 @@ static CUtensorMapDataType tma_dtype(int dtype) {
   return dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-bool use_pair_kernel(const GemmArgs& g) {
-  if (g.pair >= 0) return g.pair >= 1;
-  // Measured on B200: the 1-SM kernel is faster on long power-capped runs of
-  // the large TP shapes, the 2-SM kernel on short ones; default to 1-SM.
-  return false;
+// 0: 1-SM 128x256 kernel, 1: 2-SM 256x256, 2: wide 2-SM 256x512.
+int pick_kernel(const GemmArgs& g) {
+  if (g.pair >= 0) return g.pair;
+  // Measured on B200 under the 1 kW cap (sustained, TP-MLP shapes): the wide
+  // kernel beats the 1-SM kernel on every operand layout once there are enough
+  // 256x512 pair tiles to give every SM pair work; small problems keep the
+  // 1-SM kernel's finer tiles.
+  const long long pair_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 511) / 512) * g.batch;
+  return pair_tiles >= g.num_sms / 2 ? 2 : 0;
 }
+
+bool use_pair_kernel(const GemmArgs& g) { return pick_kernel(g) >= 1; }
 
 void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb, bool pair) {
   const CUtensorMapDataType dt = tma_dtype(g.dtype);
@@ -47,7 +53,9 @@ GemmShape make_shape(const GemmArgs& g) {
   s.in_bf16 = g.dtype == kDtypeBF16 ? 1 : 0;
   s.group_m = g.group_m > 0 ? g.group_m : 16;
   s.pair = 0;
+  s.split = 0;
   s.err = g.err;
+  s.prof = g.prof;
   return s;
 }
 
@@ -126,8 +134,9 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
   GemmShape s = make_shape(g);
   s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
   s.num_n = (g.N + kBN3 - 1) / kBN3;
-  s.group_m = g.group_m > 0 ? g.group_m : 8;
+  s.group_m = g.group_m > 0 ? g.group_m : 16;
   s.pair = 1;
+  s.split = g.split;
   auto kernel = gemm_tc3_kernel<Epi>;
   static unsigned long long attr_set = 0;
   int dev = 0;
@@ -171,7 +180,7 @@ static int launch_store(const GemmArgs& g0, cudaStream_t stream) {
   const int esz = sizeof(OutT);
   epi.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * esz) % 16 == 0) &&
                (g.batch == 1 || (g.c_batch_stride * esz) % 16 == 0);
-  if (pair && g.pair == 2) return launch_wide(ma, mb, g, epi, stream);
+  if (pair && pick_kernel(g) == 2) return launch_wide(ma, mb, g, epi, stream);
   if (pair) return launch_pair(ma, mb, s, epi, g.num_sms, stream);
   auto kernel = gemm_tc_kernel<StoreEpilogue<OutT>>;
   static unsigned long long attr_set = 0;  // one bit per device

@@ -32,6 +32,8 @@ struct GemmArgs {
   int num_sms = 148;
   int pair = -1;     // -1: choose; 0: 1-SM kernel; 1: 2-SM (CTA pair) kernel
   int group_m = 0;   // raster group height in M tiles (0: default)
+  int split = 0;     // wide kernel cluster split (see GemmShape::split)
+  unsigned long long* prof = nullptr;  // optional wait-cycle counters (wide kernel)
 };
 
 const char* check_gemm_args(const GemmArgs& g);

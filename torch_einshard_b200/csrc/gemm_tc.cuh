@@ -48,7 +48,10 @@ struct GemmShape {
   int in_bf16;
   int group_m;     // raster group height (M tiles) for L2 reuse
   int pair;        // 1: 2-SM kernel; tile t is half (t & 1) of 256-row pair tile t >> 1
+  int split;       // wide kernel: 0 one tile sequence; 1/2 the clusters split in two sets (first/second
+                   // half of the cluster ids, or even/odd ids), each walking one half of the M tiles
   int* err;
+  unsigned long long* prof;  // optional: per-CTA wait-cycle counters (see gemm_tc3.cuh), null when off
 };
 
 struct TileCoord {

@@ -59,6 +59,31 @@ __device__ __forceinline__ TileCoord tile_coord3(const GemmShape& s, int p, int 
   return {b, mb * 2 * kBM + rank * kBM, nb * kBN3};
 }
 
+// The i-th pair tile of this cluster, or false when it has no more.  With a
+// split, the two cluster sets walk disjoint halves of the M tiles (each set
+// keeps its own A panels in L2 and the sets share B).
+__device__ __forceinline__ bool pair_tile_at(const GemmShape& s, int cluster, int nclusters, int i, int rank,
+                                             TileCoord* out) {
+  if (s.split == 0 || (nclusters & 1) || s.num_m < 2) {
+    const int p = cluster + i * nclusters;
+    if (p >= s.num_m * s.num_n * s.batch) return false;
+    *out = tile_coord3(s, p, rank);
+    return true;
+  }
+  const int per = nclusters >> 1;
+  const int half = s.split == 1 ? (cluster >= per ? 1 : 0) : (cluster & 1);
+  const int idx = s.split == 1 ? cluster - half * per : (cluster >> 1);
+  const int m_lo = (s.num_m + 1) >> 1;
+  GemmShape h = s;
+  h.num_m = half ? s.num_m - m_lo : m_lo;
+  const int p = idx + i * per;
+  if (p >= h.num_m * h.num_n * h.batch) return false;
+  TileCoord c = tile_coord3(h, p, rank);
+  c.m0 += half * m_lo * 2 * kBM;
+  *out = c;
+  return true;
+}
+
 template <class Epi>
 __global__ void __launch_bounds__(kThreads3, 1)
     gemm_tc3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -74,7 +99,6 @@ __global__ void __launch_bounds__(kThreads3, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  const int pairs = shp.num_m * shp.num_n * shp.batch;
   const int cluster = static_cast<int>(cluster_id_x());
   const int nclusters = static_cast<int>(nclusters_x());
 
@@ -112,8 +136,8 @@ __global__ void __launch_bounds__(kThreads3, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
     uint32_t it = 0;
-    for (int p = cluster; p < pairs; p += nclusters) {
-      const TileCoord c = tile_coord3(shp, p, static_cast<int>(rank));
+    TileCoord c;
+    for (int ti = 0; pair_tile_at(shp, cluster, nclusters, ti, static_cast<int>(rank), &c); ++ti) {
       const int nq0 = c.n0 + static_cast<int>(rank) * (kBN / 2);  // this CTA's quarter in each 256-col half
       for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
         const int s = it % kStages3;
@@ -165,13 +189,20 @@ __global__ void __launch_bounds__(kThreads3, 1)
       const uint32_t b_kstep = shp.b_mn ? 2048u : 32u;
       uint32_t it = 0, tc = 0;
       bool issued_any = false;
-      for (int p = cluster; p < pairs; p += nclusters, ++tc) {
+      long long wait_full = 0, wait_tempty = 0;
+      const long long t_start = clock64();
+      TileCoord cm;
+      for (; pair_tile_at(shp, cluster, nclusters, static_cast<int>(tc), 0, &cm); ++tc) {
+        const long long t_e0 = shp.prof ? clock64() : 0;
         if (!mbar_wait_lane0(&st->tempty, (tc & 1u) ^ 1u, abort_flag, shp.err, kErrWaitTmemEmpty)) goto mma_done;
+        if (shp.prof) wait_tempty += clock64() - t_e0;
         tc_fence_after();
         for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
           const int s = it % kStages3;
           const uint32_t ph = (it / kStages3) & 1u;
+          const long long t_f0 = shp.prof ? clock64() : 0;
           if (!mbar_wait_lane0(&st->full[s], ph, abort_flag, shp.err, kErrWaitFull)) goto mma_done;
+          if (shp.prof) wait_full += clock64() - t_f0;
           tc_fence_after();
           if (lane == 0) {
             const uint32_t a_addr = smem_u32(sA + s * kA3Bytes);
@@ -197,6 +228,12 @@ __global__ void __launch_bounds__(kThreads3, 1)
       }
     mma_done:
       __syncwarp();
+      if (shp.prof && lane == 0) {
+        // counters: [0] MMA-warp cycles, [1] waiting for a filled stage, [2] waiting for the epilogue
+        atomicAdd(&shp.prof[0], static_cast<unsigned long long>(clock64() - t_start));
+        atomicAdd(&shp.prof[1], static_cast<unsigned long long>(wait_full));
+        atomicAdd(&shp.prof[2], static_cast<unsigned long long>(wait_tempty));
+      }
       if (*abort_flag && issued_any && lane == 0) {
         umma_commit_pair_mc(&st->drain, 0x1);
         int dummy_abort = 0;
@@ -208,12 +245,13 @@ __global__ void __launch_bounds__(kThreads3, 1)
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
     const int half = (warp - 2) >> 2;  // 256-column half of the tile
     uint32_t tc = 0;
-    for (int p = cluster; p < pairs; p += nclusters, ++tc) {
+    TileCoord ce;
+    for (; pair_tile_at(shp, cluster, nclusters, static_cast<int>(tc), static_cast<int>(rank), &ce); ++tc) {
       if (!mbar_wait(&st->tfull, tc & 1u, abort_flag, shp.err, kErrWaitTmemFull)) break;
       tc_fence_after();
       EpiTile et;
-      et.t = 2 * p + static_cast<int>(rank);
-      et.c = tile_coord3(shp, p, static_cast<int>(rank));
+      et.t = 2 * (cluster + static_cast<int>(tc) * nclusters) + static_cast<int>(rank);
+      et.c = ce;
       et.c.n0 += half * kBN;
       et.tmem = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + half * kBN;
       et.row = q * 32 + lane;

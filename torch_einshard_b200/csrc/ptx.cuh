@@ -207,6 +207,20 @@ __device__ __forceinline__ int atomic_add_release_sys(int* p, int v) {
   return old;
 }
 
+// Spin until *flag >= target (system scope) for at most timeout_ns.
+__device__ __forceinline__ bool wait_flag_geq_for(const int* flag, int target, int* err, int code,
+                                                  uint64_t timeout_ns) {
+  if (ld_acquire_sys(flag) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (ld_acquire_sys(flag) >= target) return true;
+    if ((i & 15u) == 0 && global_timer_ns() - t0 > timeout_ns) {
+      if (err) atomicCAS(err, 0, code);
+      return false;
+    }
+  }
+}
+
 // Spin until *flag >= target (system scope).  Bounded like mbar_wait.
 __device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, int* err, int code) {
   if (ld_acquire_sys(flag) >= target) return true;

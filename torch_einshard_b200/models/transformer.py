@@ -20,6 +20,7 @@ identical on every tp rank because activations entering them are replicated.
 import math
 
 import torch
+import torch.utils.checkpoint
 import torch.nn.functional as F
 
 from ..api import einshard
@@ -88,9 +89,10 @@ class _Block(torch.nn.Module):
 
 
 class TPTransformer(torch.nn.Module):
-    def __init__(self, cfg, mesh, *, tp_dim="tp", device=None, seed=0):
+    def __init__(self, cfg, mesh, *, tp_dim="tp", device=None, seed=0, checkpoint=False):
         super().__init__()
         self.cfg, self.mesh = cfg, mesh
+        self.checkpoint = checkpoint  # recompute each block in backward (activation checkpointing)
         tp_mesh = mesh[tp_dim]
         tp = tp_mesh.size()
         tp_rank = tp_mesh.get_local_rank()
@@ -120,7 +122,10 @@ class TPTransformer(torch.nn.Module):
     def forward(self, tokens, targets=None):
         x = F.embedding(tokens, self.embed)
         for block in self.blocks:
-            x = block(x, self.mesh)
+            if self.checkpoint and torch.is_grad_enabled():
+                x = torch.utils.checkpoint.checkpoint(block, x, self.mesh, use_reentrant=False)
+            else:
+                x = block(x, self.mesh)
         x = self.ln_f(x)
         logits = einshard("b s d, v d -> b s v", x, self.embed)
         if targets is None:

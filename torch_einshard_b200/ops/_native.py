@@ -11,7 +11,7 @@ import os
 
 import torch
 
-__all__ = ["module", "available", "require", "error_word", "check_errors", "reset_errors"]
+__all__ = ["module", "available", "require", "error_word", "check_errors", "reset_errors", "EinshardCommTimeout"]
 
 _state = {"loaded": False, "module": None, "error": None}
 _ERROR_WORDS = {}
@@ -65,8 +65,15 @@ _CODES = {
 }
 
 
+class EinshardCommTimeout(RuntimeError):
+    """A native kernel gave up a bounded wait (a peer never arrived, a pipeline
+    stage never completed).  The kernel returned cleanly; the CUDA context is
+    still usable, but the op's output is invalid."""
+
+
 def check_errors(device=None):
-    """Raise if any native kernel on ``device`` reported a timeout (synchronises)."""
+    """Raise :class:`EinshardCommTimeout` if any native kernel on ``device``
+    reported a timeout (synchronises)."""
     devices = [torch.device(device).index] if device is not None else list(_ERROR_WORDS)
     for index in devices:
         word = _ERROR_WORDS.get(index)
@@ -74,7 +81,7 @@ def check_errors(device=None):
             continue
         code = int(word[0].item())
         if code:
-            raise RuntimeError(f"einshard native kernel on cuda:{index} aborted: {_CODES.get(code, code)}")
+            raise EinshardCommTimeout(f"einshard native kernel on cuda:{index} aborted: {_CODES.get(code, code)}")
 
 
 def reset_errors():

@@ -123,10 +123,35 @@ class Communicator:
                            sequential, self._blocks(max(stage_bytes, out.numel() * esize)), self.err)
         return True
 
+    # -- health -------------------------------------------------------------
+    def _skip_injected(self):
+        """Host-side fault injection for tests: ``EINSHARD_FAULT_INJECT=skip:<rank>:<n>``
+        makes the given global rank skip its n-th native collective (it launches
+        nothing, so peers' bounded waits expire).  Returns True to skip."""
+        spec = os.environ.get("EINSHARD_FAULT_INJECT", "")
+        if not spec.startswith("skip:"):
+            return False
+        _, rank, nth = spec.split(":")
+        self.calls = getattr(self, "calls", 0) + 1
+        return int(rank) == dist.get_rank() and self.calls == int(nth)
+
+    def check_health(self):
+        """Synchronise and raise :class:`EinshardCommTimeout` if a kernel of this
+        device gave up a wait; the communicator is then marked broken and later
+        collectives fall back to ``torch.distributed``."""
+        try:
+            _native.check_errors(self.device)
+        except _native.EinshardCommTimeout:
+            self.broken = True
+            _native.reset_errors()
+            raise
+
     # -- collectives --------------------------------------------------------
     def all_reduce_(self, t, scale=1.0):
         if self.broken or t.dtype not in (torch.bfloat16, torch.float16, torch.float32) or not t.is_contiguous():
             return False
+        if self._skip_injected():
+            return True
         nbytes = t.numel() * t.element_size()
         if nbytes == 0:
             return True
