@@ -8,6 +8,8 @@
 #include "gemm_tc3.cuh"
 #include "tma_desc.h"
 
+#include <string.h>
+
 namespace es {
 
 static CUtensorMapDataType tma_dtype(int dtype) {
@@ -130,7 +132,22 @@ static bool want_swap(const GemmArgs& g) { return g.N < kBN && g.M > g.N; }
 
 // Launch the wide 2-SM kernel (256 x 512 pair tiles) on clusters of two CTAs.
 template <class Epi>
-int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, const Epi& epi, cudaStream_t stream) {
+int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, Epi epi, cudaStream_t stream) {
+  // output map for the TMA-store epilogue: 16-bit C, 16-byte aligned rows
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  const int out_bytes = g.out_dtype == kDtypeF32 ? 4 : 2;
+  const bool tma_ok = out_bytes == 2 && !epi.trans && (reinterpret_cast<uintptr_t>(g.C) & 15) == 0 &&
+                      (g.ldc * 2) % 16 == 0 && (g.batch == 1 || (g.c_batch_stride * 2) % 16 == 0);
+  if (tma_ok) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(g.N), static_cast<uint64_t>(g.M), static_cast<uint64_t>(g.batch)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(g.ldc) * 2,
+                                 static_cast<uint64_t>(g.batch > 1 ? g.c_batch_stride : g.ldc * g.M) * 2};
+    const uint32_t box[3] = {64, 32, 1};
+    mc = make_tmap_nd(g.C, g.out_dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                      3, dims, strides, box);
+  }
+  epi.tma = tma_ok ? 1 : 0;
   GemmShape s = make_shape(g);
   s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
   s.num_n = (g.N + kBN3 - 1) / kBN3;
@@ -160,7 +177,7 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, s, epi));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, s, epi));
 }
 
 template <typename OutT>
@@ -177,6 +194,7 @@ static int launch_store(const GemmArgs& g0, cudaStream_t stream) {
   epi.batch_stride = g.c_batch_stride;
   epi.act = g.act;
   epi.trans = trans ? 1 : 0;
+  epi.tma = 0;
   const int esz = sizeof(OutT);
   epi.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * esz) % 16 == 0) &&
                (g.batch == 1 || (g.c_batch_stride * esz) % 16 == 0);

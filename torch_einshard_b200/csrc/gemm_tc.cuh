@@ -24,6 +24,8 @@
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 
+#include <type_traits>
+
 #include "ptx.cuh"
 
 namespace es {
@@ -97,6 +99,8 @@ struct EpiTile {
   int row;        // this thread's tile row (0..127)
   int q;          // lane quadrant of this warp
   int lane;
+  const CUtensorMap* tmc = nullptr;  // output map for TMA stores (kernels that provide one)
+  uint8_t* stage = nullptr;          // this warp's 4 KB staging buffer (1024-byte aligned)
 };
 
 // Operand loads of one K block for the plain GEMM: A and B tiles by TMA from
@@ -334,11 +338,64 @@ struct StoreEpilogue {
   int vec_ok;
   int act;
   int trans;  // 1: the kernel computes C^T (operands swapped); tile rows are columns of C
+  int tma;    // 1: 16-bit output written by TMA stores through the warp's staging buffer
 
   __device__ __forceinline__ void setup(SharedState*, const GemmShape&) {}
   __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
 
+  // 32 rows x 256 columns of this warp, as four 32 x 64 boxes: TMEM -> registers
+  // (bf16/fp16) -> 128-byte-swizzled staging buffer -> one TMA store per box.
+  // The stores are coalesced by the TMA engine and clipped at the tensor edges.
+  __device__ __forceinline__ bool tile_tma(const EpiTile& et, const GemmShape& s) {
+    const int row0 = et.c.m0 + et.q * 32;
+    uint4* stage = reinterpret_cast<uint4*>(et.stage);
+#pragma unroll 1
+    for (int sub = 0; sub < kBN / 64; ++sub) {
+      const int col0 = et.c.n0 + sub * 64;
+      if (col0 >= s.N) break;  // uniform across the warp
+      uint32_t r0[32], r1[32];
+      tmem_ld32(et.tmem + sub * 64, r0);
+      tmem_ld32(et.tmem + sub * 64 + 32, r1);
+      tmem_ld_wait();
+      if (act == kActSilu) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          r0[i] = __float_as_uint(silu_f(__uint_as_float(r0[i])));
+          r1[i] = __float_as_uint(silu_f(__uint_as_float(r1[i])));
+        }
+      }
+      if (et.lane == 0) bulk_wait_group_read<0>();  // the previous box has left the staging buffer
+      __syncwarp();
+      const int sw = et.lane & 7;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t* src = j < 4 ? &r0[8 * j] : &r1[8 * (j - 4)];
+        uint4 v;
+        if (sizeof(OutT) == 2 && std::is_same<OutT, __half>::value) {
+          v = make_uint4(pack_f16(__uint_as_float(src[0]), __uint_as_float(src[1])),
+                         pack_f16(__uint_as_float(src[2]), __uint_as_float(src[3])),
+                         pack_f16(__uint_as_float(src[4]), __uint_as_float(src[5])),
+                         pack_f16(__uint_as_float(src[6]), __uint_as_float(src[7])));
+        } else {
+          v = make_uint4(pack_bf16(__uint_as_float(src[0]), __uint_as_float(src[1])),
+                         pack_bf16(__uint_as_float(src[2]), __uint_as_float(src[3])),
+                         pack_bf16(__uint_as_float(src[4]), __uint_as_float(src[5])),
+                         pack_bf16(__uint_as_float(src[6]), __uint_as_float(src[7])));
+        }
+        stage[et.lane * 8 + (j ^ sw)] = v;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (et.lane == 0) {
+        tma_store_3d(et.tmc, et.stage, col0, row0, et.c.b);
+        bulk_commit_group();
+      }
+    }
+    return true;
+  }
+
   __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape& s, volatile int*) {
+    if (tma && !trans && et.tmc != nullptr) return tile_tma(et, s);
     const int row = et.c.m0 + et.row;
     const bool row_ok = row < s.M;
     if (trans) {

@@ -30,7 +30,8 @@ constexpr int kB3Bytes = (kBN3 / 2) * kBK * 2;     // 32 KB: this CTA's two 128-
 constexpr int kStage3Bytes = kA3Bytes + kB3Bytes;
 constexpr int kThreads3 = 320;
 constexpr int kEpiWarps3 = 8;
-constexpr int kSmem3Bytes = kStages3 * kStage3Bytes + 1024 + 1024;
+constexpr int kStage3Out = 4096;                    // per epilogue warp: 32 rows x 64 cols x 2 B
+constexpr int kSmem3Bytes = kStages3 * kStage3Bytes + 1024 + kEpiWarps3 * kStage3Out + 1024;
 
 struct SharedState3 {
   uint64_t full[kStages3];
@@ -87,12 +88,13 @@ __device__ __forceinline__ bool pair_tile_at(const GemmShape& s, int cluster, in
 template <class Epi>
 __global__ void __launch_bounds__(kThreads3, 1)
     gemm_tc3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmShape shp, Epi epi) {
+                    const __grid_constant__ CUtensorMap tmC, const GemmShape shp, Epi epi) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages3 * kA3Bytes;
   SharedState3* st = reinterpret_cast<SharedState3*>(smem + kStages3 * kStage3Bytes);
+  uint8_t* out_stage = smem + kStages3 * kStage3Bytes + 1024;  // 1024-byte aligned (TMA swizzle atom)
   SharedState* st_common = reinterpret_cast<SharedState*>(st);  // epilogue policies use only common fields
 
   const int warp = threadIdx.x >> 5;
@@ -257,6 +259,8 @@ __global__ void __launch_bounds__(kThreads3, 1)
       et.row = q * 32 + lane;
       et.q = q;
       et.lane = lane;
+      et.tmc = &tmC;
+      et.stage = out_stage + (warp - 2) * kStage3Out;
       const bool ok = et.c.n0 < shp.N ? epi.tile(et, shp, abort_flag) : true;
       tc_fence_before();
       __syncwarp();
@@ -267,6 +271,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
       }
     }
     epi.finish(shp, abort_flag);
+    if (lane == 0) bulk_wait_group<0>();  // every TMA store of this warp has landed
   }
 
   __syncthreads();
