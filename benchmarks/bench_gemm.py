@@ -105,6 +105,8 @@ def main():
     p.add_argument("--kernels", default="cublas,1sm,2sm")
     p.add_argument("--group-m", type=int, default=0)
     p.add_argument("--split", type=int, default=0, help="wide kernel: cluster split mode 0/1/2")
+    p.add_argument("--sleep-ns", type=int, default=0, help="wide kernel: epilogue back-off between polls")
+    p.add_argument("--l2-promotion", type=int, default=3, help="TMA L2 promotion 0 none .. 3 256B")
     args = p.parse_args()
     device = torch.device(args.device)
     from torch_einshard_b200.ops import _native, gemm
@@ -121,6 +123,8 @@ def main():
                 mod.set_gemm_pair_mode({"1sm": 0, "2sm": 1, "wide": 2, "auto": -1}[kern])
                 mod.set_gemm_group_m(args.group_m)
                 mod.set_gemm_split(args.split)
+                mod.set_gemm_sleep_ns(args.sleep_ns)
+                mod.set_tma_l2_promotion(args.l2_promotion)
                 fn = lambda: gemm.native_bmm(a, b)  # noqa: E731
             label = f"gemm_{name}_{kern}"
             if args.mode == "burst":

@@ -73,3 +73,69 @@ def test_fused_gemm_allreduce_all_gpus():
     if n < 4:
         pytest.skip("needs 4+ GPUs")
     run_gpus(_fused, min(n, 8))
+
+
+def _sequence_parallel(rank, world):
+    """Megatron sequence parallelism: AG(x) -> GEMM and GEMM -> RS, fused, against NCCL."""
+    import torch.distributed as dist
+    from torch.distributed.device_mesh import init_device_mesh
+
+    import torch_einshard_b200 as es
+    from torch_einshard_b200.ops import _native, fused_native
+    from torch_einshard_b200.parallel import native_comm
+
+    mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
+    assert es.setup_native_comm(mesh)
+    group = mesh["tp"].get_group()
+    comm = native_comm.communicator_for(group)
+
+    # raw fused GEMM + reduce-scatter of row segments
+    torch.manual_seed(1)
+    for (segs, seg, n, k) in [(2, 256 * world, 512, 128), (1, 128 * world, 300, 64)]:
+        a = torch.randn(1, segs * seg, k, device="cuda", dtype=torch.bfloat16) * (rank + 1)
+        b = torch.randn(1, n, k, device="cuda", dtype=torch.bfloat16).transpose(1, 2)
+        for _ in range(2):
+            got = fused_native.gemm_reducescatter(comm, a, b, seg, seg // world)
+            full = (a.float() @ b.float())
+            dist.all_reduce(full, group=group)
+            shard = seg // world
+            want = full.reshape(segs, seg, n)[:, rank * shard:(rank + 1) * shard].reshape(1, -1, n)
+            scale = want.abs().max().item() + 1
+            assert (got.float() - want).abs().max().item() < 3e-2 * scale
+    _native.check_errors()
+
+    # through einshard: l/tp e, e f/tp -> l f/tp (AG -> GEMM) and back l f/tp, f/tp e -> l/tp e (GEMM -> RS)
+    torch.manual_seed(0)
+    L, E, F_ = 256 * world, 256, 512 * world
+    x_full = torch.randn(2, L, E, device="cuda", dtype=torch.bfloat16)
+    w1 = torch.randn(F_ // world, E, device="cuda", dtype=torch.bfloat16) * 0.05
+    w2 = torch.randn(E, F_ // world, device="cuda", dtype=torch.bfloat16) * 0.05
+    dy = torch.randn(2, L // world, E, device="cuda", dtype=torch.bfloat16)
+
+    def run():
+        x = x_full[:, rank * (L // world):(rank + 1) * (L // world)].clone().requires_grad_(True)
+        a = w1.clone().requires_grad_(True)
+        b = w2.clone().requires_grad_(True)
+        h = es.einshard("s l/tp e, f/tp e -> s l f/tp", x, a, mesh=mesh)
+        plan1 = [s.name for s in es.last_plan()]
+        y = es.einshard("s l f/tp, e f/tp -> s l/tp e", h, b, mesh=mesh)
+        plan2 = [s.name for s in es.last_plan()]
+        y.backward(dy)
+        return (h.detach().float(), y.detach().float(), x.grad.float(), a.grad.float(), b.grad.float()), plan1, plan2
+
+    got, p1, p2 = run()
+    assert p1 == ["allgather_forward_reducescatter_backward", "rank_local_einsum"], p1
+    assert p2 == ["rank_local_einsum", "reducescatter_forward_allgather_backward"], p2
+    native_comm.disable()
+    want, q1, q2 = run()
+    native_comm._state["enabled"] = True
+    assert (p1, p2) == (q1, q2)
+    for g, w in zip(got, want):
+        scale = w.abs().max().item() + 1e-3
+        assert (g - w).abs().max().item() < 3e-2 * scale
+    torch.cuda.synchronize()
+    _native.check_errors()
+
+
+def test_sequence_parallel_fused_2gpu():
+    run_gpus(_sequence_parallel, 2)

@@ -11,6 +11,7 @@
 #include "fft.h"
 #include "gemm.h"
 #include "gemm_ar.h"
+#include "tma_desc.h"
 
 #include <memory>
 #include <vector>
@@ -23,6 +24,7 @@ std::atomic<long long> g_launches{0};
 int g_pair_mode = -1;
 int g_group_m = 0;  // raster group override (0: kernel default)
 int g_split = 0;    // wide-kernel cluster split mode (tuning)
+int g_sleep_ns = 0;  // wide-kernel epilogue back-off (tuning)
 unsigned long long* g_prof = nullptr;  // wide-kernel wait counters (tuning), device pointer or null
 
 int dtype_code(at::ScalarType t) {
@@ -74,29 +76,23 @@ void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
-es::GemmArgs gemm_args(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t act, const at::Tensor& err) {
-  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "einshard native gemm: CUDA tensors required");
-  TORCH_CHECK(a.dim() == 3 && b.dim() == 3 && out.dim() == 3, "einshard native gemm: 3-D operands required");
+// Operand fields of a GEMM (the output fields are filled by the caller).
+es::GemmArgs gemm_operand_args(const at::Tensor& a, const at::Tensor& b, int64_t act, const at::Tensor& err) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda(), "einshard native gemm: CUDA tensors required");
+  TORCH_CHECK(a.dim() == 3 && b.dim() == 3, "einshard native gemm: 3-D operands required");
   TORCH_CHECK(a.scalar_type() == b.scalar_type(), "einshard native gemm: operand dtypes differ");
   TORCH_CHECK(a.size(0) == b.size(0) && a.size(2) == b.size(1), "einshard native gemm: shape mismatch");
-  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == a.size(1) && out.size(2) == b.size(2),
-              "einshard native gemm: output shape mismatch");
-  TORCH_CHECK(out.stride(2) == 1, "einshard native gemm: output must be row-major");
   es::GemmArgs g;
   g.A = a.data_ptr();
   g.B = b.data_ptr();
-  g.C = out.data_ptr();
   g.dtype = dtype_code(a.scalar_type());
   TORCH_CHECK(g.dtype != es::kDtypeF32, "einshard native gemm: bf16/fp16 operands required");
-  g.out_dtype = dtype_code(out.scalar_type());
   g.batch = a.size(0);
   g.M = a.size(1);
   g.K = a.size(2);
   g.N = b.size(2);
   operand_layout(a, true, g.a_mn, g.lda, g.a_batch_stride);
   operand_layout(b, false, g.b_mn, g.ldb, g.b_batch_stride);
-  g.ldc = out.stride(1);
-  g.c_batch_stride = out.stride(0);
   g.act = static_cast<int>(act);
   g.err = err.data_ptr<int>();
   g.num_sms = num_sms(a.get_device());
@@ -104,6 +100,20 @@ es::GemmArgs gemm_args(const at::Tensor& a, const at::Tensor& b, at::Tensor& out
   g.group_m = g_group_m;
   g.split = g_split;
   g.prof = g_prof;
+  g.sleep_ns = g_sleep_ns;
+  return g;
+}
+
+es::GemmArgs gemm_args(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t act, const at::Tensor& err) {
+  TORCH_CHECK(out.is_cuda() && out.dim() == 3, "einshard native gemm: 3-D CUDA output required");
+  TORCH_CHECK(out.size(0) == a.size(0) && out.size(1) == a.size(1) && out.size(2) == b.size(2),
+              "einshard native gemm: output shape mismatch");
+  TORCH_CHECK(out.stride(2) == 1, "einshard native gemm: output must be row-major");
+  es::GemmArgs g = gemm_operand_args(a, b, act, err);
+  g.C = out.data_ptr();
+  g.out_dtype = dtype_code(out.scalar_type());
+  g.ldc = out.stride(1);
+  g.c_batch_stride = out.stride(0);
   const char* why = es::check_gemm_args(g);
   TORCH_CHECK(why == nullptr, "einshard native gemm: ", why ? why : "");
   return g;
@@ -277,6 +287,38 @@ void gemm_allreduce(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Te
   hc.arrive += static_cast<uint32_t>(grid);
   const int rc = es::gemm_allreduce_launch(g, d, at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "einshard fused gemm+allreduce: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// out (this rank's rows) = reduce-scatter over the communicator's ranks of (a @ b)
+// along row segments: rows [seg * i + rank * shard, ... + shard) for every i.
+void gemm_reducescatter(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out, int64_t seg,
+                        int64_t shard, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open, "einshard fused gemm+reduce-scatter: communicator not connected");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && a.size(0) == 1 && out.dim() == 3 && out.stride(2) == 1,
+              "einshard fused gemm+reduce-scatter: bf16, batch 1");
+  TORCH_CHECK(seg > 0 && shard * hc.size == seg && a.size(1) % seg == 0 && out.size(1) == a.size(1) / hc.size &&
+                  out.size(2) == b.size(2),
+              "einshard fused gemm+reduce-scatter: bad segment geometry");
+  const c10::cuda::CUDAGuard guard(a.device());
+  // the GEMM's full-size output view is only used for its shape; rows go to `out`
+  es::GemmArgs g = gemm_operand_args(a, b, 0, err);
+  g.C = out.data_ptr();
+  g.out_dtype = es::kDtypeBF16;
+  g.ldc = out.stride(1);
+  g.c_batch_stride = out.stride(0);
+  const char* why = es::check_gemm_args(g);
+  TORCH_CHECK(why == nullptr, "einshard fused gemm+reduce-scatter: ", why ? why : "");
+  const long long tiles = (long long)((g.M + 127) / 128) * ((g.N + 255) / 256);
+  TORCH_CHECK(tiles * 128 * 256 * 2 <= (long long)hc.data_bytes && tiles <= es::kMaxTiles,
+              "einshard fused gemm+reduce-scatter: output too large for the symmetric buffer");
+  const int grid = es::gemm_allreduce_grid(g);
+  es::CommDev d = make_dev(hc, err, 0, 0);
+  d.arrive_base = hc.arrive;
+  hc.arrive += static_cast<uint32_t>(grid);
+  const int rc = es::gemm_allreduce_launch(g, d, at::cuda::getCurrentCUDAStream(), seg, shard);
+  TORCH_CHECK(rc == 0, "einshard fused gemm+reduce-scatter: launch failed (", rc, ")");
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
@@ -495,6 +537,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_region", &comm_region, "this rank's symmetric data region as a uint8 tensor");
   m.def("comm_acquire", &comm_acquire, "wait until peers finished reading this rank's region");
   m.def("fft_slab", &fft_slab, "slab transpose fused with the FFT along the exchanged axis");
+  m.def("gemm_reducescatter", &gemm_reducescatter, "fused tcgen05 GEMM + NVLink reduce-scatter of row segments (bf16)");
   m.def("comm_data_bytes", &comm_data_bytes, "data capacity of a communicator");
   m.def("set_gemm_pair_mode", [](int64_t m) { g_pair_mode = static_cast<int>(m); },
         "-1 heuristic, 0 force 1-SM, 1 force 2-SM GEMM kernel");
@@ -503,5 +546,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_gemm_profile", [](const at::Tensor& t) {
         g_prof = t.numel() >= 3 ? reinterpret_cast<unsigned long long*>(t.data_ptr()) : nullptr;
       }, "int64 CUDA tensor of >= 3 wait-cycle counters for the wide GEMM (empty tensor: off)");
+  m.def("set_gemm_sleep_ns", [](int64_t v) { g_sleep_ns = static_cast<int>(v); }, "wide-kernel epilogue back-off ns");
+  m.def("set_tma_l2_promotion", [](int64_t v) { es::tma_l2_promotion() = static_cast<int>(v); },
+        "L2 promotion of TMA loads: 0 none, 1 64B, 2 128B, 3 256B (tuning)");
   m.def("launch_count", []() { return g_launches.load(); }, "native kernel launches so far");
 }

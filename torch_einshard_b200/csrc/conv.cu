@@ -118,6 +118,7 @@ int launch(const ConvArgs& a, cudaStream_t stream) {
   s.split = 0;
   s.err = a.err;
   s.prof = nullptr;
+  s.sleep_ns = 0;
 
   ConvLoads loads{a.C, a.KW, Hout, Wv, a.ph, a.pw};
   ConvStoreEpilogue<OutT> epi{reinterpret_cast<OutT*>(a.out), a.bias, a.O, Wout, Wv};

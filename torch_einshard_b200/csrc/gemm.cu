@@ -58,6 +58,7 @@ GemmShape make_shape(const GemmArgs& g) {
   s.split = 0;
   s.err = g.err;
   s.prof = g.prof;
+  s.sleep_ns = g.sleep_ns;
   return s;
 }
 

@@ -34,6 +34,7 @@ struct GemmArgs {
   int group_m = 0;   // raster group height in M tiles (0: default)
   int split = 0;     // wide kernel cluster split (see GemmShape::split)
   unsigned long long* prof = nullptr;  // optional wait-cycle counters (wide kernel)
+  int sleep_ns = 0;  // wide kernel epilogue back-off (tuning)
 };
 
 const char* check_gemm_args(const GemmArgs& g);

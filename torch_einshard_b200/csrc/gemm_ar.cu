@@ -38,6 +38,23 @@ struct ArEpilogue {
   long long ldc;
   int vec_ok;  // C rows 16-byte aligned
   int* sm;     // SharedState::epi
+  // Reduce-scatter mode (rs = 1): rows form segments of `seg` rows, each split
+  // into size blocks of `shard` rows; rank p owns block p of every segment and
+  // C is its local [segments * shard, N] output.  Tile t's owner is the owner
+  // of its rows; nobody pulls reduced tiles back.
+  int rs;
+  long long seg, shard;
+
+  __device__ __forceinline__ int owner_of(int t, const GemmShape& s) const {
+    if (!rs) return t % c.size;
+    const long long m0 = tile_coord(s, t).m0;
+    return static_cast<int>((m0 % seg) / shard);
+  }
+  // row of this rank's C that holds global row `row`
+  __device__ __forceinline__ long long out_row(long long row) const {
+    if (!rs) return row;
+    return (row / seg) * shard + (row % seg) - static_cast<long long>(c.rank) * shard;
+  }
 
   __device__ __forceinline__ int* flag(int rank, int slot) const { return reinterpret_cast<int*>(c.flags[rank]) + slot; }
   __device__ __forceinline__ uint8_t* tile_buf(int rank, int t) const {
@@ -112,7 +129,8 @@ struct ArEpilogue {
     const int e = et.row;  // epilogue thread index == tile row
     const int t = et.t;
     if (sm[kAbortEpi]) return false;
-    const bool mine = (t % c.size) == c.rank;
+    const int owner = owner_of(t, s);
+    const bool mine = owner == c.rank;
     uint8_t* my_buf = tile_buf(c.rank, t);
     if (!mine) {
 #pragma unroll 1
@@ -133,9 +151,11 @@ struct ArEpilogue {
       if (e == 0) {
         fence_acq_rel_sys();
         st_release_sys(flag(c.rank, kFlagTile0 + t), c.epoch);
-        // queue the pull of the reduced tile; make room first if the queue is full
-        sm[kQBase + (sm[kQTail] % kQueue)] = t;
-        ++sm[kQTail];
+        if (!rs) {
+          // queue the pull of the reduced tile; make room first if the queue is full
+          sm[kQBase + (sm[kQTail] % kQueue)] = t;
+          ++sm[kQTail];
+        }
       }
       epi_bar();
       const bool full = (sm[kQTail] - sm[kQHead]) >= kQueue;
@@ -155,7 +175,7 @@ struct ArEpilogue {
     epi_bar();
     if (sm[kAbortEpi]) return false;
     const int row = et.c.m0 + e;
-    __nv_bfloat16* crow = C + static_cast<long long>(row) * ldc;
+    __nv_bfloat16* crow = C + out_row(row) * ldc;
 #pragma unroll 1
     for (int chunk = 0; chunk < kBN / 32; ++chunk) {
       uint32_t r[32];
@@ -188,7 +208,7 @@ struct ArEpilogue {
       for (int q = 0; q < 4; ++q) {
         o[q] = make_uint4(pack_bf16(acc[8 * q + 0], acc[8 * q + 1]), pack_bf16(acc[8 * q + 2], acc[8 * q + 3]),
                           pack_bf16(acc[8 * q + 4], acc[8 * q + 5]), pack_bf16(acc[8 * q + 6], acc[8 * q + 7]));
-        *reinterpret_cast<uint4*>(my_buf + (static_cast<size_t>(chunk * 4 + q) * kBM + e) * 16) = o[q];
+        if (!rs) *reinterpret_cast<uint4*>(my_buf + (static_cast<size_t>(chunk * 4 + q) * kBM + e) * 16) = o[q];
       }
       const int col0 = et.c.n0 + chunk * 32;
       if (row < s.M && col0 < s.N) {
@@ -204,7 +224,7 @@ struct ArEpilogue {
       }
     }
     epi_bar();
-    if (e == 0) {
+    if (e == 0 && !rs) {
       fence_acq_rel_sys();
       st_release_sys(flag(c.rank, kFlagTile0 + kMaxTiles + t), c.epoch);
     }
@@ -238,8 +258,10 @@ struct ArEpilogue {
   }
 };
 
-int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t stream) {
+int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t stream, long long rs_seg,
+                          long long rs_shard) {
   if (check_gemm_args(g)) return -1;
+  if (rs_seg > 0 && (rs_seg % kBM || rs_shard % kBM || rs_shard * comm.size != rs_seg || g.M % rs_seg)) return -4;
   if (g.out_dtype != kDtypeBF16 || g.batch != 1) return -2;
   CUtensorMap ma, mb;
   make_operand_maps(g, &ma, &mb);
@@ -252,6 +274,9 @@ int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t s
   epi.ldc = g.ldc;
   epi.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && (g.ldc % 8 == 0);
   epi.sm = nullptr;
+  epi.rs = rs_seg > 0 ? 1 : 0;
+  epi.seg = rs_seg > 0 ? rs_seg : 1;
+  epi.shard = rs_shard > 0 ? rs_shard : 1;
   auto kernel = gemm_tc_kernel<ArEpilogue>;
   static unsigned long long attr_set = 0;
   int dev = 0;

@@ -13,6 +13,9 @@ inline int gemm_allreduce_grid(const GemmArgs& g) {
   return tiles < g.num_sms ? tiles : g.num_sms;
 }
 
-int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t stream);
+// rs_seg > 0 selects reduce-scatter: rows form segments of rs_seg rows, rank p
+// keeps rows [p * rs_shard, (p + 1) * rs_shard) of every segment in its C.
+int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t stream, long long rs_seg = 0,
+                          long long rs_shard = 0);
 
 }  // namespace es

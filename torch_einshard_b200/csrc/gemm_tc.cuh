@@ -54,6 +54,7 @@ struct GemmShape {
                    // half of the cluster ids, or even/odd ids), each walking one half of the M tiles
   int* err;
   unsigned long long* prof;  // optional: per-CTA wait-cycle counters (see gemm_tc3.cuh), null when off
+  int sleep_ns;              // wide kernel: epilogue back-off between accumulator polls (0: spin)
 };
 
 struct TileCoord {

@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
     uint32_t tc = 0;
     TileCoord ce;
     for (; pair_tile_at(shp, cluster, nclusters, static_cast<int>(tc), static_cast<int>(rank), &ce); ++tc) {
-      if (!mbar_wait(&st->tfull, tc & 1u, abort_flag, shp.err, kErrWaitTmemFull)) break;
+      if (!mbar_wait_sleepy(&st->tfull, tc & 1u, abort_flag, shp.err, kErrWaitTmemFull, shp.sleep_ns)) break;
       tc_fence_after();
       EpiTile et;
       et.t = 2 * (cluster + static_cast<int>(tc) * nclusters) + static_cast<int>(rank);

@@ -84,6 +84,27 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   }
 }
 
+// Like mbar_wait, but backs off with __nanosleep between polls: for waits that
+// usually last a whole tile (the epilogue waiting for the accumulator).
+__device__ __forceinline__ bool mbar_wait_sleepy(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,
+                                                 int code, int sleep_ns) {
+  if (sleep_ns <= 0) return mbar_wait(bar, parity, abort_flag, err, code);
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (uint32_t i = 1;; ++i) {
+    __nanosleep(sleep_ns);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 15u) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > ES_WAIT_TIMEOUT_NS) {
+        *abort_flag = 1;
+        if (err) atomicCAS(err, 0, code);
+        return false;
+      }
+    }
+  }
+}
+
 // Warp-uniform wait in which only lane 0 polls the barrier (the other lanes
 // park on the shuffle), for the single-issuer producer and MMA warps.
 __device__ __forceinline__ bool mbar_wait_lane0(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int* err,

@@ -11,6 +11,20 @@
 
 namespace es {
 
+// L2 promotion of TMA loads (0 none, 1 64B, 2 128B, 3 256B); 256B by default.
+inline int& tma_l2_promotion() {
+  static int mode = 3;
+  return mode;
+}
+inline CUtensorMapL2promotion l2_promotion() {
+  switch (tma_l2_promotion()) {
+    case 0: return CU_TENSOR_MAP_L2_PROMOTION_NONE;
+    case 1: return CU_TENSOR_MAP_L2_PROMOTION_L2_64B;
+    case 2: return CU_TENSOR_MAP_L2_PROMOTION_L2_128B;
+    default: return CU_TENSOR_MAP_L2_PROMOTION_L2_256B;
+  }
+}
+
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
                                    CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
@@ -41,7 +55,7 @@ inline CUtensorMap make_tmap_3d(const void* base, CUtensorMapDataType dtype, int
   cuuint32_t estr[3] = {1, 1, 1};
   auto encode = [&]() {
     return encode_tiled_fn()(&map, dtype, 3, const_cast<void*>(base), dims, strides, box, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, l2_promotion(),
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   };
   CUresult r = encode();
@@ -75,7 +89,7 @@ inline CUtensorMap make_tmap_nd(const void* base, CUtensorMapDataType dtype, int
   }
   auto encode = [&]() {
     return encode_tiled_fn()(&map, dtype, rank, const_cast<void*>(base), d, st, bx, estr,
-                             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                             CU_TENSOR_MAP_INTERLEAVE_NONE, swz, l2_promotion(),
                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   };
   CUresult r = encode();

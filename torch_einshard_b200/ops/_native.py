@@ -74,7 +74,11 @@ class EinshardCommTimeout(RuntimeError):
 def check_errors(device=None):
     """Raise :class:`EinshardCommTimeout` if any native kernel on ``device``
     reported a timeout (synchronises)."""
-    devices = [torch.device(device).index] if device is not None else list(_ERROR_WORDS)
+    if device is None:
+        devices = list(_ERROR_WORDS)
+    else:
+        index = torch.device(device).index if not isinstance(device, int) else device
+        devices = [torch.cuda.current_device() if index is None else index]
     for index in devices:
         word = _ERROR_WORDS.get(index)
         if word is None:

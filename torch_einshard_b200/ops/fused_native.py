@@ -22,7 +22,7 @@ from .contraction import canonical_gemm
 from .einsum import equation_for
 from .gemm import _prepare, native_bmm
 
-__all__ = ["install", "gemm_allreduce"]
+__all__ = ["install", "gemm_allreduce", "gemm_reducescatter"]
 
 
 def _comm(group):
@@ -37,6 +37,94 @@ def gemm_allreduce(comm, a, b):
     out = torch.empty((1, a.shape[1], b.shape[2]), dtype=torch.bfloat16, device=a.device)
     mod.gemm_allreduce(comm.cid, a, b, out, _native.error_word(a.device))
     return out
+
+
+def gemm_reducescatter(comm, a, b, seg, shard):
+    """This rank's rows of the reduce-scatter of ``a @ b`` over the ranks: rows are
+    segments of ``seg`` rows, rank p keeps rows [p*shard, (p+1)*shard) of each."""
+    mod = _native.require()
+    a, b = _prepare(a), _prepare(b)
+    out = torch.empty((1, a.shape[1] // comm.size, b.shape[2]), dtype=torch.bfloat16, device=a.device)
+    mod.gemm_reducescatter(comm.cid, a, b, out, seg, shard, _native.error_word(a.device))
+    return out
+
+
+def _gather_rows(comm, x, seg, shard):
+    """Inverse layout of the row reduce-scatter: [1, M/P, N] -> [1, M, N]."""
+    m_local, n = x.shape[1], x.shape[2]
+    segments = m_local // shard
+    view = x.reshape(segments, shard, n)
+    full = comm.all_gather(view, 1, [shard] * comm.size)
+    if full is None:
+        parts = [torch.empty_like(view) for _ in range(comm.size)]
+        dist.all_gather(parts, view.contiguous(), group=comm.group)
+        full = torch.cat(parts, dim=1)
+    return full.reshape(1, segments * seg, n)
+
+
+def _scatter_rows(comm, full, seg, shard):
+    """Row reduce-scatter of an unfused [1, M, N] tensor (fallback)."""
+    m, n = full.shape[1], full.shape[2]
+    view = full.reshape(m // seg, seg, n)
+    out = comm.reduce_scatter(view, 1, [shard] * comm.size)
+    if out is None:
+        dist.all_reduce(view, group=comm.group)
+        out = view[:, comm.rank * shard:(comm.rank + 1) * shard].contiguous()
+    return out.reshape(1, (m // seg) * shard, n)
+
+
+def _rs_fits(comm, m, n, seg, shard):
+    return _fits(comm, m, n) and seg % 128 == 0 and shard % 128 == 0 and shard * comm.size == seg and m % seg == 0
+
+
+class _GemmReduceScatter(torch.autograd.Function):
+    """Forward: rows of RS(a @ b) in one kernel.  Backward: gather dC, then the
+    plain GEMMs (the reduce-scatter's adjoint is the all-gather)."""
+
+    @staticmethod
+    def forward(ctx, a, b, comm, seg, shard):
+        ctx.save_for_backward(a, b)
+        ctx.args = (comm, seg, shard)
+        if _rs_fits(comm, a.shape[1], b.shape[2], seg, shard):
+            return gemm_reducescatter(comm, a, b, seg, shard)
+        return _scatter_rows(comm, native_bmm(a, b), seg, shard)
+
+    @staticmethod
+    def backward(ctx, grad):
+        a, b = ctx.saved_tensors
+        comm, seg, shard = ctx.args
+        full = _gather_rows(comm, grad.contiguous(), seg, shard)
+        ga = native_bmm(full, b.transpose(1, 2)) if ctx.needs_input_grad[0] else None
+        gb = _grad_b(a, b, full) if ctx.needs_input_grad[1] else None
+        return ga, gb, None, None, None
+
+
+class _AllGatherGemm(torch.autograd.Function):
+    """Forward: gather the row-sharded operand a, then the GEMM.  Backward: the
+    gradient of the local rows is the row reduce-scatter of dC @ b^T, computed
+    by the fused GEMM + reduce-scatter kernel; db uses the gathered a."""
+
+    @staticmethod
+    def forward(ctx, a_local, b, comm, seg, shard):
+        a_full = _gather_rows(comm, a_local.contiguous(), seg, shard)
+        ctx.save_for_backward(a_full, b)
+        ctx.args = (comm, seg, shard)
+        return native_bmm(a_full, b)
+
+    @staticmethod
+    def backward(ctx, grad):
+        a_full, b = ctx.saved_tensors
+        comm, seg, shard = ctx.args
+        ga = gb = None
+        if ctx.needs_input_grad[0]:
+            bt = b.transpose(1, 2)
+            if _rs_fits(comm, grad.shape[1], bt.shape[2], seg, shard):
+                ga = gemm_reducescatter(comm, grad, bt, seg, shard)
+            else:
+                ga = _scatter_rows(comm, native_bmm(grad, bt), seg, shard)
+        if ctx.needs_input_grad[1]:
+            gb = _grad_b(a_full, b, grad)
+        return ga, gb, None, None, None
 
 
 def _fits(comm, m, n):
@@ -98,9 +186,10 @@ class _GemmDgradAllReduce(torch.autograd.Function):
 
 
 class _Fusion:
-    def __init__(self, kind, operand=None):
+    def __init__(self, kind, operand=None, axis=None):
         self.kind = kind
         self.operand = operand
+        self.axis = axis  # gathered / scattered axis name
 
     @staticmethod
     def _gemm_views(shard, x, y):
@@ -128,6 +217,95 @@ class _Fusion:
         shape = [size[c] for c in order]
         perm = [order.index(c) for c in ez]
         return a, b, shape, perm
+
+    @staticmethod
+    def _row_segment(shard, x, y, name, P):
+        """(views, seg, shard_rows) when ``name`` is a GEMM row axis whose blocks
+        per rank are whole row ranges of the flattened rows; else None."""
+        views = _Fusion._gemm_views(shard, x, y)
+        if views is None:
+            return None
+        equation = equation_for(shard)
+        plan = canonical_gemm(equation, tuple(x.shape), tuple(y.shape))
+        ez = plan["ez"]
+        out_axes = [a for a in shard[2].axes]
+        letter = ez[[a.name for a in out_axes].index(name)]
+        rows, size = plan["rows"], plan["size"]
+        if letter not in rows or size[letter] % P:
+            return None
+        seg = 1
+        for c in rows[rows.index(letter):]:
+            seg *= size[c]
+        return views, seg, seg // P, letter, plan
+
+    def run_gemm_reducescatter(self, shard, x, y, group, name):
+        comm = _comm(group)
+        found = self._row_segment(shard, x, y, name, comm.size) if comm is not None else None
+        if found is None:
+            return None
+        (a, b, shape, perm), seg, rows_per_rank, letter, plan = found
+        out = _GemmReduceScatter.apply(a, b, comm, seg, rows_per_rank)
+        order = plan["rows"] + plan["cols"]
+        shape = list(shape)
+        shape[order.index(letter)] //= comm.size
+        return out.reshape(shape).permute(perm)
+
+    def run_allgather_gemm(self, shard, x_local, y, group, name, dim):
+        """Operand ``self.operand`` is sharded along ``name`` (tensor dim ``dim``)."""
+        comm = _comm(group)
+        if comm is None:
+            return None
+        P = comm.size
+        # plan against the gathered shapes
+        full_shape = list((x_local if self.operand == 0 else y).shape)
+        full_shape[dim] *= P
+        xs = torch.empty(full_shape, device="meta", dtype=x_local.dtype) if self.operand == 0 else x_local
+        ys = y if self.operand == 0 else torch.empty(full_shape, device="meta", dtype=y.dtype)
+        found = self._row_segment_input(shard, xs, ys, name, P)
+        if found is None:
+            return None
+        a_perm, b_perm, m, n, k, seg, rows_per_rank, shape, perm = found
+        if self.operand == 0:
+            a_local = x_local.permute(a_perm).reshape(1, m // P, k)
+            b = y.permute(b_perm).reshape(1, k, n)
+        else:
+            return None
+        out = _AllGatherGemm.apply(a_local, b, comm, seg, rows_per_rank)
+        return out.reshape(shape).permute(perm)
+
+    @staticmethod
+    def _row_segment_input(shard, x, y, name, P):
+        equation = equation_for(shard)
+        plan = canonical_gemm(equation, tuple(x.shape), tuple(y.shape))
+        if plan is None or plan["batch"] or plan["x_only"] or plan["y_only"]:
+            return None
+        ex, ey, ez = plan["ex"], plan["ey"], plan["ez"]
+        rows, cols, red, size = plan["rows"], plan["cols"], plan["red"], plan["size"]
+        in_axes = [a.name for a in shard[0].axes]
+        letter = ex[in_axes.index(name)]
+        if letter not in rows or size[letter] % P or rows[0] != letter and False:
+            return None
+        # the local rows must be whole blocks: every row axis before `letter` is outer
+        seg = 1
+        for c in rows[rows.index(letter):]:
+            seg *= size[c]
+        m = 1
+        for c in rows:
+            m *= size[c]
+        n = 1
+        for c in cols:
+            n *= size[c]
+        k = 1
+        for c in red:
+            k *= size[c]
+        if min(m, n, k) == 0:
+            return None
+        a_perm = [ex.index(c) for c in rows + red]
+        b_perm = [ey.index(c) for c in red + cols]
+        order = rows + cols
+        shape = [size[c] for c in order]
+        perm = [order.index(c) for c in ez]
+        return a_perm, b_perm, m, n, k, seg, seg // P, shape, perm
 
     def run_gemm_allreduce(self, shard, x, y, group):
         views = self._gemm_views(shard, x, y)
@@ -167,6 +345,18 @@ def provider(executor):
         return None
     tp = executor.tp
     out_steps = [s for s in tp.output_steps if s.name != "rank_local_einsum"]
+    if (len(out_steps) == 1 and out_steps[0].name == "reducescatter_forward_allgather_backward"
+            and not tp.input0_steps and not tp.input1_steps):
+        name, dim = out_steps[0].args
+        if _comm(executor.group(dim)) is not None:
+            return _Fusion("gemm_reducescatter", axis=name)
+        return None
+    if (not out_steps and len(tp.input0_steps) == 1 and not tp.input1_steps
+            and tp.input0_steps[0].name == "allgather_forward_reducescatter_backward"):
+        name, dim = tp.input0_steps[0].args
+        if _comm(executor.group(dim)) is not None:
+            return _Fusion("allgather_gemm", operand=0, axis=name)
+        return None
     if (len(out_steps) == 1 and out_steps[0].name == "allreduce_forward_identity_backward"
             and not tp.input0_steps and not tp.input1_steps):
         if _comm(executor.group(out_steps[0].args[0])) is not None:

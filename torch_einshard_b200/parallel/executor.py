@@ -335,6 +335,10 @@ class BinaryExecutor:
         fuse = fused.binary_fusion(self)
         deferred0 = [] if fuse is not None and fuse.kind == "dgrad_allreduce" and fuse.operand == 0 else None
         deferred1 = [] if fuse is not None and fuse.kind == "dgrad_allreduce" and fuse.operand == 1 else None
+        if fuse is not None and fuse.kind == "allgather_gemm":
+            z = self._run_allgather_gemm(fuse)
+            if z is not None:
+                return z
         x, spec0 = self.normalize(self.x0, self.spec0, tp.input0_steps, deferred0)
         y, spec1 = self.normalize(self.y0, self.spec1, tp.input1_steps, deferred1)
         local_out_axes = Axes(
@@ -352,7 +356,14 @@ class BinaryExecutor:
         plan.add("rank_local_einsum")
         output_steps = [s for s in tp.output_steps if s.name not in ("rank_local_einsum", "alltoall_repartition")]
         fused_out = False
-        if fuse is not None and fuse.kind == "gemm_allreduce" and output_steps and \
+        fused_rs = None
+        if fuse is not None and fuse.kind == "gemm_reducescatter" and len(output_steps) == 1 and \
+                output_steps[0].name == "reducescatter_forward_allgather_backward" and self._even_split(output_steps[0]):
+            name, dim = output_steps[0].args
+            fused_rs = fuse.run_gemm_reducescatter((spec0, spec1, local_out), x, y, self.group(dim), name)
+        if fused_rs is not None:
+            z = fused_rs
+        elif fuse is not None and fuse.kind == "gemm_allreduce" and output_steps and \
                 output_steps[0].name == "allreduce_forward_identity_backward":
             z = fuse.run_gemm_allreduce((spec0, spec1, local_out), x, y, self.group(output_steps[0].args[0]))
             fused_out = True
@@ -384,6 +395,11 @@ class BinaryExecutor:
             plan.rank(ranked)
 
         for index, step in enumerate(output_steps):
+            if fused_rs is not None and index == 0:
+                # already reduce-scattered by the fused kernel
+                plan.add(step.name, *step.args)
+                current = _replace_axis(current, step.args[0], self.scatter_by_dim[step.args[1]])
+                continue
             if step.name == "allreduce_forward_identity_backward":
                 if fused_out and index == 0:
                     plan.add(step.name, *step.args)
@@ -409,6 +425,41 @@ class BinaryExecutor:
 
         if self.post is not None:
             z = self._post_repartition(z, current, ranked)
+        set_last_plan(plan)
+        return z
+
+    def _even_split(self, step):
+        name, dim = step.args
+        group = self.group(dim)
+        shapes = resolve_split_shapes(self.shapes, dim, name, group)
+        return shapes is None or len(set(shapes)) == 1
+
+    def _run_allgather_gemm(self, fuse):
+        """AG of operand 0 along a GEMM row axis + the contraction, as one fused op
+        (its backward is the fused GEMM + reduce-scatter).  None: run unfused."""
+        tp, plan = self.tp, self.plan
+        step = tp.input0_steps[0]
+        name, dim = step.args
+        if not self._even_split(step) or any(isinstance(a, EllipsisAxis) for a in _axes(self.spec0)) or \
+                any(isinstance(a, EllipsisAxis) for a in _axes(self.spec1)) or \
+                any(isinstance(a, EllipsisAxis) for a in _axes(self.spec_out)):
+            return None
+        axes0 = list(_axes(self.spec0))
+        tdim = [a.name for a in axes0].index(name)
+        spec0 = TensorSpec(Axes(Axis(a.name) if a.name == name else a for a in axes0), _partials(self.spec0))
+        local_out_axes = Axes(self._localize(a) for a in _axes(self.spec_out))
+        local_out = TensorSpec(local_out_axes, _partials(self.spec_out))
+        z = fuse.run_allgather_gemm((spec0, self.spec1, local_out), self.x0, self.y0, self.group(dim), name, tdim)
+        if z is None:
+            return None
+        plan.add(step.name, *step.args)
+        plan.add("rank_local_einsum")
+        ranked = rank_alternatives(
+            tp.alternatives,
+            self.runtime_info(self.axes0, self.x0), self.runtime_info(self.axes1, self.y0),
+            self.runtime_info(local_out_axes, z), self.mesh_sizes(), self.cost_split_shapes(), self.policy,
+        )
+        plan.rank(ranked, selected="default", reason="fallback selected")
         set_last_plan(plan)
         return z
 

@@ -126,13 +126,13 @@ class Communicator:
     # -- health -------------------------------------------------------------
     def _skip_injected(self):
         """Host-side fault injection for tests: ``EINSHARD_FAULT_INJECT=skip:<rank>:<n>``
-        makes the given global rank skip its n-th native collective (it launches
+        makes the given global rank skip its n-th native all-reduce (it launches
         nothing, so peers' bounded waits expire).  Returns True to skip."""
+        self.calls = getattr(self, "calls", 0) + 1  # native collectives issued on this communicator
         spec = os.environ.get("EINSHARD_FAULT_INJECT", "")
         if not spec.startswith("skip:"):
             return False
         _, rank, nth = spec.split(":")
-        self.calls = getattr(self, "calls", 0) + 1
         return int(rank) == dist.get_rank() and self.calls == int(nth)
 
     def check_health(self):
