@@ -104,6 +104,20 @@ def _sequence_parallel(rank, world):
             assert (got.float() - want).abs().max().item() < 3e-2 * scale
     _native.check_errors()
 
+    # raw fused all-gather -> GEMM (copy warps inside the GEMM), two calls in a row
+    for (segs, shard, n, k) in [(2, 256, 1024, 256), (1, 512, 512, 128)]:
+        a_local = torch.randn(1, segs * shard, k, device="cuda", dtype=torch.bfloat16) * (rank + 1)
+        b = torch.randn(1, n, k, device="cuda", dtype=torch.bfloat16).transpose(1, 2)
+        parts = [torch.empty_like(a_local) for _ in range(world)]
+        dist.all_gather(parts, a_local, group=group)
+        want_a = torch.cat([p.reshape(segs, shard, k) for p in parts], dim=1).reshape(1, segs * shard * world, k)
+        for _ in range(2):
+            out, gathered = fused_native.gemm_allgather(comm, a_local, b, shard * world, shard)
+            assert torch.equal(gathered, want_a)
+            want = want_a.float() @ b.float()
+            assert (out.float() - want).abs().max().item() < 3e-2 * (want.abs().max().item() + 1)
+    _native.check_errors()
+
     # through einshard: l/tp e, e f/tp -> l f/tp (AG -> GEMM) and back l f/tp, f/tp e -> l/tp e (GEMM -> RS)
     torch.manual_seed(0)
     L, E, F_ = 256 * world, 256, 512 * world

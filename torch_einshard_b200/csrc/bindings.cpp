@@ -322,6 +322,43 @@ void gemm_reducescatter(int64_t id, const at::Tensor& a, const at::Tensor& b, at
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+es::CommDev peek_dev(HostComm& hc, const at::Tensor& err);
+
+// out = gather_rows(a_local over ranks) @ b, with the gathered rows written to
+// xfull; one fused kernel (copy warps pull peers' rows while the GEMM runs).
+void gemm_allgather(int64_t id, const at::Tensor& a_local, const at::Tensor& b, at::Tensor out, at::Tensor xfull,
+                    int64_t seg, int64_t shard, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open, "einshard fused all-gather+gemm: communicator not connected");
+  TORCH_CHECK(a_local.scalar_type() == at::kBFloat16 && a_local.is_contiguous() && a_local.dim() == 3 &&
+                  a_local.size(0) == 1,
+              "einshard fused all-gather+gemm: contiguous bf16 [1, rows, K] shard required");
+  TORCH_CHECK(xfull.is_contiguous() && xfull.scalar_type() == at::kBFloat16 && xfull.size(1) == a_local.size(1) * hc.size &&
+                  xfull.size(2) == a_local.size(2),
+              "einshard fused all-gather+gemm: gathered buffer shape");
+  TORCH_CHECK(shard * hc.size == seg && a_local.size(1) % shard == 0, "einshard fused all-gather+gemm: segments");
+  const int64_t bytes = a_local.numel() * 2;
+  TORCH_CHECK((size_t)bytes <= hc.data_bytes, "einshard fused all-gather+gemm: shard larger than the symmetric region");
+  const c10::cuda::CUDAGuard guard(a_local.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  // peers finished reading this rank's region (previous op), then stage the shard
+  es::CommDev prev = peek_dev(hc, err);
+  int rc = es::comm_wait_peers(prev, es::kFlagDone, hc.epoch, stream);
+  TORCH_CHECK(rc == 0, "einshard fused all-gather+gemm: wait launch failed (", rc, ")");
+  void* region = static_cast<char*>(hc.local) + es::kFlagBytes;
+  TORCH_CHECK(cudaMemcpyAsync(region, a_local.data_ptr(), bytes, cudaMemcpyDeviceToDevice, stream) == cudaSuccess,
+              "einshard fused all-gather+gemm: staging copy failed");
+  es::GemmArgs g = gemm_args(xfull, b, out, 0, err);
+  TORCH_CHECK(g.out_dtype == es::kDtypeBF16, "einshard fused all-gather+gemm: bf16 output");
+  const int grid = es::gemm_allgather_grid(g);
+  es::CommDev d = make_dev(hc, err, 0, 0);
+  d.arrive_base = hc.arrive;
+  hc.arrive += static_cast<uint32_t>(grid);
+  rc = es::gemm_allgather_launch(g, d, xfull.data_ptr(), static_cast<int>(a_local.size(1) / shard), shard, stream);
+  TORCH_CHECK(rc == 0, "einshard fused all-gather+gemm: launch failed (", rc, ")");
+  g_launches.fetch_add(2, std::memory_order_relaxed);
+}
+
 
 // ------------------------------------------------------------------ FFT
 
@@ -538,6 +575,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_acquire", &comm_acquire, "wait until peers finished reading this rank's region");
   m.def("fft_slab", &fft_slab, "slab transpose fused with the FFT along the exchanged axis");
   m.def("gemm_reducescatter", &gemm_reducescatter, "fused tcgen05 GEMM + NVLink reduce-scatter of row segments (bf16)");
+  m.def("gemm_allgather", &gemm_allgather, "fused all-gather of row shards + tcgen05 GEMM (bf16)");
   m.def("comm_data_bytes", &comm_data_bytes, "data capacity of a communicator");
   m.def("set_gemm_pair_mode", [](int64_t m) { g_pair_mode = static_cast<int>(m); },
         "-1 heuristic, 0 force 1-SM, 1 force 2-SM GEMM kernel");

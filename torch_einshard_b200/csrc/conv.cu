@@ -19,6 +19,7 @@
 // W'[c, kh', kw', o] = W[o, KH-1-kh', KW-1-kw', c] and padding (KH-1, KW-1).
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <string.h>
 
 #include "conv.h"
 #include "gemm_tc.cuh"
@@ -55,11 +56,53 @@ struct ConvStoreEpilogue {
   OutT* out;
   const float* bias;  // may be null
   int O, Wout, Wv;
+  int tma;            // 1: TMA stores of [64 pixels x 32 channels] boxes through the warp's staging buffer
 
   __device__ __forceinline__ void setup(SharedState*, const GemmShape&) {}
   __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
 
+  // Channels are on TMEM lanes, pixels on columns: each thread holds one channel
+  // of 64 consecutive pixels.  The warp's 32 channels x 64 pixels are written
+  // into the staging buffer in NHWC order ([pixel][32 channels], 2-byte stores
+  // that are conflict-free across the warp), then one TMA store writes the box;
+  // the map is (O, Wout, rows), so boxes clip at the end of an output row.
+  __device__ __forceinline__ void tile_tma(const EpiTile& et) {
+    const int c0 = et.c.m0 + et.q * 32;
+    if (c0 >= O) return;  // this warp's channels are all beyond O (no box may start out of range)
+    const int o = c0 + et.lane;
+    const int r = et.c.n0 / Wv;
+    const int w0 = et.c.n0 - r * Wv;
+    const float bv = (o < O && bias != nullptr) ? bias[o] : 0.0f;
+    OutT* stage = reinterpret_cast<OutT*>(et.stage);
+#pragma unroll 1
+    for (int sub = 0; sub < kBN / 64; ++sub) {
+      const int col0 = w0 + sub * 64;
+      if (col0 >= Wout) break;  // uniform across the warp
+      uint32_t v0[32], v1[32];
+      tmem_ld32(et.tmem + sub * 64, v0);
+      tmem_ld32(et.tmem + sub * 64 + 32, v1);
+      tmem_ld_wait();
+      if (et.lane == 0) bulk_wait_group_read<0>();
+      __syncwarp();
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        stage[i * 32 + et.lane] = StoreOut<OutT>::cvt(__uint_as_float(v0[i]) + bv);
+        stage[(32 + i) * 32 + et.lane] = StoreOut<OutT>::cvt(__uint_as_float(v1[i]) + bv);
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (et.lane == 0) {
+        tma_store_3d(et.tmc, et.stage, c0, col0, r);
+        bulk_commit_group();
+      }
+    }
+  }
+
   __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape&, volatile int*) {
+    if (tma && et.tmc != nullptr) {
+      tile_tma(et);
+      return true;
+    }
     const int o = et.c.m0 + et.row;
     const bool ok = o < O;
     const int r = et.c.n0 / Wv;
@@ -121,7 +164,18 @@ int launch(const ConvArgs& a, cudaStream_t stream) {
   s.sleep_ns = 0;
 
   ConvLoads loads{a.C, a.KW, Hout, Wv, a.ph, a.pw};
-  ConvStoreEpilogue<OutT> epi{reinterpret_cast<OutT*>(a.out), a.bias, a.O, Wout, Wv};
+  ConvStoreEpilogue<OutT> epi{reinterpret_cast<OutT*>(a.out), a.bias, a.O, Wout, Wv, 0};
+  // output map (O, Wout, B*Hout), box 32 channels x 64 pixels, no swizzle (64-byte rows)
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));
+  if ((reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && (a.O * 2) % 16 == 0) {
+    const uint64_t odims[3] = {static_cast<uint64_t>(a.O), static_cast<uint64_t>(Wout),
+                               static_cast<uint64_t>(a.B) * Hout};
+    const uint64_t ostrides[2] = {static_cast<uint64_t>(a.O) * 2, static_cast<uint64_t>(Wout) * a.O * 2};
+    const uint32_t obox[3] = {32, 64, 1};
+    mc = make_tmap_nd(a.out, dt, 3, odims, ostrides, obox, CU_TENSOR_MAP_SWIZZLE_NONE);
+    epi.tma = 1;
+  }
   auto kernel = gemm_tc_kernel<ConvStoreEpilogue<OutT>, ConvLoads>;
   static unsigned long long attr_set = 0;
   int dev = 0;
@@ -132,7 +186,7 @@ int launch(const ConvArgs& a, cudaStream_t stream) {
   }
   const long long tiles = static_cast<long long>(s.num_m) * s.num_n;
   const int grid = tiles < a.num_sms ? static_cast<int>(tiles) : a.num_sms;
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, s, epi, loads);
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, s, epi, loads);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -132,23 +132,27 @@ static GemmArgs swapped(const GemmArgs& g) {
 static bool want_swap(const GemmArgs& g) { return g.N < kBN && g.M > g.N; }
 
 // Launch the wide 2-SM kernel (256 x 512 pair tiles) on clusters of two CTAs.
+// Output map of the TMA-store epilogue (16-bit C, 16-byte aligned rows): 32 x 64
+// boxes with 128-byte swizzle.  Returns false (map zeroed) when C does not qualify.
+bool make_output_map(const GemmArgs& g, bool trans, CUtensorMap* mc) {
+  memset(mc, 0, sizeof(*mc));
+  const int out_bytes = g.out_dtype == kDtypeF32 ? 4 : 2;
+  const bool ok = out_bytes == 2 && !trans && (reinterpret_cast<uintptr_t>(g.C) & 15) == 0 && (g.ldc * 2) % 16 == 0 &&
+                  (g.batch == 1 || (g.c_batch_stride * 2) % 16 == 0);
+  if (!ok) return false;
+  const uint64_t dims[3] = {static_cast<uint64_t>(g.N), static_cast<uint64_t>(g.M), static_cast<uint64_t>(g.batch)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(g.ldc) * 2,
+                               static_cast<uint64_t>(g.batch > 1 ? g.c_batch_stride : g.ldc * g.M) * 2};
+  const uint32_t box[3] = {64, 32, 1};
+  *mc = make_tmap_nd(g.C, g.out_dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                     3, dims, strides, box);
+  return true;
+}
+
 template <class Epi>
 int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, Epi epi, cudaStream_t stream) {
-  // output map for the TMA-store epilogue: 16-bit C, 16-byte aligned rows
   CUtensorMap mc;
-  memset(&mc, 0, sizeof(mc));
-  const int out_bytes = g.out_dtype == kDtypeF32 ? 4 : 2;
-  const bool tma_ok = out_bytes == 2 && !epi.trans && (reinterpret_cast<uintptr_t>(g.C) & 15) == 0 &&
-                      (g.ldc * 2) % 16 == 0 && (g.batch == 1 || (g.c_batch_stride * 2) % 16 == 0);
-  if (tma_ok) {
-    const uint64_t dims[3] = {static_cast<uint64_t>(g.N), static_cast<uint64_t>(g.M), static_cast<uint64_t>(g.batch)};
-    const uint64_t strides[2] = {static_cast<uint64_t>(g.ldc) * 2,
-                                 static_cast<uint64_t>(g.batch > 1 ? g.c_batch_stride : g.ldc * g.M) * 2};
-    const uint32_t box[3] = {64, 32, 1};
-    mc = make_tmap_nd(g.C, g.out_dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
-                      3, dims, strides, box);
-  }
-  epi.tma = tma_ok ? 1 : 0;
+  epi.tma = make_output_map(g, epi.trans != 0, &mc) ? 1 : 0;
   GemmShape s = make_shape(g);
   s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
   s.num_n = (g.N + kBN3 - 1) / kBN3;
@@ -178,7 +182,7 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, s, epi));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, s, epi, NoGather{}));
 }
 
 template <typename OutT>
@@ -211,7 +215,9 @@ static int launch_store(const GemmArgs& g0, cudaStream_t stream) {
   }
   const int tiles = s.num_m * s.num_n * s.batch;
   const int grid = tiles < g.num_sms ? tiles : g.num_sms;
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, s, epi, GemmLoads{});
+  CUtensorMap mc;
+  epi.tma = make_output_map(g, trans, &mc) ? 1 : 0;
+  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, s, epi, GemmLoads{});
   return static_cast<int>(cudaGetLastError());
 }
 

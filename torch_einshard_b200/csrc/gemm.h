@@ -41,5 +41,9 @@ const char* check_gemm_args(const GemmArgs& g);
 void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb, bool pair = false);
 bool use_pair_kernel(const GemmArgs& g);
 int gemm_launch(const GemmArgs& g, cudaStream_t stream);
+struct GemmShape;
+GemmShape make_shape(const GemmArgs& g);
+// Output tensor map of the TMA-store epilogues; false (map zeroed) when C does not qualify.
+bool make_output_map(const GemmArgs& g, bool trans, CUtensorMap* mc);
 
 }  // namespace es

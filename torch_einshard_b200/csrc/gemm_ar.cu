@@ -15,6 +15,7 @@
 // Only reads cross NVLink; every rank writes only its own memory.  The epoch
 // protocol of comm.h makes buffer reuse across calls safe; every wait is bounded.
 #include <cuda_bf16.h>
+#include <string.h>
 
 #include "comm.h"
 #include "gemm.h"
@@ -23,7 +24,6 @@
 
 namespace es {
 
-GemmShape make_shape(const GemmArgs& g);
 
 constexpr int kTileBytes = kBM * kBN * 2;  // bf16 partial / reduced tile
 constexpr int kQueue = 8;                  // pending pulls per CTA
@@ -31,6 +31,12 @@ constexpr int kQueue = 8;                  // pending pulls per CTA
 constexpr int kQHead = 0, kQTail = 1, kDecision = 2, kAbortEpi = 3, kQBase = 8;
 
 __device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// element k (0..7) of eight packed bf16 values, without taking the vector's address
+__device__ __forceinline__ __nv_bfloat16 bf16_at(const uint4& v, int k) {
+  const uint32_t w = (k >> 1) == 0 ? v.x : (k >> 1) == 1 ? v.y : (k >> 1) == 2 ? v.z : v.w;
+  return __ushort_as_bfloat16(static_cast<unsigned short>((k & 1) ? (w >> 16) : (w & 0xffffu)));
+}
 
 struct ArEpilogue {
   CommDev c;
@@ -75,23 +81,33 @@ struct ArEpilogue {
     }
   }
 
-  // copy the reduced tile t (owner o) into this rank's C
+  // copy the reduced tile t (owner o) into this rank's C.  The 16 loads of a
+  // batch are issued before any store (the tile buffer is always whole, only the
+  // stores are guarded), so a thread keeps 16 NVLink reads in flight.
   __device__ void pull_tile(int t, const GemmShape& s, int row_in_tile) {
     const TileCoord tc = tile_coord(s, t);
     const int row = tc.m0 + row_in_tile;
     const uint8_t* src = tile_buf(t % c.size, t);
-    if (row >= s.M) return;
-    __nv_bfloat16* crow = C + static_cast<long long>(row) * ldc;
-#pragma unroll 8
-    for (int j = 0; j < kBN / 8; ++j) {
-      const int col = tc.n0 + j * 8;
-      if (col >= s.N) break;
-      const uint4 v = *reinterpret_cast<const uint4*>(src + (static_cast<size_t>(j) * kBM + row_in_tile) * 16);
-      if (col + 8 <= s.N && vec_ok) {
-        *reinterpret_cast<uint4*>(crow + col) = v;
-      } else {
-        const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&v);
-        for (int k = 0; k < 8 && col + k < s.N; ++k) crow[col + k] = h[k];
+    const bool row_ok = row < s.M;
+    __nv_bfloat16* crow = C + static_cast<long long>(row_ok ? row : 0) * ldc;
+    constexpr int kBatch = 16;
+#pragma unroll 1
+    for (int j0 = 0; j0 < kBN / 8; j0 += kBatch) {
+      if (tc.n0 + j0 * 8 >= s.N) break;  // uniform across the epilogue threads
+      uint4 v[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u)
+        v[u] = *reinterpret_cast<const uint4*>(src + (static_cast<size_t>(j0 + u) * kBM + row_in_tile) * 16);
+      if (!row_ok) continue;
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int col = tc.n0 + (j0 + u) * 8;
+        if (col >= s.N) break;
+        if (col + 8 <= s.N && vec_ok) {
+          *reinterpret_cast<uint4*>(crow + col) = v[u];
+        } else {
+          for (int k = 0; k < 8 && col + k < s.N; ++k) crow[col + k] = bf16_at(v[u], k);
+        }
       }
     }
   }
@@ -184,22 +200,26 @@ struct ArEpilogue {
       float acc[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(r[i]);
+      // all peers' 4 x 16-byte pieces of this 32-column chunk are loaded before the sums
+      uint4 v[4][kMaxRanks - 1];
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        uint4 v[kMaxRanks - 1];
         const size_t off = (static_cast<size_t>(chunk * 4 + q) * kBM + e) * 16;
 #pragma unroll
         for (int k = 1; k < kMaxRanks; ++k)
-          if (k < c.size) v[k - 1] = *reinterpret_cast<const uint4*>(tile_buf((c.rank + k) % c.size, t) + off);
+          if (k < c.size) v[q][k - 1] = *reinterpret_cast<const uint4*>(tile_buf((c.rank + k) % c.size, t) + off);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
 #pragma unroll
         for (int k = 1; k < kMaxRanks; ++k) {
           if (k >= c.size) break;
-          const uint32_t w[4] = {v[k - 1].x, v[k - 1].y, v[k - 1].z, v[k - 1].w};
+          const uint32_t w[4] = {v[q][k - 1].x, v[q][k - 1].y, v[q][k - 1].z, v[q][k - 1].w};
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
-            acc[8 * q + 2 * j] += f.x;
-            acc[8 * q + 2 * j + 1] += f.y;
+            // a bf16 pair widened exactly: each half is the upper 16 bits of an fp32
+            acc[8 * q + 2 * j] += __uint_as_float(w[j] << 16);
+            acc[8 * q + 2 * j + 1] += __uint_as_float(w[j] & 0xffff0000u);
           }
         }
       }
@@ -216,10 +236,8 @@ struct ArEpilogue {
 #pragma unroll
           for (int q = 0; q < 4; ++q) *reinterpret_cast<uint4*>(crow + col0 + 8 * q) = o[q];
         } else {
-          for (int q = 0; q < 4; ++q) {
-            const __nv_bfloat16* h = reinterpret_cast<const __nv_bfloat16*>(&o[q]);
-            for (int k = 0; k < 8 && col0 + 8 * q + k < s.N; ++k) crow[col0 + 8 * q + k] = h[k];
-          }
+          for (int q = 0; q < 4; ++q)
+            for (int k = 0; k < 8 && col0 + 8 * q + k < s.N; ++k) crow[col0 + 8 * q + k] = bf16_at(o[q], k);
         }
       }
     }
@@ -287,7 +305,9 @@ int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t s
   }
   const int grid = tiles < g.num_sms ? tiles : g.num_sms;
   GemmLoads loads{};
-  void* args[] = {&ma, &mb, &s, &epi, &loads};
+  CUtensorMap mc;
+  memset(&mc, 0, sizeof(mc));  // the all-reduce epilogue stores without TMA
+  void* args[] = {&ma, &mb, &mc, &s, &epi, &loads};
   return static_cast<int>(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(kernel), dim3(grid),
                                                       dim3(kThreads), args, kSmemBytes, stream));
 }

@@ -18,4 +18,11 @@ inline int gemm_allreduce_grid(const GemmArgs& g) {
 int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t stream, long long rs_seg = 0,
                           long long rs_shard = 0);
 
+// All-gather -> GEMM (gemm_ag.cu): g describes the GEMM over the gathered rows
+// (A = xfull, M = segments * P * shard); this rank's shard must already be in its
+// symmetric region as [segments][shard][K].
+int gemm_allgather_grid(const GemmArgs& g);
+int gemm_allgather_launch(const GemmArgs& g, const CommDev& comm, void* xfull, int segments, long long shard,
+                          cudaStream_t stream);
+
 }  // namespace es

@@ -41,7 +41,8 @@ constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kTmemCols = 512;
 constexpr int kThreads = 192;
 constexpr int kEpiThreads = 128;
-constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+constexpr int kStageOut = 4096;  // per epilogue warp: staging buffer of the TMA-store epilogues
+constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*barriers*/ + 4 * kStageOut + 1024 /*alignment slack*/;
 
 struct GemmShape {
   int M, N, K, batch;
@@ -128,12 +129,13 @@ struct GemmLoads {
 template <class Epi, class Loads = GemmLoads>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                   const GemmShape shp, Epi epi, const Loads loads) {
+                   const __grid_constant__ CUtensorMap tmC, const GemmShape shp, Epi epi, const Loads loads) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages * kABytes;
   SharedState* st = reinterpret_cast<SharedState*>(smem + kStages * kStageBytes);
+  uint8_t* out_stage = smem + kStages * kStageBytes + 1024;  // 1024-byte aligned (TMA swizzle atom)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -258,6 +260,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       et.row = q * 32 + lane;
       et.q = q;
       et.lane = lane;
+      et.tmc = &tmC;
+      et.stage = out_stage + q * kStageOut;
       const bool ok = epi.tile(et, shp, abort_flag);
       tc_fence_before();
       __syncwarp();
@@ -268,6 +272,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     epi.finish(shp, abort_flag);
+    if (lane == 0) bulk_wait_group<0>();  // every TMA store of this warp has landed
   }
 
   __syncthreads();
@@ -290,6 +295,7 @@ struct StoreOut<float> {
                          __uint_as_float(r[base + 4 * i + 2]), __uint_as_float(r[base + 4 * i + 3]));
   }
   static __device__ __forceinline__ void store1(float* p, float v) { *p = v; }
+  static __device__ __forceinline__ float cvt(float v) { return v; }
 };
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -311,6 +317,7 @@ struct StoreOut<__nv_bfloat16> {
                         pack_bf16(__uint_as_float(r[8 * i + 6]), __uint_as_float(r[8 * i + 7])));
   }
   static __device__ __forceinline__ void store1(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+  static __device__ __forceinline__ __nv_bfloat16 cvt(float v) { return __float2bfloat16_rn(v); }
 };
 template <>
 struct StoreOut<__half> {
@@ -324,6 +331,7 @@ struct StoreOut<__half> {
                         pack_f16(__uint_as_float(r[8 * i + 6]), __uint_as_float(r[8 * i + 7])));
   }
   static __device__ __forceinline__ void store1(__half* p, float v) { *p = __float2half_rn(v); }
+  static __device__ __forceinline__ __half cvt(float v) { return __float2half_rn(v); }
 };
 
 // Activation applied in the epilogue before the store.

@@ -85,10 +85,24 @@ __device__ __forceinline__ bool pair_tile_at(const GemmShape& s, int cluster, in
   return true;
 }
 
-template <class Epi>
-__global__ void __launch_bounds__(kThreads3, 1)
+// Gather policy of the wide kernel.  The plain GEMM has none; the fused
+// all-gather -> GEMM (gemm_ag.cu) adds a copy warp that pulls peers' rows of A
+// into a local buffer, orders the M tiles local-rows-first and makes the
+// producer wait for a chunk's flag before its TMA loads read those rows.
+struct NoGather {
+  static constexpr int kCopyWarps = 0;
+  __device__ __forceinline__ int map_m0(int m0) const { return m0; }
+  __device__ __forceinline__ bool wait_rows(int, volatile int*) const { return true; }
+  __device__ __forceinline__ void start() const {}
+  __device__ __forceinline__ void copy(int, int, volatile int*) const {}
+  __device__ __forceinline__ void finish(bool) const {}
+};
+
+template <class Epi, class Gather = NoGather>
+__global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
     gemm_tc3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, const GemmShape shp, Epi epi) {
+                    const __grid_constant__ CUtensorMap tmC, const GemmShape shp, Epi epi,
+                    const Gather gather = Gather()) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -134,12 +148,15 @@ __global__ void __launch_bounds__(kThreads3, 1)
 
   const uint32_t full_leader0 = map_to_cta(&st->full[0], 0);
   const uint32_t tempty_leader = map_to_cta(&st->tempty, 0);
+  if (threadIdx.x == 0 && cluster == 0 && rank == 0) gather.start();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
     uint32_t it = 0;
     TileCoord c;
     for (int ti = 0; pair_tile_at(shp, cluster, nclusters, ti, static_cast<int>(rank), &c); ++ti) {
+      c.m0 = gather.map_m0(c.m0);
+      if (!gather.wait_rows(c.m0, abort_flag)) goto producer_done;  // rows of A gathered from their owner
       const int nq0 = c.n0 + static_cast<int>(rank) * (kBN / 2);  // this CTA's quarter in each 256-col half
       for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
         const int s = it % kStages3;
@@ -242,6 +259,9 @@ __global__ void __launch_bounds__(kThreads3, 1)
         mbar_wait(&st->drain, 0, &dummy_abort, nullptr, 0);
       }
     }
+  } else if (warp >= 2 + kEpiWarps3) {
+    // ------------------------------------------------------------ copy warp (gather policies only)
+    gather.copy(cluster * 2 + static_cast<int>(rank), nclusters * 2, abort_flag);
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs, 8 warps)
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
@@ -249,6 +269,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
     uint32_t tc = 0;
     TileCoord ce;
     for (; pair_tile_at(shp, cluster, nclusters, static_cast<int>(tc), static_cast<int>(rank), &ce); ++tc) {
+      ce.m0 = gather.map_m0(ce.m0);
       if (!mbar_wait_sleepy(&st->tfull, tc & 1u, abort_flag, shp.err, kErrWaitTmemFull, shp.sleep_ns)) break;
       tc_fence_after();
       EpiTile et;
@@ -275,6 +296,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
   }
 
   __syncthreads();
+  if (threadIdx.x == 0) gather.finish(*abort_flag == 0);
   tc_fence_before();
   cluster_sync();
   if (warp == 1) {
