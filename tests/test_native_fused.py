@@ -16,7 +16,7 @@ def _fused(rank, world):
     from torch.distributed.device_mesh import init_device_mesh
 
     import torch_einshard_b200 as es
-    from torch_einshard_b200.ops import _native, gemm
+    from torch_einshard_b200.ops import _native, fused_native, gemm
     from torch_einshard_b200.ops.fused_native import gemm_allreduce
     from torch_einshard_b200.parallel import native_comm
     from torch_einshard_b200.models.tp_mlp import TPMLP
@@ -40,15 +40,35 @@ def _fused(rank, world):
     torch.cuda.synchronize()
     _native.check_errors()
 
+    # push-model fused kernel (wide GEMM): ragged shapes, repeated calls
+    for (m, n, k) in [(512, 1024, 128), (300, 700, 136), (2048, 2048, 512)]:
+        for _ in range(2):
+            a = torch.randn(1, m, k, device="cuda", dtype=torch.bfloat16) * (rank + 1)
+            b = torch.randn(1, n, k, device="cuda", dtype=torch.bfloat16).transpose(1, 2)
+            got = fused_native.gemm_allreduce_push(comm, a, b)
+            want = gemm.native_bmm(a, b).float()
+            dist.all_reduce(want, group=group)
+            scale = want.abs().max().item() + 1
+            err = (got.float() - want).abs().max().item()
+            assert err < 3e-2 * scale, ("push", m, n, k, err, scale)
+    torch.cuda.synchronize()
+    _native.check_errors()
+
     # TP-MLP through the public API: fused native path vs the NCCL-only path
     torch.manual_seed(0)
     model = TPMLP(512, 2048, mesh, device="cuda")
     x = torch.randn(2, 256, 512, device="cuda", dtype=torch.bfloat16, requires_grad=True)
-    y = model(x)
-    assert [s.name for s in es.last_plan()] == ["rank_local_einsum", "allreduce_forward_identity_backward"]
-    dy = torch.randn_like(y)
-    y.backward(dy)
-    got = (y.detach().float(), x.grad.float(), model.w1.grad.float(), model.w2.grad.float())
+    dy = torch.randn(2, 256, 512, device="cuda", dtype=torch.bfloat16)
+    runs = []
+    for fused_limit in (0, world):  # default policy (GEMM, then the all-reduce) and the fused kernel
+        fused_native._MAX_FUSED_EPILOGUE_RANKS = fused_limit
+        xi = x.detach().clone().requires_grad_(True)
+        model.w1.grad = model.w2.grad = None
+        y = model(xi)
+        assert [s.name for s in es.last_plan()] == ["rank_local_einsum", "allreduce_forward_identity_backward"]
+        y.backward(dy)
+        runs.append((y.detach().float(), xi.grad.float(), model.w1.grad.float(), model.w2.grad.float()))
+    fused_native._MAX_FUSED_EPILOGUE_RANKS = 0
 
     native_comm.disable()
     x2 = x.detach().clone().requires_grad_(True)
@@ -57,9 +77,10 @@ def _fused(rank, world):
     y2.backward(dy)
     want = (y2.detach().float(), x2.grad.float(), model.w1.grad.float(), model.w2.grad.float())
     native_comm._state["enabled"] = True
-    for g, w in zip(got, want):
-        scale = w.abs().max().item() + 1e-3
-        assert (g - w).abs().max().item() < 3e-2 * scale
+    for got in runs:
+        for g, w in zip(got, want):
+            scale = w.abs().max().item() + 1e-3
+            assert (g - w).abs().max().item() < 3e-2 * scale
     torch.cuda.synchronize()
     _native.check_errors()
 
@@ -137,7 +158,9 @@ def _sequence_parallel(rank, world):
         y.backward(dy)
         return (h.detach().float(), y.detach().float(), x.grad.float(), a.grad.float(), b.grad.float()), plan1, plan2
 
+    fused_native._MAX_FUSED_EPILOGUE_RANKS = world  # also run the fused GEMM -> reduce-scatter
     got, p1, p2 = run()
+    fused_native._MAX_FUSED_EPILOGUE_RANKS = 0
     assert p1 == ["allgather_forward_reducescatter_backward", "rank_local_einsum"], p1
     assert p2 == ["rank_local_einsum", "reducescatter_forward_allgather_backward"], p2
     native_comm.disable()

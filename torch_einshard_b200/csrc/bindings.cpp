@@ -290,6 +290,32 @@ void gemm_allreduce(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Te
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+// out = all-reduce over the communicator's ranks of (a @ b); push-model fused
+// kernel on the wide 2-SM GEMM (partials and reduced tiles travel as NVLink stores).
+void gemm_allreduce_push(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open, "einshard fused gemm+allreduce (push): communicator not connected");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && a.size(0) == 1, "einshard fused gemm+allreduce (push): bf16, batch 1");
+  const c10::cuda::CUDAGuard guard(a.device());
+  es::GemmArgs g = gemm_args(a, b, out, 0, err);
+  TORCH_CHECK(es::gemm_push_region_bytes(g, hc.size) <= (long long)hc.data_bytes,
+              "einshard fused gemm+allreduce (push): output too large for the symmetric buffer");
+  const int grid = es::gemm_push_grid(g);
+  es::CommDev d = make_dev(hc, err, 0, 0);
+  d.arrive_base = hc.arrive;
+  hc.arrive += static_cast<uint32_t>(grid);
+  const int rc = es::gemm_push_allreduce_launch(g, d, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard fused gemm+allreduce (push): launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+int64_t gemm_push_region_bytes(int64_t m, int64_t n, int64_t size) {
+  es::GemmArgs g;
+  g.M = static_cast<int>(m);
+  g.N = static_cast<int>(n);
+  return es::gemm_push_region_bytes(g, static_cast<int>(size));
+}
+
 // out (this rank's rows) = reduce-scatter over the communicator's ranks of (a @ b)
 // along row segments: rows [seg * i + rank * shard, ... + shard) for every i.
 void gemm_reducescatter(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out, int64_t seg,
@@ -576,6 +602,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fft_slab", &fft_slab, "slab transpose fused with the FFT along the exchanged axis");
   m.def("gemm_reducescatter", &gemm_reducescatter, "fused tcgen05 GEMM + NVLink reduce-scatter of row segments (bf16)");
   m.def("gemm_allgather", &gemm_allgather, "fused all-gather of row shards + tcgen05 GEMM (bf16)");
+  m.def("gemm_allreduce_push", &gemm_allreduce_push, "push-model fused wide GEMM + NVLink all-reduce (bf16)");
+  m.def("gemm_push_region_bytes", &gemm_push_region_bytes, "symmetric bytes the push all-reduce needs");
   m.def("comm_data_bytes", &comm_data_bytes, "data capacity of a communicator");
   m.def("set_gemm_pair_mode", [](int64_t m) { g_pair_mode = static_cast<int>(m); },
         "-1 heuristic, 0 force 1-SM, 1 force 2-SM GEMM kernel");

@@ -25,4 +25,9 @@ int gemm_allgather_grid(const GemmArgs& g);
 int gemm_allgather_launch(const GemmArgs& g, const CommDev& comm, void* xfull, int segments, long long shard,
                           cudaStream_t stream);
 
+// Push-model fused GEMM + all-reduce on the wide kernel (gemm_push.cu).
+long long gemm_push_region_bytes(const GemmArgs& g, int size);
+int gemm_push_grid(const GemmArgs& g);
+int gemm_push_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t stream);
+
 }  // namespace es

@@ -33,17 +33,20 @@ constexpr int kEpiWarps3 = 8;
 constexpr int kStage3Out = 4096;                    // per epilogue warp: 32 rows x 64 cols x 2 B
 constexpr int kSmem3Bytes = kStages3 * kStage3Bytes + 1024 + kEpiWarps3 * kStage3Out + 1024;
 
+// Same layout as SharedState (gemm_tc.cuh) so that epilogue policies can use
+// its fields through that type; only tfull[0] / tempty[0] are used here.
 struct SharedState3 {
   uint64_t full[kStages3];
   uint64_t empty[kStages3];
-  uint64_t tfull;
-  uint64_t tempty;
+  uint64_t tfull_[2];
+  uint64_t tempty_[2];
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
   int consumed;
   int epi[32];
 };
+static_assert(kStages3 == kStages, "SharedState3 must mirror SharedState");
 
 // Pair tile p -> this CTA's 128-row half; columns n0 .. n0 + 511.
 __device__ __forceinline__ TileCoord tile_coord3(const GemmShape& s, int p, int rank) {
@@ -123,8 +126,8 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
       mbar_init(&st->full[s], 1);
       mbar_init(&st->empty[s], 1);
     }
-    mbar_init(&st->tfull, 1);
-    mbar_init(&st->tempty, 2 * kEpiWarps3);
+    mbar_init(&st->tfull_[0], 1);
+    mbar_init(&st->tempty_[0], 2 * kEpiWarps3);
     mbar_init(&st->drain, 1);
     st->abort_flag = 0;
     st->consumed = 0;
@@ -147,7 +150,7 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
   epi.setup(st_common, shp);
 
   const uint32_t full_leader0 = map_to_cta(&st->full[0], 0);
-  const uint32_t tempty_leader = map_to_cta(&st->tempty, 0);
+  const uint32_t tempty_leader = map_to_cta(&st->tempty_[0], 0);
   if (threadIdx.x == 0 && cluster == 0 && rank == 0) gather.start();
 
   if (warp == 0) {
@@ -213,7 +216,7 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
       TileCoord cm;
       for (; pair_tile_at(shp, cluster, nclusters, static_cast<int>(tc), 0, &cm); ++tc) {
         const long long t_e0 = shp.prof ? clock64() : 0;
-        if (!mbar_wait_lane0(&st->tempty, (tc & 1u) ^ 1u, abort_flag, shp.err, kErrWaitTmemEmpty)) goto mma_done;
+        if (!mbar_wait_lane0(&st->tempty_[0], (tc & 1u) ^ 1u, abort_flag, shp.err, kErrWaitTmemEmpty)) goto mma_done;
         if (shp.prof) wait_tempty += clock64() - t_e0;
         tc_fence_after();
         for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
@@ -242,7 +245,7 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
           issued_any = true;
           __syncwarp();
         }
-        if (lane == 0) umma_commit_pair_mc(&st->tfull, 0x3);
+        if (lane == 0) umma_commit_pair_mc(&st->tfull_[0], 0x3);
         __syncwarp();
       }
     mma_done:
@@ -270,7 +273,7 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
     TileCoord ce;
     for (; pair_tile_at(shp, cluster, nclusters, static_cast<int>(tc), static_cast<int>(rank), &ce); ++tc) {
       ce.m0 = gather.map_m0(ce.m0);
-      if (!mbar_wait_sleepy(&st->tfull, tc & 1u, abort_flag, shp.err, kErrWaitTmemFull, shp.sleep_ns)) break;
+      if (!mbar_wait_sleepy(&st->tfull_[0], tc & 1u, abort_flag, shp.err, kErrWaitTmemFull, shp.sleep_ns)) break;
       tc_fence_after();
       EpiTile et;
       et.t = 2 * (cluster + static_cast<int>(tc) * nclusters) + static_cast<int>(rank);

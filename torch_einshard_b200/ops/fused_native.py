@@ -39,6 +39,23 @@ def gemm_allreduce(comm, a, b):
     return out
 
 
+def gemm_allreduce_push(comm, a, b):
+    """``sum over ranks of a @ b`` with the push-model fused kernel (wide GEMM;
+    partials and reduced tiles cross NVLink as stores)."""
+    mod = _native.require()
+    a, b = _prepare(a), _prepare(b)
+    out = torch.empty((1, a.shape[1], b.shape[2]), dtype=torch.bfloat16, device=a.device)
+    mod.gemm_allreduce_push(comm.cid, a, b, out, _native.error_word(a.device))
+    return out
+
+
+def _push_fits(comm, m, n):
+    mod = _native.module()
+    return (mod is not None and hasattr(mod, "gemm_allreduce_push")
+            and mod.gemm_push_region_bytes(m, n, comm.size) <= comm.capacity
+            and -(-m // 128) * -(-n // 256) <= 120000)
+
+
 def gemm_reducescatter(comm, a, b, seg, shard):
     """This rank's rows of the reduce-scatter of ``a @ b`` over the ranks: rows are
     segments of ``seg`` rows, rank p keeps rows [p*shard, (p+1)*shard) of each."""
@@ -156,6 +173,8 @@ def _fits(comm, m, n):
 
 
 def _ar_or_fallback(comm, a, b):
+    if _push_fits(comm, a.shape[1], b.shape[2]):
+        return gemm_allreduce_push(comm, a, b)
     if _fits(comm, a.shape[1], b.shape[2]):
         return gemm_allreduce(comm, a, b)
     out = native_bmm(a, b)
@@ -357,17 +376,23 @@ class _Fusion:
         return out.reshape(shape).permute(perm)
 
 
-# The fused epilogues pull peers' tiles with per-thread loads; with more ranks the
-# tiles are shorter and those pulls dominate (measured at 8 ranks on B200: 31.5 ms
-# fused vs 1.3 ms GEMM + 1.3 ms NCCL all-reduce for the TP-MLP row-parallel step).
-# Until the epilogue moves bulk data, fuse only up to this many ranks.
+# Measured on B200 (CUDA events, max over ranks), TP-MLP shapes:
+#   GEMM + all-reduce, 2 ranks: fused pull epilogue 7.64 ms, fused push epilogue
+#     7.51 ms, wide GEMM + NCCL all-reduce 6.16 ms; 8 ranks: fused 31.5 ms,
+#     GEMM + NCCL 2.6 ms.  The single-buffered accumulator of the wide kernel
+#     leaves the epilogue's NVLink traffic on the critical path.
+#   all-gather + GEMM, 2 ranks: fused (copy warps inside the GEMM) 5.48 ms,
+#     NCCL all-gather + GEMM 6.12 ms, GEMM alone 5.20 ms.
+# So the fused epilogue kernels (all-reduce / reduce-scatter) are off by default
+# and the fused all-gather runs for groups up to the size it was measured at.
 import os
 
-_MAX_FUSED_RANKS = int(os.environ.get("EINSHARD_FUSED_MAX_RANKS", "2"))
+_MAX_FUSED_EPILOGUE_RANKS = int(os.environ.get("EINSHARD_FUSED_EPILOGUE_MAX_RANKS", "0"))
+_MAX_FUSED_GATHER_RANKS = int(os.environ.get("EINSHARD_FUSED_GATHER_MAX_RANKS", "2"))
 
 
-def _fusable(comm):
-    return comm is not None and comm.size <= _MAX_FUSED_RANKS
+def _fusable(comm, limit):
+    return comm is not None and 2 <= comm.size <= limit
 
 
 def _eligible_tensors(executor):
@@ -384,18 +409,18 @@ def provider(executor):
     if (len(out_steps) == 1 and out_steps[0].name == "reducescatter_forward_allgather_backward"
             and not tp.input0_steps and not tp.input1_steps):
         name, dim = out_steps[0].args
-        if _fusable(_comm(executor.group(dim))):
+        if _fusable(_comm(executor.group(dim)), _MAX_FUSED_EPILOGUE_RANKS):
             return _Fusion("gemm_reducescatter", axis=name)
         return None
     if (not out_steps and len(tp.input0_steps) == 1 and not tp.input1_steps
             and tp.input0_steps[0].name == "allgather_forward_reducescatter_backward"):
         name, dim = tp.input0_steps[0].args
-        if _fusable(_comm(executor.group(dim))):
+        if _fusable(_comm(executor.group(dim)), _MAX_FUSED_GATHER_RANKS):
             return _Fusion("allgather_gemm", operand=0, axis=name)
         return None
     if (len(out_steps) == 1 and out_steps[0].name == "allreduce_forward_identity_backward"
             and not tp.input0_steps and not tp.input1_steps):
-        if _fusable(_comm(executor.group(out_steps[0].args[0]))):
+        if _fusable(_comm(executor.group(out_steps[0].args[0])), _MAX_FUSED_EPILOGUE_RANKS):
             return _Fusion("gemm_allreduce")
         return None
     if out_steps:
@@ -403,7 +428,7 @@ def provider(executor):
     in0, in1 = tp.input0_steps, tp.input1_steps
     for operand, (mine, other) in enumerate(((in0, in1), (in1, in0))):
         if len(mine) == 1 and not other and mine[0].name == "identity_forward_allreduce_backward":
-            if _fusable(_comm(executor.group(mine[0].args[0]))):
+            if _fusable(_comm(executor.group(mine[0].args[0])), _MAX_FUSED_EPILOGUE_RANKS):
                 return _Fusion("dgrad_allreduce", operand)
     return None
 
