@@ -107,6 +107,7 @@ def main():
     p.add_argument("--split", type=int, default=0, help="wide kernel: cluster split mode 0/1/2")
     p.add_argument("--sleep-ns", type=int, default=0, help="wide kernel: epilogue back-off between polls")
     p.add_argument("--l2-promotion", type=int, default=3, help="TMA L2 promotion 0 none .. 3 256B")
+    p.add_argument("--persistent", type=int, default=0, help="wide kernel: 1 persistent grid, 0 one tile per cluster")
     args = p.parse_args()
     device = torch.device(args.device)
     from torch_einshard_b200.ops import _native, gemm
@@ -125,6 +126,7 @@ def main():
                 mod.set_gemm_split(args.split)
                 mod.set_gemm_sleep_ns(args.sleep_ns)
                 mod.set_tma_l2_promotion(args.l2_promotion)
+                mod.set_gemm_persistent(args.persistent)
                 fn = lambda: gemm.native_bmm(a, b)  # noqa: E731
             label = f"gemm_{name}_{kern}"
             if args.mode == "burst":

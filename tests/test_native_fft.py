@@ -127,3 +127,48 @@ def test_einfft_slab_two_gpus():
 def test_einfft_slab_four_gpus():
     from gpu_harness import run_gpus
     run_gpus(_slab, 4)
+
+
+@pytest.mark.parametrize("shape,dim", [((16, 1024), 1), ((3, 1024, 16), 1), ((1024, 40), 0), ((2, 1024, 8, 2), 1),
+                                       ((300, 1024), 1)])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_fft_1024_pipelined_kernel(shape, dim, inverse):
+    """1024-point lines in whole tiles take the persistent cp.async-pipelined kernel."""
+    mod = _native.require()
+    x = torch.randn(*shape, dtype=torch.complex64, device="cuda")
+    got = fft_c2c(mod, x, dim, inverse, scale=0.25)
+    want = (torch.fft.ifft(x.cdouble(), dim=dim, norm="forward") if inverse else torch.fft.fft(x.cdouble(), dim=dim)) * 0.25
+    _close(got.cdouble(), want, tol=2e-4)
+    assert torch.equal(fft_c2c(mod, x, dim, inverse, scale=0.25), got)
+
+
+@pytest.mark.parametrize("n", [4, 64, 512, 2048])
+def test_real_fft_native_matches_torch(n):
+    from torch_einshard_b200.ops.fft_impl import irfft_native, rfft_native
+    x = torch.randn(3, n, 5, device="cuda", dtype=torch.float32)
+    got = rfft_native(x, 1)
+    want = torch.fft.rfft(x.double(), dim=1)
+    _close(got.cdouble(), want, tol=2e-5 * n.bit_length())
+    back = irfft_native(got, n, 1)
+    want_back = torch.fft.irfft(want, n=n, dim=1, norm="forward")
+    _close(back.double(), want_back, tol=2e-5 * n.bit_length())
+    # gradients flow through the native pieces
+    xr = x.clone().requires_grad_(True)
+    rfft_native(xr, 1).abs().sum().backward()
+    xt = x.clone().requires_grad_(True)
+    torch.fft.rfft(xt, dim=1).abs().sum().backward()
+    _close(xr.grad, xt.grad, tol=1e-3)
+
+
+def test_einfft_real_local_uses_native(monkeypatch):
+    import torch_einshard_b200 as es
+    from torch_einshard_b200.ops import fft_impl
+    calls = []
+    real = fft_impl._run
+    monkeypatch.setattr(fft_impl, "_run", lambda *a, **k: calls.append(1) or real(*a, **k))
+    x = torch.randn(4, 64, 32, device="cuda")
+    y = es.einfft("b x y -> b kx ky", x, {"x": "kx", "y": "ky"}, real=True)
+    torch.testing.assert_close(y, torch.fft.rfftn(x, dim=(1, 2)), rtol=1e-4, atol=1e-3)
+    back = es.einfft("b kx ky -> b x y", y, {"kx": "x", "ky": "y"}, real=True, inverse=True, signal_sizes={"y": 32})
+    torch.testing.assert_close(back, x, rtol=1e-4, atol=1e-4)
+    assert calls

@@ -25,6 +25,7 @@ int g_pair_mode = -1;
 int g_group_m = 0;  // raster group override (0: kernel default)
 int g_split = 0;    // wide-kernel cluster split mode (tuning)
 int g_sleep_ns = 0;  // wide-kernel epilogue back-off (tuning)
+int g_persistent = 0;  // wide-kernel grid: 0 one pair tile per cluster (default, measured faster under the power cap), 1 persistent
 unsigned long long* g_prof = nullptr;  // wide-kernel wait counters (tuning), device pointer or null
 
 int dtype_code(at::ScalarType t) {
@@ -101,6 +102,7 @@ es::GemmArgs gemm_operand_args(const at::Tensor& a, const at::Tensor& b, int64_t
   g.split = g_split;
   g.prof = g_prof;
   g.sleep_ns = g_sleep_ns;
+  g.persistent = g_persistent;
   return g;
 }
 
@@ -612,6 +614,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_gemm_profile", [](const at::Tensor& t) {
         g_prof = t.numel() >= 3 ? reinterpret_cast<unsigned long long*>(t.data_ptr()) : nullptr;
       }, "int64 CUDA tensor of >= 3 wait-cycle counters for the wide GEMM (empty tensor: off)");
+  m.def("set_gemm_persistent", [](int64_t v) { g_persistent = static_cast<int>(v); }, "wide kernel: 1 persistent, 0 one tile per cluster");
   m.def("set_gemm_sleep_ns", [](int64_t v) { g_sleep_ns = static_cast<int>(v); }, "wide-kernel epilogue back-off ns");
   m.def("set_tma_l2_promotion", [](int64_t v) { es::tma_l2_promotion() = static_cast<int>(v); },
         "L2 promotion of TMA loads: 0 none, 1 64B, 2 128B, 3 256B (tuning)");

@@ -277,6 +277,143 @@ int log2_exact(long long n) {
   return (1LL << l) == n ? l : -1;
 }
 
+
+// Persistent, software-pipelined variant for local transforms: each CTA walks
+// tiles of LPC lines; while it transforms tile i out of shared memory, the
+// cp.async copies of tile i + 1 are in flight, so HBM reads overlap the
+// register FFTs and the (direct, coalesced) stores of the previous tile.
+// Requires whole tiles: contiguous lines (inner == 1), or LPC neighbouring
+// lines (inner % LPC == 0) so a tile is one 8*LPC-byte run per point.
+template <int LOG1, int LOG2, bool INV>
+__global__ void __launch_bounds__(kFftThreads) fft2_pipelined_kernel(const float2* __restrict__ in,
+                                                                     float2* __restrict__ out, long long tiles,
+                                                                     long long inner, long long os, long long ps,
+                                                                     const float2* __restrict__ tw_g, float scale,
+                                                                     int strided) {
+  constexpr int N1 = 1 << LOG1;
+  constexpr int N2 = 1 << LOG2;
+  constexpr int LOGN = LOG1 + LOG2;
+  constexpr int N = 1 << LOGN;
+  constexpr int T = N1 > N2 ? N1 : N2;
+  constexpr int LPC = kFftThreads / T;
+  constexpr int RP = N2 + 1;
+  constexpr int LP0 = N1 * RP;
+  constexpr int LP = LP0 + ((2 - LP0 % 16) + 16) % 16;
+  constexpr int TILE = N * LPC;              // complex values per tile
+  constexpr int CHUNKS = TILE / 2;           // 16-byte pieces per tile
+  extern __shared__ float2 fft_smem[];
+  float2* tw = fft_smem;
+  float2* buf = tw + N;                      // transpose tile (LPC * LP)
+  float2* inb = buf + LPC * LP;              // two input tiles, 16-byte aligned
+  for (int j = threadIdx.x; j < N; j += blockDim.x) tw[j] = tw_g[j];
+
+  const int tid = threadIdx.x;
+  const int line = strided ? tid % LPC : tid / T;
+  const int t = strided ? tid / LPC : tid % T;
+
+  // tile k: lines [k*LPC, (k+1)*LPC) = outer o, inner [i0, i0 + LPC) (strided) or outer k*LPC.. (contiguous)
+  auto issue = [&](long long k, int slot) {
+    float2* dst = inb + slot * TILE;
+    if (strided) {
+      const long long l0 = k * LPC;
+      const long long o = l0 / inner;
+      const long long i0 = l0 - o * inner;
+      const float2* src = in + o * os + i0;
+      // point p, pair q (two neighbouring lines): global src + p*ps + 2q, smem p*LPC + 2q
+      for (int c = tid; c < CHUNKS; c += kFftThreads) {
+        const int p = c / (LPC / 2);
+        const int q = c - p * (LPC / 2);
+        cp_async16(dst + p * LPC + 2 * q, src + p * ps + 2 * q);
+      }
+    } else {
+      const float2* src = in + k * LPC * os;  // os = N for contiguous lines
+      for (int c = tid; c < CHUNKS; c += kFftThreads) cp_async16(dst + 2 * c, src + 2 * c);
+    }
+    cp_async_commit();
+  };
+
+  long long k = blockIdx.x;
+  if (k < tiles) issue(k, 0);
+  int slot = 0;
+  for (; k < tiles; k += gridDim.x, slot ^= 1) {
+    const long long next = k + gridDim.x;
+    if (next < tiles) {
+      issue(next, slot ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();  // tile k (and the twiddles) visible to every thread
+    const float2* tin = inb + slot * TILE;
+    float2* lb = buf + line * LP;
+    if (t < N2) {
+      float2 v[N1];
+#pragma unroll
+      for (int n1 = 0; n1 < N1; ++n1) {
+        const int p = n1 * N2 + t;
+        v[fft_bitrev<LOG1>(n1)] = strided ? tin[p * LPC + line] : tin[line * N + p];
+      }
+      reg_fft<LOG1, LOGN, INV>(v, tw);
+#pragma unroll
+      for (int k1 = 0; k1 < N1; ++k1) lb[k1 * RP + t] = k1 == 0 ? v[0] : cmul(v[k1], tw[t * k1]);
+    }
+    __syncthreads();
+    if (t < N1) {
+      float2 v[N2];
+#pragma unroll
+      for (int n2 = 0; n2 < N2; ++n2) v[fft_bitrev<LOG2>(n2)] = lb[t * RP + n2];
+      reg_fft<LOG2, LOGN, INV>(v, tw);
+      const long long gl = k * LPC + line;
+      const long long o = gl / inner;
+      const long long i = gl - o * inner;
+      float2* ob = out + o * os + i;
+#pragma unroll
+      for (int k2 = 0; k2 < N2; ++k2)
+        ob[static_cast<long long>(t + k2 * N1) * ps] = make_float2(v[k2].x * scale, v[k2].y * scale);
+    }
+    __syncthreads();  // the transpose tile and input slot are reused two tiles later
+  }
+}
+
+template <int LOG1, int LOG2, bool INV>
+int launch_fft_pipelined(const FftLines& f, long long lines, cudaStream_t stream) {
+  constexpr int N1 = 1 << LOG1, N2 = 1 << LOG2, N = N1 * N2;
+  constexpr int T = N1 > N2 ? N1 : N2;
+  constexpr int LPC = kFftThreads / T;
+  constexpr int RP = N2 + 1;
+  constexpr int LP0 = N1 * RP;
+  constexpr int LP = LP0 + ((2 - LP0 % 16) + 16) % 16;
+  const size_t smem = static_cast<size_t>(N + LPC * LP + 2 * N * LPC) * sizeof(float2);
+  auto kern = fft2_pipelined_kernel<LOG1, LOG2, INV>;
+  static int attr_set[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    attr_set[dev] = 1;
+  }
+  int sms = 148;
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long tiles = lines / LPC;
+  const long long grid = tiles < sms ? tiles : sms;
+  kern<<<static_cast<unsigned>(grid), kFftThreads, smem, stream>>>(f.in, f.out, tiles, f.inner, f.in_os, f.in_ps, f.tw,
+                                                                   f.scale, f.inner > 1 ? 1 : 0);
+  return static_cast<int>(cudaGetLastError());
+}
+
+// The pipelined kernel covers 1024-point lines (the shape that dominates the
+// 3-D transforms); out-of-place or in-place, whole tiles only.
+bool pipelined_ok(const FftLines& f) {
+  if (log2_exact(f.n) != 10) return false;
+  constexpr int kLpc = kFftThreads / 32;
+  if (f.in_is != 1 || f.out_is != 1 || f.in_os != f.out_os || f.in_ps != f.out_ps) return false;
+  if (f.inner == 1) return f.in_ps == 1 && f.in_os == f.n && (f.outer % kLpc) == 0 &&
+                           ((reinterpret_cast<uintptr_t>(f.in) & 15) == 0);
+  return (f.inner % kLpc) == 0 && ((reinterpret_cast<uintptr_t>(f.in) & 15) == 0) && (f.in_ps % 2) == 0 &&
+         (f.in_os % 2) == 0;
+}
+
 }  // namespace
 
 bool fft_supported(long long n) {
@@ -294,9 +431,13 @@ long long fft_grid(long long n, long long lines) {
 int fft_lines(const FftLines& f, cudaStream_t stream) {
   const int logn = log2_exact(f.n);
   if (logn < 1 || logn > kFftMaxLog) return static_cast<int>(cudaErrorInvalidValue);
+  const long long lines = f.outer * f.inner;
+  if (f.pipelined && pipelined_ok(f) && f.in != f.out) {
+    return f.inverse ? launch_fft_pipelined<5, 5, true>(f, lines, stream)
+                     : launch_fft_pipelined<5, 5, false>(f, lines, stream);
+  }
   PlainLoader ld{f.in, f.in_os, f.in_ps, f.in_is};
   SlabSync sync{};
-  const long long lines = f.outer * f.inner;
   return f.inverse ? dispatch<true>(logn, ld, f.out, lines, f.inner, f.out_os, f.out_ps, f.out_is, f.tw, f.scale, sync,
                                     stream)
                    : dispatch<false>(logn, ld, f.out, lines, f.inner, f.out_os, f.out_ps, f.out_is, f.tw, f.scale,

@@ -19,6 +19,7 @@ struct FftLines {
   const float2* tw;                  // n entries exp(-+2 pi i j / n) for the direction
   float scale;
   int inverse;
+  int pipelined = 1;                 // use the persistent cp.async-pipelined kernel where it applies
 };
 
 // Slab transpose + FFT along the exchanged axis S (length n, Sl = n / size per

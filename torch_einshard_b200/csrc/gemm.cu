@@ -169,7 +169,7 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
   }
   const int pairs = s.num_m * s.num_n * s.batch;
   int clusters = g.num_sms / 2;
-  if (pairs < clusters) clusters = pairs;
+  if (pairs < clusters || g.persistent == 0) clusters = pairs;  // 0: one pair tile per cluster (tuning)
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
   cfg.blockDim = dim3(kThreads3);

@@ -35,6 +35,7 @@ struct GemmArgs {
   int split = 0;     // wide kernel cluster split (see GemmShape::split)
   unsigned long long* prof = nullptr;  // optional wait-cycle counters (wide kernel)
   int sleep_ns = 0;  // wide kernel epilogue back-off (tuning)
+  int persistent = 0;  // wide kernel: 0 one pair tile per cluster (default), 1 persistent clusters
 };
 
 const char* check_gemm_args(const GemmArgs& g);

@@ -107,6 +107,20 @@ def _local_fft(x, dim, inverse, scale=1.0):
     return out if scale == 1.0 else out * scale
 
 
+def _rfft(x, dim):
+    """Unnormalised real-to-half-spectrum DFT: native kernels when they apply."""
+    from . import fft_impl
+    out = fft_impl.rfft_native(x, dim) if x.is_cuda else None
+    return out if out is not None else torch.fft.rfft(x, dim=dim)
+
+
+def _irfft(x, n, dim):
+    """Unnormalised half-spectrum-to-real inverse DFT of length ``n``."""
+    from . import fft_impl
+    out = fft_impl.irfft_native(x, n, dim) if x.is_cuda else None
+    return out if out is not None else torch.fft.irfft(x, n=n, dim=dim, norm="forward")
+
+
 def _norm_scale(*, n, inverse, norm):
     if norm == "ortho":
         return 1.0 / math.sqrt(n)
@@ -430,11 +444,11 @@ def _run_real_plan(z, current, out_by, tmap, plan, *, inverse, norm, signal_size
     if inverse:
         z, _ = _run_items(z, current, out_by, plan, inverse=True, per_axis_norm=per_axis)
         hdim = _dim(current, half_src)
-        z = torch.fft.irfft(z, n=sizes[-1], dim=hdim, norm="forward")
+        z = _irfft(z, sizes[-1], hdim)
         current[hdim] = Axis(half_dst)
     else:
         hdim = _dim(current, half_src)
-        z = torch.fft.rfft(z, dim=hdim)
+        z = _rfft(z, hdim)
         current[hdim] = Axis(half_dst)
         z, _ = _run_items(z, current, out_by, plan, inverse=False, per_axis_norm=per_axis)
     return _normalize(z, n=total, inverse=inverse, norm=norm)

@@ -19,7 +19,7 @@ import torch
 
 from . import _native
 
-__all__ = ["supported_length", "fft_c2c", "slab_fft"]
+__all__ = ["supported_length", "fft_c2c", "slab_fft", "rfft_native", "irfft_native"]
 
 _MAX_LOG = 10
 _TWIDDLES = {}
@@ -175,3 +175,65 @@ def slab_fft(x, comm, P, rank, *, pre_dims, gather_dim, split_dim, post_dims=(),
     if torch.is_grad_enabled() and x.requires_grad:
         return _SlabFFT.apply(x, spec)
     return _slab_run(x, spec)
+
+
+# ------------------------------------------------------------------ real transforms
+
+_HALF_TW = {}
+
+
+def _half_twiddles(n, device):
+    """exp(-2 pi i k / n) for k < n/2 (float64 on the host, complex64 on device)."""
+    key = (device, n)
+    tw = _HALF_TW.get(key)
+    if tw is None:
+        k = torch.arange(n // 2, dtype=torch.float64)
+        angle = -2.0 * math.pi * k / n
+        tw = torch.complex(torch.cos(angle), torch.sin(angle)).to(torch.complex64).to(device)
+        _HALF_TW[key] = tw
+    return tw
+
+
+def _real_ok(n):
+    return n % 2 == 0 and supported_length(n // 2)
+
+
+def rfft_native(x, dim):
+    """Unnormalised real-to-half-spectrum DFT along ``dim`` (``torch.fft.rfft``
+    contract) as a complex DFT of half length: z[m] = x[2m] + i x[2m+1],
+    Z = DFT(z), then X[k] = (Z[k] + conj Z[-k]) / 2 - i w^k (Z[k] - conj Z[-k]) / 2
+    with w = exp(-2 pi i / n).  ``None`` when the native kernels do not apply."""
+    mod = _native.module()
+    dim = dim % x.dim()
+    n = x.shape[dim]
+    if mod is None or not x.is_cuda or x.dtype != torch.float32 or not _real_ok(n):
+        return None
+    xm = x.movedim(dim, -1).contiguous()
+    z = torch.view_as_complex(xm.reshape(*xm.shape[:-1], n // 2, 2))
+    Z = fft_c2c(mod, z, z.dim() - 1, False)
+    Zc = torch.conj(torch.roll(torch.flip(Z, dims=(-1,)), 1, dims=-1))  # conj Z[-k mod n/2]
+    even = (Z + Zc) * 0.5
+    odd = (Z - Zc) * (-0.5j)
+    w = _half_twiddles(n, x.device)
+    head = even + w * odd
+    nyquist = (even[..., :1] - odd[..., :1])
+    return torch.cat([head, nyquist], dim=-1).movedim(-1, dim)
+
+
+def irfft_native(X, n, dim):
+    """Unnormalised half-spectrum-to-real inverse DFT (``torch.fft.irfft(...,
+    norm="forward")`` contract) of output length ``n`` along ``dim``."""
+    mod = _native.module()
+    dim = dim % X.dim()
+    if (mod is None or not X.is_cuda or X.dtype != torch.complex64 or not _real_ok(n)
+            or X.shape[dim] != n // 2 + 1):
+        return None
+    Xm = X.movedim(dim, -1)
+    h = n // 2
+    lo = Xm[..., :h]
+    hi = torch.conj(torch.flip(Xm[..., 1:h + 1], dims=(-1,)))  # conj X[h - k]
+    even = (lo + hi) * 0.5
+    odd = (lo - hi) * 0.5 * torch.conj(_half_twiddles(n, X.device))
+    Z = (even + 1j * odd).contiguous()
+    z = fft_c2c(mod, Z, Z.dim() - 1, True, scale=2.0)
+    return torch.view_as_real(z).reshape(*z.shape[:-1], n).movedim(-1, dim)
