@@ -37,6 +37,7 @@ def main():
     p = argparse.ArgumentParser()
     p.add_argument("--impl", choices=("native", "reference"), default="native")
     p.add_argument("--n", type=int, default=1024)
+    p.add_argument("--nx", type=int, default=0, help="length of the x axis (default n); smaller for profiling")
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
     args = p.parse_args()
@@ -49,7 +50,8 @@ def main():
     from torch.distributed.device_mesh import init_device_mesh
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("sp",))
     n = args.n
-    xl = n // world
+    nx = args.nx or n
+    xl = nx // world
     shapes = {"sp": {"x": [xl] * world, "ky": [n // world] * world, "y": [n // world] * world,
                      "kx": [xl] * world}}
     gen = torch.Generator(device="cuda").manual_seed(0)
@@ -108,7 +110,7 @@ def main():
     if rank == 0:
         print(json.dumps({"metric": "dist-FFT ms (forward + inverse)", "value": round(ms, 3), "unit": "ms",
                           "higher_is_better": False, "n_gpus": world, "impl": args.impl,
-                          "config": {"shape": [1, n, n, n], "dtype": "complex64", "layout": "b x/sp y z <-> b kx ky/sp kz",
+                          "config": {"shape": [1, nx, n, n], "dtype": "complex64", "layout": "b x/sp y z <-> b kx ky/sp kz",
                                      "l2": "inputs larger than L2; no flush"},
                           "roundtrip_rel_err": err, "roofline_ms": round(roofline_ms, 3),
                           "roofline_frac": round(roofline_ms / ms, 3),

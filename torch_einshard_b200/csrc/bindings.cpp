@@ -25,6 +25,7 @@ int g_pair_mode = -1;
 int g_group_m = 0;  // raster group override (0: kernel default)
 int g_split = 0;    // wide-kernel cluster split mode (tuning)
 int g_sleep_ns = 0;  // wide-kernel epilogue back-off (tuning)
+int g_small_persistent = 1;  // 1-SM GEMM and conv grids (tuning)
 int g_persistent = 0;  // wide-kernel grid: 0 one pair tile per cluster (default, measured faster under the power cap), 1 persistent
 unsigned long long* g_prof = nullptr;  // wide-kernel wait counters (tuning), device pointer or null
 
@@ -103,6 +104,7 @@ es::GemmArgs gemm_operand_args(const at::Tensor& a, const at::Tensor& b, int64_t
   g.prof = g_prof;
   g.sleep_ns = g_sleep_ns;
   g.persistent = g_persistent;
+  g.small_persistent = g_small_persistent;
   return g;
 }
 
@@ -537,6 +539,7 @@ void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
   }
   a.err = err.data_ptr<int>();
   a.num_sms = num_sms(x.get_device());
+  a.persistent = g_small_persistent;
   const char* why = es::check_conv_args(a);
   TORCH_CHECK(why == nullptr, "einshard conv: ", why ? why : "");
   const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
@@ -615,6 +618,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         g_prof = t.numel() >= 3 ? reinterpret_cast<unsigned long long*>(t.data_ptr()) : nullptr;
       }, "int64 CUDA tensor of >= 3 wait-cycle counters for the wide GEMM (empty tensor: off)");
   m.def("set_gemm_persistent", [](int64_t v) { g_persistent = static_cast<int>(v); }, "wide kernel: 1 persistent, 0 one tile per cluster");
+  m.def("set_small_persistent", [](int64_t v) { g_small_persistent = static_cast<int>(v); },
+        "1-SM GEMM and conv: 1 persistent CTAs, 0 one tile per CTA");
   m.def("set_gemm_sleep_ns", [](int64_t v) { g_sleep_ns = static_cast<int>(v); }, "wide-kernel epilogue back-off ns");
   m.def("set_tma_l2_promotion", [](int64_t v) { es::tma_l2_promotion() = static_cast<int>(v); },
         "L2 promotion of TMA loads: 0 none, 1 64B, 2 128B, 3 256B (tuning)");

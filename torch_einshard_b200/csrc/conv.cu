@@ -58,7 +58,7 @@ struct ConvStoreEpilogue {
   int O, Wout, Wv;
   int tma;            // 1: TMA stores of [64 pixels x 32 channels] boxes through the warp's staging buffer
 
-  __device__ __forceinline__ void setup(SharedState*, const GemmShape&) {}
+  __device__ __forceinline__ void setup(int*, const GemmShape&) {}
   __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
 
   // Channels are on TMEM lanes, pixels on columns: each thread holds one channel
@@ -185,8 +185,8 @@ int launch(const ConvArgs& a, cudaStream_t stream) {
     attr_set |= 1ull << dev;
   }
   const long long tiles = static_cast<long long>(s.num_m) * s.num_n;
-  const int grid = tiles < a.num_sms ? static_cast<int>(tiles) : a.num_sms;
-  kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, s, epi, loads);
+  const long long grid = (tiles < a.num_sms || a.persistent == 0) ? tiles : a.num_sms;
+  kernel<<<static_cast<unsigned>(grid), kThreads, kSmemBytes, stream>>>(ma, mb, mc, s, epi, loads);
   return static_cast<int>(cudaGetLastError());
 }
 

@@ -17,6 +17,7 @@ struct ConvArgs {
   int ph = 0, pw = 0;          // zero padding on each side
   int* err = nullptr;
   int num_sms = 148;
+  int persistent = 1;          // 1 persistent CTAs (default), 0 one tile per CTA (tuning)
 };
 
 const char* check_conv_args(const ConvArgs& a);

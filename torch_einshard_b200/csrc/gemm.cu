@@ -214,7 +214,7 @@ static int launch_store(const GemmArgs& g0, cudaStream_t stream) {
     attr_set |= 1ull << dev;
   }
   const int tiles = s.num_m * s.num_n * s.batch;
-  const int grid = tiles < g.num_sms ? tiles : g.num_sms;
+  const int grid = (tiles < g.num_sms || g.small_persistent == 0) ? tiles : g.num_sms;
   CUtensorMap mc;
   epi.tma = make_output_map(g, trans, &mc) ? 1 : 0;
   kernel<<<grid, kThreads, kSmemBytes, stream>>>(ma, mb, mc, s, epi, GemmLoads{});

@@ -36,6 +36,7 @@ struct GemmArgs {
   unsigned long long* prof = nullptr;  // optional wait-cycle counters (wide kernel)
   int sleep_ns = 0;  // wide kernel epilogue back-off (tuning)
   int persistent = 0;  // wide kernel: 0 one pair tile per cluster (default), 1 persistent clusters
+  int small_persistent = 1;  // 1-SM kernel: 1 persistent CTAs (default), 0 one tile per CTA (tuning)
 };
 
 const char* check_gemm_args(const GemmArgs& g);
@@ -44,6 +45,7 @@ bool use_pair_kernel(const GemmArgs& g);
 int gemm_launch(const GemmArgs& g, cudaStream_t stream);
 struct GemmShape;
 GemmShape make_shape(const GemmArgs& g);
+GemmShape make_shape_pair(const GemmArgs& g);
 // Output tensor map of the TMA-store epilogues; false (map zeroed) when C does not qualify.
 bool make_output_map(const GemmArgs& g, bool trans, CUtensorMap* mc);
 

@@ -67,8 +67,8 @@ struct ArEpilogue {
     return reinterpret_cast<uint8_t*>(c.data[rank]) + static_cast<size_t>(t) * kTileBytes;
   }
 
-  __device__ void setup(SharedState* st, const GemmShape&) {
-    sm = st->epi;
+  __device__ void setup(int* scratch, const GemmShape&) {
+    sm = scratch;
     // peers must be done reading our buffer from the previous operation
     if (threadIdx.x == 64) {
       for (int p = 0; p < c.size; ++p) {

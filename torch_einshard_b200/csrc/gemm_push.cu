@@ -1,10 +1,11 @@
-// GEMM fused with an all-reduce of its output, push model, on the wide 2-SM
-// tcgen05 kernel.
+// GEMM fused with an all-reduce of its output, push model, on the 2-SM
+// (256 x 256 pair tile) tcgen05 kernel with its double-buffered accumulators,
+// so a tile's NVLink pushes overlap the next tile's MMAs.
 //
 //   C = sum over ranks of (A_r @ B_r)        every rank gets the full C
 //
-// Sub-tile t (128 rows x 256 columns, one 4-warp epilogue group of a CTA) is
-// owned by rank t % P.  In the epilogue:
+// Sub-tile t (128 rows x 256 columns: one CTA's half of a pair tile, handled by
+// a 4-warp epilogue group) is owned by rank t % P.  In the epilogue:
 //   * a non-owner converts its fp32 accumulator to bf16 and STORES it straight
 //     into its slot of the owner's symmetric region (NVLink writes do not wait
 //     for a round trip), then releases a flag in the owner's flag region;
@@ -23,7 +24,7 @@
 #include "comm.h"
 #include "gemm.h"
 #include "gemm_ar.h"
-#include "gemm_tc3.cuh"
+#include "gemm_tc2.cuh"
 #include "tma_desc.h"
 
 namespace es {
@@ -51,6 +52,7 @@ struct PushArEpilogue {
   int vec_ok;
   int n256;             // sub-tiles per row of sub-tiles
   long long red_base;   // byte offset of the reduced slots in a data region
+  int groups;           // 4-warp epilogue groups per CTA (1: 2-SM kernel, 2: wide kernel)
   int* sm;
 
   __device__ __forceinline__ int* flag(int rank, int slot) const { return reinterpret_cast<int*>(c.flags[rank]) + slot; }
@@ -69,8 +71,8 @@ struct PushArEpilogue {
 
   // every rank must have finished the previous op (reading its region) before
   // anyone writes into it: all threads wait for the check
-  __device__ void setup(SharedState* st, const GemmShape&) {
-    sm = st->epi;
+  __device__ void setup(int* scratch, const GemmShape&) {
+    sm = scratch;
     if (threadIdx.x == 0) {
       int ok = 1;
       for (int p = 0; p < c.size && ok; ++p) {
@@ -272,9 +274,13 @@ struct PushArEpilogue {
       }
     }
     if (!ok) q[kPAbort] = 1;
-    epi_all_bar();  // both groups of this CTA are done
+    if (groups == 2) {
+      epi_all_bar();  // both groups of this CTA are done
+    } else {
+      group_bar(0);
+    }
     if (threadIdx.x == 64) {
-      const bool all_ok = !sm[kPAbort] && !sm[16 + kPAbort] && !*abort_flag;
+      const bool all_ok = !sm[kPAbort] && (groups == 1 || !sm[16 + kPAbort]) && !*abort_flag;
       fence_acq_rel_sys();
       const int prev = atomicAdd(flag(c.rank, kFlagArrive), 1);
       if (static_cast<uint32_t>(prev + 1) - c.arrive_base == gridDim.x && all_ok) {
@@ -294,7 +300,7 @@ long long gemm_push_region_bytes(const GemmArgs& g, int size) {
 }
 
 int gemm_push_grid(const GemmArgs& g) {
-  const long long pair_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 511) / 512);
+  const long long pair_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 255) / 256);
   const int clusters = pair_tiles < g.num_sms / 2 ? static_cast<int>(pair_tiles) : g.num_sms / 2;
   return 2 * clusters;
 }
@@ -304,14 +310,9 @@ int gemm_push_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStrea
   if (g.out_dtype != kDtypeBF16 || g.batch != 1) return -2;
   const long long tiles = static_cast<long long>((g.M + kBM - 1) / kBM) * ((g.N + kBN - 1) / kBN);
   if (tiles + comm.size > kMaxTiles) return -3;  // partial-slot flags stay below the reduced-tile flags
-  CUtensorMap ma, mb, mc;
+  CUtensorMap ma, mb;
   make_operand_maps(g, &ma, &mb, true);
-  memset(&mc, 0, sizeof(mc));
-  GemmShape s = make_shape(g);
-  s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
-  s.num_n = (g.N + kBN3 - 1) / kBN3;
-  s.group_m = g.group_m > 0 ? g.group_m : 16;
-  s.pair = 1;
+  GemmShape s = make_shape_pair(g);
   s.split = 0;
   PushArEpilogue epi;
   epi.c = comm;
@@ -321,19 +322,21 @@ int gemm_push_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStrea
   epi.n256 = (g.N + kBN - 1) / kBN;
   const long long owned = (tiles + comm.size - 1) / comm.size;
   epi.red_base = owned * (comm.size - 1) * kSubBytes;
+  epi.groups = 1;
   epi.sm = nullptr;
-  auto kernel = gemm_tc3_kernel<PushArEpilogue>;
+  auto kernel = gemm_tc2_kernel<PushArEpilogue>;
   static unsigned long long attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!(attr_set >> dev & 1ull)) {
-    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3Bytes);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem2Bytes);
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
     attr_set |= 1ull << dev;
   }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(gemm_push_grid(g));
-  cfg.blockDim = dim3(kThreads3);
-  cfg.dynamicSmemBytes = kSmem3Bytes;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmem2Bytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -342,7 +345,7 @@ int gemm_push_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStrea
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, s, epi, NoGather{}));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, s, epi));
 }
 
 }  // namespace es

@@ -169,7 +169,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = st->tmem_base;
   volatile int* abort_flag = &st->abort_flag;
-  epi.setup(st, shp);
+  epi.setup(st->epi, shp);  // the policy's scratch words in shared memory
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -349,7 +349,7 @@ struct StoreEpilogue {
   int trans;  // 1: the kernel computes C^T (operands swapped); tile rows are columns of C
   int tma;    // 1: 16-bit output written by TMA stores through the warp's staging buffer
 
-  __device__ __forceinline__ void setup(SharedState*, const GemmShape&) {}
+  __device__ __forceinline__ void setup(int*, const GemmShape&) {}
   __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
 
   // 32 rows x 256 columns of this warp, as four 32 x 64 boxes: TMEM -> registers

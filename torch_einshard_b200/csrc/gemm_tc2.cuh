@@ -49,8 +49,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages2 * kA2Bytes;
   SharedState2* st = reinterpret_cast<SharedState2*>(smem + kStages2 * kStage2Bytes);
-  // the epilogue policies only touch the common fields through this alias
-  SharedState* st_common = reinterpret_cast<SharedState*>(st);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -88,7 +86,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = st->tmem_base;
   volatile int* abort_flag = &st->abort_flag;
-  epi.setup(st_common, shp);
+  epi.setup(st->epi, shp);
 
   const uint32_t full_leader0 = map_to_cta(&st->full[0], 0);
   const uint32_t tempty_leader0 = map_to_cta(&st->tempty[0], 0);

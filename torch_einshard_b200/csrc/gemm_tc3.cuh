@@ -33,8 +33,8 @@ constexpr int kEpiWarps3 = 8;
 constexpr int kStage3Out = 4096;                    // per epilogue warp: 32 rows x 64 cols x 2 B
 constexpr int kSmem3Bytes = kStages3 * kStage3Bytes + 1024 + kEpiWarps3 * kStage3Out + 1024;
 
-// Same layout as SharedState (gemm_tc.cuh) so that epilogue policies can use
-// its fields through that type; only tfull[0] / tempty[0] are used here.
+// Pipeline barriers of the wide kernel (only tfull_[0] / tempty_[0] are used:
+// one accumulator) and the epilogue policy's scratch words.
 struct SharedState3 {
   uint64_t full[kStages3];
   uint64_t empty[kStages3];
@@ -112,7 +112,6 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
   uint8_t* sB = smem + kStages3 * kA3Bytes;
   SharedState3* st = reinterpret_cast<SharedState3*>(smem + kStages3 * kStage3Bytes);
   uint8_t* out_stage = smem + kStages3 * kStage3Bytes + 1024;  // 1024-byte aligned (TMA swizzle atom)
-  SharedState* st_common = reinterpret_cast<SharedState*>(st);  // epilogue policies use only common fields
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -147,7 +146,7 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
   tc_fence_after();
   const uint32_t tmem_base = st->tmem_base;
   volatile int* abort_flag = &st->abort_flag;
-  epi.setup(st_common, shp);
+  epi.setup(st->epi, shp);
 
   const uint32_t full_leader0 = map_to_cta(&st->full[0], 0);
   const uint32_t tempty_leader = map_to_cta(&st->tempty_[0], 0);
