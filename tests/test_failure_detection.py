@@ -58,9 +58,12 @@ def _skip_one_allreduce(rank, world):
     comm.check_health()
     assert torch.all(x == world)
     os.environ["EINSHARD_FAULT_INJECT"] = "skip:1:2"
+    previous = _native.wait_timeout_us()
+    _native.set_wait_timeout_us(300_000)  # the peer wait gives up after 0.3 s
     y = torch.ones(1024, device="cuda")
     comm.all_reduce_(y)                  # call 2: rank 1 launches nothing
     os.environ.pop("EINSHARD_FAULT_INJECT")
+    _native.set_wait_timeout_us(previous)
     if rank == 0:
         with pytest.raises(_native.EinshardCommTimeout):
             comm.check_health()

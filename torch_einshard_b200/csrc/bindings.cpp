@@ -26,6 +26,7 @@ int g_group_m = 0;  // raster group override (0: kernel default)
 int g_split = 0;    // wide-kernel cluster split mode (tuning)
 int g_sleep_ns = 0;  // wide-kernel epilogue back-off (tuning)
 int g_small_persistent = 1;  // 1-SM GEMM and conv grids (tuning)
+uint64_t g_wait_timeout_ns = 4000000000ull;  // bound of device waits on peers (EINSHARD_WAIT_TIMEOUT_US)
 int g_persistent = 0;  // wide-kernel grid: 0 one pair tile per cluster (default, measured faster under the power cap), 1 persistent
 unsigned long long* g_prof = nullptr;  // wide-kernel wait counters (tuning), device pointer or null
 
@@ -208,6 +209,7 @@ es::CommDev make_dev(HostComm& hc, const at::Tensor& err, int nblocks, int nbarr
   d.bar_base = hc.bar;
   d.arrive_base = 0;
   d.err = err.data_ptr<int>();
+  d.timeout_ns = g_wait_timeout_ns;
   hc.bar += static_cast<uint32_t>(nblocks * nbarriers);
   return d;
 }
@@ -447,6 +449,7 @@ es::CommDev peek_dev(HostComm& hc, const at::Tensor& err) {
   d.bar_base = hc.bar;
   d.arrive_base = hc.arrive;
   d.err = err.data_ptr<int>();
+  d.timeout_ns = g_wait_timeout_ns;
   return d;
 }
 
@@ -620,6 +623,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_gemm_persistent", [](int64_t v) { g_persistent = static_cast<int>(v); }, "wide kernel: 1 persistent, 0 one tile per cluster");
   m.def("set_small_persistent", [](int64_t v) { g_small_persistent = static_cast<int>(v); },
         "1-SM GEMM and conv: 1 persistent CTAs, 0 one tile per CTA");
+  m.def("set_wait_timeout_ns", [](int64_t v) { g_wait_timeout_ns = static_cast<uint64_t>(v > 0 ? v : 1); },
+        "bound (ns) of every device-side wait on a peer rank");
+  m.def("get_wait_timeout_ns", []() { return static_cast<int64_t>(g_wait_timeout_ns); });
   m.def("set_gemm_sleep_ns", [](int64_t v) { g_sleep_ns = static_cast<int>(v); }, "wide-kernel epilogue back-off ns");
   m.def("set_tma_l2_promotion", [](int64_t v) { es::tma_l2_promotion() = static_cast<int>(v); },
         "L2 promotion of TMA loads: 0 none, 1 64B, 2 128B, 3 256B (tuning)");

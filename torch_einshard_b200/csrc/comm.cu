@@ -65,7 +65,7 @@ __device__ bool grid_barrier(const CommDev& c, uint32_t target) {
     atomicAdd(ctr, 1u);
     const uint64_t t0 = global_timer_ns();
     while (static_cast<int>(ld_acquire_gpu_u32(ctr) - target) < 0) {
-      if (global_timer_ns() - t0 > ES_WAIT_TIMEOUT_NS) {
+      if (global_timer_ns() - t0 > c.timeout_ns) {
         atomicCAS(c.err, 0, kErrWaitPeerFlag);
         ok = false;
         break;
@@ -81,7 +81,7 @@ __device__ bool wait_peers(const CommDev& c, int slot, int target) {
   if (threadIdx.x == 0) {
     for (int p = 0; p < c.size && ok; ++p) {
       if (p == c.rank) continue;
-      ok = wait_flag_geq(flag_at(c, p, slot), target, c.err, kErrWaitPeerFlag);
+      ok = wait_flag_geq_for(flag_at(c, p, slot), target, c.err, kErrWaitPeerFlag, c.timeout_ns);
     }
   }
   return __syncthreads_and(ok) != 0;

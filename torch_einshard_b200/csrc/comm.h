@@ -37,6 +37,7 @@ struct CommDev {
   uint32_t bar_base;          // value of the local barrier counter at kernel start
   uint32_t arrive_base;       // value of the local completion counter at kernel start
   int* err;
+  uint64_t timeout_ns;        // bound of every wait on a peer (EINSHARD_WAIT_TIMEOUT_US)
 };
 
 // A strided box copy (or reduction) in bytes: dims[0..3] sizes (innermost last),

@@ -138,6 +138,7 @@ struct SlabSync {
   int* peer_flags[kMaxRanks];
   int* local_flags;  // this rank's flag block (arrive counter, done flag)
   int* err;
+  uint64_t timeout_ns;
 };
 
 template <int LOG1, int LOG2, bool INV, class Loader>
@@ -170,7 +171,7 @@ __global__ void __launch_bounds__(kFftThreads) fft2_kernel(Loader ld, float2* __
 #pragma unroll
       for (int p = 0; p < kMaxRanks; ++p)
         if (p < sync.size && ok)
-          ok = wait_flag_geq(sync.peer_flags[p] + kFlagStaged, sync.epoch, sync.err, kErrWaitPeerFlag) ? 1 : 0;
+          ok = wait_flag_geq_for(sync.peer_flags[p] + kFlagStaged, sync.epoch, sync.err, kErrWaitPeerFlag, sync.timeout_ns) ? 1 : 0;
     }
     s_ok = ok;
   }
@@ -453,7 +454,7 @@ __global__ void wait_peers_kernel(const CommDev c, int slot, int target) {
   if (threadIdx.x != 0) return;
   for (int p = 0; p < c.size; ++p) {
     if (p == c.rank) continue;
-    if (!wait_flag_geq(reinterpret_cast<int*>(c.flags[p]) + slot, target, c.err, kErrWaitPeerFlag)) return;
+    if (!wait_flag_geq_for(reinterpret_cast<int*>(c.flags[p]) + slot, target, c.err, kErrWaitPeerFlag, c.timeout_ns)) return;
   }
 }
 
@@ -486,6 +487,7 @@ int fft_slab(const CommDev& c, const FftSlab& f, cudaStream_t stream) {
   sync.epoch = c.epoch;
   sync.arrive_base = c.arrive_base;
   sync.err = c.err;
+  sync.timeout_ns = c.timeout_ns;
   for (int p = 0; p < c.size; ++p) sync.peer_flags[p] = reinterpret_cast<int*>(c.flags[p]);
   sync.local_flags = reinterpret_cast<int*>(c.flags[c.rank]);
   long long lines, inner, os, ps, is;

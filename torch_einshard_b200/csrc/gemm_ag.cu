@@ -57,7 +57,7 @@ struct AgGather {
   __device__ __forceinline__ bool wait_rows(int m0, volatile int* abort_flag) const {
     int ok = 1;
     if ((threadIdx.x & 31) == 0) {
-      ok = wait_flag_geq(flag(c.rank, kFlagAg0 + (m0 >> 7)), c.epoch, c.err, kErrWaitPeerFlag) ? 1 : 0;
+      ok = wait_flag_geq_for(flag(c.rank, kFlagAg0 + (m0 >> 7)), c.epoch, c.err, kErrWaitPeerFlag, c.timeout_ns) ? 1 : 0;
       fence_proxy_async_global();  // the TMA (async proxy) reads rows written by the copy warps
       if (!ok) *abort_flag = 1;
     }
@@ -83,7 +83,7 @@ struct AgGather {
       const int q = (c.rank + o) % c.size;
       if (!(staged_peers >> q & 1u)) {
         int ok = 1;
-        if (lane == 0) ok = wait_flag_geq(flag(q, kFlagStaged), c.epoch, c.err, kErrWaitPeerFlag) ? 1 : 0;
+        if (lane == 0) ok = wait_flag_geq_for(flag(q, kFlagStaged), c.epoch, c.err, kErrWaitPeerFlag, c.timeout_ns) ? 1 : 0;
         if (!__shfl_sync(0xffffffffu, ok, 0)) {
           *abort_flag = 1;
           return;

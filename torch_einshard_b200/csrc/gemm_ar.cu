@@ -73,7 +73,7 @@ struct ArEpilogue {
     if (threadIdx.x == 64) {
       for (int p = 0; p < c.size; ++p) {
         if (p == c.rank) continue;
-        if (!wait_flag_geq(flag(p, kFlagDone), c.epoch - 1, c.err, kErrWaitPeerFlag)) {
+        if (!wait_flag_geq_for(flag(p, kFlagDone), c.epoch - 1, c.err, kErrWaitPeerFlag, c.timeout_ns)) {
           sm[kAbortEpi] = 1;
           break;
         }
@@ -123,7 +123,7 @@ struct ArEpilogue {
           const int* f = flag(t % c.size, kFlagTile0 + kMaxTiles + t);
           bool ready = ld_acquire_sys(f) >= c.epoch;
           if (!ready && blocking) {
-            ready = wait_flag_geq(f, c.epoch, c.err, kErrWaitPeerFlag);
+            ready = wait_flag_geq_for(f, c.epoch, c.err, kErrWaitPeerFlag, c.timeout_ns);
             if (!ready) sm[kAbortEpi] = 1;
           }
           if (ready) decision = t;
@@ -181,7 +181,7 @@ struct ArEpilogue {
     if (e == 0) {
       for (int p = 0; p < c.size; ++p) {
         if (p == c.rank) continue;
-        if (!wait_flag_geq(flag(p, kFlagTile0 + t), c.epoch, c.err, kErrWaitPeerFlag)) {
+        if (!wait_flag_geq_for(flag(p, kFlagTile0 + t), c.epoch, c.err, kErrWaitPeerFlag, c.timeout_ns)) {
           sm[kAbortEpi] = 1;
           *abort_flag = 1;
           break;

@@ -77,7 +77,7 @@ struct PushArEpilogue {
       int ok = 1;
       for (int p = 0; p < c.size && ok; ++p) {
         if (p == c.rank) continue;
-        ok = wait_flag_geq(flag(p, kFlagDone), c.epoch - 1, c.err, kErrWaitPeerFlag) ? 1 : 0;
+        ok = wait_flag_geq_for(flag(p, kFlagDone), c.epoch - 1, c.err, kErrWaitPeerFlag, c.timeout_ns) ? 1 : 0;
       }
       if (!ok) sm[kPAbort] = sm[16 + kPAbort] = 1;
     }
@@ -118,7 +118,7 @@ struct PushArEpilogue {
           const int* f = flag(c.rank, rf_flag(t));
           bool ready = ld_acquire_sys(f) >= c.epoch;
           if (!ready && blocking) {
-            ready = wait_flag_geq(f, c.epoch, c.err, kErrWaitPeerFlag);
+            ready = wait_flag_geq_for(f, c.epoch, c.err, kErrWaitPeerFlag, c.timeout_ns);
             if (!ready) q[kPAbort] = 1;
           }
           if (ready) decision = t;
@@ -181,7 +181,7 @@ struct PushArEpilogue {
     if (e == 0) {
       for (int p = 0; p < c.size; ++p) {
         if (p == c.rank) continue;
-        if (!wait_flag_geq(flag(c.rank, pf_flag(part_slot(t, p, owner))), c.epoch, c.err, kErrWaitPeerFlag)) {
+        if (!wait_flag_geq_for(flag(c.rank, pf_flag(part_slot(t, p, owner))), c.epoch, c.err, kErrWaitPeerFlag, c.timeout_ns)) {
           q[kPAbort] = 1;
           *abort_flag = 1;
           break;

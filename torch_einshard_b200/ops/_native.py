@@ -5,13 +5,18 @@ The extension is built in place (``python setup.py build_ext --inplace`` or
 broken extension is an error as soon as a native op is requested (set
 ``EINSHARD_ALLOW_TORCH_FALLBACK=1`` to run the torch reference path instead);
 on CPU-only machines the torch path is used silently.
+
+``EINSHARD_WAIT_TIMEOUT_US`` (default 4 s) bounds every device-side wait on a
+peer rank (flag spins of the fused and collective kernels); a wait that runs
+out records its code in the error word and the kernel returns.
 """
 
 import os
 
 import torch
 
-__all__ = ["module", "available", "require", "error_word", "check_errors", "reset_errors", "EinshardCommTimeout"]
+__all__ = ["module", "available", "require", "error_word", "check_errors", "reset_errors", "EinshardCommTimeout",
+           "set_wait_timeout_us", "wait_timeout_us"]
 
 _state = {"loaded": False, "module": None, "error": None}
 _ERROR_WORDS = {}
@@ -23,6 +28,9 @@ def module():
         try:
             from .. import _C  # noqa: F401
             _state["module"] = _C
+            env = os.environ.get("EINSHARD_WAIT_TIMEOUT_US")
+            if env:
+                _C.set_wait_timeout_ns(int(float(env) * 1000))
         except Exception as error:  # noqa: BLE001 - reported through require()
             _state["error"] = error
     return _state["module"]
@@ -44,6 +52,16 @@ def require():
             f"({_state['error']!r}); run `python setup.py build_ext --inplace`"
         )
     return mod
+
+
+def set_wait_timeout_us(us):
+    """Bound (microseconds) of device-side waits on peer ranks for kernels
+    launched from now on."""
+    require().set_wait_timeout_ns(max(1, int(us * 1000)))
+
+
+def wait_timeout_us():
+    return require().get_wait_timeout_ns() / 1000.0
 
 
 def error_word(device) -> torch.Tensor:
