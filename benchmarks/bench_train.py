@@ -124,6 +124,9 @@ def main():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--small", action="store_true", help="reduced model for smoke runs (not a bench number)")
     p.add_argument("--checkpoint", choices=("auto", "on", "off"), default="auto")
+    p.add_argument("--kernel-table", type=int, default=0, metavar="N",
+                   help="after the timed steps, run one more step under torch.profiler and print the N kernels "
+                        "with the most device time to stderr (a breakdown, not a bench number)")
     args = p.parse_args()
     if "RANK" not in os.environ:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT="29651", RANK="0", WORLD_SIZE="1", LOCAL_RANK="0")
@@ -189,6 +192,16 @@ def main():
     ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device="cuda", dtype=torch.float64)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = ms.item()
+    if args.kernel_table and rank == 0:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+        print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=args.kernel_table, max_name_column_width=90),
+              file=sys.stderr, flush=True)
+    elif args.kernel_table:
+        step()
+        torch.cuda.synchronize()
     global_tokens = dp * cfg.batch * cfg.seq
     tok_s = global_tokens / (ms / 1e3)
     if rank == 0:

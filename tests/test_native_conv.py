@@ -109,3 +109,25 @@ def test_einconv_pads_in_kernel_without_copy(monkeypatch):
     y = es.einconv("b h w c, kh kw c o -> b h w o", x, w, {"h": "kh", "w": "kw"}, checkpoint=None)
     _close(y, _ref(x, w.permute(3, 0, 1, 2), None, pad=1))
     assert calls == []
+
+
+@pytest.mark.parametrize("B,H,W,C,O,KH,KW,ph,pw", [
+    (2, 12, 33, 64, 128, 3, 3, 0, 0),     # one partial column block per row
+    (1, 9, 130, 128, 64, 3, 3, 1, 1),     # O < one M tile, three column blocks, padding
+    (3, 5, 64, 64, 192, 1, 3, 0, 1),      # two M tiles, 1 x 3 kernel, exact column blocks
+    (2, 7, 20, 192, 64, 5, 5, 2, 2),      # N = 25 * 192 spans many N tiles
+])
+def test_conv_weight_gradient_native(B, H, W, C, O, KH, KW, ph, pw):
+    torch.manual_seed(2)
+    mod = _native.require()
+    x = torch.randn(B, H, W, C, device="cuda", dtype=torch.bfloat16)
+    Ho, Wo = H + 2 * ph - KH + 1, W + 2 * pw - KW + 1
+    dy = torch.randn(B, Ho, Wo, O, device="cuda", dtype=torch.bfloat16)
+    dw = torch.empty(O, KH, KW, C, device="cuda", dtype=torch.float32)
+    mod.conv2d_wgrad(x, dy, dw, ph, pw, _native.error_word(x.device))
+    torch.cuda.synchronize()
+    _native.check_errors()
+    ref = torch.nn.grad.conv2d_weight(x.float().permute(0, 3, 1, 2), (O, C, KH, KW), dy.float().permute(0, 3, 1, 2),
+                                      padding=(ph, pw)).permute(0, 2, 3, 1)
+    scale = ref.abs().max().item()
+    assert (dw - ref).abs().max().item() <= 1e-4 * scale + 1e-3, (dw - ref).abs().max().item()

@@ -591,6 +591,46 @@ int64_t comm_data_bytes(int64_t id) { return static_cast<int64_t>(comm_ref(id).d
 
 }  // namespace
 
+// dw (fp32 [O][KH][KW][C], zeroed here) = weight gradient of the implicit-GEMM
+// conv with input x [B][Hin][Win][C], output gradient dy [B][Hout][Wout][O].
+void conv2d_wgrad(const at::Tensor& x, const at::Tensor& dy, at::Tensor dw, int64_t ph, int64_t pw,
+                  const at::Tensor& err) {
+  TORCH_CHECK(x.is_cuda() && dy.is_cuda() && dw.is_cuda() && x.dim() == 4 && dy.dim() == 4 && dw.dim() == 4,
+              "einshard conv wgrad: 4-D CUDA tensors required");
+  TORCH_CHECK(x.is_contiguous() && dy.is_contiguous() && dw.is_contiguous(), "einshard conv wgrad: contiguous required");
+  TORCH_CHECK(x.scalar_type() == dy.scalar_type() && (x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kHalf),
+              "einshard conv wgrad: bf16/fp16 x and dy of one dtype required");
+  TORCH_CHECK(dw.scalar_type() == at::kFloat, "einshard conv wgrad: fp32 dw required");
+  es::ConvWgradArgs a;
+  a.x = x.data_ptr();
+  a.dy = dy.data_ptr();
+  a.dw = dw.data_ptr<float>();
+  a.dtype = dtype_code(x.scalar_type());
+  a.B = x.size(0);
+  a.Hin = x.size(1);
+  a.Win = x.size(2);
+  a.C = x.size(3);
+  a.O = dw.size(0);
+  a.KH = dw.size(1);
+  a.KW = dw.size(2);
+  a.ph = static_cast<int>(ph);
+  a.pw = static_cast<int>(pw);
+  a.err = err.data_ptr<int>();
+  a.num_sms = num_sms(x.get_device());
+  TORCH_CHECK(dw.size(3) == a.C, "einshard conv wgrad: channel mismatch");
+  const char* why = es::check_conv_wgrad_args(a);
+  TORCH_CHECK(why == nullptr, "einshard conv wgrad: ", why ? why : "");
+  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
+  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  TORCH_CHECK(dy.size(0) == a.B && dy.size(1) == Hout && dy.size(2) == Wout && dy.size(3) == a.O,
+              "einshard conv wgrad: output-gradient shape");
+  const c10::cuda::CUDAGuard guard(x.device());
+  dw.zero_();
+  const int rc = es::conv_wgrad_launch(a, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard conv wgrad: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "einshard sm_100a native kernels";
   m.def("gemm", &gemm, "C = act(A @ B), tcgen05 GEMM (A [B,M,K], B [B,K,N])");
@@ -601,6 +641,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_all_reduce", &comm_all_reduce, "two-shot NVLink all-reduce in place");
   m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)");
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
+  m.def("conv2d_wgrad", &conv2d_wgrad, "weight gradient of the implicit-GEMM conv (split-K tcgen05, fp32 out)");
   m.def("conv2d_implicit", &conv2d_implicit, "implicit-GEMM NHWC conv2d on tcgen05 (stride 1)");
   m.def("wait_probe", &wait_probe, "bounded wait on a flag (tests the timeout path)");
   m.def("strided_copy", &strided_copy, "materialise a strided view contiguously");

@@ -23,4 +23,20 @@ struct ConvArgs {
 const char* check_conv_args(const ConvArgs& a);
 int conv_launch(const ConvArgs& a, cudaStream_t stream);
 
+// Weight gradient of conv_launch's convolution: dw[o][kh][kw][c] (fp32, must be
+// zero on entry) += sum over output pixels of dy[b][h][w][o] * x[b][h+kh-ph][w+kw-pw][c].
+struct ConvWgradArgs {
+  const void* x = nullptr;     // [B][Hin][Win][C]
+  const void* dy = nullptr;    // [B][Hout][Wout][O]
+  float* dw = nullptr;         // [O][KH][KW][C] fp32
+  int dtype = kDtypeBF16;      // x and dy share it
+  int B = 0, Hin = 0, Win = 0, C = 0, O = 0, KH = 0, KW = 0;
+  int ph = 0, pw = 0;
+  int* err = nullptr;
+  int num_sms = 148;
+};
+
+const char* check_conv_wgrad_args(const ConvWgradArgs& a);
+int conv_wgrad_launch(const ConvWgradArgs& a, cudaStream_t stream);
+
 }  // namespace es

@@ -7,8 +7,11 @@ windows straight from the NHWC tensor with shifted TMA boxes (no im2col).
 
 Backward: the input gradient runs on the same kernel as a full correlation of
 dY with the flipped, channel-transposed weights (zero padding KH-1, KW-1 done
-by the TMA zero fill); the weight gradient uses
-``torch.nn.grad.conv2d_weight`` and the bias gradient a reduction.
+by the TMA zero fill); the weight gradient runs on the split-K implicit-GEMM
+kernel (``_C.conv2d_wgrad``: dY and the shifted input windows as MN-major
+operands, fp32 partial tiles added atomically) when both channel counts are
+multiples of 64, else ``torch.nn.grad.conv2d_weight``; the bias gradient is a
+reduction.
 """
 
 import torch
@@ -51,7 +54,11 @@ class _Conv2dNHWC(torch.autograd.Function):
             else:
                 gx = torch.nn.grad.conv2d_input(x.permute(0, 3, 1, 2).shape, w.permute(0, 3, 1, 2),
                                                 grad.permute(0, 3, 1, 2), padding=(ph, pw)).permute(0, 2, 3, 1)
-        if ctx.needs_input_grad[1]:
+        if ctx.needs_input_grad[1] and O % 64 == 0:
+            dw = torch.empty(O, KH, KW, C, dtype=torch.float32, device=x.device)
+            _native.require().conv2d_wgrad(x, grad, dw, ph, pw, _native.error_word(x.device))
+            gw = dw.to(w.dtype)
+        elif ctx.needs_input_grad[1]:
             gw = torch.nn.grad.conv2d_weight(x.permute(0, 3, 1, 2), w.permute(0, 3, 1, 2).shape,
                                              grad.permute(0, 3, 1, 2), padding=(ph, pw)).permute(0, 2, 3, 1)
         if ctx.has_bias and ctx.needs_input_grad[2]:
