@@ -8,6 +8,9 @@ TP-MLP config produces all four: forward NT (both K-major), backward dX NN
 Two modes:
   burst      CUDA events per iteration (inputs larger than L2 at the default
              sizes, so no flush is needed)
+Kernels: cublas, 1sm, 2sm, wide (one pair tile per cluster), widep (wide,
+persistent clusters), streamk (wide, stream-K forced), auto (the heuristics).
+
   sustained  back-to-back launches for --seconds while nvidia-smi samples SM
              clock and power; reports TFLOP/s with the median clock/power, the
              regime in which a long training step runs under the 1 kW cap
@@ -32,6 +35,21 @@ SHAPES = {
     "cube_nt": (8192, 8192, 8192, 0, 0),
     "cube_nn": (8192, 8192, 8192, 0, 1),
     "cube_tt": (8192, 8192, 8192, 1, 1),
+    # transformer training config (65536 tokens per rank, d=2048, MLP 8192, vocab 32000):
+    # forward x W^T, input gradient dY W, weight gradient dY^T x
+    "tr_d_fwd": (65536, 2048, 2048, 0, 0),
+    "tr_up_fwd": (65536, 8192, 2048, 0, 0),
+    "tr_dn_fwd": (65536, 2048, 8192, 0, 0),
+    "tr_d_dx": (65536, 2048, 2048, 0, 1),
+    "tr_up_dx": (65536, 2048, 8192, 0, 1),
+    "tr_dn_dx": (65536, 8192, 2048, 0, 1),
+    "tr_d_dw": (2048, 2048, 65536, 1, 1),
+    "tr_up_dw": (8192, 2048, 65536, 1, 1),
+    "tr_dn_dw": (2048, 8192, 65536, 1, 1),
+    "tr_head_fwd": (65536, 32000, 2048, 0, 0),
+    "tr_head_dw": (32000, 2048, 65536, 1, 1),
+    # TP-MLP at tp=8 (h/tp = 3584): weight gradient with 224 pair tiles
+    "tp8_dw_tt": (3584, 8192, 32768, 1, 1),
 }
 
 
@@ -121,12 +139,13 @@ def main():
             if kern == "cublas":
                 fn = lambda: torch.matmul(a, b)  # noqa: E731
             else:
-                mod.set_gemm_pair_mode({"1sm": 0, "2sm": 1, "wide": 2, "auto": -1}[kern])
+                mod.set_gemm_pair_mode({"1sm": 0, "2sm": 1, "wide": 2, "widep": 2, "streamk": -1, "auto": -1}[kern])
                 mod.set_gemm_group_m(args.group_m)
                 mod.set_gemm_split(args.split)
                 mod.set_gemm_sleep_ns(args.sleep_ns)
                 mod.set_tma_l2_promotion(args.l2_promotion)
-                mod.set_gemm_persistent(args.persistent)
+                mod.set_gemm_persistent(1 if kern == "widep" else args.persistent)
+                mod.set_gemm_streamk(1 if kern == "streamk" else (0 if kern != "auto" else -1))
                 fn = lambda: gemm.native_bmm(a, b)  # noqa: E731
             label = f"gemm_{name}_{kern}"
             if args.mode == "burst":
@@ -144,6 +163,8 @@ def main():
         mod.set_gemm_pair_mode(-1)
         mod.set_gemm_group_m(0)
         mod.set_gemm_split(0)
+        mod.set_gemm_persistent(0)
+        mod.set_gemm_streamk(-1)
         del a, b
         torch.cuda.empty_cache()
     _native.check_errors()

@@ -116,6 +116,7 @@ def test_einconv_pads_in_kernel_without_copy(monkeypatch):
     (1, 9, 130, 128, 64, 3, 3, 1, 1),     # O < one M tile, three column blocks, padding
     (3, 5, 64, 64, 192, 1, 3, 0, 1),      # two M tiles, 1 x 3 kernel, exact column blocks
     (2, 7, 20, 192, 64, 5, 5, 2, 2),      # N = 25 * 192 spans many N tiles
+    (4, 64, 256, 128, 128, 3, 3, 1, 1),   # split-K over 59 slices, the last one past the end
 ])
 def test_conv_weight_gradient_native(B, H, W, C, O, KH, KW, ph, pw):
     torch.manual_seed(2)

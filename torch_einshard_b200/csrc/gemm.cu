@@ -221,6 +221,143 @@ static int launch_store(const GemmArgs& g0, cudaStream_t stream) {
   return static_cast<int>(cudaGetLastError());
 }
 
+// ------------------------------------------------------------------ stream-K
+
+// Epilogue of a stream-K segment: the warp's 32 rows x 256 columns as eight
+// 32 x 32 fp32 boxes (128-byte rows, 128-byte swizzle), each added into the
+// fp32 workspace by one TMA reduce-add (the addition happens at L2, so
+// segments of one tile from different clusters need no ordering).
+struct ReduceF32Epilogue {
+  __device__ __forceinline__ void setup(int*, const GemmShape&) {}
+  __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
+  __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape& s, volatile int*) {
+    const int row0 = et.c.m0 + et.q * 32;
+    if (row0 >= s.M) return true;  // no box may start outside the tensor
+    uint4* stage = reinterpret_cast<uint4*>(et.stage);
+#pragma unroll 1
+    for (int sub = 0; sub < kBN / 32; ++sub) {
+      const int col0 = et.c.n0 + sub * 32;
+      if (col0 >= s.N) break;  // uniform across the warp
+      uint32_t r[32];
+      tmem_ld32(et.tmem + sub * 32, r);
+      tmem_ld_wait();
+      if (et.lane == 0) bulk_wait_group_read<0>();  // the previous box has left the staging buffer
+      __syncwarp();
+      const int sw = et.lane & 7;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) stage[et.lane * 8 + (j ^ sw)] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (et.lane == 0) {
+        tma_reduce_add_3d(et.tmc, et.stage, col0, row0, et.c.b);
+        bulk_commit_group();
+      }
+    }
+    return true;
+  }
+};
+
+// C = act(ws) converted to the output type; ws is [M][ldw] fp32.  One thread
+// per 4 consecutive columns.
+template <typename OutT>
+__global__ void streamk_finish_kernel(const float* __restrict__ ws, long long ldw, OutT* __restrict__ C, long long ldc,
+                                      int M, int N, int act) {
+  const int groups = (N + 3) >> 2;
+  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (idx >= static_cast<long long>(M) * groups) return;
+  const int row = static_cast<int>(idx / groups);
+  const int col = static_cast<int>(idx - static_cast<long long>(row) * groups) * 4;
+  const float4 v = *reinterpret_cast<const float4*>(ws + row * ldw + col);
+  float f[4] = {v.x, v.y, v.z, v.w};
+  OutT* dst = C + row * ldc + col;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (col + i >= N) break;
+    const float x = act == kActSilu ? silu_f(f[i]) : f[i];
+    StoreOut<OutT>::store1(dst + i, x);
+  }
+}
+
+long long gemm_streamk_ws_ld(const GemmArgs& g) { return (static_cast<long long>(g.N) + 3) / 4 * 4; }
+
+int gemm_streamk_iters(const GemmArgs& g, int mode) {
+  if (mode == 0 || g.batch != 1 || g.M < 2 * kBM || g.N < kBN3 || g.num_sms < 2) return 0;
+  const long long pair_tiles = static_cast<long long>((g.M + 2 * kBM - 1) / (2 * kBM)) * ((g.N + kBN3 - 1) / kBN3);
+  const long long nkb = (g.K + kBK - 1) / kBK;
+  const long long clusters = g.num_sms / 2;
+  const long long per = (pair_tiles * nkb + clusters - 1) / clusters;
+  if (per <= 0 || per > 0x7fffffffLL) return 0;
+  if (mode > 0) return static_cast<int>(per);
+  if (nkb < 64) return 0;
+  // Whole tiles run in waves of `clusters` pair tiles; stream-K balances the
+  // last wave away but moves the fp32 tile through L2/DRAM (memset, reduce-adds,
+  // the finishing pass: ~14 bytes per output against 2K FLOPs).
+  const long long waves = (pair_tiles + clusters - 1) / clusters;
+  const double eff = static_cast<double>(pair_tiles) / static_cast<double>(waves * clusters);
+  const double gain = 1.0 / eff - 1.0;
+  const double cost = 1400.0 / static_cast<double>(g.K) + 0.02;
+  return gain > cost ? static_cast<int>(per) : 0;
+}
+
+int gemm_launch_streamk(const GemmArgs& g, int sk_iters, float* ws, cudaStream_t stream) {
+  if (check_gemm_args(g) || sk_iters <= 0 || g.batch != 1) return -1;
+  if ((reinterpret_cast<uintptr_t>(ws) & 15) != 0) return -2;
+  CUtensorMap ma, mb;
+  make_operand_maps(g, &ma, &mb, true);
+  GemmShape s = make_shape(g);
+  s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
+  s.num_n = (g.N + kBN3 - 1) / kBN3;
+  s.group_m = g.group_m > 0 ? g.group_m : 16;
+  s.pair = 1;
+  s.split = 0;
+  s.sk_iters = sk_iters;
+  const long long ldw = gemm_streamk_ws_ld(g);
+  const CUtensorMap mw = make_tmap_3d(ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.N, g.M, 1, ldw, ldw * g.M, 32, 32);
+  cudaError_t e = cudaMemsetAsync(ws, 0, static_cast<size_t>(ldw) * g.M * sizeof(float), stream);
+  if (e != cudaSuccess) return static_cast<int>(e);
+  auto kernel = gemm_tc3_kernel<ReduceF32Epilogue>;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> dev & 1ull)) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3Bytes);
+    attr_set |= 1ull << dev;
+  }
+  const long long total = static_cast<long long>(s.num_m) * s.num_n * s.num_kb;
+  const int clusters = static_cast<int>((total + sk_iters - 1) / sk_iters);
+  if (clusters > g.num_sms / 2) return -3;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kThreads3);
+  cfg.dynamicSmemBytes = kSmem3Bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mw, s, ReduceF32Epilogue{}, NoGather{});
+  if (e != cudaSuccess) return static_cast<int>(e);
+  const long long threads = static_cast<long long>(g.M) * ((g.N + 3) / 4);
+  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  switch (g.out_dtype) {
+    case kDtypeBF16:
+      streamk_finish_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
+          ws, ldw, reinterpret_cast<__nv_bfloat16*>(g.C), g.ldc, g.M, g.N, g.act);
+      break;
+    case kDtypeF16:
+      streamk_finish_kernel<__half><<<blocks, 256, 0, stream>>>(ws, ldw, reinterpret_cast<__half*>(g.C), g.ldc, g.M,
+                                                                  g.N, g.act);
+      break;
+    default:
+      streamk_finish_kernel<float><<<blocks, 256, 0, stream>>>(ws, ldw, reinterpret_cast<float*>(g.C), g.ldc, g.M,
+                                                                 g.N, g.act);
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
 int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (check_gemm_args(g)) return -1;
   switch (g.out_dtype) {

@@ -49,4 +49,14 @@ GemmShape make_shape_pair(const GemmArgs& g);
 // Output tensor map of the TMA-store epilogues; false (map zeroed) when C does not qualify.
 bool make_output_map(const GemmArgs& g, bool trans, CUtensorMap* mc);
 
+// Stream-K on the wide 2-SM kernel (batch 1): every SM pair takes the same
+// number of K blocks of the tile-major K-block sequence; partial tiles are
+// reduce-added in fp32 into a workspace ws[M][gemm_streamk_ws_ld(g)], which a
+// finishing pass converts (with the activation) into C.
+// gemm_streamk_iters: K blocks per cluster, or 0 when whole tiles are better
+// (mode -1 heuristic, 0 never, 1 always where the shape allows it).
+int gemm_streamk_iters(const GemmArgs& g, int mode);
+long long gemm_streamk_ws_ld(const GemmArgs& g);
+int gemm_launch_streamk(const GemmArgs& g, int sk_iters, float* ws, cudaStream_t stream);
+
 }  // namespace es

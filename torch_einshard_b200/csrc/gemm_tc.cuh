@@ -56,6 +56,7 @@ struct GemmShape {
   int* err;
   unsigned long long* prof;  // optional: per-CTA wait-cycle counters (see gemm_tc3.cuh), null when off
   int sleep_ns;              // wide kernel: epilogue back-off between accumulator polls (0: spin)
+  int sk_iters = 0;          // wide kernel: > 0 stream-K, K blocks per cluster (0: whole tiles per cluster)
 };
 
 struct TileCoord {

@@ -17,6 +17,13 @@
 // Warps (320 threads): 0 TMA producer, 1 MMA issuer (leader CTA) + TMEM owner,
 // 2..9 epilogue.  Barriers as in gemm_tc2.cuh; tempty counts the 16 epilogue
 // warps of the pair.
+//
+// Stream-K (shp.sk_iters > 0): the K blocks of all tiles form one sequence
+// (tile-major) and cluster c takes blocks [c * sk_iters, (c + 1) * sk_iters),
+// i.e. whole tiles and at most two partial ones, so every SM pair gets the
+// same work however few tiles there are.  A segment (one tile's K-block range)
+// accumulates in TMEM from zero and its epilogue adds the fp32 partial into a
+// zero-initialised workspace (ReduceF32Epilogue: TMA reduce-add stores).
 #pragma once
 
 #include "gemm_tc.cuh"
@@ -88,6 +95,49 @@ __device__ __forceinline__ bool pair_tile_at(const GemmShape& s, int cluster, in
   return true;
 }
 
+// The work of one cluster as a sequence of segments: a pair tile and a K-block
+// range [kb0, kb1).  Tile mode: whole tiles from pair_tile_at; stream-K: the
+// cluster's share of the tile-major K-block sequence.
+struct SegIter {
+  long long g = 0, end = 0;  // stream-K cursor and end (K blocks)
+  int i = 0;                 // tile mode: tiles taken so far
+};
+
+__device__ __forceinline__ SegIter seg_begin(const GemmShape& s, int cluster) {
+  SegIter it;
+  if (s.sk_iters > 0) {
+    const long long total = static_cast<long long>(s.num_m) * s.num_n * s.batch * s.num_kb;
+    it.g = min(total, static_cast<long long>(cluster) * s.sk_iters);
+    it.end = min(total, it.g + s.sk_iters);
+  }
+  return it;
+}
+
+// Next segment: tile coordinates (this CTA's half), linear pair tile index and
+// K-block range; false when the cluster has no more work.
+__device__ __forceinline__ bool seg_next(const GemmShape& s, int cluster, int nclusters, int rank, SegIter& it,
+                                         TileCoord* c, int* pair_index, int* kb0, int* kb1) {
+  if (s.sk_iters > 0) {
+    if (it.g >= it.end) return false;
+    const long long p = it.g / s.num_kb;
+    const int k0 = static_cast<int>(it.g - p * s.num_kb);
+    const long long left = it.end - it.g;
+    const int k1 = left < s.num_kb - k0 ? k0 + static_cast<int>(left) : s.num_kb;
+    *c = tile_coord3(s, static_cast<int>(p), rank);
+    *pair_index = static_cast<int>(p);
+    *kb0 = k0;
+    *kb1 = k1;
+    it.g += k1 - k0;
+    return true;
+  }
+  if (!pair_tile_at(s, cluster, nclusters, it.i, rank, c)) return false;
+  *pair_index = cluster + it.i * nclusters;
+  *kb0 = 0;
+  *kb1 = s.num_kb;
+  ++it.i;
+  return true;
+}
+
 // Gather policy of the wide kernel.  The plain GEMM has none; the fused
 // all-gather -> GEMM (gemm_ag.cu) adds a copy warp that pulls peers' rows of A
 // into a local buffer, orders the M tiles local-rows-first and makes the
@@ -156,11 +206,13 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
     // ------------------------------------------------------------ producer (both CTAs)
     uint32_t it = 0;
     TileCoord c;
-    for (int ti = 0; pair_tile_at(shp, cluster, nclusters, ti, static_cast<int>(rank), &c); ++ti) {
+    int pidx, kb0, kb1;
+    SegIter seg = seg_begin(shp, cluster);
+    while (seg_next(shp, cluster, nclusters, static_cast<int>(rank), seg, &c, &pidx, &kb0, &kb1)) {
       c.m0 = gather.map_m0(c.m0);
       if (!gather.wait_rows(c.m0, abort_flag)) goto producer_done;  // rows of A gathered from their owner
       const int nq0 = c.n0 + static_cast<int>(rank) * (kBN / 2);  // this CTA's quarter in each 256-col half
-      for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
+      for (int kb = kb0; kb < kb1; ++kb, ++it) {
         const int s = it % kStages3;
         const uint32_t ph = (it / kStages3) & 1u;
         if (!mbar_wait_lane0(&st->empty[s], ph ^ 1u, abort_flag, shp.err, kErrWaitEmpty)) goto producer_done;
@@ -213,12 +265,14 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
       long long wait_full = 0, wait_tempty = 0;
       const long long t_start = clock64();
       TileCoord cm;
-      for (; pair_tile_at(shp, cluster, nclusters, static_cast<int>(tc), 0, &cm); ++tc) {
+      int pidx, kb0, kb1;
+      SegIter seg = seg_begin(shp, cluster);
+      for (; seg_next(shp, cluster, nclusters, 0, seg, &cm, &pidx, &kb0, &kb1); ++tc) {
         const long long t_e0 = shp.prof ? clock64() : 0;
         if (!mbar_wait_lane0(&st->tempty_[0], (tc & 1u) ^ 1u, abort_flag, shp.err, kErrWaitTmemEmpty)) goto mma_done;
         if (shp.prof) wait_tempty += clock64() - t_e0;
         tc_fence_after();
-        for (int kb = 0; kb < shp.num_kb; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % kStages3;
           const uint32_t ph = (it / kStages3) & 1u;
           const long long t_f0 = shp.prof ? clock64() : 0;
@@ -231,7 +285,7 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
 #pragma unroll
             for (int k = 0; k < kBK / kUmmaK; ++k) {
               const uint64_t ad = umma_desc_sw128(a_addr + k * a_kstep, a_lbo, 1024u);
-              const uint32_t acc = (kb | k) != 0 ? 1u : 0u;
+              const uint32_t acc = (kb != kb0 || k != 0) ? 1u : 0u;
 #pragma unroll
               for (int h = 0; h < 2; ++h) {
                 const uint64_t bd = umma_desc_sw128(b_addr + h * (kB3Bytes / 2) + k * b_kstep, b_lbo, 1024u);
@@ -270,12 +324,14 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
     const int half = (warp - 2) >> 2;  // 256-column half of the tile
     uint32_t tc = 0;
     TileCoord ce;
-    for (; pair_tile_at(shp, cluster, nclusters, static_cast<int>(tc), static_cast<int>(rank), &ce); ++tc) {
+    int pidx, kb0, kb1;
+    SegIter seg = seg_begin(shp, cluster);
+    for (; seg_next(shp, cluster, nclusters, static_cast<int>(rank), seg, &ce, &pidx, &kb0, &kb1); ++tc) {
       ce.m0 = gather.map_m0(ce.m0);
       if (!mbar_wait_sleepy(&st->tfull_[0], tc & 1u, abort_flag, shp.err, kErrWaitTmemFull, shp.sleep_ns)) break;
       tc_fence_after();
       EpiTile et;
-      et.t = 2 * (cluster + static_cast<int>(tc) * nclusters) + static_cast<int>(rank);
+      et.t = 2 * pidx + static_cast<int>(rank);
       et.c = ce;
       et.c.n0 += half * kBN;
       et.tmem = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + half * kBN;
