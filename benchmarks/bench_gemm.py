@@ -125,7 +125,8 @@ def main():
     p.add_argument("--split", type=int, default=0, help="wide kernel: cluster split mode 0/1/2")
     p.add_argument("--sleep-ns", type=int, default=0, help="wide kernel: epilogue back-off between polls")
     p.add_argument("--l2-promotion", type=int, default=3, help="TMA L2 promotion 0 none .. 3 256B")
-    p.add_argument("--persistent", type=int, default=0, help="wide kernel: 1 persistent grid, 0 one tile per cluster")
+    p.add_argument("--persistent", type=int, default=-1,
+                   help="wide kernel under 'auto': 1 persistent grid, 0 one tile per cluster, -1 by K")
     args = p.parse_args()
     device = torch.device(args.device)
     from torch_einshard_b200.ops import _native, gemm
@@ -144,8 +145,8 @@ def main():
                 mod.set_gemm_split(args.split)
                 mod.set_gemm_sleep_ns(args.sleep_ns)
                 mod.set_tma_l2_promotion(args.l2_promotion)
-                mod.set_gemm_persistent(1 if kern == "widep" else args.persistent)
-                mod.set_gemm_streamk(1 if kern == "streamk" else (0 if kern != "auto" else -1))
+                mod.set_gemm_persistent({"widep": 1, "wide": 0}.get(kern, args.persistent))
+                mod.set_gemm_streamk(1 if kern == "streamk" else 0)
                 fn = lambda: gemm.native_bmm(a, b)  # noqa: E731
             label = f"gemm_{name}_{kern}"
             if args.mode == "burst":
@@ -163,8 +164,8 @@ def main():
         mod.set_gemm_pair_mode(-1)
         mod.set_gemm_group_m(0)
         mod.set_gemm_split(0)
-        mod.set_gemm_persistent(0)
-        mod.set_gemm_streamk(-1)
+        mod.set_gemm_persistent(-1)
+        mod.set_gemm_streamk(0)
         del a, b
         torch.cuda.empty_cache()
     _native.check_errors()

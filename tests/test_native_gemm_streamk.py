@@ -18,7 +18,7 @@ def streamk():
     mod.set_gemm_pair_mode(-1)
     mod.set_gemm_streamk(1)
     yield mod
-    mod.set_gemm_streamk(-1)
+    mod.set_gemm_streamk(0)
 
 
 def _check(a, b, out_dtype=None, act=None):
@@ -62,15 +62,24 @@ def test_streamk_fp32_out_and_silu(streamk):
     _check(a, b, act="silu")
 
 
-def test_streamk_heuristic_picks_weight_gradient_shape():
+def test_streamk_weight_gradient_shape(streamk):
     """2048 x 2048 output with K = 65536 (a transformer weight gradient): 32
-    pair tiles for 74 SM pairs, so the heuristic takes stream-K."""
-    mod = _native.require()
-    mod.set_gemm_pair_mode(-1)
-    mod.set_gemm_streamk(-1)
+    pair tiles for 74 SM pairs, every pair gets an equal K slice."""
     g = torch.randn(1, 65536, 2048, device="cuda", dtype=torch.bfloat16)
     x = torch.randn(1, 65536, 2048, device="cuda", dtype=torch.bfloat16)
     _check(g.transpose(1, 2), x)
+
+
+def test_streamk_off_by_default():
+    mod = _native.require()
+    mod.set_gemm_pair_mode(-1)
+    mod.set_gemm_streamk(0)
+    a = torch.randn(1, 2048, 16384, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(1, 16384, 2048, device="cuda", dtype=torch.bfloat16)
+    before = mod.launch_count()
+    gemm.native_bmm(a, b)
+    torch.cuda.synchronize()
+    assert mod.launch_count() - before == 1
 
 
 def test_streamk_off_under_deterministic_algorithms(streamk):

@@ -27,8 +27,8 @@ int g_split = 0;    // wide-kernel cluster split mode (tuning)
 int g_sleep_ns = 0;  // wide-kernel epilogue back-off (tuning)
 int g_small_persistent = 1;  // 1-SM GEMM and conv grids (tuning)
 uint64_t g_wait_timeout_ns = 4000000000ull;  // bound of device waits on peers (EINSHARD_WAIT_TIMEOUT_US)
-int g_streamk = -1;  // stream-K on the wide kernel: -1 heuristic, 0 never, 1 always where the shape allows
-int g_persistent = 0;  // wide-kernel grid: 0 one pair tile per cluster (default, measured faster under the power cap), 1 persistent
+int g_streamk = 0;  // stream-K on the wide kernel: 1 where the shape allows, 0 never (default)
+int g_persistent = -1;  // wide-kernel grid: 0 one pair tile per cluster, 1 persistent, -1 by K (default)
 unsigned long long* g_prof = nullptr;  // wide-kernel wait counters (tuning), device pointer or null
 
 int dtype_code(at::ScalarType t) {
@@ -673,14 +673,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_gemm_profile", [](const at::Tensor& t) {
         g_prof = t.numel() >= 3 ? reinterpret_cast<unsigned long long*>(t.data_ptr()) : nullptr;
       }, "int64 CUDA tensor of >= 3 wait-cycle counters for the wide GEMM (empty tensor: off)");
-  m.def("set_gemm_persistent", [](int64_t v) { g_persistent = static_cast<int>(v); }, "wide kernel: 1 persistent, 0 one tile per cluster");
+  m.def("set_gemm_persistent", [](int64_t v) { g_persistent = static_cast<int>(v); }, "wide kernel: 1 persistent, 0 one tile per cluster, -1 by K");
   m.def("set_small_persistent", [](int64_t v) { g_small_persistent = static_cast<int>(v); },
         "1-SM GEMM and conv: 1 persistent CTAs, 0 one tile per CTA");
   m.def("set_wait_timeout_ns", [](int64_t v) { g_wait_timeout_ns = static_cast<uint64_t>(v > 0 ? v : 1); },
         "bound (ns) of every device-side wait on a peer rank");
   m.def("get_wait_timeout_ns", []() { return static_cast<int64_t>(g_wait_timeout_ns); });
   m.def("set_gemm_streamk", [](int64_t v) { g_streamk = static_cast<int>(v); },
-        "stream-K wide GEMM: -1 heuristic, 0 never, 1 always where the shape allows");
+        "stream-K wide GEMM: 1 where the shape allows, 0/-1 never (default)");
   m.def("set_gemm_sleep_ns", [](int64_t v) { g_sleep_ns = static_cast<int>(v); }, "wide-kernel epilogue back-off ns");
   m.def("set_tma_l2_promotion", [](int64_t v) { es::tma_l2_promotion() = static_cast<int>(v); },
         "L2 promotion of TMA loads: 0 none, 1 64B, 2 128B, 3 256B (tuning)");

@@ -21,10 +21,15 @@ int pick_kernel(const GemmArgs& g) {
   if (g.pair >= 0) return g.pair;
   // Measured on B200 under the 1 kW cap (sustained, TP-MLP shapes): the wide
   // kernel beats the 1-SM kernel on every operand layout once there are enough
-  // 256x512 pair tiles to give every SM pair work; small problems keep the
-  // 1-SM kernel's finer tiles.
-  const long long pair_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 511) / 512) * g.batch;
-  return pair_tiles >= g.num_sms / 2 ? 2 : 0;
+  // 256x512 pair tiles to give every SM pair work.  With fewer, the 256x256
+  // pair kernel still fills the GPU when it has at least half as many pair
+  // tiles as SM pairs (2048 x 2048 x 65536 weight gradient: 0.43 ms against
+  // 0.49 ms on the 1-SM kernel); small problems keep the 1-SM kernel.
+  const long long wide_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 511) / 512) * g.batch;
+  const long long pair_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 255) / 256) * g.batch;
+  if (wide_tiles >= g.num_sms / 2) return 2;
+  if (2 * pair_tiles >= g.num_sms / 2 && g.M >= 256 && g.N >= 256 && g.K >= 16 * kBK) return 1;
+  return 0;
 }
 
 bool use_pair_kernel(const GemmArgs& g) { return pick_kernel(g) >= 1; }
@@ -82,8 +87,8 @@ GemmShape make_shape_pair(const GemmArgs& g) {
 
 // Launch a 2-SM kernel instantiation on clusters of two CTAs.
 template <class Epi>
-int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShape& s, const Epi& epi, int num_sms,
-                cudaStream_t stream) {
+int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const CUtensorMap& mc, const GemmShape& s,
+                const Epi& epi, int num_sms, cudaStream_t stream) {
   auto kernel = gemm_tc2_kernel<Epi>;
   static unsigned long long attr_set = 0;
   int dev = 0;
@@ -108,7 +113,7 @@ int launch_pair(const CUtensorMap& ma, const CUtensorMap& mb, const GemmShape& s
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, s, epi));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, s, epi));
 }
 
 // C = A B computed as C^T = B^T A^T: operand roles and majorness swap, the
@@ -169,7 +174,11 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
   }
   const int pairs = s.num_m * s.num_n * s.batch;
   int clusters = g.num_sms / 2;
-  if (pairs < clusters || g.persistent == 0) clusters = pairs;  // 0: one pair tile per cluster (tuning)
+  // One pair tile per cluster held higher clocks under the power cap for long K;
+  // with K <= 2048 the per-CTA setup and the unhidden pipeline fill dominate and
+  // persistent clusters win (65536 x 2048 x 2048: 0.37 against 0.40 ms).
+  const bool persist = g.persistent > 0 || (g.persistent < 0 && (g.K + kBK - 1) / kBK <= 32);
+  if (pairs < clusters || !persist) clusters = pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
   cfg.blockDim = dim3(kThreads3);
@@ -204,7 +213,11 @@ static int launch_store(const GemmArgs& g0, cudaStream_t stream) {
   epi.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * esz) % 16 == 0) &&
                (g.batch == 1 || (g.c_batch_stride * esz) % 16 == 0);
   if (pair && pick_kernel(g) == 2) return launch_wide(ma, mb, g, epi, stream);
-  if (pair) return launch_pair(ma, mb, s, epi, g.num_sms, stream);
+  if (pair) {
+    CUtensorMap mc;
+    epi.tma = make_output_map(g, trans, &mc) ? 1 : 0;
+    return launch_pair(ma, mb, mc, s, epi, g.num_sms, stream);
+  }
   auto kernel = gemm_tc_kernel<StoreEpilogue<OutT>>;
   static unsigned long long attr_set = 0;  // one bit per device
   int dev = 0;
@@ -281,22 +294,18 @@ __global__ void streamk_finish_kernel(const float* __restrict__ ws, long long ld
 long long gemm_streamk_ws_ld(const GemmArgs& g) { return (static_cast<long long>(g.N) + 3) / 4 * 4; }
 
 int gemm_streamk_iters(const GemmArgs& g, int mode) {
-  if (mode == 0 || g.batch != 1 || g.M < 2 * kBM || g.N < kBN3 || g.num_sms < 2) return 0;
+  // Only on request: measured on B200 (training weight-gradient shapes, K =
+  // 65536), the fp32 TMA reduce-adds of the partial tiles (about 3.3 TB/s over
+  // the GPU, not overlapped with the MMAs because the accumulator is single
+  // buffered) cost more than the balanced waves gain: 8192 x 2048 took 1.91 ms
+  // against 1.43 ms in whole tiles, 2048 x 2048 0.46 ms against 0.43 ms on the
+  // 256 x 256 pair kernel.
+  if (mode <= 0 || g.batch != 1 || g.M < 2 * kBM || g.N < kBN3 || g.num_sms < 2) return 0;
   const long long pair_tiles = static_cast<long long>((g.M + 2 * kBM - 1) / (2 * kBM)) * ((g.N + kBN3 - 1) / kBN3);
   const long long nkb = (g.K + kBK - 1) / kBK;
   const long long clusters = g.num_sms / 2;
   const long long per = (pair_tiles * nkb + clusters - 1) / clusters;
-  if (per <= 0 || per > 0x7fffffffLL) return 0;
-  if (mode > 0) return static_cast<int>(per);
-  if (nkb < 64) return 0;
-  // Whole tiles run in waves of `clusters` pair tiles; stream-K balances the
-  // last wave away but moves the fp32 tile through L2/DRAM (memset, reduce-adds,
-  // the finishing pass: ~14 bytes per output against 2K FLOPs).
-  const long long waves = (pair_tiles + clusters - 1) / clusters;
-  const double eff = static_cast<double>(pair_tiles) / static_cast<double>(waves * clusters);
-  const double gain = 1.0 / eff - 1.0;
-  const double cost = 1400.0 / static_cast<double>(g.K) + 0.02;
-  return gain > cost ? static_cast<int>(per) : 0;
+  return per > 0 && per <= 0x7fffffffLL ? static_cast<int>(per) : 0;
 }
 
 int gemm_launch_streamk(const GemmArgs& g, int sk_iters, float* ws, cudaStream_t stream) {

@@ -35,7 +35,7 @@ struct GemmArgs {
   int split = 0;     // wide kernel cluster split (see GemmShape::split)
   unsigned long long* prof = nullptr;  // optional wait-cycle counters (wide kernel)
   int sleep_ns = 0;  // wide kernel epilogue back-off (tuning)
-  int persistent = 0;  // wide kernel: 0 one pair tile per cluster (default), 1 persistent clusters
+  int persistent = -1;  // wide kernel: 0 one pair tile per cluster, 1 persistent clusters, -1 by K (persistent for K <= 2048)
   int small_persistent = 1;  // 1-SM kernel: 1 persistent CTAs (default), 0 one tile per CTA (tuning)
 };
 
@@ -54,7 +54,7 @@ bool make_output_map(const GemmArgs& g, bool trans, CUtensorMap* mc);
 // reduce-added in fp32 into a workspace ws[M][gemm_streamk_ws_ld(g)], which a
 // finishing pass converts (with the activation) into C.
 // gemm_streamk_iters: K blocks per cluster, or 0 when whole tiles are better
-// (mode -1 heuristic, 0 never, 1 always where the shape allows it).
+// (mode 1: where the shape allows it; 0 or -1: never, the measured default).
 int gemm_streamk_iters(const GemmArgs& g, int mode);
 long long gemm_streamk_ws_ld(const GemmArgs& g);
 int gemm_launch_streamk(const GemmArgs& g, int sk_iters, float* ws, cudaStream_t stream);

@@ -324,6 +324,8 @@ int gemm_push_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStrea
   epi.red_base = owned * (comm.size - 1) * kSubBytes;
   epi.groups = 1;
   epi.sm = nullptr;
+  CUtensorMap mc;  // the push epilogue stores with plain NVLink writes: no output map
+  memset(&mc, 0, sizeof(mc));
   auto kernel = gemm_tc2_kernel<PushArEpilogue>;
   static unsigned long long attr_set = 0;
   int dev = 0;
@@ -345,7 +347,7 @@ int gemm_push_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStrea
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, s, epi));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, s, epi));
 }
 
 }  // namespace es

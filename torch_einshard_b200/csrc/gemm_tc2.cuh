@@ -15,7 +15,8 @@
 //   tfull[a]  in both CTAs; multicast commit after the last K step of a tile.
 //   tempty[a] leader only; all 8 epilogue warps of the pair arrive on it.
 // Tiles are handed to the epilogue policy as 128-row halves (EpiTile.t =
-// 2 * pair_tile + rank), so the policies of gemm_tc.cuh work unchanged.
+// 2 * pair_tile + rank), so the policies of gemm_tc.cuh work unchanged; each
+// epilogue warp has a 4 KB staging buffer for TMA-store epilogues (tmC).
 #pragma once
 
 #include "gemm_tc.cuh"
@@ -26,7 +27,8 @@ constexpr int kStages2 = 6;
 constexpr int kA2Bytes = kBM * kBK * 2;          // 16 KB: this CTA's 128 A rows
 constexpr int kB2Bytes = (kBN / 2) * kBK * 2;    // 16 KB: this CTA's 128 B columns
 constexpr int kStage2Bytes = kA2Bytes + kB2Bytes;
-constexpr int kSmem2Bytes = kStages2 * kStage2Bytes + 1024 + 1024;
+constexpr int kStage2Out = 4096;  // per epilogue warp: staging of one 32 x 64 16-bit output box
+constexpr int kSmem2Bytes = kStages2 * kStage2Bytes + 1024 + 4 * kStage2Out + 1024;
 
 struct SharedState2 {
   uint64_t full[kStages2];
@@ -43,12 +45,13 @@ struct SharedState2 {
 template <class Epi>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const GemmShape shp, Epi epi) {
+                    const __grid_constant__ CUtensorMap tmC, const GemmShape shp, Epi epi) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + kStages2 * kA2Bytes;
   SharedState2* st = reinterpret_cast<SharedState2*>(smem + kStages2 * kStage2Bytes);
+  uint8_t* out_stage = smem + kStages2 * kStage2Bytes + 1024;  // 1024-byte aligned (TMA swizzle atom)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -195,6 +198,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       et.row = q * 32 + lane;
       et.q = q;
       et.lane = lane;
+      et.tmc = &tmC;
+      et.stage = out_stage + q * kStage2Out;
       const bool ok = epi.tile(et, shp, abort_flag);
       tc_fence_before();
       __syncwarp();
@@ -205,6 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     epi.finish(shp, abort_flag);
+    if (lane == 0) bulk_wait_group<0>();  // every TMA store of this warp has landed
   }
 
   __syncthreads();
