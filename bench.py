@@ -18,6 +18,7 @@ import argparse
 import json
 import os
 import subprocess
+import tempfile
 import sys
 import time
 from datetime import timedelta
@@ -65,7 +66,9 @@ class ClockSampler:
     def __init__(self, devices):
         self.devices = set(devices)
         self.proc = None
-        self.path = os.path.join(HERE, "gpurun_out", f"clocks_{os.getpid()}.csv")
+        # raw samples (one CSV per process); EINSHARD_CLOCKS_DIR keeps them somewhere else
+        self.path = os.path.join(os.environ.get("EINSHARD_CLOCKS_DIR", tempfile.gettempdir()),
+                                 f"einshard_clocks_{os.getpid()}.csv")
 
     def start(self):
         try:

@@ -9,7 +9,8 @@ Two modes:
   burst      CUDA events per iteration (inputs larger than L2 at the default
              sizes, so no flush is needed)
 Kernels: cublas, 1sm, 2sm, wide (one pair tile per cluster), widep (wide,
-persistent clusters), streamk (wide, stream-K forced), auto (the heuristics).
+persistent clusters), streamk (wide, every tile split), auto (the heuristics:
+stream-K tail for the partial last wave of long-K GEMMs).
 
   sustained  back-to-back launches for --seconds while nvidia-smi samples SM
              clock and power; reports TFLOP/s with the median clock/power, the
@@ -146,7 +147,7 @@ def main():
                 mod.set_gemm_sleep_ns(args.sleep_ns)
                 mod.set_tma_l2_promotion(args.l2_promotion)
                 mod.set_gemm_persistent({"widep": 1, "wide": 0}.get(kern, args.persistent))
-                mod.set_gemm_streamk(1 if kern == "streamk" else 0)
+                mod.set_gemm_streamk({"streamk": 1, "auto": -1}.get(kern, 0))
                 fn = lambda: gemm.native_bmm(a, b)  # noqa: E731
             label = f"gemm_{name}_{kern}"
             if args.mode == "burst":
@@ -165,7 +166,7 @@ def main():
         mod.set_gemm_group_m(0)
         mod.set_gemm_split(0)
         mod.set_gemm_persistent(-1)
-        mod.set_gemm_streamk(0)
+        mod.set_gemm_streamk(-1)
         del a, b
         torch.cuda.empty_cache()
     _native.check_errors()

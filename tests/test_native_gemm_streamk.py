@@ -1,5 +1,6 @@
-"""Stream-K wide GEMM (K blocks balanced over all SM pairs, fp32 partial tiles
-reduce-added by TMA) against a plain fp32 PyTorch matmul."""
+"""Stream-K on the wide GEMM against a plain fp32 PyTorch matmul: every tile
+split (forced) and the default hybrid (whole tiles for the full waves, the
+partial last wave split over all SM pairs, fp32 partials reduce-added by TMA)."""
 
 import pytest
 import torch
@@ -18,7 +19,7 @@ def streamk():
     mod.set_gemm_pair_mode(-1)
     mod.set_gemm_streamk(1)
     yield mod
-    mod.set_gemm_streamk(0)
+    mod.set_gemm_streamk(-1)
 
 
 def _check(a, b, out_dtype=None, act=None):
@@ -70,12 +71,25 @@ def test_streamk_weight_gradient_shape(streamk):
     _check(g.transpose(1, 2), x)
 
 
-def test_streamk_off_by_default():
+def test_streamk_tail_by_default():
+    """80 pair tiles for 74 SM pairs and 72 K blocks: one whole wave, the
+    other 6 tiles split over all pairs (ragged M and N)."""
     mod = _native.require()
     mod.set_gemm_pair_mode(-1)
-    mod.set_gemm_streamk(0)
-    a = torch.randn(1, 2048, 16384, device="cuda", dtype=torch.bfloat16)
-    b = torch.randn(1, 16384, 2048, device="cuda", dtype=torch.bfloat16)
+    mod.set_gemm_streamk(-1)
+    torch.manual_seed(5)
+    a = torch.randn(1, 2500, 4608, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(1, 4608, 4000, device="cuda", dtype=torch.bfloat16)
+    _check(a, b)
+    _check(a, b, act="silu")
+
+
+def test_streamk_not_for_short_k():
+    mod = _native.require()
+    mod.set_gemm_pair_mode(-1)
+    mod.set_gemm_streamk(-1)
+    a = torch.randn(1, 2500, 2048, device="cuda", dtype=torch.bfloat16)
+    b = torch.randn(1, 2048, 4000, device="cuda", dtype=torch.bfloat16)
     before = mod.launch_count()
     gemm.native_bmm(a, b)
     torch.cuda.synchronize()

@@ -27,7 +27,7 @@ int g_split = 0;    // wide-kernel cluster split mode (tuning)
 int g_sleep_ns = 0;  // wide-kernel epilogue back-off (tuning)
 int g_small_persistent = 1;  // 1-SM GEMM and conv grids (tuning)
 uint64_t g_wait_timeout_ns = 4000000000ull;  // bound of device waits on peers (EINSHARD_WAIT_TIMEOUT_US)
-int g_streamk = 0;  // stream-K on the wide kernel: 1 where the shape allows, 0 never (default)
+int g_streamk = -1;  // stream-K on the wide kernel: -1 the partial last wave of long-K GEMMs (default), 1 every tile, 0 never
 int g_persistent = -1;  // wide-kernel grid: 0 one pair tile per cluster, 1 persistent, -1 by K (default)
 unsigned long long* g_prof = nullptr;  // wide-kernel wait counters (tuning), device pointer or null
 
@@ -76,12 +76,12 @@ void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t
   const c10::cuda::CUDAGuard guard(a.device());
   es::GemmArgs g = gemm_args(a, b, out, act, err);
   // stream-K adds fp32 partial tiles in arrival order: skipped when torch asks for deterministic algorithms
-  const bool deterministic = at::globalContext().deterministicAlgorithms();
-  const int sk = (g.pair < 0 || g_streamk > 0) && !deterministic ? es::gemm_streamk_iters(g, g_streamk) : 0;
-  if (sk > 0) {
+  es::StreamKPlan plan;
+  if ((g.pair < 0 || g_streamk > 0) && !at::globalContext().deterministicAlgorithms() &&
+      es::gemm_streamk_plan(g, g_streamk, &plan)) {
     // fp32 workspace from the caching allocator (the stream orders its reuse)
-    at::Tensor ws = at::empty({static_cast<int64_t>(g.M) * es::gemm_streamk_ws_ld(g)}, a.options().dtype(at::kFloat));
-    const int rc = es::gemm_launch_streamk(g, sk, ws.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
+    at::Tensor ws = at::empty({es::gemm_streamk_ws_elems(plan)}, a.options().dtype(at::kFloat));
+    const int rc = es::gemm_launch_streamk(g, plan, ws.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
     TORCH_CHECK(rc == 0, "einshard native gemm: stream-K launch failed (", rc, ")");
     g_launches.fetch_add(2, std::memory_order_relaxed);
     return;
@@ -680,7 +680,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "bound (ns) of every device-side wait on a peer rank");
   m.def("get_wait_timeout_ns", []() { return static_cast<int64_t>(g_wait_timeout_ns); });
   m.def("set_gemm_streamk", [](int64_t v) { g_streamk = static_cast<int>(v); },
-        "stream-K wide GEMM: 1 where the shape allows, 0/-1 never (default)");
+        "stream-K wide GEMM: -1 split the partial last wave (default), 1 split every tile, 0 never");
   m.def("set_gemm_sleep_ns", [](int64_t v) { g_sleep_ns = static_cast<int>(v); }, "wide-kernel epilogue back-off ns");
   m.def("set_tma_l2_promotion", [](int64_t v) { es::tma_l2_promotion() = static_cast<int>(v); },
         "L2 promotion of TMA loads: 0 none, 1 64B, 2 128B, 3 256B (tuning)");

@@ -191,7 +191,9 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, s, epi, NoGather{}));
+  CUtensorMap mw;  // no stream-K workspace
+  memset(&mw, 0, sizeof(mw));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, mw, s, epi, NoGather{}));
 }
 
 template <typename OutT>
@@ -234,23 +236,28 @@ static int launch_store(const GemmArgs& g0, cudaStream_t stream) {
   return static_cast<int>(cudaGetLastError());
 }
 
-// ------------------------------------------------------------------ stream-K
+// ------------------------------------------------------------------ stream-K tail
 
-// Epilogue of a stream-K segment: the warp's 32 rows x 256 columns as eight
-// 32 x 32 fp32 boxes (128-byte rows, 128-byte swizzle), each added into the
-// fp32 workspace by one TMA reduce-add (the addition happens at L2, so
-// segments of one tile from different clusters need no ordering).
-struct ReduceF32Epilogue {
+// Whole tiles (pair tile < sk_first) store through the plain TMA-store
+// epilogue; tail segments add their fp32 partial into the workspace
+// [tail tile][256][512]: the warp's 32 rows x 256 columns as eight 32 x 32
+// boxes (128-byte rows, 128-byte swizzle), one TMA reduce-add each (the sum
+// happens at L2, so segments of one tile from different clusters need no
+// ordering).
+template <typename OutT>
+struct StreamKEpilogue {
+  StoreEpilogue<OutT> store;
+  int sk_first;
   __device__ __forceinline__ void setup(int*, const GemmShape&) {}
   __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
-  __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape& s, volatile int*) {
-    const int row0 = et.c.m0 + et.q * 32;
-    if (row0 >= s.M) return true;  // no box may start outside the tensor
+  __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape& s, volatile int* abort_flag) {
+    const int p = et.t >> 1;
+    if (p < sk_first) return store.tile(et, s, abort_flag);
+    const int x0 = et.c.n0 & (kBN3 - 1);          // column inside the 512-wide pair tile
+    const int y0 = (et.c.m0 & (2 * kBM - 1)) + et.q * 32;  // row inside the 256-row pair tile
     uint4* stage = reinterpret_cast<uint4*>(et.stage);
 #pragma unroll 1
     for (int sub = 0; sub < kBN / 32; ++sub) {
-      const int col0 = et.c.n0 + sub * 32;
-      if (col0 >= s.N) break;  // uniform across the warp
       uint32_t r[32];
       tmem_ld32(et.tmem + sub * 32, r);
       tmem_ld_wait();
@@ -258,11 +265,12 @@ struct ReduceF32Epilogue {
       __syncwarp();
       const int sw = et.lane & 7;
 #pragma unroll
-      for (int j = 0; j < 8; ++j) stage[et.lane * 8 + (j ^ sw)] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
+      for (int j = 0; j < 8; ++j)
+        stage[et.lane * 8 + (j ^ sw)] = make_uint4(r[4 * j], r[4 * j + 1], r[4 * j + 2], r[4 * j + 3]);
       fence_proxy_async_smem();
       __syncwarp();
       if (et.lane == 0) {
-        tma_reduce_add_3d(et.tmc, et.stage, col0, row0, et.c.b);
+        tma_reduce_add_3d(et.tmw, et.stage, x0 + sub * 32, y0, p - sk_first);
         bulk_commit_group();
       }
     }
@@ -270,48 +278,69 @@ struct ReduceF32Epilogue {
   }
 };
 
-// C = act(ws) converted to the output type; ws is [M][ldw] fp32.  One thread
-// per 4 consecutive columns.
+// C[tail tile] = act(workspace tile), converted to the output type.  Block
+// (q, r): tail tile q, rows 16 r .. 16 r + 15; one thread per 4 columns.
 template <typename OutT>
-__global__ void streamk_finish_kernel(const float* __restrict__ ws, long long ldw, OutT* __restrict__ C, long long ldc,
-                                      int M, int N, int act) {
-  const int groups = (N + 3) >> 2;
-  const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (idx >= static_cast<long long>(M) * groups) return;
-  const int row = static_cast<int>(idx / groups);
-  const int col = static_cast<int>(idx - static_cast<long long>(row) * groups) * 4;
-  const float4 v = *reinterpret_cast<const float4*>(ws + row * ldw + col);
-  float f[4] = {v.x, v.y, v.z, v.w};
-  OutT* dst = C + row * ldc + col;
+__global__ void streamk_finish_kernel(const float* __restrict__ ws, OutT* __restrict__ C, long long ldc,
+                                      const GemmShape s, int act) {
+  const int q = blockIdx.x;
+  const TileCoord c = tile_coord3(s, s.sk_first + q, 0);
+  const float* tile = ws + static_cast<long long>(q) * (2 * kBM) * kBN3;
+  for (int i = threadIdx.x; i < 16 * (kBN3 / 4); i += blockDim.x) {
+    const int r = blockIdx.y * 16 + i / (kBN3 / 4);
+    const int col = (i % (kBN3 / 4)) * 4;
+    const int row = c.m0 + r;
+    if (row >= s.M || c.n0 + col >= s.N) continue;
+    const float4 v = *reinterpret_cast<const float4*>(tile + r * kBN3 + col);
+    const float f[4] = {v.x, v.y, v.z, v.w};
+    OutT* dst = C + row * ldc + c.n0 + col;
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    if (col + i >= N) break;
-    const float x = act == kActSilu ? silu_f(f[i]) : f[i];
-    StoreOut<OutT>::store1(dst + i, x);
+    for (int j = 0; j < 4; ++j) {
+      if (c.n0 + col + j >= s.N) break;
+      StoreOut<OutT>::store1(dst + j, act == kActSilu ? silu_f(f[j]) : f[j]);
+    }
   }
 }
 
-long long gemm_streamk_ws_ld(const GemmArgs& g) { return (static_cast<long long>(g.N) + 3) / 4 * 4; }
-
-int gemm_streamk_iters(const GemmArgs& g, int mode) {
-  // Only on request: measured on B200 (training weight-gradient shapes, K =
-  // 65536), the fp32 TMA reduce-adds of the partial tiles (about 3.3 TB/s over
-  // the GPU, not overlapped with the MMAs because the accumulator is single
-  // buffered) cost more than the balanced waves gain: 8192 x 2048 took 1.91 ms
-  // against 1.43 ms in whole tiles, 2048 x 2048 0.46 ms against 0.43 ms on the
-  // 256 x 256 pair kernel.
-  if (mode <= 0 || g.batch != 1 || g.M < 2 * kBM || g.N < kBN3 || g.num_sms < 2) return 0;
+bool gemm_streamk_plan(const GemmArgs& g, int mode, StreamKPlan* plan) {
+  // On request (mode 1) every tile is split; by default (mode -1) only the
+  // partial last wave of a long-K GEMM, when the SM pairs it leaves idle cost
+  // more than the tail's fp32 round trip.  Measured on B200: splitting all
+  // tiles of 8192 x 2048 x 65536 took 1.91 ms against 1.43 ms in whole tiles
+  // (each segment's fp32 reduce-adds, about 3.3 TB/s over the GPU, are not
+  // hidden behind MMAs with the single-buffered wide accumulator), so the full
+  // waves stay whole tiles.
+  if (mode == 0 || g.batch != 1 || g.M < 2 * kBM || g.N < kBN3 || g.num_sms < 2) return false;
   const long long pair_tiles = static_cast<long long>((g.M + 2 * kBM - 1) / (2 * kBM)) * ((g.N + kBN3 - 1) / kBN3);
   const long long nkb = (g.K + kBK - 1) / kBK;
   const long long clusters = g.num_sms / 2;
-  const long long per = (pair_tiles * nkb + clusters - 1) / clusters;
-  return per > 0 && per <= 0x7fffffffLL ? static_cast<int>(per) : 0;
+  long long whole = 0;
+  if (mode < 0) {
+    const long long tail = pair_tiles % clusters;
+    // whole waves first; an idle SM pair in the last wave loses a tile's worth of
+    // K blocks, a tail segment costs about 60 blocks of reduce-add and finish
+    if (pair_tiles < clusters || tail == 0 || nkb <= 32) return false;
+    if (static_cast<double>(clusters - tail) / clusters * nkb < 60.0) return false;
+    whole = pair_tiles - tail;
+  }
+  if ((pair_tiles - whole) * (2 * kBM) * kBN3 * 4 > (1LL << 30)) return false;  // workspace above 1 GiB
+  const long long work = (pair_tiles - whole) * nkb;
+  const long long per = (work + clusters - 1) / clusters;
+  if (per <= 0 || per > 0x7fffffffLL) return false;
+  plan->sk_first = static_cast<int>(whole);
+  plan->sk_iters = static_cast<int>(per);
+  plan->tail_tiles = static_cast<int>(pair_tiles - whole);
+  plan->clusters = static_cast<int>(whole + (work + per - 1) / per);
+  return true;
 }
 
-int gemm_launch_streamk(const GemmArgs& g, int sk_iters, float* ws, cudaStream_t stream) {
-  if (check_gemm_args(g) || sk_iters <= 0 || g.batch != 1) return -1;
-  if ((reinterpret_cast<uintptr_t>(ws) & 15) != 0) return -2;
-  CUtensorMap ma, mb;
+long long gemm_streamk_ws_elems(const StreamKPlan& plan) {
+  return static_cast<long long>(plan.tail_tiles) * (2 * kBM) * kBN3;
+}
+
+template <typename OutT>
+static int launch_streamk(const GemmArgs& g, const StreamKPlan& plan, float* ws, cudaStream_t stream) {
+  CUtensorMap ma, mb, mc, mw;
   make_operand_maps(g, &ma, &mb, true);
   GemmShape s = make_shape(g);
   s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
@@ -319,12 +348,26 @@ int gemm_launch_streamk(const GemmArgs& g, int sk_iters, float* ws, cudaStream_t
   s.group_m = g.group_m > 0 ? g.group_m : 16;
   s.pair = 1;
   s.split = 0;
-  s.sk_iters = sk_iters;
-  const long long ldw = gemm_streamk_ws_ld(g);
-  const CUtensorMap mw = make_tmap_3d(ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.N, g.M, 1, ldw, ldw * g.M, 32, 32);
-  cudaError_t e = cudaMemsetAsync(ws, 0, static_cast<size_t>(ldw) * g.M * sizeof(float), stream);
+  s.sk_iters = plan.sk_iters;
+  s.sk_first = plan.sk_first;
+  StreamKEpilogue<OutT> epi;
+  epi.sk_first = plan.sk_first;
+  epi.store.C = reinterpret_cast<OutT*>(g.C);
+  epi.store.ldc = g.ldc;
+  epi.store.batch_stride = g.c_batch_stride;
+  epi.store.act = g.act;
+  epi.store.trans = 0;
+  const int esz = sizeof(OutT);
+  epi.store.vec_ok = ((reinterpret_cast<uintptr_t>(g.C) & 15) == 0) && ((g.ldc * esz) % 16 == 0);
+  epi.store.tma = make_output_map(g, false, &mc) ? 1 : 0;
+  const uint64_t wdims[3] = {static_cast<uint64_t>(kBN3), static_cast<uint64_t>(2 * kBM),
+                             static_cast<uint64_t>(plan.tail_tiles)};
+  const uint64_t wstrides[2] = {static_cast<uint64_t>(kBN3) * 4, static_cast<uint64_t>(2 * kBM) * kBN3 * 4};
+  const uint32_t wbox[3] = {32, 32, 1};
+  mw = make_tmap_nd(ws, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, wdims, wstrides, wbox);
+  cudaError_t e = cudaMemsetAsync(ws, 0, static_cast<size_t>(gemm_streamk_ws_elems(plan)) * sizeof(float), stream);
   if (e != cudaSuccess) return static_cast<int>(e);
-  auto kernel = gemm_tc3_kernel<ReduceF32Epilogue>;
+  auto kernel = gemm_tc3_kernel<StreamKEpilogue<OutT>>;
   static unsigned long long attr_set = 0;
   int dev = 0;
   cudaGetDevice(&dev);
@@ -332,11 +375,8 @@ int gemm_launch_streamk(const GemmArgs& g, int sk_iters, float* ws, cudaStream_t
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3Bytes);
     attr_set |= 1ull << dev;
   }
-  const long long total = static_cast<long long>(s.num_m) * s.num_n * s.num_kb;
-  const int clusters = static_cast<int>((total + sk_iters - 1) / sk_iters);
-  if (clusters > g.num_sms / 2) return -3;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(2 * clusters);
+  cfg.gridDim = dim3(2 * plan.clusters);
   cfg.blockDim = dim3(kThreads3);
   cfg.dynamicSmemBytes = kSmem3Bytes;
   cfg.stream = stream;
@@ -347,24 +387,25 @@ int gemm_launch_streamk(const GemmArgs& g, int sk_iters, float* ws, cudaStream_t
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mw, s, ReduceF32Epilogue{}, NoGather{});
+  e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, mw, s, epi, NoGather{});
   if (e != cudaSuccess) return static_cast<int>(e);
-  const long long threads = static_cast<long long>(g.M) * ((g.N + 3) / 4);
-  const unsigned blocks = static_cast<unsigned>((threads + 255) / 256);
+  streamk_finish_kernel<OutT><<<dim3(plan.tail_tiles, (2 * kBM) / 16), 256, 0, stream>>>(
+      ws, reinterpret_cast<OutT*>(g.C), g.ldc, s, g.act);
+  return static_cast<int>(cudaGetLastError());
+}
+
+int gemm_launch_streamk(const GemmArgs& g, const StreamKPlan& plan, float* ws, cudaStream_t stream) {
+  if (check_gemm_args(g) || plan.sk_iters <= 0 || plan.tail_tiles <= 0 || g.batch != 1) return -1;
+  if ((reinterpret_cast<uintptr_t>(ws) & 15) != 0) return -2;
+  if (plan.clusters - plan.sk_first > g.num_sms / 2) return -3;
   switch (g.out_dtype) {
     case kDtypeBF16:
-      streamk_finish_kernel<__nv_bfloat16><<<blocks, 256, 0, stream>>>(
-          ws, ldw, reinterpret_cast<__nv_bfloat16*>(g.C), g.ldc, g.M, g.N, g.act);
-      break;
+      return launch_streamk<__nv_bfloat16>(g, plan, ws, stream);
     case kDtypeF16:
-      streamk_finish_kernel<__half><<<blocks, 256, 0, stream>>>(ws, ldw, reinterpret_cast<__half*>(g.C), g.ldc, g.M,
-                                                                  g.N, g.act);
-      break;
+      return launch_streamk<__half>(g, plan, ws, stream);
     default:
-      streamk_finish_kernel<float><<<blocks, 256, 0, stream>>>(ws, ldw, reinterpret_cast<float*>(g.C), g.ldc, g.M,
-                                                                 g.N, g.act);
+      return launch_streamk<float>(g, plan, ws, stream);
   }
-  return static_cast<int>(cudaGetLastError());
 }
 
 int gemm_launch(const GemmArgs& g, cudaStream_t stream) {

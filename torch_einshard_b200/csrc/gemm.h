@@ -49,14 +49,21 @@ GemmShape make_shape_pair(const GemmArgs& g);
 // Output tensor map of the TMA-store epilogues; false (map zeroed) when C does not qualify.
 bool make_output_map(const GemmArgs& g, bool trans, CUtensorMap* mc);
 
-// Stream-K on the wide 2-SM kernel (batch 1): every SM pair takes the same
-// number of K blocks of the tile-major K-block sequence; partial tiles are
-// reduce-added in fp32 into a workspace ws[M][gemm_streamk_ws_ld(g)], which a
-// finishing pass converts (with the activation) into C.
-// gemm_streamk_iters: K blocks per cluster, or 0 when whole tiles are better
-// (mode 1: where the shape allows it; 0 or -1: never, the measured default).
-int gemm_streamk_iters(const GemmArgs& g, int mode);
-long long gemm_streamk_ws_ld(const GemmArgs& g);
-int gemm_launch_streamk(const GemmArgs& g, int sk_iters, float* ws, cudaStream_t stream);
+// Stream-K tail on the wide 2-SM kernel (batch 1): pair tiles [0, sk_first)
+// run whole, one per cluster; the K blocks of the other tail_tiles are split
+// evenly over the remaining clusters, whose fp32 partials are reduce-added into
+// a workspace of gemm_streamk_ws_elems floats and converted (with the
+// activation) into C by a finishing pass.
+struct StreamKPlan {
+  int sk_first = 0;    // whole pair tiles
+  int sk_iters = 0;    // K blocks per tail cluster
+  int tail_tiles = 0;  // pair tiles split over the tail clusters
+  int clusters = 0;    // clusters launched (whole + tail)
+};
+// mode -1: split only the partial last wave of long-K GEMMs (default);
+// 1: split every tile; 0: never.  False when whole tiles are used.
+bool gemm_streamk_plan(const GemmArgs& g, int mode, StreamKPlan* plan);
+long long gemm_streamk_ws_elems(const StreamKPlan& plan);
+int gemm_launch_streamk(const GemmArgs& g, const StreamKPlan& plan, float* ws, cudaStream_t stream);
 
 }  // namespace es

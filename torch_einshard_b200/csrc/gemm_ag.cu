@@ -183,7 +183,9 @@ int gemm_allgather_launch(const GemmArgs& g, const CommDev& comm, void* xfull, i
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, s, epi, ag));
+  CUtensorMap mw;  // no stream-K workspace
+  memset(&mw, 0, sizeof(mw));
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, mw, s, epi, ag));
 }
 
 }  // namespace es

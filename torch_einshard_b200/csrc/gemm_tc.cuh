@@ -56,7 +56,8 @@ struct GemmShape {
   int* err;
   unsigned long long* prof;  // optional: per-CTA wait-cycle counters (see gemm_tc3.cuh), null when off
   int sleep_ns;              // wide kernel: epilogue back-off between accumulator polls (0: spin)
-  int sk_iters = 0;          // wide kernel: > 0 stream-K, K blocks per cluster (0: whole tiles per cluster)
+  int sk_iters = 0;          // wide kernel: > 0 stream-K tail, K blocks per tail cluster (0: whole tiles only)
+  int sk_first = 0;          // wide kernel with sk_iters: pair tiles [0, sk_first) whole, the rest split
 };
 
 struct TileCoord {
@@ -104,6 +105,7 @@ struct EpiTile {
   int lane;
   const CUtensorMap* tmc = nullptr;  // output map for TMA stores (kernels that provide one)
   uint8_t* stage = nullptr;          // this warp's 4 KB staging buffer (1024-byte aligned)
+  const CUtensorMap* tmw = nullptr;  // fp32 workspace map of stream-K partial tiles (wide kernel)
 };
 
 // Operand loads of one K block for the plain GEMM: A and B tiles by TMA from

@@ -18,12 +18,14 @@
 // 2..9 epilogue.  Barriers as in gemm_tc2.cuh; tempty counts the 16 epilogue
 // warps of the pair.
 //
-// Stream-K (shp.sk_iters > 0): the K blocks of all tiles form one sequence
-// (tile-major) and cluster c takes blocks [c * sk_iters, (c + 1) * sk_iters),
-// i.e. whole tiles and at most two partial ones, so every SM pair gets the
-// same work however few tiles there are.  A segment (one tile's K-block range)
-// accumulates in TMEM from zero and its epilogue adds the fp32 partial into a
-// zero-initialised workspace (ReduceF32Epilogue: TMA reduce-add stores).
+// Stream-K tail (shp.sk_iters > 0): pair tiles [0, sk_first) are whole tiles,
+// one per cluster (the full waves); the K blocks of the remaining tiles (the
+// partial last wave) form one tile-major sequence that clusters sk_first,
+// sk_first + 1, ... take in equal slices of sk_iters blocks, so the last wave
+// keeps every SM pair busy.  A tail segment accumulates in TMEM from zero and
+// its epilogue adds the fp32 partial into a zero-initialised workspace
+// [tail tile][256][512] (TMA reduce-add through tmW); a finishing pass converts
+// the tail tiles.  sk_first = 0 splits every tile.
 #pragma once
 
 #include "gemm_tc.cuh"
@@ -106,9 +108,16 @@ struct SegIter {
 __device__ __forceinline__ SegIter seg_begin(const GemmShape& s, int cluster) {
   SegIter it;
   if (s.sk_iters > 0) {
-    const long long total = static_cast<long long>(s.num_m) * s.num_n * s.batch * s.num_kb;
-    it.g = min(total, static_cast<long long>(cluster) * s.sk_iters);
-    it.end = min(total, it.g + s.sk_iters);
+    const long long nkb = s.num_kb;
+    const long long total = static_cast<long long>(s.num_m) * s.num_n * s.batch * nkb;
+    if (cluster < s.sk_first) {
+      it.g = static_cast<long long>(cluster) * nkb;
+      it.end = it.g + nkb;
+    } else {
+      it.g = min(total, static_cast<long long>(s.sk_first) * nkb +
+                            static_cast<long long>(cluster - s.sk_first) * s.sk_iters);
+      it.end = min(total, it.g + s.sk_iters);
+    }
   }
   return it;
 }
@@ -154,8 +163,8 @@ struct NoGather {
 template <class Epi, class Gather = NoGather>
 __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
     gemm_tc3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, const GemmShape shp, Epi epi,
-                    const Gather gather = Gather()) {
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmW,
+                    const GemmShape shp, Epi epi, const Gather gather = Gather()) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -339,6 +348,7 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
       et.q = q;
       et.lane = lane;
       et.tmc = &tmC;
+      et.tmw = &tmW;
       et.stage = out_stage + (warp - 2) * kStage3Out;
       const bool ok = et.c.n0 < shp.N ? epi.tile(et, shp, abort_flag) : true;
       tc_fence_before();
