@@ -681,6 +681,30 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("get_wait_timeout_ns", []() { return static_cast<int64_t>(g_wait_timeout_ns); });
   m.def("set_gemm_streamk", [](int64_t v) { g_streamk = static_cast<int>(v); },
         "stream-K wide GEMM: -1 split the partial last wave (default), 1 split every tile, 0 never");
+  m.def("gemm_plan",
+        [](int64_t M, int64_t N, int64_t K, int64_t batch, bool a_mn, bool b_mn, int64_t num_sms) {
+          es::GemmArgs g;
+          g.M = static_cast<int>(M);
+          g.N = static_cast<int>(N);
+          g.K = static_cast<int>(K);
+          g.batch = static_cast<int>(batch);
+          g.a_mn = a_mn ? 1 : 0;
+          g.b_mn = b_mn ? 1 : 0;
+          g.num_sms = static_cast<int>(num_sms);
+          g.pair = g_pair_mode;
+          g.persistent = g_persistent;
+          const es::GemmPlanInfo info = es::gemm_plan_info(g, g_streamk);
+          py::dict d;
+          d["kernel"] = info.kernel;
+          d["swapped"] = info.swapped;
+          d["persistent"] = info.persistent;
+          d["sk_first"] = info.sk_first;
+          d["sk_iters"] = info.sk_iters;
+          d["tail_tiles"] = info.tail_tiles;
+          d["clusters"] = info.clusters;
+          return d;
+        },
+        "kernel choice for a GEMM shape (no launch; runs without a GPU)");
   m.def("set_gemm_sleep_ns", [](int64_t v) { g_sleep_ns = static_cast<int>(v); }, "wide-kernel epilogue back-off ns");
   m.def("set_tma_l2_promotion", [](int64_t v) { es::tma_l2_promotion() = static_cast<int>(v); },
         "L2 promotion of TMA loads: 0 none, 1 64B, 2 128B, 3 256B (tuning)");

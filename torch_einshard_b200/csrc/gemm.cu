@@ -408,6 +408,27 @@ int gemm_launch_streamk(const GemmArgs& g, const StreamKPlan& plan, float* ws, c
   }
 }
 
+GemmPlanInfo gemm_plan_info(const GemmArgs& g0, int streamk_mode) {
+  GemmPlanInfo info;
+  info.swapped = want_swap(g0) ? 1 : 0;
+  const GemmArgs g = info.swapped ? swapped(g0) : g0;
+  StreamKPlan plan;
+  if ((g0.pair < 0 || streamk_mode > 0) && gemm_streamk_plan(g0, streamk_mode, &plan)) {
+    info.kernel = 2;
+    info.swapped = 0;
+    info.sk_first = plan.sk_first;
+    info.sk_iters = plan.sk_iters;
+    info.tail_tiles = plan.tail_tiles;
+    info.clusters = plan.clusters;
+    return info;
+  }
+  info.kernel = pick_kernel(g);
+  if (info.kernel == 2) {
+    info.persistent = g.persistent > 0 || (g.persistent < 0 && (g.K + kBK - 1) / kBK <= 32) ? 1 : 0;
+  }
+  return info;
+}
+
 int gemm_launch(const GemmArgs& g, cudaStream_t stream) {
   if (check_gemm_args(g)) return -1;
   switch (g.out_dtype) {

@@ -66,4 +66,13 @@ bool gemm_streamk_plan(const GemmArgs& g, int mode, StreamKPlan* plan);
 long long gemm_streamk_ws_elems(const StreamKPlan& plan);
 int gemm_launch_streamk(const GemmArgs& g, const StreamKPlan& plan, float* ws, cudaStream_t stream);
 
+// Host-side plan of a GEMM call (no launch): the kernel run_gemm would use
+// (0 1-SM, 1 2-SM, 2 wide), operands swapped for a narrow N, wide-grid
+// persistence and the stream-K tail.  For tests and diagnostics.
+struct GemmPlanInfo {
+  int kernel = 0, swapped = 0, persistent = 0;
+  int sk_first = 0, sk_iters = 0, tail_tiles = 0, clusters = 0;
+};
+GemmPlanInfo gemm_plan_info(const GemmArgs& g, int streamk_mode);
+
 }  // namespace es
