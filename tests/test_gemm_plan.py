@@ -31,8 +31,15 @@ def test_partial_last_wave_gets_a_stream_k_tail():
     assert p["sk_first"] == 222 and p["tail_tiles"] == 2
     assert p["clusters"] - p["sk_first"] <= SMS // 2
     assert p["sk_iters"] * (p["clusters"] - p["sk_first"]) >= 2 * 512
-    q = plan(8192, 2048, 65536, True, True)  # transformer MLP weight gradient: 128 pair tiles
-    assert q["sk_first"] == 74 and q["tail_tiles"] == 54
+    q = plan(28672, 8192, 32768, True, True)  # the same at tp = 1: 1792 pair tiles, 16 left over
+    assert q["sk_first"] == 1776 and q["tail_tiles"] == 16
+
+
+def test_large_remainder_stays_whole_tiles():
+    # transformer MLP weight gradient: 128 pair tiles, 54 left over (the tail
+    # phase would stream from DRAM: measured slower)
+    p = plan(8192, 2048, 65536, True, True)
+    assert p["kernel"] == 2 and p["tail_tiles"] == 0
 
 
 def test_underfilled_long_k_uses_the_pair_kernel():

@@ -28,7 +28,8 @@ def _check(a, b, out_dtype=None, act=None):
     c = gemm.native_bmm(a, b, out_dtype=out_dtype, act=act)
     torch.cuda.synchronize()
     _native.check_errors(a.device)
-    assert _native.require().launch_count() - before == 2  # the stream-K GEMM and its finishing pass
+    # the tail kernel and its finishing pass, plus the whole-tile launch when there are full waves
+    assert _native.require().launch_count() - before in (2, 3)
     ref = torch.matmul(a.float(), b.float())
     if act == "silu":
         ref = torch.nn.functional.silu(ref)
@@ -72,8 +73,8 @@ def test_streamk_weight_gradient_shape(streamk):
 
 
 def test_streamk_tail_by_default():
-    """80 pair tiles for 74 SM pairs and 72 K blocks: one whole wave, the
-    other 6 tiles split over all pairs (ragged M and N)."""
+    """80 pair tiles for 74 SM pairs and 72 K blocks: one whole wave (a plain
+    launch), the other 6 tiles split over all pairs (ragged M and N)."""
     mod = _native.require()
     mod.set_gemm_pair_mode(-1)
     mod.set_gemm_streamk(-1)

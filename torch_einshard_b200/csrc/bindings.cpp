@@ -83,7 +83,8 @@ void run_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, int64_t
     at::Tensor ws = at::empty({es::gemm_streamk_ws_elems(plan)}, a.options().dtype(at::kFloat));
     const int rc = es::gemm_launch_streamk(g, plan, ws.data_ptr<float>(), at::cuda::getCurrentCUDAStream());
     TORCH_CHECK(rc == 0, "einshard native gemm: stream-K launch failed (", rc, ")");
-    g_launches.fetch_add(2, std::memory_order_relaxed);
+    // whole tiles (when any), the tail and the finishing pass
+    g_launches.fetch_add(plan.sk_first > 0 ? 3 : 2, std::memory_order_relaxed);
     return;
   }
   const int rc = es::gemm_launch(g, at::cuda::getCurrentCUDAStream());

@@ -154,8 +154,10 @@ bool make_output_map(const GemmArgs& g, bool trans, CUtensorMap* mc) {
   return true;
 }
 
+// tile_limit > 0: only pair tiles [0, tile_limit) (the whole tiles before a stream-K tail).
 template <class Epi>
-int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, Epi epi, cudaStream_t stream) {
+int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, Epi epi, cudaStream_t stream,
+                int tile_limit = 0) {
   CUtensorMap mc;
   epi.tma = make_output_map(g, epi.trans != 0, &mc) ? 1 : 0;
   GemmShape s = make_shape(g);
@@ -163,7 +165,8 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
   s.num_n = (g.N + kBN3 - 1) / kBN3;
   s.group_m = g.group_m > 0 ? g.group_m : 16;
   s.pair = 1;
-  s.split = g.split;
+  s.split = tile_limit > 0 ? 0 : g.split;
+  s.sk_first = tile_limit;
   auto kernel = gemm_tc3_kernel<Epi>;
   static unsigned long long attr_set = 0;
   int dev = 0;
@@ -172,7 +175,7 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3Bytes);
     attr_set |= 1ull << dev;
   }
-  const int pairs = s.num_m * s.num_n * s.batch;
+  const int pairs = tile_limit > 0 ? tile_limit : s.num_m * s.num_n * s.batch;
   int clusters = g.num_sms / 2;
   // One pair tile per cluster held higher clocks under the power cap for long K;
   // with K <= 2048 the per-CTA setup and the unhidden pipeline fill dominate and
@@ -319,7 +322,11 @@ bool gemm_streamk_plan(const GemmArgs& g, int mode, StreamKPlan* plan) {
     const long long tail = pair_tiles % clusters;
     // whole waves first; an idle SM pair in the last wave loses a tile's worth of
     // K blocks, a tail segment costs about 60 blocks of reduce-add and finish
-    if (pair_tiles < clusters || tail == 0 || nkb <= 32) return false;
+    // The tail segments read K ranges of their tiles that no other running
+    // cluster shares, so the tail phase streams ~96 KB per K block from DRAM:
+    // worth it only for a small remainder (224 tiles at tp = 8, 2 left over:
+    // 1.17 ms against 1.41 ms; 128 tiles, 54 left over: 1.58 against 1.40 ms).
+    if (pair_tiles < clusters || tail == 0 || nkb <= 32 || 3 * tail > clusters) return false;
     if (static_cast<double>(clusters - tail) / clusters * nkb < 60.0) return false;
     whole = pair_tiles - tail;
   }
@@ -387,6 +394,13 @@ static int launch_streamk(const GemmArgs& g, const StreamKPlan& plan, float* ws,
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (plan.sk_first > 0) {
+    // the full waves: the plain wide kernel on the first sk_first tiles
+    const int rc = launch_wide(ma, mb, g, epi.store, stream, plan.sk_first);
+    if (rc != 0) return rc;
+  }
+  s.sk_cluster0 = plan.sk_first;
+  cfg.gridDim = dim3(2 * (plan.clusters - plan.sk_first));
   e = cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, mw, s, epi, NoGather{});
   if (e != cudaSuccess) return static_cast<int>(e);
   streamk_finish_kernel<OutT><<<dim3(plan.tail_tiles, (2 * kBM) / 16), 256, 0, stream>>>(

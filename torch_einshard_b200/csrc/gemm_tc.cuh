@@ -57,7 +57,9 @@ struct GemmShape {
   unsigned long long* prof;  // optional: per-CTA wait-cycle counters (see gemm_tc3.cuh), null when off
   int sleep_ns;              // wide kernel: epilogue back-off between accumulator polls (0: spin)
   int sk_iters = 0;          // wide kernel: > 0 stream-K tail, K blocks per tail cluster (0: whole tiles only)
-  int sk_first = 0;          // wide kernel with sk_iters: pair tiles [0, sk_first) whole, the rest split
+  int sk_first = 0;          // wide kernel: pair tiles [0, sk_first) whole, the rest split (with sk_iters);
+                             // without sk_iters a nonzero sk_first limits the launch to those whole tiles
+  int sk_cluster0 = 0;       // wide kernel, stream-K: cluster id of this launch's first cluster
 };
 
 struct TileCoord {

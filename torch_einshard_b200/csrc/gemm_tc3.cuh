@@ -25,7 +25,9 @@
 // keeps every SM pair busy.  A tail segment accumulates in TMEM from zero and
 // its epilogue adds the fp32 partial into a zero-initialised workspace
 // [tail tile][256][512] (TMA reduce-add through tmW); a finishing pass converts
-// the tail tiles.  sk_first = 0 splits every tile.
+// the tail tiles.  sk_first = 0 splits every tile.  A launch may hold only the
+// tail clusters (sk_cluster0 = sk_first), the whole tiles running before it in
+// a plain launch limited to sk_first tiles.
 #pragma once
 
 #include "gemm_tc.cuh"
@@ -79,7 +81,7 @@ __device__ __forceinline__ bool pair_tile_at(const GemmShape& s, int cluster, in
                                              TileCoord* out) {
   if (s.split == 0 || (nclusters & 1) || s.num_m < 2) {
     const int p = cluster + i * nclusters;
-    if (p >= s.num_m * s.num_n * s.batch) return false;
+    if (p >= (s.sk_first > 0 ? s.sk_first : s.num_m * s.num_n * s.batch)) return false;
     *out = tile_coord3(s, p, rank);
     return true;
   }
@@ -110,12 +112,13 @@ __device__ __forceinline__ SegIter seg_begin(const GemmShape& s, int cluster) {
   if (s.sk_iters > 0) {
     const long long nkb = s.num_kb;
     const long long total = static_cast<long long>(s.num_m) * s.num_n * s.batch * nkb;
-    if (cluster < s.sk_first) {
-      it.g = static_cast<long long>(cluster) * nkb;
+    const int cl = cluster + s.sk_cluster0;
+    if (cl < s.sk_first) {
+      it.g = static_cast<long long>(cl) * nkb;
       it.end = it.g + nkb;
     } else {
       it.g = min(total, static_cast<long long>(s.sk_first) * nkb +
-                            static_cast<long long>(cluster - s.sk_first) * s.sk_iters);
+                            static_cast<long long>(cl - s.sk_first) * s.sk_iters);
       it.end = min(total, it.g + s.sk_iters);
     }
   }
