@@ -18,7 +18,7 @@ import argparse
 import json
 import os
 import subprocess
-import tempfile
+import threading
 import sys
 import time
 from datetime import timedelta
@@ -57,7 +57,11 @@ def init_dist(args):
 
 
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+    """Samples SM clocks and throttle reasons with nvidia-smi (every 100 ms) and
+    keeps the samples that arrive during the timed region (host-stamped on
+    arrival).  Started before the warm-up so the sampler is running when the
+    timed region begins; a region shorter than the interval keeps the sample
+    nearest to it."""
 
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -66,18 +70,27 @@ class ClockSampler:
     def __init__(self, devices):
         self.devices = set(devices)
         self.proc = None
-        # raw samples (one CSV per process); EINSHARD_CLOCKS_DIR keeps them somewhere else
-        self.path = os.path.join(os.environ.get("EINSHARD_CLOCKS_DIR", tempfile.gettempdir()),
-                                 f"einshard_clocks_{os.getpid()}.csv")
+        self.lines = []
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.file = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
         except Exception:  # noqa: BLE001 - clocks are best-effort metadata
             self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line))
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
 
     def stop(self):
         if self.proc is None:
@@ -87,25 +100,40 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        self.file.close()
-        sm, mx, reasons = [], [], set()
-        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        with open(self.path) as f:
-            for line in f:
-                cols = [c.strip() for c in line.split(",")]
-                if len(cols) < 9 or not cols[0].isdigit() or int(cols[0]) not in self.devices:
-                    continue
-                try:
-                    sm.append(float(cols[1]))
-                    mx.append(float(cols[2]))
-                except ValueError:
-                    continue
-                for name, value in zip(names[1:], cols[5:9]):
-                    if value.lower() == "active":
-                        reasons.add(name)
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        self.thread.join(timeout=5)
+        rows = []
+        for stamp, line in self.lines:
+            cols = [c.strip() for c in line.split(",")]
+            if len(cols) < 9 or not cols[0].isdigit() or int(cols[0]) not in self.devices:
+                continue
+            try:
+                rows.append((stamp, float(cols[1]), float(cols[2]), cols[5:9]))
+            except ValueError:
+                continue
+        t0, t1 = self.t0 or 0.0, self.t1 or time.time()
+        inside = [r for r in rows if t0 <= r[0] <= t1 + 0.1]
+        if not inside and rows:
+            mid = 0.5 * (t0 + t1)
+            nearest = min(abs(r[0] - mid) for r in rows)
+            inside = [r for r in rows if abs(r[0] - mid) == nearest]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = {name for r in inside for name, value in zip(names, r[3]) if value.lower() == "active"}
+        sm = sorted(r[1] for r in inside)
+        out = {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(r[2] for r in inside) if inside else None,
+               "reasons": sorted(reasons), "samples": len(sm)}
+        keep = os.environ.get("EINSHARD_CLOCKS_DIR")
+        if keep:
+            with open(os.path.join(keep, f"einshard_clocks_{os.getpid()}.csv"), "w") as f:
+                f.writelines(f"{stamp:.3f},{line}" for stamp, line in self.lines)
+        return out
+
+
+def visible_gpu_indices(world):
+    """nvidia-smi indices of this job's GPUs (CUDA_VISIBLE_DEVICES when it lists indices)."""
+    listed = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    if listed and all(v.isdigit() for v in listed):
+        return [int(v) for v in listed[:world]]
+    return list(range(world))
 
 
 def max_over_ranks(value):
@@ -210,14 +238,18 @@ def main():
         y.backward(dy)
 
     # ---------------------------------------------------------------- device-timed
+    sampler = ClockSampler(visible_gpu_indices(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     launches0 = native_launches(es)
-    sampler = ClockSampler(range(world)) if rank == 0 else None
     if sampler:
-        sampler.start()
+        sampler.mark_start()
     ms = timed(step, args.steps)
+    if sampler:
+        sampler.mark_end()
     clocks = sampler.stop() if sampler else None
     launches = native_launches(es) - launches0
     flops = 12.0 * b * n * c * h  # 2 forward GEMMs + 4 backward GEMMs of 2*b*n*c*h each

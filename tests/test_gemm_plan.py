@@ -31,8 +31,12 @@ def test_partial_last_wave_gets_a_stream_k_tail():
     assert p["sk_first"] == 222 and p["tail_tiles"] == 2
     assert p["clusters"] - p["sk_first"] <= SMS // 2
     assert p["sk_iters"] * (p["clusters"] - p["sk_first"]) >= 2 * 512
-    q = plan(28672, 8192, 32768, True, True)  # the same at tp = 1: 1792 pair tiles, 16 left over
-    assert q["sk_first"] == 1776 and q["tail_tiles"] == 16
+    q = plan(14336, 8192, 32768, True, True)  # the same at tp = 2: 896 pair tiles, 8 left over
+    assert q["sk_first"] == 888 and q["tail_tiles"] == 8
+
+
+def test_remainders_above_a_ninth_of_a_wave_stay_whole_tiles():
+    assert plan(28672, 8192, 32768, True, True)["tail_tiles"] == 0   # tp = 1: 16 left over
 
 
 def test_large_remainder_stays_whole_tiles():

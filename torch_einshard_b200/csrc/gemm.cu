@@ -322,11 +322,11 @@ bool gemm_streamk_plan(const GemmArgs& g, int mode, StreamKPlan* plan) {
     const long long tail = pair_tiles % clusters;
     // whole waves first; an idle SM pair in the last wave loses a tile's worth of
     // K blocks, a tail segment costs about 60 blocks of reduce-add and finish
-    // The tail segments read K ranges of their tiles that no other running
-    // cluster shares, so the tail phase streams ~96 KB per K block from DRAM:
-    // worth it only for a small remainder (224 tiles at tp = 8, 2 left over:
-    // 1.17 ms against 1.41 ms; 128 tiles, 54 left over: 1.58 against 1.40 ms).
-    if (pair_tiles < clusters || tail == 0 || nkb <= 32 || 3 * tail > clusters) return false;
+    // Worth it only for a small remainder: 224 tiles at tp = 8, 2 left over:
+    // 1.17-1.19 ms against 1.41 ms whole; 1792 tiles, 16 left over: 11.2-12.2
+    // against 11.0-11.2 ms; 128 tiles, 54 left over: 1.58 against 1.40 ms (the
+    // tail segments read K ranges no other running cluster shares).
+    if (pair_tiles < clusters || tail == 0 || nkb <= 32 || 9 * tail > clusters) return false;
     if (static_cast<double>(clusters - tail) / clusters * nkb < 60.0) return false;
     whole = pair_tiles - tail;
   }
