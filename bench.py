@@ -39,6 +39,9 @@ def parse():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["native", "reference"], default="native")
     p.add_argument("--small", action="store_true", help="reduced shapes for smoke runs (not a bench number)")
+    p.add_argument("--kernel-table", type=int, default=0, metavar="N",
+                   help="after the timed steps, profile one more step (torch.profiler) and print the N kernels "
+                        "with the most device time to stderr (a breakdown, not a bench number)")
     return p.parse_args()
 
 
@@ -254,6 +257,15 @@ def main():
     launches = native_launches(es) - launches0
     flops = 12.0 * b * n * c * h  # 2 forward GEMMs + 4 backward GEMMs of 2*b*n*c*h each
     value = flops * args.steps / (ms / 1e3) / 1e12
+
+    if args.kernel_table:
+        from torch.profiler import ProfilerActivity, profile
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+        if rank == 0:
+            print(prof.key_averages().table(sort_by="cuda_time_total", row_limit=args.kernel_table,
+                                            max_name_column_width=90), file=sys.stderr, flush=True)
 
     # ---------------------------------------------------------------- end to end
     host_x = torch.randn(b, n, c, dtype=torch.bfloat16).pin_memory()
