@@ -29,8 +29,6 @@ __all__ = ["Communicator", "activate", "deactivate", "communicator_for_group"]
 _DEFAULT_MB = int(os.environ.get("EINSHARD_SYMM_MB", "1280"))
 # 512 MiB all-reduce at 8 ranks on B200: this two-shot kernel 2.19 ms, NCCL 1.34 ms.
 _NCCL_AR_MIN_BYTES = int(os.environ.get("EINSHARD_NCCL_AR_MIN_BYTES", str(1 << 20)))
-# all-reduce + scale (the DDP bucket reduction) stays one native kernel on 2-rank groups up to this size
-_NATIVE_SCALED_AR_MAX_BYTES = int(os.environ.get("EINSHARD_NATIVE_SCALED_AR_MAX_BYTES", str(64 << 20)))
 _COMMS = {}
 _REJECTED = set()
 _LARGE = {}  # group key -> larger communicators created on demand (kept until deactivate)
@@ -159,12 +157,11 @@ class Communicator:
         nbytes = t.numel() * t.element_size()
         if nbytes == 0:
             return True
-        if nbytes >= _NCCL_AR_MIN_BYTES and not (scale != 1.0 and self.size == 2
-                                                 and nbytes <= _NATIVE_SCALED_AR_MAX_BYTES):
-            # measured (512 MiB bf16): NCCL 1.28-1.38 ms against 1.48-1.53 ms native on 2 ranks,
-            # 1.34 against 2.19 ms on 8; the native kernel keeps the latency-bound small buffers
-            # and, on 2 ranks, the DDP buckets (reduce and 1/dp scale in one pass, no separate
-            # scaling kernel over the bucket)
+        if nbytes >= _NCCL_AR_MIN_BYTES:
+            # measured on 2 ranks: NCCL 0.025 / 0.056 / 0.28 / 0.99-1.38 ms against native
+            # 0.062 / 0.148 / 0.36 / 1.33-1.53 ms at 1 / 16 / 128 / 512 MiB (a DDP bucket's
+            # separate 1/dp scaling pass costs less than that difference); on 8 ranks 512 MiB
+            # 1.34 against 2.19 ms.  The native kernel keeps the latency-bound small buffers.
             return False
         if nbytes % 16 or t.data_ptr() % 16:
             return False
