@@ -1,0 +1,57 @@
+"""Host-side routing of the native all-reduce (no GPU): which calls the native
+kernel takes and which go back to torch.distributed, with a recording fake of
+the extension."""
+
+import pytest
+import torch
+
+from torch_einshard_b200.parallel import symmetric
+
+
+class FakeMod:
+    def __init__(self):
+        self.calls = []
+
+    def comm_all_reduce(self, cid, piece, scale, blocks, err):
+        self.calls.append((piece.numel() * piece.element_size(), scale))
+
+
+def make_comm(size=2, capacity=64 << 20):
+    comm = object.__new__(symmetric.Communicator)
+    comm.mod = FakeMod()
+    comm.cid = 0
+    comm.size = size
+    comm.capacity = capacity
+    comm.broken = False
+    comm.sms = 148
+    comm.err = None
+    return comm
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_small_buffers_take_the_native_kernel(size, monkeypatch):
+    monkeypatch.delenv("EINSHARD_FAULT_INJECT", raising=False)
+    comm = make_comm(size)
+    t = torch.zeros(1 << 16, dtype=torch.bfloat16)   # 128 KiB
+    assert comm.all_reduce_(t, 0.5) is True
+    assert comm.mod.calls == [(1 << 17, 0.5)]
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_buffers_from_one_mib_go_to_nccl(size, monkeypatch):
+    monkeypatch.delenv("EINSHARD_FAULT_INJECT", raising=False)
+    comm = make_comm(size)
+    t = torch.zeros(1 << 19, dtype=torch.bfloat16)   # 1 MiB
+    assert comm.all_reduce_(t) is False
+    assert comm.mod.calls == []
+
+
+def test_declines_what_the_kernel_cannot_take(monkeypatch):
+    monkeypatch.delenv("EINSHARD_FAULT_INJECT", raising=False)
+    comm = make_comm()
+    assert comm.all_reduce_(torch.zeros(7, dtype=torch.float32)) is False          # not a multiple of 16 bytes
+    assert comm.all_reduce_(torch.zeros(8, 8).t()) is False                        # not contiguous
+    assert comm.all_reduce_(torch.zeros(16, dtype=torch.int32)) is False           # dtype
+    comm.broken = True
+    assert comm.all_reduce_(torch.zeros(16)) is False                              # after a timeout
+    assert comm.mod.calls == []
