@@ -247,6 +247,22 @@ void comm_all_reduce(int64_t id, at::Tensor buf, double scale, int64_t nblocks, 
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+void comm_all_reduce_push(int64_t id, at::Tensor buf, double scale, int64_t nblocks, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open && buf.is_cuda() && buf.is_contiguous(), "einshard comm all_reduce (push): bad arguments");
+  TORCH_CHECK(buf.scalar_type() == at::kBFloat16 || buf.scalar_type() == at::kHalf || buf.scalar_type() == at::kFloat,
+              "einshard comm all_reduce (push): dtype");
+  const int64_t bytes = buf.numel() * buf.element_size();
+  TORCH_CHECK(bytes % 16 == 0 && es::comm_all_reduce_push_bytes(bytes / 16, hc.size) <= (long long)hc.data_bytes,
+              "einshard comm all_reduce (push): size");
+  const c10::cuda::CUDAGuard guard(buf.device());
+  es::CommDev d = make_dev(hc, err, static_cast<int>(nblocks), 3);
+  const int rc = es::comm_all_reduce_push(d, buf.data_ptr(), buf.numel(), es_dtype(buf), static_cast<float>(scale),
+                                          static_cast<int>(nblocks), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard comm all_reduce (push): launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
 // boxes: list of (src_rank, (d0,d1,d2,d3), src_off, dst_off, (s0,s1,s2), (t0,t1,t2)) in bytes for offsets/strides
 void comm_copy(int64_t id, at::Tensor src, int64_t stage_bytes, at::Tensor dst, py::list boxes, int64_t esize,
                bool reduce, bool accumulate, double scale, bool sequential, int64_t nblocks, const at::Tensor& err) {
@@ -652,6 +668,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("comm_connect", &comm_connect, "map every rank's buffer");
   m.def("comm_destroy", &comm_destroy, "unmap and free");
   m.def("comm_all_reduce", &comm_all_reduce, "two-shot NVLink all-reduce in place");
+  m.def("comm_all_reduce_push", &comm_all_reduce_push, "two-shot NVLink all-reduce in place, stores only");
   m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)");
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
   m.def("conv2d_wgrad", &conv2d_wgrad, "weight gradient of the implicit-GEMM conv (split-K tcgen05, fp32 out)");

@@ -346,6 +346,101 @@ __global__ void __launch_bounds__(512) k_all_reduce(CommDev c, uint4* buf, long 
   publish(c, kFlagDone);
 }
 
+// acc += v (8 bf16/fp16 or 4 fp32 values in one 16-byte vector)
+template <int DT>
+__device__ __forceinline__ void add_vec(float (&acc)[8], const uint4 v) {
+  if (DT == 2) {
+    acc[0] += __uint_as_float(v.x);
+    acc[1] += __uint_as_float(v.y);
+    acc[2] += __uint_as_float(v.z);
+    acc[3] += __uint_as_float(v.w);
+  } else {
+    const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 f;
+      if (DT == 0) {
+        f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+      } else {
+        f = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+      }
+      acc[2 * j] += f.x;
+      acc[2 * j + 1] += f.y;
+    }
+  }
+}
+
+// Push-model two-shot all-reduce: every transfer over NVLink is a store into a
+// peer's symmetric region, never a load.  Region of rank q (16-byte vectors,
+// per = ceil(n16 / size)): in[p] = [p * per, (p + 1) * per) receives chunk q of
+// rank p's buffer; out[p] = [(size + p) * per, ...) receives rank p's reduced
+// chunk p.
+//   1. rank r stores chunk q of buf into rank q's in[r] (q = r is local), then
+//      publishes `staged`;
+//   2. after every peer's `staged`, rank r sums in[0..size) from its own HBM,
+//      scales, writes buf chunk r and stores the result into every peer's
+//      out[r], then publishes `reduced`;
+//   3. after every peer's `reduced`, rank r copies out[q] (local) into buf
+//      chunk q for q != r and publishes `done`.
+// NVLink carries 2 (size - 1) / size of the buffer per rank, all as posted
+// writes; no staging copy of the whole buffer.  All waits are bounded.
+template <int DT>
+__global__ void __launch_bounds__(512) k_all_reduce_push(CommDev c, uint4* buf, long long n16, float scale) {
+  uint32_t bars = 0;
+  const uint32_t nb = gridDim.x;
+  const long long per = (n16 + c.size - 1) / c.size;
+  const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  const long long nth = (long long)gridDim.x * blockDim.x;
+  // region pointers in shared memory: a dynamic index into the kernel parameter
+  // array would go through local memory
+  __shared__ uint4* s_data[kMaxRanks];
+#pragma unroll
+  for (int p = 0; p < kMaxRanks; ++p)
+    if (threadIdx.x == p) s_data[p] = reinterpret_cast<uint4*>(c.data[p]);
+  __syncthreads();
+  if (!wait_peers(c, kFlagDone, c.epoch - 1)) return;  // peers no longer read our region
+  for (int k = 0; k < c.size; ++k) {
+    const int q = (c.rank + k) % c.size;  // every rank starts with a different target
+    const long long lo = min((long long)q * per, n16);
+    const long long hi = min(lo + per, n16);
+    uint4* dst = s_data[q] + (long long)c.rank * per - lo;
+    for (long long i = lo + tid; i < hi; i += nth) dst[i] = buf[i];
+  }
+  if (!grid_barrier(c, c.bar_base + nb * ++bars)) return;
+  publish(c, kFlagStaged);
+  if (!wait_peers(c, kFlagStaged, c.epoch)) return;
+  {
+    const long long lo = min((long long)c.rank * per, n16);
+    const long long hi = min(lo + per, n16);
+    const uint4* in = s_data[c.rank];
+    for (long long i = lo + tid; i < hi; i += nth) {
+      float acc[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+      for (int p = 0; p < c.size; ++p) add_vec<DT>(acc, in[(long long)p * per + (i - lo)]);
+      const uint4 o = pack_vec<DT>(acc, scale);
+      buf[i] = o;
+      for (int k = 1; k < c.size; ++k) {
+        const int q = (c.rank + k) % c.size;
+        s_data[q][(long long)(c.size + c.rank) * per + (i - lo)] = o;
+      }
+    }
+  }
+  if (!grid_barrier(c, c.bar_base + nb * ++bars)) return;
+  publish(c, kFlagReduced);
+  if (!wait_peers(c, kFlagReduced, c.epoch)) return;
+  const uint4* own = s_data[c.rank];
+  for (int k = 1; k < c.size; ++k) {
+    const int q = (c.rank + k) % c.size;
+    const long long lo = min((long long)q * per, n16);
+    const long long hi = min(lo + per, n16);
+    const uint4* src = own + (long long)(c.size + q) * per - lo;
+    for (long long i = lo + tid; i < hi; i += nth) buf[i] = src[i];
+  }
+  if (!grid_barrier(c, c.bar_base + nb * ++bars)) return;
+  publish(c, kFlagDone);
+}
+
 // ------------------------------------------------------------------ host launchers
 
 static int launch_coop(const void* fn, int nblocks, void** args, cudaStream_t stream) {
@@ -389,6 +484,26 @@ int comm_all_reduce(const CommDev& c, void* buf, long long n, int dtype, float s
   const void* fn = dtype == 0 ? reinterpret_cast<const void*>(k_all_reduce<0>)
                    : dtype == 1 ? reinterpret_cast<const void*>(k_all_reduce<1>)
                                 : reinterpret_cast<const void*>(k_all_reduce<2>);
+  return launch_coop(fn, nblocks, args, stream);
+}
+
+// Region bytes the push all-reduce needs for n16 16-byte vectors on `size` ranks.
+long long comm_all_reduce_push_bytes(long long n16, int size) {
+  return 2LL * size * ((n16 + size - 1) / size) * 16;
+}
+
+int comm_all_reduce_push(const CommDev& c, void* buf, long long n, int dtype, float scale, int nblocks,
+                         cudaStream_t stream) {
+  const int esize = dtype == 2 ? 4 : 2;
+  if ((n * esize) % 16 || (reinterpret_cast<uintptr_t>(buf) & 15)) return -1;
+  CommDev cc = c;
+  uint4* b = reinterpret_cast<uint4*>(buf);
+  long long n16 = n * esize / 16;
+  float sc = scale;
+  void* args[] = {&cc, &b, &n16, &sc};
+  const void* fn = dtype == 0 ? reinterpret_cast<const void*>(k_all_reduce_push<0>)
+                   : dtype == 1 ? reinterpret_cast<const void*>(k_all_reduce_push<1>)
+                                : reinterpret_cast<const void*>(k_all_reduce_push<2>);
   return launch_coop(fn, nblocks, args, stream);
 }
 

@@ -80,6 +80,11 @@ int comm_stage_and_reduce(const CommDev& c, const void* src, size_t nbytes, size
                           const CopyPlan& plan, int nblocks, cudaStream_t stream);
 // Two-shot all-reduce of `n` elements in place in `buf` (dtype 0 bf16, 1 f16, 2 f32),
 // result multiplied by `scale`.
+// Push-model variant (every NVLink transfer a store into a peer's region);
+// needs comm_all_reduce_push_bytes(n16, size) bytes of symmetric region.
+long long comm_all_reduce_push_bytes(long long n16, int size);
+int comm_all_reduce_push(const CommDev& c, void* buf, long long n, int dtype, float scale, int nblocks,
+                         cudaStream_t stream);
 int comm_all_reduce(const CommDev& c, void* buf, long long n, int dtype, float scale, int nblocks,
                     cudaStream_t stream);
 

@@ -29,6 +29,9 @@ __all__ = ["Communicator", "activate", "deactivate", "communicator_for_group"]
 _DEFAULT_MB = int(os.environ.get("EINSHARD_SYMM_MB", "1280"))
 # 512 MiB all-reduce at 8 ranks on B200: this two-shot kernel 2.19 ms, NCCL 1.34 ms.
 _NCCL_AR_MIN_BYTES = int(os.environ.get("EINSHARD_NCCL_AR_MIN_BYTES", str(1 << 20)))
+# native all-reduce kernel: "pull" (peers' chunks read over NVLink) or "push" (every
+# NVLink transfer a store into a peer's region, no staging copy)
+_AR_ALGO = os.environ.get("EINSHARD_AR_ALGO", "pull")
 _COMMS = {}
 _REJECTED = set()
 _LARGE = {}  # group key -> larger communicators created on demand (kept until deactivate)
@@ -166,13 +169,15 @@ class Communicator:
         if nbytes % 16 or t.data_ptr() % 16:
             return False
         quantum = 16 * self.size
-        chunk = (int(self.capacity / (1.0 + 1.0 / self.size)) // quantum) * quantum
+        push = _AR_ALGO == "push"
+        # region per piece: pull stages the piece plus one reduced chunk, push takes two copies
+        chunk = ((self.capacity // 2 if push else int(self.capacity / (1.0 + 1.0 / self.size))) // quantum) * quantum
+        run = self.mod.comm_all_reduce_push if push else self.mod.comm_all_reduce
         flat = t.view(-1)
         per = chunk // t.element_size()
         for start in range(0, t.numel(), per):
             piece = flat[start:start + per]
-            self.mod.comm_all_reduce(self.cid, piece, float(scale),
-                                     self._blocks(piece.numel() * t.element_size()), self.err)
+            run(self.cid, piece, float(scale), self._blocks(piece.numel() * t.element_size()), self.err)
         return True
 
     def all_reduce_div_(self, t, divisor):
