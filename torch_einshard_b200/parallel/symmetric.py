@@ -29,9 +29,10 @@ __all__ = ["Communicator", "activate", "deactivate", "communicator_for_group"]
 _DEFAULT_MB = int(os.environ.get("EINSHARD_SYMM_MB", "1280"))
 # 512 MiB all-reduce at 8 ranks on B200: this two-shot kernel 2.19 ms, NCCL 1.34 ms.
 _NCCL_AR_MIN_BYTES = int(os.environ.get("EINSHARD_NCCL_AR_MIN_BYTES", str(1 << 20)))
-# native all-reduce kernel: "pull" (peers' chunks read over NVLink) or "push" (every
-# NVLink transfer a store into a peer's region, no staging copy)
-_AR_ALGO = os.environ.get("EINSHARD_AR_ALGO", "pull")
+# native all-reduce kernel: "push" (every NVLink transfer a store into a peer's region,
+# no staging copy; 15-47 % faster than "pull" on 2 ranks from 1 to 512 MiB) or "pull"
+# (peers' chunks read over NVLink)
+_AR_ALGO = os.environ.get("EINSHARD_AR_ALGO", "push")
 _COMMS = {}
 _REJECTED = set()
 _LARGE = {}  # group key -> larger communicators created on demand (kept until deactivate)
@@ -161,10 +162,11 @@ class Communicator:
         if nbytes == 0:
             return True
         if nbytes >= _NCCL_AR_MIN_BYTES:
-            # measured on 2 ranks: NCCL 0.025 / 0.056 / 0.28 / 0.99-1.38 ms against native
-            # 0.062 / 0.148 / 0.36 / 1.33-1.53 ms at 1 / 16 / 128 / 512 MiB (a DDP bucket's
-            # separate 1/dp scaling pass costs less than that difference); on 8 ranks 512 MiB
-            # 1.34 against 2.19 ms.  The native kernel keeps the latency-bound small buffers.
+            # measured on 2 ranks (bf16): NCCL 0.026 / 0.056 / 0.28 / 0.99 ms against the
+            # native push kernel 0.043 / 0.078 / 0.31 / 1.14 ms (pull 0.064 / 0.147 / 0.36 /
+            # 1.33 ms) at 1 / 16 / 128 / 512 MiB; on 8 ranks 512 MiB NCCL 1.34 against pull
+            # 2.19 ms.  A DDP bucket's separate 1/dp scaling pass costs less than that
+            # difference.  The native kernel keeps the buffers below 1 MiB.
             return False
         if nbytes % 16 or t.data_ptr() % 16:
             return False
