@@ -13,7 +13,10 @@ class FakeMod:
         self.calls = []
 
     def comm_all_reduce(self, cid, piece, scale, blocks, err):
-        self.calls.append((piece.numel() * piece.element_size(), scale))
+        self.calls.append(("pull", piece.numel() * piece.element_size(), scale))
+
+    def comm_all_reduce_push(self, cid, piece, scale, blocks, err):
+        self.calls.append(("push", piece.numel() * piece.element_size(), scale))
 
 
 def make_comm(size=2, capacity=64 << 20):
@@ -34,7 +37,24 @@ def test_small_buffers_take_the_native_kernel(size, monkeypatch):
     comm = make_comm(size)
     t = torch.zeros(1 << 16, dtype=torch.bfloat16)   # 128 KiB
     assert comm.all_reduce_(t, 0.5) is True
-    assert comm.mod.calls == [(1 << 17, 0.5)]
+    assert comm.mod.calls == [("push", 1 << 17, 0.5)]   # the push kernel is the default
+
+
+def test_pull_kernel_on_request(monkeypatch):
+    monkeypatch.delenv("EINSHARD_FAULT_INJECT", raising=False)
+    monkeypatch.setattr(symmetric, "_AR_ALGO", "pull")
+    comm = make_comm(2)
+    assert comm.all_reduce_(torch.zeros(1 << 16, dtype=torch.bfloat16)) is True
+    assert comm.mod.calls == [("pull", 1 << 17, 1.0)]
+
+
+def test_push_pieces_fit_two_copies_in_the_region(monkeypatch):
+    monkeypatch.delenv("EINSHARD_FAULT_INJECT", raising=False)
+    monkeypatch.setattr(symmetric, "_NCCL_AR_MIN_BYTES", 1 << 62)
+    comm = make_comm(2, capacity=1 << 20)
+    assert comm.all_reduce_(torch.zeros(1 << 20, dtype=torch.bfloat16)) is True   # 2 MiB through a 1 MiB region
+    sizes = [c[1] for c in comm.mod.calls]
+    assert sum(sizes) == 2 << 20 and all(2 * b <= comm.capacity for b in sizes)
 
 
 @pytest.mark.parametrize("size", [2, 4, 8])
