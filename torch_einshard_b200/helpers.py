@@ -1,4 +1,8 @@
-"""Collective helpers (module path kept for users of ``es.helpers``)."""
+"""Collective helpers (module path kept for users of ``es.helpers``).
+
+Reference counterpart: ``src/torch_einshard/helpers.py:5-354`` (process-group
+bootstrap, collective helpers, split shapes).
+"""
 
 import torch  # noqa: F401  (exposed for callers that patch torch.cuda through this module)
 import torch.distributed as dist  # noqa: F401

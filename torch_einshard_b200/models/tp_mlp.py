@@ -9,6 +9,10 @@ The column-parallel step plans ``identity_forward_allreduce_backward`` on x
 (its gradient is all-reduced in backward) and the row-parallel step ends with
 an all-reduce; on the native path both the forward all-reduce and the
 backward input-gradient all-reduce are fused into the GEMM that produces them.
+
+The pattern is the reference's tensor-parallel MLP
+(``docs/user-guide/tensor-parallel.md``, ``tests/test_scigpt_patterns.py``);
+the reference ships no model class.
 """
 
 import torch

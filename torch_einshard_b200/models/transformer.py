@@ -15,6 +15,9 @@ Data parallelism over ``dp`` uses PyTorch DDP with
 or replicated) and need no extra reduction groups.  The
 embedding, norms and LM head are replicated over ``tp``; their gradients are
 identical on every tp rank because activations entering them are replicated.
+
+Built from the reference's tensor-parallel patterns
+(``docs/user-guide/tensor-parallel.md``); the reference ships no model.
 """
 
 import math

@@ -17,6 +17,9 @@ K-major or MN-major order, so transposed views need no copy.
 Equations with repeated letters inside one operand (diagonals), ellipses that
 cannot be aligned, a single operand, or dtypes/devices the native kernel does
 not cover go to ``torch.einsum``.
+
+Replaces the reference's local ``torch.einsum`` call
+(``src/torch_einshard/einsum.py:132``) for bf16/fp16 CUDA operands.
 """
 
 import math

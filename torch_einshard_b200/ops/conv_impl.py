@@ -12,6 +12,8 @@ kernel (``_C.conv2d_wgrad``: dY and the shifted input windows as MN-major
 operands, fp32 partial tiles added atomically) when both channel counts are
 multiples of 64, else ``torch.nn.grad.conv2d_weight``; the bias gradient is a
 reduction.
+
+Replaces the reference's ``F.conv2d`` call in ``einconv`` (``src/torch_einshard/conv.py:48-52``).
 """
 
 import torch

@@ -3,6 +3,8 @@
 ``try_conv`` returns ``None`` when the call is outside the native envelope
 (not CUDA bf16/fp16, not 2-D, dilation != 1, channel counts the TMA boxes
 cannot address) and ``einconv`` then uses ``torch.nn.functional``.
+
+Replaces the reference's ``F.conv2d`` call in ``einconv`` (``src/torch_einshard/conv.py:48-52``).
 """
 
 __all__ = ["try_conv"]

@@ -11,6 +11,8 @@ which is what the backward passes run.
 
 Twiddle tables exp(-+2 pi i j / n) are computed on the host in float64, rounded
 to complex64 and cached per (device, n, direction).
+
+Replaces the reference's ``torch.fft`` calls (``src/torch_einshard/fft.py:202-205,549-553,861-870``).
 """
 
 import math

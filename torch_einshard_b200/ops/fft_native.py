@@ -3,6 +3,8 @@
 ``try_fft`` returns ``None`` when the native kernels do not cover the call
 (not CUDA complex64, length not a supported power of two) and the caller then
 uses ``torch.fft``.
+
+Replaces the reference's ``torch.fft`` calls (``src/torch_einshard/fft.py:202-205``).
 """
 
 __all__ = ["try_fft"]

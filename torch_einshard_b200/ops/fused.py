@@ -12,6 +12,13 @@ group); otherwise ``None`` and the executor runs the unfused steps.
   then ``rank_local_einsum`` (column-parallel ``b n c, h/tp c -> b n h/tp``):
   forward is the plain GEMM, and backward's input-gradient GEMM is fused with
   the all-reduce of that gradient.
+
+Fuses the planner steps ``rank_local_einsum`` +
+``allreduce_forward_identity_backward`` /
+``reducescatter_forward_allgather_backward`` and
+``allgather_forward_reducescatter_backward`` + ``rank_local_einsum``
+(``src/torch_einshard/mappings.py:169-187``,
+``src/torch_einshard/distributed.py:84-620``).
 """
 
 __all__ = ["binary_fusion", "register_fusion_provider"]

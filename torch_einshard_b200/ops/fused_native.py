@@ -12,6 +12,9 @@ Provides the fusion descriptors consumed by :mod:`.fused`:
 
 Both apply to two-operand contractions that canonicalise to a single
 (batch-free) GEMM of CUDA bf16 tensors whose output fits the symmetric buffer.
+
+Fuses the reference's ``mappings.py:169-187`` collectives with the contraction
+of ``einsum.py:132``.
 """
 
 import torch

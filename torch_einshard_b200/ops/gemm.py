@@ -6,6 +6,8 @@ kernel reads either operand K-major or MN-major, so ``dA = dC @ B^T`` and
 ``dB = A^T @ dC`` need no transpose copies.  Operands whose strides the TMA
 engine cannot address (row stride not a multiple of 16 bytes, unaligned base)
 are first copied into a padded buffer.
+
+Replaces the reference's ``torch.einsum`` (``src/torch_einshard/einsum.py:132``).
 """
 
 import torch

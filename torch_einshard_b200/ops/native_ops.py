@@ -2,6 +2,9 @@
 
 Each function returns ``None`` when the native path does not apply, and the
 caller then uses the torch implementation.
+
+Replaces the reference's window build (``src/torch_einshard/halo.py:36-55``)
+and ``torch.roll`` (``src/torch_einshard/roll.py:23``).
 """
 
 import torch

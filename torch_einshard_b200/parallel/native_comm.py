@@ -5,6 +5,9 @@ device of this node with peer access and the native extension is loaded; the
 collective helpers ask :func:`communicator_for` and fall back to
 ``torch.distributed`` when it returns ``None``.  The implementation is filled in
 by :mod:`torch_einshard_b200.parallel.symmetric`.
+
+Native backend of the reference's collective helpers
+(``src/torch_einshard/helpers.py:27-309``).
 """
 
 __all__ = ["communicator_for", "workspace_for", "world_communicator", "enable", "disable", "enabled"]

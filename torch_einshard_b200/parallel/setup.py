@@ -1,4 +1,7 @@
-"""One-call setup of the native NVLink communicators for a mesh."""
+"""One-call setup of the native NVLink communicators for a mesh.
+
+No reference counterpart (the reference only uses ``torch.distributed``).
+"""
 
 __all__ = ["setup_native_comm"]
 

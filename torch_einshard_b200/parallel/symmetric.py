@@ -12,6 +12,11 @@ boxes, so uneven shards and arbitrary dimensions need no pack/unpack copies.
 A communicator is only created for groups whose ranks all live on this node
 and whose devices can access each other; otherwise the collective helpers use
 ``torch.distributed`` (NCCL).  Set ``EINSHARD_NATIVE_COMM=0`` to disable.
+
+Native backend of the reference's collective helpers: all_reduce
+``src/torch_einshard/helpers.py:27``, broadcast ``:35``, all_gather ``:61``,
+reduce_scatter ``:114``, all_to_all_repartition ``:142``, owner_swap ``:184``,
+roll ``:224-309``.
 """
 
 import math

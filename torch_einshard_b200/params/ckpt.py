@@ -6,6 +6,10 @@ shard with its metadata (global shape, local slices, local shape, shard dims).
 recorded slices and copies the slice that this rank owns under the *current*
 layout, so a checkpoint can be loaded on a different mesh or world size.
 Parameters without attached metadata are saved whole by rank 0.
+
+Builds on the reference's ``ParamShardMetadata``
+(``src/torch_einshard/params.py:557-562,1660-1669``); the reference itself has
+no save/load.
 """
 
 import dataclasses
