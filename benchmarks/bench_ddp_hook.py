@@ -20,8 +20,19 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 from common import ROOT, Writer, benchmark, init_distributed, parser  # noqa: E402
 
-sys.path.insert(0, ROOT)
-import torch_einshard_b200 as es  # noqa: E402
+
+
+def load_impl(impl):
+    """The package under test: this framework, or the unmodified reference from
+    baseline/_ref (its parser dependency supplied by baseline/parsley_shim)."""
+    if impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "parsley_shim"))
+        import torch_einshard
+        return torch_einshard
+    sys.path.insert(0, ROOT)
+    import torch_einshard_b200
+    return torch_einshard_b200
 
 WIDTH = {"small": (256, 4), "medium": (1024, 8), "large": (4096, 8)}
 
@@ -42,7 +53,9 @@ def main():
     p = parser(__doc__)
     p.add_argument("--mode", choices=("per_spec", "combined", "mixed"), default="combined")
     p.add_argument("--bucket-cap-mb", type=int, default=25)
+    p.add_argument("--impl", choices=("native", "reference"), default="native")
     args = p.parse_args()
+    es = load_impl(args.impl)
     device = torch.device(args.device)
     init_distributed(device)
     from torch.distributed.device_mesh import init_device_mesh
@@ -50,7 +63,7 @@ def main():
     dp = 2 if world % 2 == 0 else 1
     mesh = init_device_mesh(device.type, (dp, world // dp), mesh_dim_names=("dp", "sp"))
     wrapped = es.wrap_mesh(mesh)
-    if device.type == "cuda":
+    if device.type == "cuda" and args.impl == "native":
         es.setup_native_comm(mesh)
     dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
     width, depth = WIDTH[args.size]
@@ -74,7 +87,7 @@ def main():
             param.grad = None
 
     benchmark(f"ddp_hook_{args.mode}", step, args=args, device=device, writer=Writer(args.output), grad=True,
-              extra={"mode": args.mode, "bucket_cap_mb": args.bucket_cap_mb, "width": width, "depth": depth,
+              extra={"impl": args.impl, "mode": args.mode, "bucket_cap_mb": args.bucket_cap_mb, "width": width, "depth": depth,
                      "params": sum(p.numel() for p in model.parameters())})
     dist.destroy_process_group()
 

@@ -15,10 +15,30 @@ import torch.distributed as dist
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
-from common import ROOT, Writer, benchmark, init_distributed, parser  # noqa: E402
+from common import ROOT, Writer, init_distributed, parser  # noqa: E402
+from common import benchmark as _benchmark  # noqa: E402
 
-sys.path.insert(0, ROOT)
-import torch_einshard_b200 as es  # noqa: E402
+
+
+def load_impl(impl):
+    """The package under test: this framework, or the unmodified reference from
+    baseline/_ref (its parser dependency supplied by baseline/parsley_shim)."""
+    if impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "_ref"))
+        sys.path.insert(0, os.path.join(ROOT, "baseline", "parsley_shim"))
+        import torch_einshard
+        return torch_einshard
+    sys.path.insert(0, ROOT)
+    import torch_einshard_b200
+    return torch_einshard_b200
+
+IMPL = {"impl": "native"}
+
+
+def benchmark(name, fn, **kw):
+    kw["extra"] = dict(kw.get("extra") or {}, **IMPL)
+    return _benchmark(name, fn, **kw)
+
 
 SHAPES = {"small": dict(rows=128, cols=96, hidden=128, batch=4, seq=16),
           "medium": dict(rows=1024, cols=768, hidden=1024, batch=8, seq=64),
@@ -26,7 +46,10 @@ SHAPES = {"small": dict(rows=128, cols=96, hidden=128, batch=4, seq=16),
 
 
 def main():
-    args = parser(__doc__).parse_args()
+    p = parser(__doc__)
+    p.add_argument("--impl", choices=("native", "reference"), default="native")
+    args = p.parse_args()
+    es = load_impl(args.impl)
     device = torch.device(args.device)
     init_distributed(device)
     from torch.distributed.device_mesh import init_device_mesh
@@ -39,11 +62,12 @@ def main():
     side = int(round(world ** 0.5))
     mesh2 = init_device_mesh(device.type, (side, world // side), mesh_dim_names=("dp", "sp")) if side * side == world \
         else None
-    if device.type == "cuda":
+    if device.type == "cuda" and args.impl == "native":
         es.setup_native_comm(mesh1)
     torch.manual_seed(args.seed)
     cfg = SHAPES[args.size]
     writer = Writer(args.output)
+    IMPL["impl"] = args.impl
     dtype = torch.bfloat16 if device.type == "cuda" else torch.float32
     group = mesh1["dp"].get_group()
     rank = dist.get_rank(group)
