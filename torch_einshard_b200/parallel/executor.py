@@ -20,6 +20,7 @@ all-reduce run as one sm_100a kernel (:mod:`..ops.fused`).  The recorded plan
 steps are unchanged.
 """
 
+import weakref
 import warnings
 
 import torch
@@ -111,6 +112,9 @@ def distributed_1d(shard, *xs, mesh, shapes, policy=None):
 
 # ============================================================================ binary
 
+_MESH_SIZES = {}  # id(mesh) -> (weakref to the mesh, {dim name: size})
+
+
 class BinaryExecutor:
     def __init__(self, shard, x, y, mesh, shapes, policy):
         self.plan = ExecutionPlan()
@@ -145,7 +149,17 @@ class BinaryExecutor:
         return TensorRuntimeInfo(tuple(_no_ellipsis(axes)), tuple(tensor.shape), tensor.element_size())
 
     def mesh_sizes(self):
-        return {name: int(self.mesh.mesh.shape[i]) for i, name in enumerate(self.mesh.mesh_dim_names)}
+        # DeviceMesh.mesh rebuilds a tensor on every access: cache the sizes per mesh object
+        mesh = self.mesh
+        hit = _MESH_SIZES.get(id(mesh))
+        if hit is None or hit[0]() is not mesh:
+            sizes = {name: int(mesh.mesh.shape[i]) for i, name in enumerate(mesh.mesh_dim_names)}
+            try:
+                hit = (weakref.ref(mesh), sizes)
+            except TypeError:
+                return sizes
+            _MESH_SIZES[id(mesh)] = hit
+        return dict(hit[1])
 
     def cost_split_shapes(self):
         known = {}
