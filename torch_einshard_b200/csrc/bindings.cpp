@@ -723,6 +723,22 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           return d;
         },
         "kernel choice for a GEMM shape (no launch; runs without a GPU)");
+  m.def("gemm_wide_schedule",
+        [](int64_t M, int64_t N, int64_t K, int64_t num_sms) {
+          es::GemmArgs g;
+          g.M = static_cast<int>(M);
+          g.N = static_cast<int>(N);
+          g.K = static_cast<int>(K);
+          g.num_sms = static_cast<int>(num_sms);
+          g.pair = g_pair_mode;
+          g.persistent = g_persistent;
+          g.group_m = g_group_m;
+          py::list out;
+          for (const es::GemmSegment& sg : es::gemm_wide_schedule(g, g_streamk))
+            out.append(py::make_tuple(sg.launch, sg.cluster, sg.pair_tile, sg.m0, sg.n0, sg.kb0, sg.kb1));
+          return out;
+        },
+        "wide-kernel schedule (launch, cluster, pair tile, m0, n0, kb0, kb1) of a GEMM shape (host walk)");
   m.def("set_gemm_sleep_ns", [](int64_t v) { g_sleep_ns = static_cast<int>(v); }, "wide-kernel epilogue back-off ns");
   m.def("set_tma_l2_promotion", [](int64_t v) { es::tma_l2_promotion() = static_cast<int>(v); },
         "L2 promotion of TMA loads: 0 none, 1 64B, 2 128B, 3 256B (tuning)");

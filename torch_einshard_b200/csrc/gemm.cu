@@ -154,18 +154,30 @@ bool make_output_map(const GemmArgs& g, bool trans, CUtensorMap* mc) {
   return true;
 }
 
+// Tile schedule of the wide kernel: 256 x 512 pair tiles, raster groups of 16.
+static GemmShape wide_shape(const GemmArgs& g) {
+  GemmShape s = make_shape(g);
+  s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
+  s.num_n = (g.N + kBN3 - 1) / kBN3;
+  s.group_m = g.group_m > 0 ? g.group_m : 16;
+  s.pair = 1;
+  s.split = g.split;
+  return s;
+}
+
+// One pair tile per cluster (K > 2048 by default) or persistent clusters.
+static bool wide_persistent(const GemmArgs& g) {
+  return g.persistent > 0 || (g.persistent < 0 && (g.K + kBK - 1) / kBK <= 32);
+}
+
 // tile_limit > 0: only pair tiles [0, tile_limit) (the whole tiles before a stream-K tail).
 template <class Epi>
 int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, Epi epi, cudaStream_t stream,
                 int tile_limit = 0) {
   CUtensorMap mc;
   epi.tma = make_output_map(g, epi.trans != 0, &mc) ? 1 : 0;
-  GemmShape s = make_shape(g);
-  s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
-  s.num_n = (g.N + kBN3 - 1) / kBN3;
-  s.group_m = g.group_m > 0 ? g.group_m : 16;
-  s.pair = 1;
-  s.split = tile_limit > 0 ? 0 : g.split;
+  GemmShape s = wide_shape(g);
+  if (tile_limit > 0) s.split = 0;
   s.sk_first = tile_limit;
   auto kernel = gemm_tc3_kernel<Epi>;
   static unsigned long long attr_set = 0;
@@ -180,8 +192,7 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
   // One pair tile per cluster held higher clocks under the power cap for long K;
   // with K <= 2048 the per-CTA setup and the unhidden pipeline fill dominate and
   // persistent clusters win (65536 x 2048 x 2048: 0.37 against 0.40 ms).
-  const bool persist = g.persistent > 0 || (g.persistent < 0 && (g.K + kBK - 1) / kBK <= 32);
-  if (pairs < clusters || !persist) clusters = pairs;
+  if (pairs < clusters || !wide_persistent(g)) clusters = pairs;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * clusters);
   cfg.blockDim = dim3(kThreads3);
@@ -349,11 +360,7 @@ template <typename OutT>
 static int launch_streamk(const GemmArgs& g, const StreamKPlan& plan, float* ws, cudaStream_t stream) {
   CUtensorMap ma, mb, mc, mw;
   make_operand_maps(g, &ma, &mb, true);
-  GemmShape s = make_shape(g);
-  s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
-  s.num_n = (g.N + kBN3 - 1) / kBN3;
-  s.group_m = g.group_m > 0 ? g.group_m : 16;
-  s.pair = 1;
+  GemmShape s = wide_shape(g);
   s.split = 0;
   s.sk_iters = plan.sk_iters;
   s.sk_first = plan.sk_first;
@@ -437,10 +444,41 @@ GemmPlanInfo gemm_plan_info(const GemmArgs& g0, int streamk_mode) {
     return info;
   }
   info.kernel = pick_kernel(g);
-  if (info.kernel == 2) {
-    info.persistent = g.persistent > 0 || (g.persistent < 0 && (g.K + kBK - 1) / kBK <= 32) ? 1 : 0;
-  }
+  if (info.kernel == 2) info.persistent = wide_persistent(g) ? 1 : 0;
   return info;
+}
+
+std::vector<GemmSegment> gemm_wide_schedule(const GemmArgs& g, int streamk_mode) {
+  std::vector<GemmSegment> out;
+  StreamKPlan plan;
+  const bool sk = g.pair < 0 && gemm_streamk_plan(g, streamk_mode, &plan);
+  GemmShape s = wide_shape(g);
+  const int pairs = s.num_m * s.num_n * s.batch;
+  auto walk = [&](const GemmShape& sh, int launch, int clusters) {
+    for (int cl = 0; cl < clusters; ++cl) {
+      SegIter it = seg_begin(sh, cl);
+      TileCoord c;
+      int p, k0, k1;
+      while (seg_next(sh, cl, clusters, 0, it, &c, &p, &k0, &k1)) out.push_back({launch, cl, p, c.m0, c.n0, k0, k1});
+    }
+  };
+  if (sk) {
+    GemmShape whole = s;
+    whole.split = 0;
+    whole.sk_first = plan.sk_first;
+    if (plan.sk_first > 0) walk(whole, 0, plan.sk_first);  // the plain launch, one tile per cluster
+    GemmShape tail = s;
+    tail.split = 0;
+    tail.sk_iters = plan.sk_iters;
+    tail.sk_first = plan.sk_first;
+    tail.sk_cluster0 = plan.sk_first;
+    walk(tail, 1, plan.clusters - plan.sk_first);
+  } else {
+    int clusters = g.num_sms / 2;
+    if (pairs < clusters || !wide_persistent(g)) clusters = pairs;
+    walk(s, 0, clusters);
+  }
+  return out;
 }
 
 int gemm_launch(const GemmArgs& g, cudaStream_t stream) {

@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <vector>
+
 namespace es {
 
 enum Dtype : int { kDtypeBF16 = 0, kDtypeF16 = 1, kDtypeF32 = 2 };
@@ -74,5 +76,13 @@ struct GemmPlanInfo {
   int sk_first = 0, sk_iters = 0, tail_tiles = 0, clusters = 0;
 };
 GemmPlanInfo gemm_plan_info(const GemmArgs& g, int streamk_mode);
+
+// The wide kernel's work for a GEMM (host walk of the device schedule, for
+// tests): per launch and cluster, each segment's pair tile, its CTA-0 tile
+// origin and K-block range.
+struct GemmSegment {
+  int launch, cluster, pair_tile, m0, n0, kb0, kb1;
+};
+std::vector<GemmSegment> gemm_wide_schedule(const GemmArgs& g, int streamk_mode);
 
 }  // namespace es

@@ -66,7 +66,13 @@ struct TileCoord {
   int b, m0, n0;
 };
 
-__device__ __forceinline__ TileCoord tile_coord(const GemmShape& s, int t) {
+template <typename T>
+__host__ __device__ __forceinline__ T es_min(T a, T b) {
+  return a < b ? a : b;
+}
+
+// Host-callable too: the host tests walk the same tile schedule.
+__host__ __device__ __forceinline__ TileCoord tile_coord(const GemmShape& s, int t) {
   int half = 0;
   if (s.pair) {
     half = t & 1;
@@ -78,7 +84,7 @@ __device__ __forceinline__ TileCoord tile_coord(const GemmShape& s, int t) {
   const int per_group = s.group_m * s.num_n;
   const int g = r / per_group;
   const int first_m = g * s.group_m;
-  const int gm = min(s.num_m - first_m, s.group_m);
+  const int gm = es_min(s.num_m - first_m, s.group_m);
   const int in_group = r - g * per_group;
   const int mb = first_m + in_group % gm;
   const int nb = in_group / gm;

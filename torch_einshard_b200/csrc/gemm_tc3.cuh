@@ -60,14 +60,14 @@ struct SharedState3 {
 static_assert(kStages3 == kStages, "SharedState3 must mirror SharedState");
 
 // Pair tile p -> this CTA's 128-row half; columns n0 .. n0 + 511.
-__device__ __forceinline__ TileCoord tile_coord3(const GemmShape& s, int p, int rank) {
+__host__ __device__ __forceinline__ TileCoord tile_coord3(const GemmShape& s, int p, int rank) {
   const int per_batch = s.num_m * s.num_n;
   const int b = p / per_batch;
   const int r = p - b * per_batch;
   const int per_group = s.group_m * s.num_n;
   const int g = r / per_group;
   const int first_m = g * s.group_m;
-  const int gm = min(s.num_m - first_m, s.group_m);
+  const int gm = es_min(s.num_m - first_m, s.group_m);
   const int in_group = r - g * per_group;
   const int mb = first_m + in_group % gm;
   const int nb = in_group / gm;
@@ -77,7 +77,7 @@ __device__ __forceinline__ TileCoord tile_coord3(const GemmShape& s, int p, int 
 // The i-th pair tile of this cluster, or false when it has no more.  With a
 // split, the two cluster sets walk disjoint halves of the M tiles (each set
 // keeps its own A panels in L2 and the sets share B).
-__device__ __forceinline__ bool pair_tile_at(const GemmShape& s, int cluster, int nclusters, int i, int rank,
+__host__ __device__ __forceinline__ bool pair_tile_at(const GemmShape& s, int cluster, int nclusters, int i, int rank,
                                              TileCoord* out) {
   if (s.split == 0 || (nclusters & 1) || s.num_m < 2) {
     const int p = cluster + i * nclusters;
@@ -107,7 +107,7 @@ struct SegIter {
   int i = 0;                 // tile mode: tiles taken so far
 };
 
-__device__ __forceinline__ SegIter seg_begin(const GemmShape& s, int cluster) {
+__host__ __device__ __forceinline__ SegIter seg_begin(const GemmShape& s, int cluster) {
   SegIter it;
   if (s.sk_iters > 0) {
     const long long nkb = s.num_kb;
@@ -117,9 +117,9 @@ __device__ __forceinline__ SegIter seg_begin(const GemmShape& s, int cluster) {
       it.g = static_cast<long long>(cl) * nkb;
       it.end = it.g + nkb;
     } else {
-      it.g = min(total, static_cast<long long>(s.sk_first) * nkb +
-                            static_cast<long long>(cl - s.sk_first) * s.sk_iters);
-      it.end = min(total, it.g + s.sk_iters);
+      it.g = es_min(total, static_cast<long long>(s.sk_first) * nkb +
+                               static_cast<long long>(cl - s.sk_first) * s.sk_iters);
+      it.end = es_min(total, it.g + s.sk_iters);
     }
   }
   return it;
@@ -127,7 +127,7 @@ __device__ __forceinline__ SegIter seg_begin(const GemmShape& s, int cluster) {
 
 // Next segment: tile coordinates (this CTA's half), linear pair tile index and
 // K-block range; false when the cluster has no more work.
-__device__ __forceinline__ bool seg_next(const GemmShape& s, int cluster, int nclusters, int rank, SegIter& it,
+__host__ __device__ __forceinline__ bool seg_next(const GemmShape& s, int cluster, int nclusters, int rank, SegIter& it,
                                          TileCoord* c, int* pair_index, int* kb0, int* kb1) {
   if (s.sk_iters > 0) {
     if (it.g >= it.end) return false;
