@@ -723,6 +723,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           return d;
         },
         "kernel choice for a GEMM shape (no launch; runs without a GPU)");
+  m.def("gemm_allgather_row_order",
+        [](int64_t rank, int64_t size, int64_t segments, int64_t shard) {
+          return es::gemm_allgather_row_order(static_cast<int>(rank), static_cast<int>(size),
+                                              static_cast<int>(segments), shard);
+        },
+        "row-block order of the fused all-gather GEMM on one rank (host walk)");
   m.def("gemm_wide_schedule",
         [](int64_t M, int64_t N, int64_t K, int64_t num_sms) {
           es::GemmArgs g;

@@ -41,7 +41,7 @@ struct AgGather {
   __device__ __forceinline__ int* flag(int rank, int slot) const { return reinterpret_cast<int*>(c.flags[rank]) + slot; }
 
   // virtual pair block vb -> physical pair block: local shard first, then rank + 1, ...
-  __device__ __forceinline__ int map_block(int vb, int blocks_per_shard) const {
+  __host__ __device__ __forceinline__ int map_block(int vb, int blocks_per_shard) const {
     const int per_offset = segments * blocks_per_shard;
     const int o = vb / per_offset;
     const int r = vb - o * per_offset;
@@ -50,7 +50,7 @@ struct AgGather {
     const int q = (c.rank + o) % c.size;
     return (g * c.size + q) * blocks_per_shard + j;
   }
-  __device__ __forceinline__ int map_m0(int m0) const {
+  __host__ __device__ __forceinline__ int map_m0(int m0) const {
     const int vb = m0 >> 8;
     return (map_block(vb, shard_blocks) << 8) + (m0 & 255);
   }
@@ -124,6 +124,19 @@ struct AgGather {
     }
   }
 };
+
+std::vector<int> gemm_allgather_row_order(int rank, int size, int segments, long long shard) {
+  AgGather ag;
+  memset(&ag, 0, sizeof(ag));
+  ag.c.rank = rank;
+  ag.c.size = size;
+  ag.segments = segments;
+  ag.shard_blocks = static_cast<int>(shard / 256);
+  std::vector<int> out;
+  const long long rows = static_cast<long long>(segments) * size * shard;
+  for (long long m0 = 0; m0 < rows; m0 += 256) out.push_back(ag.map_m0(static_cast<int>(m0)));
+  return out;
+}
 
 int gemm_allgather_grid(const GemmArgs& g) {
   const long long pair_tiles = static_cast<long long>((g.M + 255) / 256) * ((g.N + 511) / 512);

@@ -1,6 +1,8 @@
 // GEMM fused with an NVLink all-reduce of its output (see gemm_ar.cu).
 #pragma once
 
+#include <vector>
+
 #include "comm.h"
 #include "gemm.h"
 
@@ -22,6 +24,10 @@ int gemm_allreduce_launch(const GemmArgs& g, const CommDev& comm, cudaStream_t s
 // (A = xfull, M = segments * P * shard); this rank's shard must already be in its
 // symmetric region as [segments][shard][K].
 int gemm_allgather_grid(const GemmArgs& g);
+// Row origin (multiple of 256) of the gathered A that the i-th 256-row block of
+// the schedule reads on `rank`: this rank's shard first, then rank + 1, ...
+// (host walk of the kernel's mapping, for tests).
+std::vector<int> gemm_allgather_row_order(int rank, int size, int segments, long long shard);
 int gemm_allgather_launch(const GemmArgs& g, const CommDev& comm, void* xfull, int segments, long long shard,
                           cudaStream_t stream);
 
