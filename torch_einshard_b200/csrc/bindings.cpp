@@ -723,6 +723,29 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           return d;
         },
         "kernel choice for a GEMM shape (no launch; runs without a GPU)");
+  m.def("fft_slab_sources",
+        [](int64_t mode, int64_t n, int64_t A, int64_t B, int64_t C, int64_t D, int64_t Dl, int64_t doff,
+           int64_t size) {
+          es::FftSlab f{};
+          f.mode = static_cast<int>(mode);
+          f.n = n;
+          f.A = A;
+          f.B = B;
+          f.C = C;
+          f.D = D;
+          f.Dl = Dl;
+          f.doff = doff;
+          const int64_t total = A * B * C * Dl * n;
+          at::Tensor out_off = at::empty({total}, at::kLong), src_off = at::empty({total}, at::kLong);
+          at::Tensor src_rank = at::empty({total}, at::kInt);
+          const int rc = es::fft_slab_sources(f, static_cast<int>(size),
+                                              reinterpret_cast<long long*>(out_off.data_ptr<int64_t>()),
+                                              src_rank.data_ptr<int>(),
+                                              reinterpret_cast<long long*>(src_off.data_ptr<int64_t>()));
+          TORCH_CHECK(rc == 0, "fft_slab_sources: unsupported geometry");
+          return py::make_tuple(out_off, src_rank, src_off);
+        },
+        "host walk of the slab exchange's loads: output offsets, source ranks and offsets");
   m.def("gemm_allgather_row_order",
         [](int64_t rank, int64_t size, int64_t segments, int64_t shard) {
           return es::gemm_allgather_row_order(static_cast<int>(rank), static_cast<int>(size),

@@ -104,7 +104,7 @@ struct SlabLoader {
   int mode;  // 0: peer layout [A, Sl, B, D, C], output [A, S, B, Dl, C]; 1: [A, D, B, Sl, C] -> [A, Dl, B, S, C]
   int log_sl;
   long long B, C, D, Dl, doff, ps;
-  __device__ __forceinline__ long long base(long long o, long long i) const {
+  __host__ __device__ __forceinline__ long long base(long long o, long long i) const {
     if (mode == 0) {
       const long long dlc = Dl * C;
       const long long b = i / dlc;
@@ -463,16 +463,25 @@ int comm_wait_peers(const CommDev& c, int slot, int target, cudaStream_t stream)
   return static_cast<int>(cudaGetLastError());
 }
 
-int fft_slab(const CommDev& c, const FftSlab& f, cudaStream_t stream) {
-  const int logn = log2_exact(f.n);
-  const int log_sl = log2_exact(f.n / c.size);
-  if (logn < 1 || logn > kFftMaxLog || log_sl < 0 || f.n % c.size) return static_cast<int>(cudaErrorInvalidValue);
-  // publish: this rank's region holds its staged input for this epoch
-  publish_kernel<<<1, 1, 0, stream>>>(reinterpret_cast<int*>(c.flags[c.rank]) + kFlagStaged, c.epoch);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return static_cast<int>(e);
+namespace {
+
+// Output line geometry of the slab exchange: lines of length n, `inner`
+// neighbouring lines per outer index, output strides (outer, point, inner).
+struct SlabLines {
+  long long lines, inner, os, ps, is;
+};
+
+SlabLines slab_lines(const FftSlab& f) {
+  if (f.mode == 0) {  // output [A, S, B, Dl, C]
+    const long long inner = f.B * f.Dl * f.C;
+    return {f.A * inner, inner, f.n * inner, inner, 1};
+  }
+  // output [A, Dl, B, S, C]
+  return {f.A * f.Dl * f.B * f.C, f.C, f.n * f.C, f.C, 1};
+}
+
+SlabLoader slab_loader(const FftSlab& f, int log_sl) {
   SlabLoader ld{};
-  for (int p = 0; p < c.size; ++p) ld.peer[p] = reinterpret_cast<const float2*>(c.data[p]);
   ld.mode = f.mode;
   ld.log_sl = log_sl;
   ld.B = f.B;
@@ -481,6 +490,39 @@ int fft_slab(const CommDev& c, const FftSlab& f, cudaStream_t stream) {
   ld.Dl = f.Dl;
   ld.doff = f.doff;
   ld.ps = f.mode == 0 ? f.B * f.D * f.C : f.C;
+  return ld;
+}
+
+}  // namespace
+
+int fft_slab_sources(const FftSlab& f, int size, long long* out_off, int* src_rank, long long* src_off) {
+  const int log_sl = log2_exact(f.n / size);
+  if (log2_exact(f.n) < 1 || log_sl < 0 || f.n % size) return -1;
+  const SlabLoader ld = slab_loader(f, log_sl);
+  const SlabLines g = slab_lines(f);
+  long long k = 0;
+  for (long long l = 0; l < g.lines; ++l) {
+    const long long o = l / g.inner, i = l - (l / g.inner) * g.inner;
+    const long long b = ld.base(o, i);
+    for (long long p = 0; p < f.n; ++p, ++k) {
+      out_off[k] = o * g.os + i * g.is + p * g.ps;
+      src_rank[k] = static_cast<int>(p >> log_sl);
+      src_off[k] = b + (p & ((1LL << log_sl) - 1)) * ld.ps;
+    }
+  }
+  return 0;
+}
+
+int fft_slab(const CommDev& c, const FftSlab& f, cudaStream_t stream) {
+  const int logn = log2_exact(f.n);
+  const int log_sl = log2_exact(f.n / c.size);
+  if (logn < 1 || logn > kFftMaxLog || log_sl < 0 || f.n % c.size) return static_cast<int>(cudaErrorInvalidValue);
+  // publish: this rank's region holds its staged input for this epoch
+  publish_kernel<<<1, 1, 0, stream>>>(reinterpret_cast<int*>(c.flags[c.rank]) + kFlagStaged, c.epoch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return static_cast<int>(e);
+  SlabLoader ld = slab_loader(f, log_sl);
+  for (int p = 0; p < c.size; ++p) ld.peer[p] = reinterpret_cast<const float2*>(c.data[p]);
   SlabSync sync{};
   sync.enabled = 1;
   sync.size = c.size;
@@ -490,20 +532,8 @@ int fft_slab(const CommDev& c, const FftSlab& f, cudaStream_t stream) {
   sync.timeout_ns = c.timeout_ns;
   for (int p = 0; p < c.size; ++p) sync.peer_flags[p] = reinterpret_cast<int*>(c.flags[p]);
   sync.local_flags = reinterpret_cast<int*>(c.flags[c.rank]);
-  long long lines, inner, os, ps, is;
-  if (f.mode == 0) {  // output [A, S, B, Dl, C]
-    inner = f.B * f.Dl * f.C;
-    lines = f.A * inner;
-    os = f.n * inner;
-    ps = inner;
-    is = 1;
-  } else {  // output [A, Dl, B, S, C]
-    inner = f.C;
-    lines = f.A * f.Dl * f.B * inner;
-    os = f.n * f.C;
-    ps = f.C;
-    is = 1;
-  }
+  const SlabLines g = slab_lines(f);
+  const long long lines = g.lines, inner = g.inner, os = g.os, ps = g.ps, is = g.is;
   return f.inverse ? dispatch<true>(logn, ld, f.out, lines, inner, os, ps, is, f.tw, f.scale, sync, stream)
                    : dispatch<false>(logn, ld, f.out, lines, inner, os, ps, is, f.tw, f.scale, sync, stream);
 }

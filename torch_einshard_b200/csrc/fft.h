@@ -43,5 +43,9 @@ int fft_lines(const FftLines& f, cudaStream_t stream);
 // Wait (bounded, one thread) until every peer's flag `slot` reaches `target`.
 int comm_wait_peers(const CommDev& c, int slot, int target, cudaStream_t stream);
 int fft_slab(const CommDev& c, const FftSlab& f, cudaStream_t stream);
+// Host walk of the slab exchange's loads (for tests): for every output element
+// in line order, its output offset and the (rank, element offset) it is read
+// from in the peers' staged inputs.  Arrays hold lines * n entries.
+int fft_slab_sources(const FftSlab& f, int size, long long* out_off, int* src_rank, long long* src_off);
 
 }  // namespace es
