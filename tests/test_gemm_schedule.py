@@ -13,7 +13,8 @@ mod = _native.module()
 pytestmark = pytest.mark.skipif(mod is None, reason="native extension not built")
 
 SHAPES = [(3584, 8192, 32768), (2500, 4000, 4608), (2048, 2048, 65536), (65536, 2048, 2048), (512, 1024, 8192),
-          (1000, 1536, 4160), (768, 2048, 4100), (14336, 8192, 32768), (257, 513, 65)]
+          (1000, 1536, 4160), (768, 2048, 4100), (14336, 8192, 32768), (257, 513, 65),
+          (32768, 3584, 8192), (7168, 8192, 32768), (32768, 8192, 3584)]   # TP-MLP GEMMs at tp = 8 and 4
 
 
 def _check(m, n, k, sms=148):
@@ -63,6 +64,13 @@ def test_stream_k_tail_layout():
     for _, c, _, _, _, k0, k1 in tail:
         per_cluster[c] = per_cluster.get(c, 0) + k1 - k0
     assert len(per_cluster) <= 74 and max(per_cluster.values()) <= plan["sk_iters"]
+
+
+def test_tp8_forward_gets_a_tail_of_eight_tiles():
+    mod.set_gemm_pair_mode(-1)
+    mod.set_gemm_streamk(-1)
+    plan = mod.gemm_plan(32768, 3584, 8192, 1, False, False, 148)
+    assert plan["sk_first"] == 888 and plan["tail_tiles"] == 8
 
 
 def test_persistent_clusters_walk_strided_tiles():
