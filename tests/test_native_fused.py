@@ -176,3 +176,48 @@ def _sequence_parallel(rank, world):
 
 def test_sequence_parallel_fused_2gpu():
     run_gpus(_sequence_parallel, 2)
+
+
+def _overlap_ar(rank, world):
+    import torch.distributed as dist
+    from torch.distributed.device_mesh import init_device_mesh
+
+    import torch_einshard_b200 as es
+    from torch_einshard_b200.ops import _native, fused_native, gemm
+    from torch_einshard_b200.models.tp_mlp import TPMLP
+
+    mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
+    assert es.setup_native_comm(mesh)
+    group = mesh["tp"].get_group()
+    # the row pieces on the native GEMM, all-reduced on NCCL while the next piece runs
+    for m, chunks in [(2048, 4), (1000, 3)]:
+        a = torch.randn(1, m, 256, device="cuda", dtype=torch.bfloat16) * (rank + 1)
+        b = torch.randn(1, 384, 256, device="cuda", dtype=torch.bfloat16).transpose(1, 2)
+        got = fused_native.gemm_allreduce_overlapped(a, b, group, chunks, fused_native._native_gemm_into)
+        want = gemm.native_bmm(a, b).float()
+        dist.all_reduce(want, group=group)
+        scale = want.abs().max().item() + 1
+        assert (got.float() - want).abs().max().item() < 3e-2 * scale
+    # the TP-MLP with the overlap path selected, forward and backward against the plain path
+    old = fused_native._OVERLAP_AR_CHUNKS
+    try:
+        results = []
+        for chunks in (0, 4):
+            fused_native._OVERLAP_AR_CHUNKS = chunks
+            torch.manual_seed(7)
+            model = TPMLP(512, 2048, mesh, device="cuda")
+            x = torch.randn(4, 512, 512, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+            y = model(x)
+            y.float().square().mean().backward()
+            results.append((y.float(), model.w1.grad.float(), model.w2.grad.float()))
+        for plain, overlapped in zip(*results):
+            scale = plain.abs().max().item() + 1
+            assert (plain - overlapped).abs().max().item() < 2e-2 * scale
+    finally:
+        fused_native._OVERLAP_AR_CHUNKS = old
+    torch.cuda.synchronize()
+    _native.check_errors()
+
+
+def test_overlapped_row_parallel_allreduce_2gpu():
+    run_gpus(_overlap_ar, 2)

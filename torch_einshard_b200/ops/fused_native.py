@@ -206,6 +206,49 @@ class _GemmAllReduce(torch.autograd.Function):
         return ga, gb, None
 
 
+def gemm_allreduce_overlapped(a, b, group, chunks, gemm_into):
+    """out = all_reduce(a @ b) with the rows in ``chunks`` pieces: piece i's
+    all-reduce (``torch.distributed``, asynchronous) runs while piece i + 1's
+    GEMM runs, so the collective overlaps the contraction without a fused
+    kernel.  ``gemm_into(a_rows, b, out_rows)`` computes one piece in place.
+    Pieces are whole multiples of 256 rows (one wide-kernel tile row)."""
+    m, n = a.shape[1], b.shape[2]
+    out = torch.empty(a.shape[0], m, n, dtype=a.dtype, device=a.device)
+    step = -(-m // max(1, chunks))
+    step = -(-step // 256) * 256
+    works = []
+    for lo in range(0, m, step):
+        hi = min(m, lo + step)
+        piece = out[:, lo:hi]
+        gemm_into(a[:, lo:hi], b, piece)
+        works.append(dist.all_reduce(piece, group=group, async_op=True))
+    for work in works:
+        work.wait()
+    return out
+
+
+def _native_gemm_into(a, b, out):
+    _native.require().gemm_out(_prepare(a), _prepare(b), out, 0, _native.error_word(a.device))
+
+
+class _GemmAllReduceOverlap(torch.autograd.Function):
+    """Row-parallel contraction whose all-reduce overlaps the GEMM in row
+    pieces (forward); backward is the plain GEMM pair (the all-reduce's
+    adjoint is the identity)."""
+
+    @staticmethod
+    def forward(ctx, a, b, group, chunks):
+        ctx.save_for_backward(a, b)
+        return gemm_allreduce_overlapped(a, b, group, chunks, _native_gemm_into)
+
+    @staticmethod
+    def backward(ctx, grad):
+        a, b = ctx.saved_tensors
+        ga = native_bmm(grad, b.transpose(1, 2)) if ctx.needs_input_grad[0] else None
+        gb = _grad_b(a, b, grad) if ctx.needs_input_grad[1] else None
+        return ga, gb, None, None
+
+
 class _GemmDgradAllReduce(torch.autograd.Function):
     """Plain GEMM forward; the replicated operand's gradient is all-reduced in backward."""
 
@@ -231,10 +274,11 @@ class _GemmDgradAllReduce(torch.autograd.Function):
 
 
 class _Fusion:
-    def __init__(self, kind, operand=None, axis=None):
+    def __init__(self, kind, operand=None, axis=None, overlap_chunks=0):
         self.kind = kind
         self.operand = operand
         self.axis = axis  # gathered / scattered axis name
+        self.overlap_chunks = overlap_chunks  # gemm_allreduce: > 1 row pieces on torch.distributed, no fused kernel
 
     @staticmethod
     def _gemm_views(shard, x, y):
@@ -355,12 +399,15 @@ class _Fusion:
     def run_gemm_allreduce(self, shard, x, y, group):
         views = self._gemm_views(shard, x, y)
         comm = _comm(group)
-        if views is None or comm is None:
+        if views is None or (comm is None and self.overlap_chunks <= 1):
             from .einsum import einsum
             from ..parallel.mappings import allreduce_forward_identity_backward
             return allreduce_forward_identity_backward(einsum(shard, x, y), group)
         a, b, shape, perm = views
-        out = _GemmAllReduce.apply(a, b, comm)
+        if self.overlap_chunks > 1:
+            out = _GemmAllReduceOverlap.apply(a, b, group, self.overlap_chunks)
+        else:
+            out = _GemmAllReduce.apply(a, b, comm)
         return out.reshape(shape).permute(perm)
 
     def run_dgrad_allreduce(self, shard, x, y, group):
@@ -392,6 +439,10 @@ import os
 
 _MAX_FUSED_EPILOGUE_RANKS = int(os.environ.get("EINSHARD_FUSED_EPILOGUE_MAX_RANKS", "0"))
 _MAX_FUSED_GATHER_RANKS = int(os.environ.get("EINSHARD_FUSED_GATHER_MAX_RANKS", "2"))
+# Row-parallel all-reduce overlapped with the GEMM in this many row pieces (0: off,
+# the default until measured on B200): piece i's NCCL all-reduce runs while piece
+# i + 1's GEMM runs.
+_OVERLAP_AR_CHUNKS = int(os.environ.get("EINSHARD_OVERLAP_AR_CHUNKS", "0"))
 
 
 def _fusable(comm, limit):
@@ -423,8 +474,11 @@ def provider(executor):
         return None
     if (len(out_steps) == 1 and out_steps[0].name == "allreduce_forward_identity_backward"
             and not tp.input0_steps and not tp.input1_steps):
-        if _fusable(_comm(executor.group(out_steps[0].args[0])), _MAX_FUSED_EPILOGUE_RANKS):
+        group = executor.group(out_steps[0].args[0])
+        if _fusable(_comm(group), _MAX_FUSED_EPILOGUE_RANKS):
             return _Fusion("gemm_allreduce")
+        if _OVERLAP_AR_CHUNKS > 1 and dist.get_world_size(group) > 1:
+            return _Fusion("gemm_allreduce", overlap_chunks=_OVERLAP_AR_CHUNKS)
         return None
     if out_steps:
         return None
