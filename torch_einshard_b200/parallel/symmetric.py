@@ -19,7 +19,6 @@ reduce_scatter ``:114``, all_to_all_repartition ``:142``, owner_swap ``:184``,
 roll ``:224-309``.
 """
 
-import math
 import os
 import socket
 
