@@ -104,6 +104,7 @@ class ClockSampler:
         except subprocess.TimeoutExpired:
             self.proc.kill()
         self.thread.join(timeout=5)
+        self.proc.stdout.close()
         rows = []
         for stamp, line in self.lines:
             cols = [c.strip() for c in line.split(",")]
