@@ -2,8 +2,8 @@
 
     python benchmarks/compare.py BASE.jsonl NEW.jsonl [--metric max_over_ranks_ms] [--threshold 0.05]
 
-Records are matched on (name, world_size, size, device) and the chosen time
-metric (lower is better) is compared; when a record carries ``tflops`` or
+Records are matched on (name, world_size, size, device) (``bench.py`` lines on
+metric, n_gpus and impl) and the chosen time metric (lower is better) is compared; when a record carries ``tflops`` or
 ``gbs`` the throughput ratio is printed next to it.  Exit status 1 when any
 matched record is slower than ``1 + threshold`` times its base (a CI gate),
 0 otherwise.  The reference ships the same tool
@@ -18,6 +18,13 @@ import sys
 KEY_FIELDS = ("name", "world_size", "size", "device")
 
 
+def record_key(rec):
+    """(name, world_size, size, device); bench.py lines key on metric, n_gpus and impl."""
+    if "name" not in rec and "metric" in rec:
+        return (rec["metric"], rec.get("n_gpus"), rec.get("impl", "native"), None)
+    return tuple(rec.get(k) for k in KEY_FIELDS)
+
+
 def load(path):
     out = {}
     with open(path, encoding="utf-8") as f:
@@ -29,7 +36,7 @@ def load(path):
                 rec = json.loads(line)
             except ValueError as e:
                 raise SystemExit(f"{path}:{lineno}: not JSON: {e}")
-            key = tuple(rec.get(k) for k in KEY_FIELDS)
+            key = record_key(rec)
             out[key] = rec  # a later record of the same key replaces an earlier one
     return out
 

@@ -23,3 +23,13 @@ def test_compare_flags_regressions(tmp_path, capsys):
     out = capsys.readouterr().out
     assert "REGRESSION" in out and "faster" in out and "only in base" in out and "only in new" in out
     assert compare.main([str(base), str(new), "--threshold", "0.25"]) == 0
+
+
+def test_compare_reads_bench_lines(tmp_path):
+    base, new = tmp_path / "a.jsonl", tmp_path / "b.jsonl"
+    line = {"metric": "TP-contraction TFLOP/s", "n_gpus": 1, "impl": "native", "value": 1300.0}
+    _write(base, [dict(line, ms_per_step=70.0)])
+    _write(new, [dict(line, ms_per_step=80.0)])
+    assert compare.main([str(base), str(new)]) == 1
+    _write(new, [dict(line, ms_per_step=70.5)])
+    assert compare.main([str(base), str(new)]) == 0
