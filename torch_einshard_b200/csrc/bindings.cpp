@@ -16,6 +16,10 @@
 #include <memory>
 #include <vector>
 
+namespace es {
+int* noalloc_status_word();  // noalloc_gemm.cu
+}
+
 namespace {
 
 // Number of native kernel launches issued through these bindings (all devices).
@@ -593,6 +597,19 @@ void wait_probe(const at::Tensor& flag, int64_t target, int64_t timeout_ns, at::
   TORCH_CHECK(rc == 0, "einshard wait_probe: launch failed (", rc, ")");
 }
 
+// The same bounded wait, recording its code in the status word of the
+// allocation-free GEMM entry point (tests of es_gemm_bf16_noalloc_status).
+void wait_probe_noalloc_status(const at::Tensor& flag, int64_t target, int64_t timeout_ns, at::Tensor result) {
+  TORCH_CHECK(flag.is_cuda() && flag.scalar_type() == at::kInt && result.is_cuda() && result.scalar_type() == at::kInt,
+              "einshard wait_probe_noalloc_status: int32 CUDA tensors required");
+  const c10::cuda::CUDAGuard guard(flag.device());
+  int* status = es::noalloc_status_word();
+  TORCH_CHECK(status != nullptr, "einshard wait_probe_noalloc_status: no scratch address");
+  const int rc = es::wait_probe(flag.data_ptr<int>(), static_cast<int>(target), status, timeout_ns,
+                                result.data_ptr<int>(), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard wait_probe_noalloc_status: launch failed (", rc, ")");
+}
+
 // out (contiguous) = view (any strides, rank <= 8), one gather kernel.
 void strided_copy(const at::Tensor& view, at::Tensor out) {
   TORCH_CHECK(view.is_cuda() && out.is_cuda() && out.is_contiguous() && out.sizes() == view.sizes() &&
@@ -674,6 +691,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("conv2d_wgrad", &conv2d_wgrad, "weight gradient of the implicit-GEMM conv (split-K tcgen05, fp32 out)");
   m.def("conv2d_implicit", &conv2d_implicit, "implicit-GEMM NHWC conv2d on tcgen05 (stride 1)");
   m.def("wait_probe", &wait_probe, "bounded wait on a flag (tests the timeout path)");
+  m.def("wait_probe_noalloc_status", &wait_probe_noalloc_status,
+        "bounded wait recording into the allocation-free GEMM's status word (tests)");
   m.def("strided_copy", &strided_copy, "materialise a strided view contiguously");
   m.def("fft_c2c", &fft_c2c, "complex64 FFT along one dim (powers of two up to 1024)");
   m.def("comm_region", &comm_region, "this rank's symmetric data region as a uint8 tensor");

@@ -33,16 +33,27 @@
 //
 // Return codes: 0 success; -1 invalid arguments; -2 the padded operand copies
 // exceed the scratch size; -3 the scratch address could not be obtained;
-// -4 a launch or memset failed (the CUDA error is printed).
+// -4 a launch of this call failed (the CUDA error is printed);
+// -5 a CUDA error from earlier work of the caller was already pending when the
+// call began (left pending, nothing launched), so that -4 only ever reports
+// this call's own failures.
+//
+// Status word.  The GEMM's waits are bounded: if one runs out (a stalled
+// pipeline), the kernel writes an error code into the status word and exits
+// early, leaving C incomplete, while the launch itself succeeded and the call
+// returned 0.  es_gemm_bf16_noalloc_status() reports that code: it waits for
+// the caller's stream, copies the word to the host and clears it.
 //
 // Set-up and sharing.  On the first call on each device (with that device
 // current), the entry point looks the scratch array up with
 // cudaGetSymbolAddress and caches the address; make that first call before
 // any stream capture.  Every call on a device shares the one array and it
-// keeps the previous call's contents: the status word is cleared at the start
-// of each call, the padded copies are rewritten in full.  Calls that overlap
-// on the GPU (different streams without ordering between them) race on the
-// scratch and must not be issued.
+// keeps the previous call's contents: the padded copies are rewritten in full
+// by each call that needs them; the status word starts at zero (static device
+// memory is zero-initialised when the library loads), keeps the first error
+// code written into it, and is cleared only by es_gemm_bf16_noalloc_status.
+// Calls that overlap on the GPU (different streams without ordering between
+// them) race on the scratch and must not be issued.
 #include <cuda_bf16.h>
 #include <stdio.h>
 
@@ -58,6 +69,24 @@ constexpr size_t kStatusBytes = 256;                // status word (kernels set 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kStatusBytes + kNoAllocScratchBytes];
 
 void* g_scratch_addr[64] = {nullptr};  // host-side cache of the device address, per device
+
+// Device address of this device's scratch array (looked up once per device,
+// with that device current); nullptr on failure.
+unsigned char* scratch_base(int* dev_out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (dev_out) *dev_out = dev;
+  if (!g_scratch_addr[dev]) {
+    void* addr = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
+    if (e != cudaSuccess || addr == nullptr) {
+      fprintf(stderr, "es_gemm_bf16_noalloc: cudaGetSymbolAddress failed: %s\n", cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_scratch_addr[dev] = addr;
+  }
+  return static_cast<unsigned char*>(g_scratch_addr[dev]);
+}
 
 __global__ void pad_rows_kernel(const __nv_bfloat16* src, long long src_pitch, __nv_bfloat16* dst,
                                 long long dst_pitch, long long rows, long long cols) {
@@ -87,18 +116,12 @@ extern "C" int es_gemm_bf16_noalloc(const void* A, long long lda, int a_mn, cons
   if (lda < a_cols || ldb < b_cols || ldc < N) return -1;
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_handle);
 
+  // an error left pending by the caller's earlier work would be read back (and
+  // cleared) by the launch checks below and misreported as this call's failure
+  if (cudaPeekAtLastError() != cudaSuccess) return -5;
   int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return -3;
-  if (!g_scratch_addr[dev]) {
-    void* addr = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_scratch);
-    if (e != cudaSuccess || addr == nullptr) {
-      fprintf(stderr, "es_gemm_bf16_noalloc: cudaGetSymbolAddress failed: %s\n", cudaGetErrorString(e));
-      return -3;
-    }
-    g_scratch_addr[dev] = addr;
-  }
-  unsigned char* scratch = static_cast<unsigned char*>(g_scratch_addr[dev]);
+  unsigned char* scratch = scratch_base(&dev);
+  if (!scratch) return -3;
   int* status = reinterpret_cast<int*>(scratch);
   unsigned char* pad_area = scratch + kStatusBytes;
 
@@ -117,7 +140,7 @@ extern "C" int es_gemm_bf16_noalloc(const void* A, long long lda, int a_mn, cons
     return -2;
   }
 
-  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int), stream);
+  cudaError_t e = cudaSuccess;
   const void* a_use = A;
   const void* b_use = B;
   if (e == cudaSuccess && pad_a) {
@@ -164,3 +187,27 @@ extern "C" int es_gemm_bf16_noalloc(const void* A, long long lda, int a_mn, cons
   }
   return 0;
 }
+
+extern "C" int es_gemm_bf16_noalloc_status(int* code, void* stream_handle) {
+  if (!code) return -1;
+  unsigned char* scratch = scratch_base(nullptr);
+  if (!scratch) return -3;
+  cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_handle);
+  int value = 0;
+  cudaError_t e = cudaMemcpyAsync(&value, scratch, sizeof(int), cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e == cudaSuccess && value != 0) e = cudaMemsetAsync(scratch, 0, sizeof(int), stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) {
+    fprintf(stderr, "es_gemm_bf16_noalloc_status: %s\n", cudaGetErrorString(e));
+    return -4;
+  }
+  *code = value;
+  return 0;
+}
+
+namespace es {
+// Device address of the status word (the first int of the scratch array), for
+// the tests that make a bounded wait run out against it; nullptr on failure.
+int* noalloc_status_word() { return reinterpret_cast<int*>(scratch_base(nullptr)); }
+}  // namespace es

@@ -5,10 +5,11 @@
     y_p = einshard("b n h/tp, c h/tp -> b n c // tp", a, w2)  row parallel, partial sums
     y   = einshard("b n c // tp -> b n c", y_p)                all-reduce over tp
 
-The column-parallel step plans ``identity_forward_allreduce_backward`` on x
-(its gradient is all-reduced in backward) and the row-parallel step ends with
-an all-reduce; on the native path both the forward all-reduce and the
-backward input-gradient all-reduce are fused into the GEMM that produces them.
+The column-parallel step is a rank-local contraction (no collective; the
+gradient of the replicated x stays a partial sum over tp, as in the
+reference's executor) and the row-parallel step ends with one all-reduce over
+tp.  Which kernel runs that all-reduce is decided by the fusion policy in
+``ops/fused_native.py`` (group size, shapes, environment overrides).
 
 The pattern is the reference's tensor-parallel MLP
 (``docs/user-guide/tensor-parallel.md``, ``tests/test_scigpt_patterns.py``);
