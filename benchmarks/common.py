@@ -16,7 +16,9 @@ import argparse
 import json
 import os
 import statistics
+import subprocess
 import sys
+import threading
 import time
 from contextlib import nullcontext
 
@@ -159,3 +161,84 @@ def benchmark(name, fn, *, args, device, writer, flops=None, bytes_moved=None, e
             record[f"ratio_to_{key}"] = worst / value
     writer.write(record)
     return record
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi (every 100 ms) and
+    keeps the samples that arrive during the timed region (host-stamped on
+    arrival).  Started before the warm-up so the sampler is running when the
+    timed region begins; a region shorter than the interval keeps the sample
+    nearest to it."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, devices):
+        self.devices = set(devices)
+        self.proc = None
+        self.lines = []
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:  # noqa: BLE001 - clocks are best-effort metadata
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line))
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.thread.join(timeout=5)
+        self.proc.stdout.close()
+        rows = []
+        for stamp, line in self.lines:
+            cols = [c.strip() for c in line.split(",")]
+            if len(cols) < 9 or not cols[0].isdigit() or int(cols[0]) not in self.devices:
+                continue
+            try:
+                rows.append((stamp, float(cols[1]), float(cols[2]), cols[5:9]))
+            except ValueError:
+                continue
+        t0, t1 = self.t0 or 0.0, self.t1 or time.time()
+        inside = [r for r in rows if t0 <= r[0] <= t1 + 0.1]
+        if not inside and rows:
+            mid = 0.5 * (t0 + t1)
+            nearest = min(abs(r[0] - mid) for r in rows)
+            inside = [r for r in rows if abs(r[0] - mid) == nearest]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = {name for r in inside for name, value in zip(names, r[3]) if value.lower() == "active"}
+        sm = sorted(r[1] for r in inside)
+        out = {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": max(r[2] for r in inside) if inside else None,
+               "reasons": sorted(reasons), "samples": len(sm)}
+        keep = os.environ.get("EINSHARD_CLOCKS_DIR")
+        if keep:
+            with open(os.path.join(keep, f"einshard_clocks_{os.getpid()}.csv"), "w") as f:
+                f.writelines(f"{stamp:.3f},{line}" for stamp, line in self.lines)
+        return out
+
+
+def visible_gpu_indices(world):
+    """nvidia-smi indices of this job's GPUs (CUDA_VISIBLE_DEVICES when it lists indices)."""
+    listed = [v.strip() for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    if listed and all(v.isdigit() for v in listed):
+        return [int(v) for v in listed[:world]]
+    return list(range(world))

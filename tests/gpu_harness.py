@@ -18,12 +18,13 @@ def _free_port():
         return sock.getsockname()[1]
 
 
-def _worker(rank, world, port, body, queue):
+def _worker(rank, world, port, body, queue, env):
     try:
         import torch
         import torch.distributed as dist
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
                           WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+        os.environ.update(env or {})
         torch.cuda.set_device(rank)
         dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
                                 device_id=torch.device("cuda", rank))
@@ -37,11 +38,12 @@ def _worker(rank, world, port, body, queue):
         queue.put((rank, traceback.format_exc()))
 
 
-def run_gpus(body, world, timeout=300):
+def run_gpus(body, world, timeout=300, env=None):
+    """``env``: extra environment variables of every rank (set before the body runs)."""
     ctx = mp.get_context("spawn")
     queue = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, body, queue)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, body, queue, env)) for r in range(world)]
     for proc in procs:
         proc.start()
     results = {}

@@ -18,6 +18,16 @@ class FakeMod:
     def comm_all_reduce_push(self, cid, piece, scale, blocks, err):
         self.calls.append(("push", piece.numel() * piece.element_size(), scale))
 
+    def nvls_all_reduce(self, cid, inp, out, scale, two_shot, err):
+        assert inp is out
+        self.calls.append(("nvls2" if two_shot else "nvls1", inp.numel() * inp.element_size(), scale))
+
+    def comm_acquire(self, cid, err):
+        self.calls.append(("acquire",))
+
+    def nvls_quiesce(self, cid, err):
+        self.calls.append(("quiesce",))
+
 
 def make_comm(size=2, capacity=64 << 20):
     comm = object.__new__(symmetric.Communicator)
@@ -26,6 +36,8 @@ def make_comm(size=2, capacity=64 << 20):
     comm.size = size
     comm.capacity = capacity
     comm.broken = False
+    comm.closed = False
+    comm.nvls = False
     comm.sms = 148
     comm.err = None
     return comm
@@ -75,3 +87,42 @@ def test_declines_what_the_kernel_cannot_take(monkeypatch):
     comm.broken = True
     assert comm.all_reduce_(torch.zeros(16)) is False                              # after a timeout
     assert comm.mod.calls == []
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_nvls_heaps_take_every_size(size, monkeypatch):
+    """With a multicast mapping every all-reduce runs through the switch:
+    one-shot up to the switch-over size, two-shot above it."""
+    monkeypatch.delenv("EINSHARD_FAULT_INJECT", raising=False)
+    comm = make_comm(size)
+    comm.nvls = True
+    small = torch.zeros(symmetric._NVLS_ONE_SHOT_MAX // 2, dtype=torch.bfloat16)
+    large = torch.zeros(8 << 20, dtype=torch.bfloat16)       # 16 MiB
+    assert comm.all_reduce_(small, 0.5) and comm.all_reduce_(large)
+    assert comm.mod.calls == [("nvls1", symmetric._NVLS_ONE_SHOT_MAX, 0.5), ("nvls2", 16 << 20, 1.0)]
+
+
+def test_nvls_pieces_when_larger_than_the_workspace(monkeypatch):
+    monkeypatch.delenv("EINSHARD_FAULT_INJECT", raising=False)
+    comm = make_comm(2, capacity=4 << 20)
+    comm.nvls = True
+    monkeypatch.setattr(symmetric, "workspace_for_group", lambda group, nbytes: comm)
+    comm.group = None
+    assert comm.all_reduce_(torch.zeros(5 << 20, dtype=torch.float32))   # 20 MiB through 4 MiB
+    sizes = [c[1] for c in comm.mod.calls]
+    assert sum(sizes) == 20 << 20 and all(b <= comm.capacity for b in sizes)
+
+
+def test_protocol_switch_waits_for_the_other_kind(monkeypatch):
+    """A copy-protocol kernel after NVLS collectives waits for their completion
+    on every rank (quiesce), and an NVLS collective after copy kernels waits for
+    peers' reads (acquire)."""
+    monkeypatch.delenv("EINSHARD_FAULT_INJECT", raising=False)
+    comm = make_comm(2)
+    comm.nvls = True
+    comm.all_reduce_(torch.zeros(64, dtype=torch.float32))
+    comm.enter("copy")
+    comm.enter("copy")
+    comm.all_reduce_(torch.zeros(64, dtype=torch.float32))
+    kinds = [c[0] for c in comm.mod.calls]
+    assert kinds == ["nvls1", "quiesce", "acquire", "nvls1"]

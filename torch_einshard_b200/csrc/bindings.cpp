@@ -11,6 +11,8 @@
 #include "fft.h"
 #include "gemm.h"
 #include "gemm_ar.h"
+#include "nvls.h"
+#include "symm.h"
 #include "tma_desc.h"
 
 #include <memory>
@@ -157,12 +159,17 @@ void gemm_out(const at::Tensor& a, const at::Tensor& b, at::Tensor out, int64_t 
 
 struct HostComm {
   int rank = 0, size = 1, device = 0;
-  void* local = nullptr;
-  std::vector<void*> bases;  // per rank: flags base (peer-mapped for peers)
+  es::SymmHeap heap;         // cuMem allocations of every rank + multicast object (symm.h)
+  void* local = nullptr;     // this rank's heap: [flags][data]
+  std::vector<void*> bases;  // per rank: heap base (peer-mapped for peers)
+  void* mc = nullptr;        // multicast view of the heap (nullptr without NVLS)
   size_t data_bytes = 0;
   int epoch = 0;
   uint32_t bar = 0;
   uint32_t arrive = 0;
+  int nvls_epoch = 0;        // collectives issued on the NVLS counters
+  int nvls_blocks = 0;       // fixed block count of every NVLS collective on this heap
+  int tile_epoch = 0;        // fused GEMM + all-reduce calls (per-unit counters)
   bool open = false;
 };
 
@@ -173,46 +180,69 @@ HostComm& comm_ref(int64_t id) {
   return *g_comms[id];
 }
 
-py::tuple comm_create(int64_t data_bytes, int64_t device) {
+bool symm_multicast_supported(int64_t device) { return es::symm_multicast_supported(static_cast<int>(device)); }
+
+// Phase 1 of creating a communicator over a symmetric heap (symm.h): allocate
+// this rank's memory (and, on rank 0, the multicast object) and open the
+// socket peers fetch the descriptors from.  Returns (id, error message).
+py::tuple symm_prepare(int64_t data_bytes, int64_t device, const std::string& tag, int64_t rank, int64_t size,
+                       bool want_mc, int64_t nvls_blocks) {
+  TORCH_CHECK(size >= 1 && size <= es::kMaxRanks, "einshard comm: 1 to 8 ranks");
+  TORCH_CHECK(nvls_blocks >= 1 && nvls_blocks <= es::kNvlsMaxBlocks, "einshard comm: NVLS block count");
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(device));
   auto hc = std::make_unique<HostComm>();
-  char handle[64];
-  hc->local = es::comm_alloc(static_cast<size_t>(data_bytes), handle);
-  TORCH_CHECK(hc->local != nullptr, "einshard comm: cudaMalloc/IPC handle failed");
-  hc->data_bytes = static_cast<size_t>(data_bytes);
+  hc->rank = static_cast<int>(rank);
+  hc->size = static_cast<int>(size);
   hc->device = static_cast<int>(device);
+  hc->nvls_blocks = static_cast<int>(nvls_blocks);
+  const std::string err = es::symm_prepare(hc->heap, es::kFlagBytes + static_cast<size_t>(data_bytes),
+                                           static_cast<int>(device), tag, hc->rank, hc->size, want_mc);
   g_comms.push_back(std::move(hc));
-  return py::make_tuple(static_cast<int64_t>(g_comms.size() - 1), py::bytes(handle, 64));
+  return py::make_tuple(static_cast<int64_t>(g_comms.size() - 1), err);
 }
 
-void comm_connect(int64_t id, int64_t rank, std::vector<std::string> handles) {
+// Phase 2: fetch peers' descriptors, map every rank's memory, join the multicast team.
+std::string symm_exchange(int64_t id, double timeout_s) {
   HostComm& hc = comm_ref(id);
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(hc.device));
-  TORCH_CHECK((int)handles.size() <= es::kMaxRanks, "einshard comm: at most 8 ranks");
-  hc.rank = static_cast<int>(rank);
-  hc.size = static_cast<int>(handles.size());
-  hc.bases.assign(hc.size, nullptr);
-  for (int p = 0; p < hc.size; ++p) {
-    if (p == hc.rank) {
-      hc.bases[p] = hc.local;
-      continue;
-    }
-    TORCH_CHECK(handles[p].size() == 64, "einshard comm: bad IPC handle");
-    hc.bases[p] = es::comm_open_peer(handles[p].data());
-    TORCH_CHECK(hc.bases[p] != nullptr, "einshard comm: cudaIpcOpenMemHandle failed for rank ", p);
-  }
-  hc.open = true;
+  return es::symm_exchange(hc.heap, timeout_s);
 }
 
+// Phase 3 (after every rank joined the team): bind this rank's memory to the multicast object.
+std::string symm_bind(int64_t id) {
+  HostComm& hc = comm_ref(id);
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(hc.device));
+  return es::symm_bind(hc.heap);
+}
+
+// Phase 4: map the multicast object, zero this rank's flag words, open the communicator.
+std::string symm_finish(int64_t id) {
+  HostComm& hc = comm_ref(id);
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(hc.device));
+  std::string err = es::symm_map_mc(hc.heap);
+  if (!err.empty()) return err;
+  const es::SymmHeap& h = hc.heap;
+  hc.bases.assign(hc.size, nullptr);
+  for (int p = 0; p < hc.size; ++p) hc.bases[p] = reinterpret_cast<void*>(h.uc_base + p * h.bytes);
+  hc.local = hc.bases[hc.rank];
+  hc.mc = h.mc_mapped ? reinterpret_cast<void*>(h.mc_base) : nullptr;
+  hc.data_bytes = h.bytes - es::kFlagBytes;
+  if (cudaMemset(hc.local, 0, es::kFlagBytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
+    return "zeroing the flag words failed";
+  hc.open = true;
+  return "";
+}
+
+// Unmap and free (after a device synchronisation and a barrier of every rank).
 void comm_destroy(int64_t id) {
   HostComm& hc = comm_ref(id);
   const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(hc.device));
   cudaDeviceSynchronize();
-  for (int p = 0; p < hc.size; ++p)
-    if (p != hc.rank) es::comm_close_peer(hc.bases[p]);
-  es::comm_free(hc.local);
+  es::symm_destroy(hc.heap);
   g_comms[id].reset();
 }
+
+bool comm_has_multicast(int64_t id) { return comm_ref(id).mc != nullptr; }
 
 es::CommDev make_dev(HostComm& hc, const at::Tensor& err, int nblocks, int nbarriers) {
   es::CommDev d;
@@ -307,6 +337,116 @@ void comm_copy(int64_t id, at::Tensor src, int64_t stage_bytes, at::Tensor dst, 
                         : es::comm_stage_and_copy(d, sp, stage_bytes, 0, dst.data_ptr(), plan, static_cast<int>(nblocks),
                                                   at::cuda::getCurrentCUDAStream());
   TORCH_CHECK(rc == 0, "einshard comm copy: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// ------------------------------------------------------------------ NVLS collectives
+
+es::NvlsDev nvls_dev(HostComm& hc, const at::Tensor& err) {
+  TORCH_CHECK(hc.open && hc.mc != nullptr, "einshard NVLS: communicator has no multicast mapping");
+  es::NvlsDev d;
+  d.uc = static_cast<uint8_t*>(hc.local) + es::kFlagBytes;
+  d.mc = static_cast<uint8_t*>(hc.mc) + es::kFlagBytes;
+  d.flags = static_cast<uint32_t*>(hc.local);
+  d.mcflags = static_cast<uint32_t*>(hc.mc);
+  d.rank = hc.rank;
+  d.size = hc.size;
+  d.epoch = ++hc.nvls_epoch;
+  d.nblocks = hc.nvls_blocks;
+  d.err = err.data_ptr<int>();
+  d.timeout_ns = g_wait_timeout_ns;
+  return d;
+}
+
+// Stream-ordered wait for the completion of this heap's NVLS collectives on every rank.
+void nvls_quiesce(int64_t id, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  if (hc.mc == nullptr || hc.nvls_epoch == 0) return;
+  const c10::cuda::CUDAGuard guard(static_cast<c10::DeviceIndex>(hc.device));
+  es::NvlsDev d = nvls_dev(hc, err);
+  d.epoch = --hc.nvls_epoch;  // the last issued collective (nvls_dev advanced the counter)
+  const int rc = es::nvls_quiesce(d, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard NVLS quiesce: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+bool aligned16(const at::Tensor& t) { return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0; }
+
+// All-reduce of a contiguous tensor through the switch: out = scale * sum over
+// ranks of `in` (out may be `in`).  The heap's data region must hold the
+// tensor rounded up to 16 bytes.
+void nvls_all_reduce(int64_t id, const at::Tensor& in, at::Tensor out, double scale, bool two_shot,
+                     const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(in.is_cuda() && in.is_contiguous() && out.is_contiguous() && out.sizes() == in.sizes() &&
+                  out.scalar_type() == in.scalar_type() && aligned16(in) && aligned16(out),
+              "einshard NVLS all-reduce: contiguous 16-byte aligned tensors of equal shape");
+  TORCH_CHECK(in.scalar_type() == at::kBFloat16 || in.scalar_type() == at::kHalf || in.scalar_type() == at::kFloat,
+              "einshard NVLS all-reduce: bf16, f16 or f32");
+  const long long nbytes = in.numel() * in.element_size();
+  TORCH_CHECK((size_t)((nbytes + 15) / 16 * 16) <= hc.data_bytes, "einshard NVLS all-reduce: larger than the heap");
+  const c10::cuda::CUDAGuard guard(in.device());
+  es::NvlsDev d = nvls_dev(hc, err);
+  const int rc = es::nvls_all_reduce(d, in.data_ptr(), out.data_ptr(), nbytes, es_dtype(in), static_cast<float>(scale),
+                                     two_shot ? 1 : 0, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard NVLS all-reduce: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+es::ShardLayout shard_layout(HostComm& hc, int64_t outer, int64_t inner_bytes, const std::vector<int64_t>& lens) {
+  TORCH_CHECK((int)lens.size() == hc.size, "einshard NVLS: one shard length per rank");
+  es::ShardLayout L;
+  L.outer = outer;
+  L.inner_bytes = inner_bytes;
+  long long off = 0, region = 0;
+  for (int q = 0; q < hc.size; ++q) {
+    TORCH_CHECK(lens[q] >= 0, "einshard NVLS: negative shard length");
+    L.off[q] = off;
+    L.len[q] = lens[q];
+    L.region[q] = region;
+    off += lens[q];
+    region += (outer * lens[q] * inner_bytes + 255) / 256 * 256;
+  }
+  L.off[hc.size] = off;
+  L.total_rows = off;
+  TORCH_CHECK((size_t)region <= hc.data_bytes, "einshard NVLS: shards larger than the heap");
+  return L;
+}
+
+// out ([outer, sum(lens), inner], contiguous) <- every rank's `in` ([outer, lens[rank], inner]).
+void nvls_all_gather(int64_t id, const at::Tensor& in, at::Tensor out, int64_t outer, int64_t inner,
+                     std::vector<int64_t> lens, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(in.is_cuda() && in.is_contiguous() && out.is_contiguous() && aligned16(in) &&
+                  out.scalar_type() == in.scalar_type(),
+              "einshard NVLS all-gather: contiguous tensors, 16-byte aligned input");
+  es::ShardLayout L = shard_layout(hc, outer, inner * in.element_size(), lens);
+  TORCH_CHECK(in.numel() == outer * lens[hc.rank] * inner && out.numel() == outer * L.total_rows * inner,
+              "einshard NVLS all-gather: sizes");
+  const c10::cuda::CUDAGuard guard(in.device());
+  es::NvlsDev d = nvls_dev(hc, err);
+  const int rc = es::nvls_all_gather(d, in.data_ptr(), out.data_ptr(), L, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard NVLS all-gather: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// out ([outer, lens[rank], inner]) <- scale * sum over ranks of this rank's rows of `in` ([outer, sum(lens), inner]).
+void nvls_reduce_scatter(int64_t id, const at::Tensor& in, at::Tensor out, int64_t outer, int64_t inner,
+                         std::vector<int64_t> lens, double scale, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(in.is_cuda() && in.is_contiguous() && out.is_contiguous() && aligned16(out) &&
+                  out.scalar_type() == in.scalar_type(),
+              "einshard NVLS reduce-scatter: contiguous tensors, 16-byte aligned output");
+  TORCH_CHECK(in.scalar_type() == at::kBFloat16 || in.scalar_type() == at::kHalf || in.scalar_type() == at::kFloat,
+              "einshard NVLS reduce-scatter: bf16, f16 or f32");
+  es::ShardLayout L = shard_layout(hc, outer, inner * in.element_size(), lens);
+  TORCH_CHECK(out.numel() == outer * lens[hc.rank] * inner && in.numel() == outer * L.total_rows * inner,
+              "einshard NVLS reduce-scatter: sizes");
+  const c10::cuda::CUDAGuard guard(in.device());
+  es::NvlsDev d = nvls_dev(hc, err);
+  const int rc = es::nvls_reduce_scatter(d, in.data_ptr(), out.data_ptr(), L, es_dtype(in), static_cast<float>(scale),
+                                         at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard NVLS reduce-scatter: launch failed (", rc, ")");
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
@@ -681,9 +821,17 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "einshard sm_100a native kernels";
   m.def("gemm", &gemm, "C = act(A @ B), tcgen05 GEMM (A [B,M,K], B [B,K,N])");
   m.def("gemm_out", &gemm_out, "gemm into a preallocated row-major output");
-  m.def("comm_create", &comm_create, "allocate a symmetric buffer; returns (id, ipc handle)");
-  m.def("comm_connect", &comm_connect, "map every rank's buffer");
+  m.def("symm_multicast_supported", &symm_multicast_supported, "whether a device supports NVLS multicast objects");
+  m.def("symm_prepare", &symm_prepare, "communicator over a symmetric heap, phase 1: returns (id, error)");
+  m.def("symm_exchange", &symm_exchange, "phase 2: exchange descriptors, map peers, join the multicast team");
+  m.def("symm_bind", &symm_bind, "phase 3: bind this rank's memory to the multicast object");
+  m.def("symm_finish", &symm_finish, "phase 4: map the multicast object, zero the flags");
   m.def("comm_destroy", &comm_destroy, "unmap and free");
+  m.def("comm_has_multicast", &comm_has_multicast, "whether the communicator has an NVLS multicast mapping");
+  m.def("nvls_quiesce", &nvls_quiesce, "wait until every rank completed this heap's NVLS collectives");
+  m.def("nvls_all_reduce", &nvls_all_reduce, "all-reduce through the NVSwitch (multimem), one- or two-shot");
+  m.def("nvls_all_gather", &nvls_all_gather, "all-gather along a dimension through multicast stores");
+  m.def("nvls_reduce_scatter", &nvls_reduce_scatter, "reduce-scatter along a dimension through the NVSwitch");
   m.def("comm_all_reduce", &comm_all_reduce, "two-shot NVLink all-reduce in place");
   m.def("comm_all_reduce_push", &comm_all_reduce_push, "two-shot NVLink all-reduce in place, stores only");
   m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)");

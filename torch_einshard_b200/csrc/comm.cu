@@ -8,41 +8,6 @@
 
 namespace es {
 
-// ------------------------------------------------------------------ host: memory
-
-void* comm_alloc(size_t data_bytes, void* ipc_handle_out) {
-  void* ptr = nullptr;
-  if (cudaMalloc(&ptr, kFlagBytes + data_bytes) != cudaSuccess) return nullptr;
-  if (cudaMemset(ptr, 0, kFlagBytes) != cudaSuccess) {
-    cudaFree(ptr);
-    return nullptr;
-  }
-  cudaIpcMemHandle_t h;
-  if (cudaIpcGetMemHandle(&h, ptr) != cudaSuccess) {
-    cudaFree(ptr);
-    return nullptr;
-  }
-  memcpy(ipc_handle_out, &h, sizeof(h));
-  cudaDeviceSynchronize();
-  return ptr;
-}
-
-void* comm_open_peer(const void* ipc_handle) {
-  cudaIpcMemHandle_t h;
-  memcpy(&h, ipc_handle, sizeof(h));
-  void* ptr = nullptr;
-  if (cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) return nullptr;
-  return ptr;
-}
-
-void comm_close_peer(void* ptr) {
-  if (ptr) cudaIpcCloseMemHandle(ptr);
-}
-
-void comm_free(void* ptr) {
-  if (ptr) cudaFree(ptr);
-}
-
 // ------------------------------------------------------------------ device helpers
 
 __device__ __forceinline__ int* flag_at(const CommDev& c, int rank, int slot) {

@@ -1,8 +1,8 @@
 // Native NVLink communicator: symmetric peer-mapped buffers and pull-based
 // collectives for one node (up to 8 ranks, one process per GPU).
 //
-// Each rank owns one device allocation: [flags (kFlagBytes)][data (data_bytes)].
-// Peers map it with CUDA IPC.  Only *reads* cross NVLink in the collectives
+// Each rank owns one device allocation: [flags (kFlagBytes)][data (data_bytes)],
+// a cuMem heap that peers map (symm.h).  Only *reads* cross NVLink in the collectives
 // (every rank writes only its own memory), which keeps buffer reuse safe with
 // three monotonic epoch flags per rank:
 //   staged  - this rank's input for op e is in its data region
@@ -18,7 +18,7 @@
 namespace es {
 
 constexpr int kMaxRanks = 8;
-constexpr size_t kFlagBytes = 1 << 20;  // 256K int32 flag slots
+constexpr size_t kFlagBytes = 2 << 20;  // 512K int32 flag slots (upper half: NVLS counters, nvls.h)
 // flag slot indices
 constexpr int kFlagDone = 0;
 constexpr int kFlagStaged = 1;
@@ -64,12 +64,7 @@ struct CopyPlan {
   CopyBox box[kMaxBoxes];
 };
 
-// host API (comm.cu)
-void* comm_alloc(size_t data_bytes, void* ipc_handle_out /*64 bytes*/);
-void* comm_open_peer(const void* ipc_handle /*64 bytes*/);
-void comm_close_peer(void* ptr);
-void comm_free(void* ptr);
-
+// host API (comm.cu); the buffers come from the symmetric heap (symm.h)
 // Stage `nbytes` of `src` into this rank's data region at `stage_off`, publish
 // it, then run `plan` (copies from peers' staged data into `dst`).  With
 // nbytes == 0 nothing is staged (the plan may read regions staged earlier).

@@ -38,6 +38,7 @@ def gemm_allreduce(comm, a, b):
     mod = _native.require()
     a, b = _prepare(a), _prepare(b)
     out = torch.empty((1, a.shape[1], b.shape[2]), dtype=torch.bfloat16, device=a.device)
+    comm.enter("copy")
     mod.gemm_allreduce(comm.cid, a, b, out, _native.error_word(a.device))
     return out
 
@@ -48,6 +49,7 @@ def gemm_allreduce_push(comm, a, b):
     mod = _native.require()
     a, b = _prepare(a), _prepare(b)
     out = torch.empty((1, a.shape[1], b.shape[2]), dtype=torch.bfloat16, device=a.device)
+    comm.enter("copy")
     mod.gemm_allreduce_push(comm.cid, a, b, out, _native.error_word(a.device))
     return out
 
@@ -65,6 +67,7 @@ def gemm_reducescatter(comm, a, b, seg, shard):
     mod = _native.require()
     a, b = _prepare(a), _prepare(b)
     out = torch.empty((1, a.shape[1] // comm.size, b.shape[2]), dtype=torch.bfloat16, device=a.device)
+    comm.enter("copy")
     mod.gemm_reducescatter(comm.cid, a, b, out, seg, shard, _native.error_word(a.device))
     return out
 
@@ -78,6 +81,7 @@ def gemm_allgather(comm, a_local, b, seg, shard):
     rows = a_local.shape[1] * comm.size
     xfull = torch.empty((1, rows, a_local.shape[2]), dtype=torch.bfloat16, device=a_local.device)
     out = torch.empty((1, rows, b.shape[2]), dtype=torch.bfloat16, device=a_local.device)
+    comm.enter("copy")
     mod.gemm_allgather(comm.cid, a_local, b, out, xfull, seg, shard, _native.error_word(a_local.device))
     return out, xfull
 
@@ -145,7 +149,10 @@ class _AllGatherGemm(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, a_local, b, comm, seg, shard):
-        if _ag_fits(comm, a_local, seg, shard):
+        from ..parallel import native_comm
+        ws = native_comm.workspace_for(comm.group, a_local.numel() * a_local.element_size())
+        if ws is not None and _ag_fits(ws, a_local, seg, shard):
+            comm = ws
             out, a_full = gemm_allgather(comm, a_local, b, seg, shard)
         else:
             a_full = _gather_rows(comm, a_local.contiguous(), seg, shard)

@@ -1,17 +1,27 @@
-"""Native NVLink communicators built on peer-mapped symmetric buffers.
+"""Native NVLink communicators built on a symmetric device heap.
 
 ``activate(mesh)`` creates one :class:`Communicator` per process group of the
-mesh (and the world group): every rank allocates a device buffer
-(``EINSHARD_SYMM_MB``, default 1280 MiB of data plus 1 MiB of flags), exports
-its CUDA IPC handle, gathers the peers' handles through the process group and
-maps them.  Collectives then run as single cooperative kernels that stage the
-local input into the buffer and pull what they need from peers over NVLink
-(``csrc/comm.cu``).  Every operation is described as a list of strided copy
-boxes, so uneven shards and arbitrary dimensions need no pack/unpack copies.
+mesh (and the world group).  Its heap (``csrc/symm.cpp``) is one ``cuMemCreate``
+allocation per rank, shared with the group's other processes as a POSIX file
+descriptor over a Unix socket and mapped by every rank, plus, where the
+devices support it, an NVLS multicast object bound over all of them.  The heap
+is created in phases with an agreement (all-reduce of a status) after each, so
+every rank either has the communicator or none has.  The default data capacity
+is ``EINSHARD_SYMM_MB`` (64 MiB); collectives that need more ask
+:func:`workspace_for_group`, which grows one extra heap per group on demand.
+
+Collectives: with multicast, all-reduce, all-gather(v) and reduce-scatter(v)
+run through the NVSwitch (``csrc/nvls.cu``: multimem loads that sum in the
+switch, multicast stores); the remaining data movement (uneven boxes,
+all-to-all, halo and roll intervals) runs as single kernels that stage the
+local input in the heap and pull strided boxes from peers (``csrc/comm.cu``).
+Every operation is described on the host, so uneven shards and arbitrary
+dimensions need no pack/unpack copies.
 
 A communicator is only created for groups whose ranks all live on this node
 and whose devices can access each other; otherwise the collective helpers use
-``torch.distributed`` (NCCL).  Set ``EINSHARD_NATIVE_COMM=0`` to disable.
+``torch.distributed`` (NCCL).  Set ``EINSHARD_NATIVE_COMM=0`` to disable, and
+``EINSHARD_NVLS=0`` to create heaps without multicast.
 
 Native backend of the reference's collective helpers: all_reduce
 ``src/torch_einshard/helpers.py:27``, broadcast ``:35``, all_gather ``:61``,
@@ -19,8 +29,11 @@ reduce_scatter ``:114``, all_to_all_repartition ``:142``, owner_swap ``:184``,
 roll ``:224-309``.
 """
 
+import atexit
 import os
 import socket
+import uuid
+import warnings
 
 import torch
 import torch.distributed as dist
@@ -30,16 +43,63 @@ from . import native_comm
 
 __all__ = ["Communicator", "activate", "deactivate", "communicator_for_group"]
 
-_DEFAULT_MB = int(os.environ.get("EINSHARD_SYMM_MB", "1280"))
-# 512 MiB all-reduce at 8 ranks on B200: this two-shot kernel 2.19 ms, NCCL 1.34 ms.
+_DEFAULT_MB = int(os.environ.get("EINSHARD_SYMM_MB", "64"))
+# Block count of every NVLS collective on a heap (the per-block counters are
+# shared by all collectives of the heap, so it is fixed when the heap is made).
+_NVLS_BLOCKS = int(os.environ.get("EINSHARD_NVLS_BLOCKS", "32"))
+_NVLS = os.environ.get("EINSHARD_NVLS", "1") not in ("0", "")
+# Without multicast: 512 MiB all-reduce at 8 ranks on B200, the two-shot copy
+# kernel 2.19 ms, NCCL 1.34 ms; NCCL takes the buffers of this size and more.
 _NCCL_AR_MIN_BYTES = int(os.environ.get("EINSHARD_NCCL_AR_MIN_BYTES", str(1 << 20)))
-# native all-reduce kernel: "push" (every NVLink transfer a store into a peer's region,
-# no staging copy; 15-47 % faster than "pull" on 2 ranks from 1 to 512 MiB) or "pull"
-# (peers' chunks read over NVLink)
+# NVLS all-reduce: every rank reduces everything (one launch, one flag round)
+# below this size; above it each rank reduces 1/P and multicasts it (two-shot).
+_NVLS_ONE_SHOT_MAX = int(os.environ.get("EINSHARD_NVLS_ONE_SHOT_MAX", str(256 << 10)))
+# Largest heap an all-reduce grows to; longer tensors run in pieces of it.
+_NVLS_AR_PIECE = int(os.environ.get("EINSHARD_NVLS_AR_PIECE_MB", "256")) << 20
+# native all-reduce kernel without multicast: "push" (every NVLink transfer a
+# store into a peer's region) or "pull" (peers' chunks read over NVLink)
 _AR_ALGO = os.environ.get("EINSHARD_AR_ALGO", "push")
 _COMMS = {}
 _REJECTED = set()
-_LARGE = {}  # group key -> larger communicators created on demand (kept until deactivate)
+_LARGE = {}  # group key -> the group's on-demand larger communicator
+
+
+def _agree(group, ok):
+    """True when ``ok`` holds on every rank of ``group`` (a collective)."""
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device="cuda")
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    return bool(flag.item())
+
+
+def _unique_tag(group):
+    tag = [f"{os.getpid():x}-{uuid.uuid4().hex[:16]}" if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(tag, src=dist.get_global_rank(group, 0), group=group)
+    return tag[0]
+
+
+def _create_heap(mod, group, data_bytes, device, want_mc):
+    """Collective creation of a heap communicator; its id, or None when any
+    rank failed (then no rank keeps one)."""
+    rank, size = dist.get_rank(group), dist.get_world_size(group)
+    tag = _unique_tag(group)
+    cid, err = mod.symm_prepare(int(data_bytes), device, tag, rank, size, bool(want_mc), _NVLS_BLOCKS)
+    phases = (lambda: mod.symm_exchange(cid, 120.0), lambda: mod.symm_bind(cid), lambda: mod.symm_finish(cid))
+    errors = [err]
+    ok = _agree(group, err == "")
+    for phase in phases:
+        if not ok:
+            break
+        err = phase()
+        errors.append(err)
+        ok = _agree(group, err == "")
+    if ok:
+        return cid
+    mine = "; ".join(e for e in errors if e)
+    warnings.warn(f"einshard: symmetric heap ({'with' if want_mc else 'without'} multicast) not created"
+                  + (f": {mine}" if mine else " (a peer failed)"), RuntimeWarning, stacklevel=3)
+    torch.cuda.synchronize()
+    mod.comm_destroy(cid)
+    return None
 
 
 def _contig_strides(shape):
@@ -88,14 +148,38 @@ class Communicator:
         self.size = dist.get_world_size(group)
         self.device = torch.cuda.current_device()
         self.err = _native.error_word(self.device)
-        cid, handle = self.mod.comm_create(int(data_bytes), self.device)
-        handles = [None] * self.size
-        dist.all_gather_object(handles, handle, group=group)
-        self.mod.comm_connect(cid, self.rank, handles)
+        want_mc = _agree(group, _NVLS and self.mod.symm_multicast_supported(self.device))
+        cid = _create_heap(self.mod, group, data_bytes, self.device, want_mc)
+        if cid is None and want_mc:
+            cid = _create_heap(self.mod, group, data_bytes, self.device, False)
+        if cid is None:
+            raise RuntimeError("einshard: the symmetric heap could not be created")
         self.cid = cid
-        self.capacity = int(data_bytes)
+        self.nvls = bool(self.mod.comm_has_multicast(cid))
+        self.capacity = int(self.mod.comm_data_bytes(cid))
         self.sms = torch.cuda.get_device_properties(self.device).multi_processor_count
-        self.broken = False
+        self._broken = False
+        self.closed = False
+
+    @property
+    def broken(self):
+        """A communicator that saw a timed-out wait, or whose heap was freed,
+        declines every collective (the callers fall back to torch.distributed)."""
+        return self._broken or self.closed
+
+    @broken.setter
+    def broken(self, value):
+        self._broken = bool(value)
+
+    def close(self):
+        """Free the heap.  Collective: every rank of the group calls it, after
+        its last use (a device synchronisation and a barrier come first)."""
+        if self.closed:
+            return
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)
+        self.mod.comm_destroy(self.cid)
+        self.closed = True
 
     # -- raw access for fused kernels ----------------------------------------
     @property
@@ -106,9 +190,24 @@ class Communicator:
     def data_bytes(self):
         return self.capacity
 
+    def enter(self, kind):
+        """Order this heap between the two protocols that use its data region:
+        "copy" (the staged copy kernels, the fused GEMM kernels and direct
+        region writes; per-rank epoch flags) and "nvls" (the NVLS collectives;
+        per-block counters).  When the kind changes, a stream-ordered wait
+        makes sure every rank finished the previous kind's accesses."""
+        last = getattr(self, "_last_kind", None)
+        if last is not None and last != kind:
+            if kind == "nvls":
+                self.mod.comm_acquire(self.cid, self.err)
+            else:
+                self.mod.nvls_quiesce(self.cid, self.err)
+        self._last_kind = kind
+
     def acquire(self):
         """Stream-ordered wait until every peer finished reading this rank's
         region for the previous op; writes into ``region()`` must follow it."""
+        self.enter("copy")
         self.mod.comm_acquire(self.cid, self.err)
 
     def region(self, nbytes):
@@ -129,6 +228,7 @@ class Communicator:
             return False
         dummy = stage if stage is not None else out
         esize = out.element_size()
+        self.enter("copy")
         self.mod.comm_copy(self.cid, dummy, stage_bytes, out, boxes, esize, reduce, accumulate, float(scale),
                            sequential, self._blocks(max(stage_bytes, out.numel() * esize)), self.err)
         return True
@@ -165,12 +265,12 @@ class Communicator:
         nbytes = t.numel() * t.element_size()
         if nbytes == 0:
             return True
+        if self.nvls:
+            return self._nvls_all_reduce(t, scale)
         if nbytes >= _NCCL_AR_MIN_BYTES:
-            # measured on 2 ranks (bf16): NCCL 0.026 / 0.056 / 0.28 / 0.99 ms against the
-            # native push kernel 0.043 / 0.078 / 0.31 / 1.14 ms (pull 0.064 / 0.147 / 0.36 /
-            # 1.33 ms) at 1 / 16 / 128 / 512 MiB; on 8 ranks 512 MiB NCCL 1.34 against pull
-            # 2.19 ms.  A DDP bucket's separate 1/dp scaling pass costs less than that
-            # difference.  The native kernel keeps the buffers below 1 MiB.
+            # without multicast, measured on 2 ranks (bf16): NCCL 0.026 / 0.056 / 0.28 / 0.99 ms
+            # against the push kernel 0.043 / 0.078 / 0.31 / 1.14 ms at 1 / 16 / 128 / 512 MiB;
+            # on 8 ranks 512 MiB NCCL 1.34 against the pull kernel 2.19 ms.
             return False
         if nbytes % 16 or t.data_ptr() % 16:
             return False
@@ -181,9 +281,33 @@ class Communicator:
         run = self.mod.comm_all_reduce_push if push else self.mod.comm_all_reduce
         flat = t.view(-1)
         per = chunk // t.element_size()
+        self.enter("copy")
         for start in range(0, t.numel(), per):
             piece = flat[start:start + per]
             run(self.cid, piece, float(scale), self._blocks(piece.numel() * t.element_size()), self.err)
+        return True
+
+    def _nvls_all_reduce(self, t, scale):
+        """In-place all-reduce through the NVSwitch; tensors longer than the
+        heap run in pieces (the heap grows up to ``EINSHARD_NVLS_AR_PIECE_MB``)."""
+        if t.data_ptr() % 16:
+            # every rank takes this path whatever its alignment (the choice must agree)
+            tmp = t.clone()
+            self._nvls_all_reduce(tmp, scale)
+            t.copy_(tmp)
+            return True
+        nbytes = t.numel() * t.element_size()
+        padded = -(-nbytes // 16) * 16
+        comm = self
+        if padded > self.capacity:
+            comm = workspace_for_group(self.group, min(padded, _NVLS_AR_PIECE)) or self
+        per = (comm.capacity // 256) * 256 // t.element_size()
+        flat = t.view(-1)
+        comm.enter("nvls")
+        for start in range(0, t.numel(), per):
+            piece = flat[start:start + per]
+            two_shot = piece.numel() * t.element_size() > _NVLS_ONE_SHOT_MAX
+            comm.mod.nvls_all_reduce(comm.cid, piece, piece, float(scale), two_shot, comm.err)
         return True
 
     def all_reduce_div_(self, t, divisor):
@@ -197,10 +321,38 @@ class Communicator:
         stage = t if self.rank == src else None
         return self._copy(stage, t, [box])
 
+    @staticmethod
+    def _outer_inner(shape, dim):
+        outer = 1
+        for n in shape[:dim]:
+            outer *= n
+        inner = 1
+        for n in shape[dim + 1:]:
+            inner *= n
+        return outer, inner
+
+    def _nvls_workspace(self, outer, inner, esize, shapes):
+        need = sum(-(-(outer * n * inner * esize) // 256) * 256 for n in shapes)
+        if need <= self.capacity:
+            return self
+        return workspace_for_group(self.group, need)
+
     def all_gather(self, x, dim, shapes):
         if self.broken:
             return None
         x = x.contiguous()
+        if self.nvls:
+            outer, inner = self._outer_inner(list(x.shape), dim)
+            comm = self._nvls_workspace(outer, inner, x.element_size(), shapes)
+            if comm is not None:
+                if x.data_ptr() % 16:
+                    x = x.clone()
+                out_shape = list(x.shape)
+                out_shape[dim] = sum(shapes)
+                out = x.new_empty(out_shape)
+                comm.enter("nvls")
+                comm.mod.nvls_all_gather(comm.cid, x, out, outer, inner, [int(n) for n in shapes], comm.err)
+                return out
         out_shape = list(x.shape)
         out_shape[dim] = sum(shapes)
         out = x.new_empty(out_shape)
@@ -214,10 +366,23 @@ class Communicator:
                                   x.element_size()))
         return out if self._copy(x, out, boxes) else None
 
-    def reduce_scatter(self, x, dim, shapes):
+    def reduce_scatter(self, x, dim, shapes, scale=1.0):
         if self.broken or x.dtype not in (torch.bfloat16, torch.float16, torch.float32):
             return None
         x = x.contiguous()
+        if self.nvls:
+            outer, inner = self._outer_inner(list(x.shape), dim)
+            comm = self._nvls_workspace(outer, inner, x.element_size(), shapes)
+            if comm is not None:
+                out_shape = list(x.shape)
+                out_shape[dim] = shapes[self.rank]
+                out = x.new_empty(out_shape)
+                comm.enter("nvls")
+                comm.mod.nvls_reduce_scatter(comm.cid, x, out, outer, inner, [int(n) for n in shapes], float(scale),
+                                             comm.err)
+                return out
+        if scale != 1.0:
+            return None
         out_shape = list(x.shape)
         out_shape[dim] = shapes[self.rank]
         out = x.new_empty(out_shape)
@@ -333,8 +498,16 @@ class Communicator:
 
 # ------------------------------------------------------------------ registry
 
+_KEYS = {}
+
+
 def _group_key(group):
-    return id(group)
+    """Groups with the same ranks share one communicator (a mesh dimension that
+    spans every rank and the world group, for instance)."""
+    key = _KEYS.get(id(group))
+    if key is None:
+        key = _KEYS[id(group)] = tuple(dist.get_process_group_ranks(group))
+    return key
 
 
 def _eligible(group):
@@ -370,22 +543,26 @@ def communicator_for_group(group):
 
 
 def workspace_for_group(group, nbytes):
-    """A communicator with at least ``nbytes`` of symmetric region.  The default
-    one is used when large enough; otherwise a dedicated one is created (a
-    collective call: every member asks with the same size) and kept, because
-    freeing peer-mapped memory while a peer might still read it is unsafe."""
-    comm = _COMMS.get(_group_key(group))
+    """A communicator with at least ``nbytes`` of symmetric region: the group's
+    default one when large enough, else the group's single larger heap, grown
+    (a collective call: every member asks with the same size) by closing the
+    previous larger heap on every rank and creating one of the new size, in
+    steps of 256 MiB."""
+    key = _group_key(group)
+    comm = _COMMS.get(key)
     if comm is None:
         return None
     if comm.capacity >= nbytes:
         return comm
-    for big in _LARGE.get(_group_key(group), []):
-        if big.capacity >= nbytes:
-            return big
+    big = _LARGE.get(key)
+    if big is not None and big.capacity >= nbytes:
+        return big
+    if big is not None:
+        big.close()
     mb = 256
     size = ((int(nbytes) + (mb << 20) - 1) // (mb << 20)) * (mb << 20)
-    big = Communicator(group, size)
-    _LARGE.setdefault(_group_key(group), []).append(big)
+    big = Communicator(comm.group, size)
+    _LARGE[key] = big
     return big
 
 
@@ -418,13 +595,43 @@ def _install_fusions():
         pass
 
 
+def _all_comms():
+    return list(_COMMS.values()) + list(_LARGE.values())
+
+
 def deactivate():
+    """Free every heap.  With the process group still initialised this is a
+    collective close (synchronise, barrier, free); otherwise see _release_at_exit."""
     native_comm.disable()
-    for comm in list(_COMMS.values()) + [c for cs in _LARGE.values() for c in cs]:
-        try:
-            comm.mod.comm_destroy(comm.cid)
-        except Exception:  # noqa: BLE001
-            pass
+    if dist.is_initialized():
+        for comm in _all_comms():
+            if not comm.closed:
+                comm.close()
+    else:
+        _release_at_exit()
     _COMMS.clear()
     _LARGE.clear()
     _REJECTED.clear()
+    _KEYS.clear()
+
+
+def _release_at_exit():
+    """Free the heaps of a process that ends without a collective close: first a
+    bounded, stream-ordered wait until every peer finished the collectives that
+    touch this rank's memory (the NVLS counters and the copy protocol's done
+    flags, written by the peers' kernels, so no process group is needed), then
+    unmap, unbind from the multicast object and free."""
+    for comm in _all_comms():
+        if comm.closed:
+            continue
+        try:
+            comm.mod.nvls_quiesce(comm.cid, comm.err)
+            comm.mod.comm_acquire(comm.cid, comm.err)
+            torch.cuda.synchronize()
+            comm.mod.comm_destroy(comm.cid)
+        except Exception:  # noqa: BLE001 - exiting; the driver frees what is left
+            pass
+        comm.closed = True
+
+
+atexit.register(_release_at_exit)
