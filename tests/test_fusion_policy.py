@@ -24,9 +24,10 @@ def executor(output_steps=(), input0_steps=(), input1_steps=()):
 
 @pytest.fixture
 def ranks(monkeypatch):
-    """Set the size of every group (and its native communicator)."""
-    def set_size(size):
-        monkeypatch.setattr(fn, "_comm", lambda group: SimpleNamespace(size=size))
+    """Set the size of every group (and its native communicator: with or
+    without an NVLS multicast mapping)."""
+    def set_size(size, nvls=False):
+        monkeypatch.setattr(fn, "_comm", lambda group: SimpleNamespace(size=size, nvls=nvls, broken=False))
         monkeypatch.setattr(fn.dist, "get_world_size", lambda group=None: size)
     return set_size
 
@@ -35,6 +36,28 @@ AR = PlanStep("allreduce_forward_identity_backward", ("tp",))
 RS = PlanStep("reducescatter_forward_allgather_backward", ("n", "tp"))
 AG = PlanStep("allgather_forward_reducescatter_backward", ("n", "tp"))
 DX = PlanStep("identity_forward_allreduce_backward", ("tp",))
+
+
+@pytest.mark.parametrize("size", [2, 4, 8])
+def test_nvls_groups_fuse_the_allreduce_by_default(ranks, monkeypatch, size):
+    """With a multicast heap, the row-parallel GEMM + all-reduce and the
+    replicated operand's gradient all-reduce run as the fused NVLS kernel at
+    every group size; the reduce-scatter output keeps the unfused steps."""
+    ranks(size, nvls=True)
+    monkeypatch.setattr(fn, "_MAX_FUSED_EPILOGUE_RANKS", 0)
+    monkeypatch.setattr(fn, "_FUSED_NVLS", True)
+    assert fn.provider(executor(output_steps=[AR])).kind == "gemm_allreduce"
+    f = fn.provider(executor(input0_steps=[DX]))
+    assert f.kind == "dgrad_allreduce" and f.operand == 0
+    assert fn.provider(executor(output_steps=[RS])) is None
+
+
+def test_nvls_fusion_can_be_switched_off(ranks, monkeypatch):
+    ranks(8, nvls=True)
+    monkeypatch.setattr(fn, "_MAX_FUSED_EPILOGUE_RANKS", 0)
+    monkeypatch.setattr(fn, "_OVERLAP_AR_CHUNKS", 0)
+    monkeypatch.setattr(fn, "_FUSED_NVLS", False)
+    assert fn.provider(executor(output_steps=[AR])) is None
 
 
 @pytest.mark.parametrize("size", [2, 4, 8])

@@ -11,6 +11,7 @@
 #include "fft.h"
 #include "gemm.h"
 #include "gemm_ar.h"
+#include "gemm_nvls.h"
 #include "nvls.h"
 #include "symm.h"
 #include "tma_desc.h"
@@ -450,6 +451,39 @@ void nvls_reduce_scatter(int64_t id, const at::Tensor& in, at::Tensor out, int64
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+// out (every rank) = sum over the communicator's ranks of (a @ b): the wide GEMM
+// and an NVLS all-reduce of its output units in one launch (gemm_nvls.cu).
+void gemm_allreduce_nvls(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out,
+                         int64_t reducer_clusters, int64_t red_warps, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open && hc.mc != nullptr, "einshard fused gemm+NVLS all-reduce: no multicast mapping");
+  TORCH_CHECK(a.size(0) == 1 && out.scalar_type() == at::kBFloat16 && a.scalar_type() == at::kBFloat16 &&
+                  out.is_contiguous(),
+              "einshard fused gemm+NVLS all-reduce: bf16, batch 1, contiguous output");
+  const c10::cuda::CUDAGuard guard(a.device());
+  es::GemmArgs g = gemm_args(a, b, out, 0, err);
+  TORCH_CHECK(g.N % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
+              "einshard fused gemm+NVLS all-reduce: N must be a multiple of 8");
+  TORCH_CHECK((size_t)g.M * g.N * 2 <= hc.data_bytes, "einshard fused gemm+NVLS all-reduce: heap too small");
+  TORCH_CHECK(es::gemm_nvls_units(g.M, g.N) <= es::kNvlsMaxUnits, "einshard fused gemm+NVLS all-reduce: too many units");
+  es::NvlsGemmJob j;
+  j.heap_uc = static_cast<char*>(hc.local) + es::kFlagBytes;
+  j.heap_mc = static_cast<char*>(hc.mc) + es::kFlagBytes;
+  for (int p = 0; p < hc.size; ++p)
+    j.ready_base[p] = reinterpret_cast<uint64_t>(static_cast<uint32_t*>(hc.bases[p]) + es::kTileReady0);
+  j.reduced = static_cast<uint32_t*>(hc.local) + es::kTileReduced0;
+  j.reduced_mc = static_cast<uint32_t*>(hc.mc) + es::kTileReduced0;
+  j.rank = hc.rank;
+  j.size = hc.size;
+  j.epoch = static_cast<uint32_t>(++hc.tile_epoch);
+  j.reducer_clusters = static_cast<int>(reducer_clusters);
+  j.red_warps = static_cast<int>(red_warps);
+  j.timeout_ns = g_wait_timeout_ns;
+  const int rc = es::gemm_nvls_allreduce_launch(g, j, at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard fused gemm+NVLS all-reduce: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
 // out = all-reduce over the communicator's ranks of (a @ b); one fused kernel.
 void gemm_allreduce(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out, const at::Tensor& err) {
   HostComm& hc = comm_ref(id);
@@ -828,6 +862,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_finish", &symm_finish, "phase 4: map the multicast object, zero the flags");
   m.def("comm_destroy", &comm_destroy, "unmap and free");
   m.def("comm_has_multicast", &comm_has_multicast, "whether the communicator has an NVLS multicast mapping");
+  m.def("gemm_allreduce_nvls", &gemm_allreduce_nvls,
+        "wide GEMM whose output units are all-reduced through the NVSwitch in the same launch");
   m.def("nvls_quiesce", &nvls_quiesce, "wait until every rank completed this heap's NVLS collectives");
   m.def("nvls_all_reduce", &nvls_all_reduce, "all-reduce through the NVSwitch (multimem), one- or two-shot");
   m.def("nvls_all_gather", &nvls_all_gather, "all-gather along a dimension through multicast stores");

@@ -18,7 +18,7 @@
 namespace es {
 
 constexpr int kMaxRanks = 8;
-constexpr size_t kFlagBytes = 2 << 20;  // 512K int32 flag slots (upper half: NVLS counters, nvls.h)
+constexpr size_t kFlagBytes = 8 << 20;  // 2M int32 flag slots; from word 262144 on: NVLS counters and unit flags (nvls.h)
 // flag slot indices
 constexpr int kFlagDone = 0;
 constexpr int kFlagStaged = 1;

@@ -1,0 +1,310 @@
+// Fused GEMM + all-reduce through the NVSwitch: C = sum over ranks of A_r @ B_r,
+// on every rank, in one launch.
+//
+// The launch holds two kinds of clusters (CTA pairs):
+//  * GEMM clusters run the wide 2-SM tcgen05 GEMM (gemm_tc3.cuh) unchanged,
+//    except that each epilogue warp stores its 32 x 256 unit of the bf16
+//    partial product into this rank's symmetric heap (TMA store) and then
+//    tells the unit's owner rank (u mod P) that the partial is there: a
+//    release store of the call's epoch into the owner's ready[u][rank] word
+//    over NVLink.  The accumulator is released to the next tile as soon as it
+//    is read, as in the plain GEMM; the transfer never holds TMEM.
+//  * The first R clusters reduce and copy out.  Their reduce warps take the
+//    units this rank owns, in tile order: once ready[u][q] carries the epoch
+//    for every rank q, one multimem.ld_reduce per 16 bytes sums the unit over
+//    all ranks inside the switch (fp32 accumulation) and one multimem.st
+//    writes the sum back into every rank's heap; a multicast release store
+//    sets reduced[u] = epoch on every rank.  Their copy warps walk all units
+//    in tile order and copy each reduced unit from the heap into the output
+//    tensor.
+// GEMM clusters never wait on anything but their own pipeline; reducers wait
+// (bounded) for partials that GEMM clusters of every rank produce, so the
+// launch cannot deadlock.  When a rank's launch ends it has seen reduced[u]
+// for every unit, so every peer's access to its heap for this call (loads of
+// its partials, stores of the sums) is over: the call needs no closing
+// barrier, and the next call may overwrite the heap at once.  Flags carry
+// epochs (one writer per word), so calls of different shapes can alternate.
+//
+// Per rank and output byte the links carry about 9/8 of the bytes each way at
+// P = 8 (see nvls.cu); the GEMM runs on the SMs left after the R reducer
+// pairs.  Replaces the reference's einsum followed by a separate all-reduce
+// (src/torch_einshard/einsum.py:132 then mappings.py:4-13, helpers.py:27-32).
+#include <cuda_bf16.h>
+
+#include "gemm.h"
+#include "gemm_nvls.h"
+#include "gemm_tc3.cuh"
+#include "nvls.h"
+#include "tma_desc.h"
+
+#include <string.h>
+
+namespace es {
+namespace {
+
+__device__ __forceinline__ uint4 ld_reduce_bf16x8(const uint8_t* p) {
+  uint4 v;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void mc_st16(uint8_t* p, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+
+__device__ __forceinline__ void mc_st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("multimem.st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void st_release_sys_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait of one thread until *p >= target (epochs, wrap-safe).
+__device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t target, uint64_t timeout_ns) {
+  if (static_cast<int>(ld_acquire_sys_u32(p) - target) >= 0) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (static_cast<int>(ld_acquire_sys_u32(p) - target) < 0) {
+    if (global_timer_ns() - t0 > timeout_ns) return false;
+  }
+  return true;
+}
+
+// Unit u -> its first output row and column (unit = 32 rows x 256 columns of
+// one CTA's half of a pair tile: u = (2 pair + cta) * 8 + half * 4 + quadrant).
+__device__ __forceinline__ void unit_origin(const GemmShape& s, long long u, int* row0, int* col0) {
+  const int tcta = static_cast<int>(u >> 3);
+  const int half = static_cast<int>((u >> 2) & 1);
+  const int q = static_cast<int>(u & 3);
+  const TileCoord c = tile_coord3(s, tcta >> 1, tcta & 1);
+  *row0 = c.m0 + q * 32;
+  *col0 = c.n0 + half * kBN;
+}
+
+// Epilogue of the GEMM clusters: the plain TMA-store epilogue into the heap,
+// then the unit's ready word on its owner.
+struct PartialEpilogue {
+  StoreEpilogue<__nv_bfloat16> store;
+  uint64_t ready[kMaxRanks];  // each rank's ready[0][0] (peer-mapped)
+  int rank, size;
+  uint32_t epoch;
+
+  __device__ __forceinline__ void setup(int*, const GemmShape&) {}
+  __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
+  __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape& s, volatile int* abort_flag) {
+    store.tile(et, s, abort_flag);
+    const int half = (et.c.n0 / kBN) & 1;
+    const long long u = static_cast<long long>(et.t) * 8 + half * 4 + et.q;
+    if (et.lane == 0) {
+      bulk_wait_group<0>();        // the unit's TMA stores have completed
+      fence_proxy_async_global();  // ... and are ordered before generic-proxy accesses
+      fence_acq_rel_sys();
+      const int owner = static_cast<int>(u % size);
+      st_release_sys_u32(reinterpret_cast<uint32_t*>(ready[owner]) + u * size + rank, epoch);
+    }
+    __syncwarp();
+    return true;
+  }
+};
+
+struct ReduceJob {
+  uint8_t* uc;         // this rank's partial / reduced C in the heap, bf16 [M][ldh]
+  uint8_t* mc;         // multicast view of the same
+  uint32_t* ready;     // this rank's ready[0][0]
+  uint32_t* reduced;   // this rank's reduced[0]
+  uint32_t* reduced_mc;
+  uint8_t* out;        // output tensor, bf16 [M][ldo]
+  long long ldh, ldo;
+  long long units;
+  int rank, size;
+  uint32_t epoch;
+  int clusters;        // reducer clusters at the front of the grid
+  int red_warps;       // warps of each reducer CTA that reduce; the others copy out
+  int* err;
+  uint64_t timeout_ns;
+};
+
+constexpr int kRowsInFlight = 16;
+
+// Reduce and copy-out roles of the first job.clusters clusters.
+__device__ void reducer_role(const ReduceJob& j, const GemmShape& s, int cta, int ncta) {
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
+  if (warp < j.red_warps) {
+    const long long gw = static_cast<long long>(cta) * j.red_warps + warp;
+    const long long W = static_cast<long long>(ncta) * j.red_warps;
+    for (long long k = gw;; k += W) {
+      const long long u = j.rank + k * j.size;
+      if (u >= j.units) break;
+      int row0, col0;
+      unit_origin(s, u, &row0, &col0);
+      if (row0 >= s.M || col0 >= s.N) continue;
+      bool ok = true;
+      if (lane < j.size) ok = wait_epoch(j.ready + u * j.size + lane, j.epoch, j.timeout_ns);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) atomicCAS(j.err, 0, kErrWaitPeerFlag);
+        return;
+      }
+      const int col = col0 + lane * 8;
+      const int rows = es_min(32, s.M - row0);
+      if (col < s.N) {
+        for (int r0 = 0; r0 < rows; r0 += kRowsInFlight) {
+          uint4 v[kRowsInFlight];
+#pragma unroll
+          for (int i = 0; i < kRowsInFlight; ++i)
+            if (r0 + i < rows) v[i] = ld_reduce_bf16x8(j.mc + ((row0 + r0 + i) * j.ldh + col) * 2);
+#pragma unroll
+          for (int i = 0; i < kRowsInFlight; ++i)
+            if (r0 + i < rows) mc_st16(j.mc + ((row0 + r0 + i) * j.ldh + col) * 2, v[i]);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        fence_acq_rel_sys();
+        mc_st_release_u32(j.reduced_mc + u, j.epoch);
+      }
+    }
+  } else {
+    const int ncw = nwarps - j.red_warps;
+    const long long gw = static_cast<long long>(cta) * ncw + (warp - j.red_warps);
+    const long long W = static_cast<long long>(ncta) * ncw;
+    for (long long u = gw; u < j.units; u += W) {
+      int row0, col0;
+      unit_origin(s, u, &row0, &col0);
+      if (row0 >= s.M || col0 >= s.N) continue;
+      bool ok = true;
+      if (lane == 0) ok = wait_epoch(j.reduced + u, j.epoch, j.timeout_ns);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
+        if (lane == 0) atomicCAS(j.err, 0, kErrWaitPeerFlag);
+        return;
+      }
+      const int col = col0 + lane * 8;
+      const int rows = es_min(32, s.M - row0);
+      if (col < s.N) {
+        for (int r0 = 0; r0 < rows; r0 += kRowsInFlight) {
+          uint4 v[kRowsInFlight];
+#pragma unroll
+          for (int i = 0; i < kRowsInFlight; ++i)
+            if (r0 + i < rows)
+              v[i] = *reinterpret_cast<const uint4*>(j.uc + ((row0 + r0 + i) * j.ldh + col) * 2);
+#pragma unroll
+          for (int i = 0; i < kRowsInFlight; ++i)
+            if (r0 + i < rows) *reinterpret_cast<uint4*>(j.out + ((row0 + r0 + i) * j.ldo + col) * 2) = v[i];
+        }
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kThreads3, 1)
+    gemm_nvls_ar_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmW,
+                        const GemmShape shp, PartialEpilogue epi, const ReduceJob job) {
+  const int cluster = static_cast<int>(cluster_id_x());
+  if (cluster < job.clusters) {
+    reducer_role(job, shp, cluster * 2 + static_cast<int>(cluster_ctarank()), job.clusters * 2);
+    return;
+  }
+  gemm_tc3_body(tmA, tmB, tmC, tmW, shp, epi, NoGather{}, cluster - job.clusters,
+                static_cast<int>(nclusters_x()) - job.clusters);
+}
+
+}  // namespace
+
+long long gemm_nvls_units(int M, int N) {
+  const long long pairs = static_cast<long long>((M + 2 * kBM - 1) / (2 * kBM)) * ((N + kBN3 - 1) / kBN3);
+  return pairs * 16;
+}
+
+int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& nj, cudaStream_t stream) {
+  if (g.batch != 1 || g.out_dtype != kDtypeBF16 || g.dtype != kDtypeBF16 || g.N % 8 != 0 || g.act != 0)
+    return static_cast<int>(cudaErrorInvalidValue);
+  const long long units = gemm_nvls_units(g.M, g.N);
+  if (units > kNvlsMaxUnits || nj.reducer_clusters < 1 || nj.red_warps < 1 || nj.red_warps >= kThreads3 / 32)
+    return static_cast<int>(cudaErrorInvalidValue);
+  CUtensorMap ma, mb, mc, mw;
+  make_operand_maps(g, &ma, &mb, true);
+  // the partial product goes to the heap (row pitch N), not to the output tensor
+  GemmArgs gh = g;
+  gh.C = nj.heap_uc;
+  gh.ldc = g.N;
+  gh.c_batch_stride = 0;
+  if (!make_output_map(gh, false, &mc)) return static_cast<int>(cudaErrorInvalidValue);
+  memset(&mw, 0, sizeof(mw));
+  GemmShape s = make_shape(g);
+  s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
+  s.num_n = (g.N + kBN3 - 1) / kBN3;
+  s.group_m = g.group_m > 0 ? g.group_m : 16;
+  s.pair = 1;
+  s.split = 0;
+  PartialEpilogue epi;
+  epi.store.C = static_cast<__nv_bfloat16*>(nj.heap_uc);
+  epi.store.ldc = g.N;
+  epi.store.batch_stride = 0;
+  epi.store.vec_ok = 1;
+  epi.store.act = 0;
+  epi.store.trans = 0;
+  epi.store.tma = 1;
+  for (int p = 0; p < kMaxRanks; ++p) epi.ready[p] = p < nj.size ? nj.ready_base[p] : 0;
+  epi.rank = nj.rank;
+  epi.size = nj.size;
+  epi.epoch = nj.epoch;
+  ReduceJob job;
+  job.uc = static_cast<uint8_t*>(nj.heap_uc);
+  job.mc = static_cast<uint8_t*>(nj.heap_mc);
+  job.ready = reinterpret_cast<uint32_t*>(nj.ready_base[nj.rank]);
+  job.reduced = nj.reduced;
+  job.reduced_mc = nj.reduced_mc;
+  job.out = static_cast<uint8_t*>(g.C);
+  job.ldh = g.N;
+  job.ldo = g.ldc;
+  job.units = units;
+  job.rank = nj.rank;
+  job.size = nj.size;
+  job.epoch = nj.epoch;
+  job.clusters = nj.reducer_clusters;
+  job.red_warps = nj.red_warps;
+  job.err = g.err;
+  job.timeout_ns = nj.timeout_ns;
+
+  auto kernel = gemm_nvls_ar_kernel;
+  static unsigned long long attr_set = 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!(attr_set >> dev & 1ull)) {
+    cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3Bytes);
+    attr_set |= 1ull << dev;
+  }
+  const int pairs = s.num_m * s.num_n;
+  const bool persistent = g.persistent > 0 || (g.persistent < 0 && s.num_kb <= 32);
+  int gemm_clusters = g.num_sms / 2 - nj.reducer_clusters;
+  if (gemm_clusters < 1) return static_cast<int>(cudaErrorInvalidValue);
+  if (pairs < gemm_clusters || !persistent) gemm_clusters = pairs;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * (gemm_clusters + nj.reducer_clusters));
+  cfg.blockDim = dim3(kThreads3);
+  cfg.dynamicSmemBytes = kSmem3Bytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, mw, s, epi, job));
+}
+
+}  // namespace es

@@ -163,11 +163,12 @@ struct NoGather {
   __device__ __forceinline__ void finish(bool) const {}
 };
 
-template <class Epi, class Gather = NoGather>
-__global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
-    gemm_tc3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmW,
-                    const GemmShape shp, Epi epi, const Gather gather = Gather()) {
+// The kernel body, for `nclusters` clusters of which this is number `cluster`
+// (kernels that give some clusters another role run it with offset indices).
+template <class Epi, class Gather>
+__device__ __forceinline__ void gemm_tc3_body(const CUtensorMap& tmA, const CUtensorMap& tmB, const CUtensorMap& tmC,
+                                              const CUtensorMap& tmW, const GemmShape& shp, Epi& epi,
+                                              const Gather& gather, const int cluster, const int nclusters) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
@@ -179,8 +180,6 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
-  const int cluster = static_cast<int>(cluster_id_x());
-  const int nclusters = static_cast<int>(nclusters_x());
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages3; ++s) {
@@ -374,6 +373,15 @@ __global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, kTmemCols);
   }
+}
+
+template <class Epi, class Gather = NoGather>
+__global__ void __launch_bounds__(kThreads3 + 32 * Gather::kCopyWarps, 1)
+    gemm_tc3_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmW,
+                    const GemmShape shp, Epi epi, const Gather gather = Gather()) {
+  gemm_tc3_body(tmA, tmB, tmC, tmW, shp, epi, gather, static_cast<int>(cluster_id_x()),
+                static_cast<int>(nclusters_x()));
 }
 
 }  // namespace es

@@ -25,9 +25,16 @@ namespace es {
 constexpr int kNvlsReady = 262144;                 // word index: per-block ready counters
 constexpr int kNvlsSeq = kNvlsReady + 1024;        // per-block completion counters
 constexpr int kNvlsMaxBlocks = 1024;
-constexpr int kNvlsTile0 = kNvlsSeq + 1024;        // fused GEMM + all-reduce: per-unit counters
-constexpr int kNvlsMaxUnits = 120000;              // ready[u] at kNvlsTile0 + u, reduced[u] at + kNvlsMaxUnits + u
-static_assert(kNvlsTile0 + 2 * kNvlsMaxUnits <= static_cast<int>(kFlagBytes / 4), "NVLS flags exceed the flag area");
+// Fused GEMM + all-reduce (gemm_nvls.cu), per 32 x 256 output unit u:
+//   reduced[u]       - the epoch of the last call whose unit u is reduced (written by its owner, multicast)
+//   ready[u][q]      - on the owner of u: the epoch of rank q's last partial of unit u
+constexpr int kNvlsMaxUnits = 120000;
+constexpr int kTileReduced0 = 270336;                              // word index of reduced[0]
+constexpr int kTileReady0 = 393216;                                // word index of ready[0][0]
+static_assert(kNvlsSeq + kNvlsMaxBlocks <= kTileReduced0, "NVLS counters overlap the unit flags");
+static_assert(kTileReduced0 + kNvlsMaxUnits <= kTileReady0, "unit flags overlap");
+static_assert(kTileReady0 + kNvlsMaxUnits * kMaxRanks <= static_cast<int>(kFlagBytes / 4),
+              "NVLS flags exceed the flag area");
 
 struct NvlsDev {
   uint8_t* uc;        // this rank's data region

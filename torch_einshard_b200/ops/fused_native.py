@@ -182,11 +182,42 @@ def _fits(comm, m, n):
     return tiles * 128 * 256 * 2 <= comm.capacity and tiles <= 120000
 
 
+def gemm_allreduce_nvls(comm, a, b):
+    """``sum over ranks of a @ b`` on every rank, one launch: the wide GEMM
+    writes its output units into the symmetric heap and reducer clusters of the
+    same launch sum each unit through the NVSwitch as soon as every rank has
+    produced it (``csrc/gemm_nvls.cu``).  None when the group has no NVLS heap."""
+    from ..parallel import native_comm
+    m, n = a.shape[1], b.shape[2]
+    ws = native_comm.workspace_for(comm.group, m * n * 2)
+    if ws is None or not ws.nvls or ws.broken:
+        return None
+    mod = _native.require()
+    a, b = _prepare(a), _prepare(b)
+    out = torch.empty((1, m, n), dtype=torch.bfloat16, device=a.device)
+    ws.enter("tile")
+    mod.gemm_allreduce_nvls(ws.cid, a, b, out, _NVLS_REDUCER_CLUSTERS, _NVLS_REDUCE_WARPS,
+                            _native.error_word(a.device))
+    return out
+
+
+def _nvls_fits(comm, a, b):
+    m, n = a.shape[1], b.shape[2]
+    tiles = -(-m // 256) * -(-n // 512)
+    return (comm.nvls and _FUSED_NVLS and a.dtype == torch.bfloat16 and b.dtype == torch.bfloat16 and a.shape[0] == 1
+            and n % 8 == 0 and tiles * 16 <= 120000)
+
+
 def _ar_or_fallback(comm, a, b):
-    if _push_fits(comm, a.shape[1], b.shape[2]):
-        return gemm_allreduce_push(comm, a, b)
-    if _fits(comm, a.shape[1], b.shape[2]):
-        return gemm_allreduce(comm, a, b)
+    if _nvls_fits(comm, a, b):
+        out = gemm_allreduce_nvls(comm, a, b)
+        if out is not None:
+            return out
+    if _fusable(comm, _MAX_FUSED_EPILOGUE_RANKS):
+        if _push_fits(comm, a.shape[1], b.shape[2]):
+            return gemm_allreduce_push(comm, a, b)
+        if _fits(comm, a.shape[1], b.shape[2]):
+            return gemm_allreduce(comm, a, b)
     out = native_bmm(a, b)
     if not comm.all_reduce_(out):
         dist.all_reduce(out, group=comm.group)
@@ -433,23 +464,33 @@ class _Fusion:
         return out.reshape(shape).permute(perm)
 
 
-# Measured on B200 (CUDA events, max over ranks), TP-MLP shapes:
-#   GEMM + all-reduce, 2 ranks: fused pull epilogue 7.64 ms, fused push epilogue
-#     7.51 ms, wide GEMM + NCCL all-reduce 6.16 ms; 8 ranks: fused 31.5 ms,
-#     GEMM + NCCL 2.6 ms.  The single-buffered accumulator of the wide kernel
-#     leaves the epilogue's NVLink traffic on the critical path.
-#   all-gather + GEMM, 2 ranks: fused (copy warps inside the GEMM) 5.48 ms,
-#     NCCL all-gather + GEMM 6.12 ms, GEMM alone 5.20 ms.
-# So the fused epilogue kernels (all-reduce / reduce-scatter) are off by default
-# and the fused all-gather runs for groups up to the size it was measured at.
+# Measured on B200 (CUDA events, max over ranks), TP-MLP shapes, before the NVLS
+# kernel: GEMM + all-reduce, 2 ranks: fused pull epilogue 7.64 ms, fused push
+# epilogue 7.51 ms, wide GEMM + NCCL all-reduce 6.16 ms; 8 ranks: fused 31.5 ms,
+# GEMM + NCCL 2.6 ms (those epilogues hold the wide kernel's single accumulator
+# while tiles cross NVLink).  all-gather + GEMM, 2 ranks: fused (copy warps
+# inside the GEMM) 5.48 ms, NCCL all-gather + GEMM 6.12 ms, GEMM alone 5.20 ms.
+# So the GEMM + all-reduce runs as the NVLS kernel (gemm_nvls.cu: the partial
+# leaves TMEM through the heap, reducer clusters sum it in the switch) wherever
+# the group's heap has a multicast mapping; the older epilogue kernels only on
+# request (EINSHARD_FUSED_EPILOGUE_MAX_RANKS), and the fused all-gather runs for
+# groups up to the size it was measured at.
 import os
 
+_FUSED_NVLS = os.environ.get("EINSHARD_FUSED_NVLS", "1") not in ("0", "")
+# reducer CTA pairs at the front of the fused launch, and how many of each reducer
+# CTA's 10 warps reduce (the others copy reduced units into the output)
+_NVLS_REDUCER_CLUSTERS = int(os.environ.get("EINSHARD_NVLS_REDUCER_CLUSTERS", "4"))
+_NVLS_REDUCE_WARPS = int(os.environ.get("EINSHARD_NVLS_REDUCE_WARPS", "3"))
 _MAX_FUSED_EPILOGUE_RANKS = int(os.environ.get("EINSHARD_FUSED_EPILOGUE_MAX_RANKS", "0"))
 _MAX_FUSED_GATHER_RANKS = int(os.environ.get("EINSHARD_FUSED_GATHER_MAX_RANKS", "2"))
 # Row-parallel all-reduce overlapped with the GEMM in this many row pieces (0: off,
-# the default until measured on B200): piece i's NCCL all-reduce runs while piece
-# i + 1's GEMM runs.
+# the default): piece i's NCCL all-reduce runs while piece i + 1's GEMM runs.
 _OVERLAP_AR_CHUNKS = int(os.environ.get("EINSHARD_OVERLAP_AR_CHUNKS", "0"))
+
+
+def _nvls_comm(comm):
+    return comm is not None and comm.nvls and _FUSED_NVLS and not comm.broken
 
 
 def _fusable(comm, limit):
@@ -482,7 +523,8 @@ def provider(executor):
     if (len(out_steps) == 1 and out_steps[0].name == "allreduce_forward_identity_backward"
             and not tp.input0_steps and not tp.input1_steps):
         group = executor.group(out_steps[0].args[0])
-        if _fusable(_comm(group), _MAX_FUSED_EPILOGUE_RANKS):
+        comm = _comm(group)
+        if _nvls_comm(comm) or _fusable(comm, _MAX_FUSED_EPILOGUE_RANKS):
             return _Fusion("gemm_allreduce")
         if _OVERLAP_AR_CHUNKS > 1 and dist.get_world_size(group) > 1:
             return _Fusion("gemm_allreduce", overlap_chunks=_OVERLAP_AR_CHUNKS)
@@ -492,7 +534,8 @@ def provider(executor):
     in0, in1 = tp.input0_steps, tp.input1_steps
     for operand, (mine, other) in enumerate(((in0, in1), (in1, in0))):
         if len(mine) == 1 and not other and mine[0].name == "identity_forward_allreduce_backward":
-            if _fusable(_comm(executor.group(mine[0].args[0])), _MAX_FUSED_EPILOGUE_RANKS):
+            comm = _comm(executor.group(mine[0].args[0]))
+            if _nvls_comm(comm) or _fusable(comm, _MAX_FUSED_EPILOGUE_RANKS):
                 return _Fusion("dgrad_allreduce", operand)
     return None
 

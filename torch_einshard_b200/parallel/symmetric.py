@@ -191,16 +191,20 @@ class Communicator:
         return self.capacity
 
     def enter(self, kind):
-        """Order this heap between the two protocols that use its data region:
-        "copy" (the staged copy kernels, the fused GEMM kernels and direct
-        region writes; per-rank epoch flags) and "nvls" (the NVLS collectives;
-        per-block counters).  When the kind changes, a stream-ordered wait
-        makes sure every rank finished the previous kind's accesses."""
+        """Order this heap between the protocols that use its data region:
+        "copy" (the staged copy kernels, the older fused GEMM kernels and direct
+        region writes; per-rank epoch flags), "nvls" (the NVLS collectives;
+        per-block counters) and "tile" (the fused GEMM + NVLS all-reduce; per-unit
+        epochs).  When the kind changes, a stream-ordered wait makes sure every
+        rank finished the previous kind's accesses to this rank's heap: peers'
+        reads of a copy op (their done flags), every block of the last NVLS
+        collective (its counters).  A fused GEMM + all-reduce needs none: when
+        it ends on this rank, no peer touches this rank's heap for it any more."""
         last = getattr(self, "_last_kind", None)
         if last is not None and last != kind:
-            if kind == "nvls":
+            if last == "copy":
                 self.mod.comm_acquire(self.cid, self.err)
-            else:
+            elif last == "nvls":
                 self.mod.nvls_quiesce(self.cid, self.err)
         self._last_kind = kind
 
