@@ -13,6 +13,7 @@ from . import params as _params
 from .notation.families import cached_expand_axis_families
 from .notation.parser import parse_sharding
 from .notation.spec import Axes, AxisGroup, EllipsisAxis, TensorSpec
+from .ops import gemm as _gemm
 from .ops.einsum import einsum
 from .parallel.executor import distributed_1d
 from .plan.policy import resolve_plan_policy
@@ -107,9 +108,9 @@ def _commit(registrations):
         _params.set_parameter_state(param, state)
 
 
-def _run(shard, xs, mesh, shapes, sizes, policy):
+def _run(shard, xs, mesh, shapes, sizes, policy, activation=None):
     if local_operation(shard):
-        out = einsum(shard, *xs, sizes=sizes)
+        out = einsum(shard, *xs, sizes=sizes, activation=activation)
         plan = ExecutionPlan()
         plan.add("rank_local_einsum")
         set_last_plan(plan)
@@ -118,16 +119,33 @@ def _run(shard, xs, mesh, shapes, sizes, policy):
         raise NotImplementedError("Factored axes are currently supported only for local reshape operations")
     if mesh is None:
         raise ValueError("Distributed einshard operations require mesh")
-    return distributed_1d(shard, *xs, mesh=mesh, shapes=shapes, policy=policy)
+    out = distributed_1d(shard, *xs, mesh=mesh, shapes=shapes, policy=policy)
+    if activation is not None:
+        if getattr(shard[2], "partials", ()):
+            raise ValueError("activation needs a complete output (no // partial sums)")
+        out = _gemm.silu(out) if activation == "silu" else None
+        if out is None:
+            raise ValueError(f"unsupported activation {activation!r} (supported: 'silu')")
+    return out
 
 
-def einshard(shard, *xs, mesh=None, shapes=None, sizes=None, families=None, optimize=None, policy=None):
-    """Run an einshard expression on ``xs`` (see module docstring)."""
+def einshard(shard, *xs, mesh=None, shapes=None, sizes=None, families=None, optimize=None, policy=None,
+             activation=None):
+    """Run an einshard expression on ``xs`` (see module docstring).
+
+    ``activation`` ("silu" or None) is an extension of this framework: the
+    elementwise activation of the result.  For a rank-local contraction it runs
+    in the GEMM's epilogue (the wide kernel writes the pre-activation, kept for
+    backward, and the activation from one pass over its accumulator); for a
+    distributed one it follows the plan's last step.  An output with ``//``
+    partial sums cannot take one."""
     policy = resolve_plan_policy(optimize=optimize, policy=policy)
     shard, sizes = cached_expand_axis_families(shard, sizes, families)
     shard = parse_sharding(shard)
+    if activation is not None and getattr(shard[2], "partials", ()):
+        raise ValueError("activation needs a complete output (no // partial sums)")
     registrations = _prepare(_operand_registrations(shard, xs, mesh))
-    out = _run(shard, xs, mesh, shapes, sizes, policy)
+    out = _run(shard, xs, mesh, shapes, sizes, policy, activation)
     _commit(registrations)
     return out
 

@@ -10,6 +10,7 @@
 #include "copy.h"
 #include "fft.h"
 #include "gemm.h"
+#include "act.h"
 #include "gemm_ar.h"
 #include "gemm_nvls.h"
 #include "nvls.h"
@@ -153,6 +154,57 @@ at::Tensor gemm(const at::Tensor& a, const at::Tensor& b, int64_t out_dtype, int
 
 void gemm_out(const at::Tensor& a, const at::Tensor& b, at::Tensor out, int64_t act, const at::Tensor& err) {
   run_gemm(a, b, out, act, err);
+}
+
+int act_dtype(const at::Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 || t.scalar_type() == at::kHalf, "einshard silu: bf16 or fp16");
+  return t.scalar_type() == at::kBFloat16 ? 0 : 1;
+}
+
+// (silu(a @ b), a @ b): one pass over the accumulator on the wide kernel, else
+// the GEMM followed by the elementwise activation.
+std::vector<at::Tensor> gemm_silu(const at::Tensor& a, const at::Tensor& b, const at::Tensor& err) {
+  at::Tensor out = at::empty({a.size(0), a.size(1), b.size(2)}, a.options());
+  at::Tensor pre = at::empty_like(out);
+  const c10::cuda::CUDAGuard guard(a.device());
+  es::GemmArgs g = gemm_args(a, b, out, es::kActSiluDual, err);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  int rc = es::gemm_launch_silu_dual(g, pre.data_ptr(), pre.stride(1), pre.stride(0), stream);
+  if (rc == 0) {
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return {out, pre};
+  }
+  TORCH_CHECK(rc == static_cast<int>(cudaErrorNotSupported), "einshard gemm+silu: launch failed (", rc, ")");
+  run_gemm(a, b, pre, 0, err);
+  rc = es::silu_forward(pre.data_ptr(), out.data_ptr(), out.numel(), act_dtype(out), num_sms(a.get_device()), stream);
+  TORCH_CHECK(rc == 0, "einshard silu: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return {out, pre};
+}
+
+at::Tensor silu_forward(const at::Tensor& h) {
+  TORCH_CHECK(h.is_cuda() && h.is_contiguous(), "einshard silu: contiguous CUDA tensor");
+  at::Tensor out = at::empty_like(h);
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int rc = es::silu_forward(h.data_ptr(), out.data_ptr(), h.numel(), act_dtype(h), num_sms(h.get_device()),
+                                  at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard silu: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return out;
+}
+
+// grad * silu'(h)
+at::Tensor silu_backward(const at::Tensor& grad, const at::Tensor& h) {
+  TORCH_CHECK(h.is_cuda() && h.is_contiguous() && grad.is_contiguous() && grad.sizes() == h.sizes() &&
+                  grad.scalar_type() == h.scalar_type(),
+              "einshard silu backward: contiguous tensors of one shape and dtype");
+  at::Tensor out = at::empty_like(h);
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int rc = es::silu_backward(grad.data_ptr(), h.data_ptr(), out.data_ptr(), h.numel(), act_dtype(h),
+                                   num_sms(h.get_device()), at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard silu backward: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return out;
 }
 
 
@@ -874,6 +926,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
   m.def("conv2d_wgrad", &conv2d_wgrad, "weight gradient of the implicit-GEMM conv (split-K tcgen05, fp32 out)");
   m.def("conv2d_implicit", &conv2d_implicit, "implicit-GEMM NHWC conv2d on tcgen05 (stride 1)");
+  m.def("gemm_silu", &gemm_silu, "(silu(a @ b), a @ b), fused on the wide kernel when it runs the GEMM");
+  m.def("silu_forward", &silu_forward, "elementwise silu");
+  m.def("silu_backward", &silu_backward, "grad * silu'(h)");
   m.def("wait_probe", &wait_probe, "bounded wait on a flag (tests the timeout path)");
   m.def("wait_probe_noalloc_status", &wait_probe_noalloc_status,
         "bounded wait recording into the allocation-free GEMM's status word (tests)");

@@ -171,9 +171,11 @@ static bool wide_persistent(const GemmArgs& g) {
 }
 
 // tile_limit > 0: only pair tiles [0, tile_limit) (the whole tiles before a stream-K tail).
+// second: the map handed to the kernel in the stream-K workspace slot (the
+// pre-activation output of the dual SiLU epilogue); zeroed when null.
 template <class Epi>
 int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, Epi epi, cudaStream_t stream,
-                int tile_limit = 0) {
+                int tile_limit = 0, const CUtensorMap* second = nullptr) {
   CUtensorMap mc;
   epi.tma = make_output_map(g, epi.trans != 0, &mc) ? 1 : 0;
   GemmShape s = wide_shape(g);
@@ -206,8 +208,46 @@ int launch_wide(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g,
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   CUtensorMap mw;  // no stream-K workspace
-  memset(&mw, 0, sizeof(mw));
+  if (second != nullptr)
+    mw = *second;
+  else
+    memset(&mw, 0, sizeof(mw));
   return static_cast<int>(cudaLaunchKernelEx(&cfg, kernel, ma, mb, mc, mw, s, epi, NoGather{}));
+}
+
+// C = silu(A @ B) and pre = A @ B from one pass over the accumulator (wide
+// kernel, TMA-store epilogue).  cudaErrorNotSupported when the GEMM would not
+// run on the wide kernel or an output does not qualify for TMA stores; the
+// caller then runs the GEMM and the activation separately.
+template <typename OutT>
+static int launch_silu_dual(const GemmArgs& g, void* pre, long long ld_pre, long long pre_batch_stride,
+                            cudaStream_t stream) {
+  if (want_swap(g) || !use_pair_kernel(g) || pick_kernel(g) != 2) return static_cast<int>(cudaErrorNotSupported);
+  GemmArgs gp = g;
+  gp.C = pre;
+  gp.ldc = ld_pre;
+  gp.c_batch_stride = pre_batch_stride;
+  CUtensorMap mpre, mc;
+  if (!make_output_map(gp, false, &mpre) || !make_output_map(g, false, &mc))
+    return static_cast<int>(cudaErrorNotSupported);
+  CUtensorMap ma, mb;
+  make_operand_maps(g, &ma, &mb, true);
+  StoreEpilogue<OutT> epi;
+  epi.C = reinterpret_cast<OutT*>(g.C);
+  epi.ldc = g.ldc;
+  epi.batch_stride = g.c_batch_stride;
+  epi.act = kActSiluDual;
+  epi.trans = 0;
+  epi.tma = 1;
+  epi.vec_ok = 1;
+  return launch_wide(ma, mb, g, epi, stream, 0, &mpre);
+}
+
+int gemm_launch_silu_dual(const GemmArgs& g, void* pre, long long ld_pre, long long pre_batch_stride,
+                          cudaStream_t stream) {
+  if (g.out_dtype == kDtypeBF16) return launch_silu_dual<__nv_bfloat16>(g, pre, ld_pre, pre_batch_stride, stream);
+  if (g.out_dtype == kDtypeF16) return launch_silu_dual<__half>(g, pre, ld_pre, pre_batch_stride, stream);
+  return static_cast<int>(cudaErrorNotSupported);
 }
 
 template <typename OutT>

@@ -12,6 +12,11 @@ namespace es {
 
 enum Dtype : int { kDtypeBF16 = 0, kDtypeF16 = 1, kDtypeF32 = 2 };
 
+// Activation applied in the epilogue before the store.  kActSiluDual (TMA-store
+// epilogue of the wide kernel only): the pre-activation goes to a second
+// output and its SiLU to the output, in one pass over the accumulator.
+enum EpiAct : int { kActNone = 0, kActSilu = 1, kActSiluDual = 2 };
+
 // C[b] = act(A[b] @ B[b]) with A: [batch, M, K], B: [batch, K, N], C: [batch, M, N] row-major.
 // a_mn = 0: A is K-contiguous, lda = elements between consecutive m rows.
 // a_mn = 1: A is M-contiguous, lda = elements between consecutive k rows.
@@ -45,6 +50,11 @@ const char* check_gemm_args(const GemmArgs& g);
 void make_operand_maps(const GemmArgs& g, CUtensorMap* ma, CUtensorMap* mb, bool pair = false);
 bool use_pair_kernel(const GemmArgs& g);
 int gemm_launch(const GemmArgs& g, cudaStream_t stream);
+// C = silu(A @ B) and pre = A @ B (same shape as C, row pitch ld_pre) in one
+// launch of the wide kernel; cudaErrorNotSupported when the shapes or layouts
+// do not allow it (nothing is launched).
+int gemm_launch_silu_dual(const GemmArgs& g, void* pre, long long ld_pre, long long pre_batch_stride,
+                          cudaStream_t stream);
 struct GemmShape;
 GemmShape make_shape(const GemmArgs& g);
 GemmShape make_shape_pair(const GemmArgs& g);

@@ -26,6 +26,7 @@
 
 #include <type_traits>
 
+#include "gemm.h"
 #include "ptx.cuh"
 
 namespace es {
@@ -345,8 +346,7 @@ struct StoreOut<__half> {
   static __device__ __forceinline__ __half cvt(float v) { return __float2half_rn(v); }
 };
 
-// Activation applied in the epilogue before the store.
-enum EpiAct : int { kActNone = 0, kActSilu = 1 };
+// Activation applied in the epilogue before the store: EpiAct (gemm.h).
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
@@ -368,7 +368,6 @@ struct StoreEpilogue {
   // The stores are coalesced by the TMA engine and clipped at the tensor edges.
   __device__ __forceinline__ bool tile_tma(const EpiTile& et, const GemmShape& s) {
     const int row0 = et.c.m0 + et.q * 32;
-    uint4* stage = reinterpret_cast<uint4*>(et.stage);
 #pragma unroll 1
     for (int sub = 0; sub < kBN / 64; ++sub) {
       const int col0 = et.c.n0 + sub * 64;
@@ -377,41 +376,50 @@ struct StoreEpilogue {
       tmem_ld32(et.tmem + sub * 64, r0);
       tmem_ld32(et.tmem + sub * 64 + 32, r1);
       tmem_ld_wait();
-      if (act == kActSilu) {
+      if (act == kActSiluDual) stage_box(et, r0, r1, et.tmw, col0, row0);  // the pre-activation
+      if (act == kActSilu || act == kActSiluDual) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           r0[i] = __float_as_uint(silu_f(__uint_as_float(r0[i])));
           r1[i] = __float_as_uint(silu_f(__uint_as_float(r1[i])));
         }
       }
-      if (et.lane == 0) bulk_wait_group_read<0>();  // the previous box has left the staging buffer
-      __syncwarp();
-      const int sw = et.lane & 7;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const uint32_t* src = j < 4 ? &r0[8 * j] : &r1[8 * (j - 4)];
-        uint4 v;
-        if (sizeof(OutT) == 2 && std::is_same<OutT, __half>::value) {
-          v = make_uint4(pack_f16(__uint_as_float(src[0]), __uint_as_float(src[1])),
-                         pack_f16(__uint_as_float(src[2]), __uint_as_float(src[3])),
-                         pack_f16(__uint_as_float(src[4]), __uint_as_float(src[5])),
-                         pack_f16(__uint_as_float(src[6]), __uint_as_float(src[7])));
-        } else {
-          v = make_uint4(pack_bf16(__uint_as_float(src[0]), __uint_as_float(src[1])),
-                         pack_bf16(__uint_as_float(src[2]), __uint_as_float(src[3])),
-                         pack_bf16(__uint_as_float(src[4]), __uint_as_float(src[5])),
-                         pack_bf16(__uint_as_float(src[6]), __uint_as_float(src[7])));
-        }
-        stage[et.lane * 8 + (j ^ sw)] = v;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (et.lane == 0) {
-        tma_store_3d(et.tmc, et.stage, col0, row0, et.c.b);
-        bulk_commit_group();
-      }
+      stage_box(et, r0, r1, et.tmc, col0, row0);
     }
     return true;
+  }
+
+  // One 32 x 64 box of this warp (registers r0: columns 0-31, r1: 32-63) ->
+  // 128-byte-swizzled staging buffer -> TMA store through `map`.
+  __device__ __forceinline__ void stage_box(const EpiTile& et, const uint32_t (&r0)[32], const uint32_t (&r1)[32],
+                                            const CUtensorMap* map, int col0, int row0) {
+    uint4* stage = reinterpret_cast<uint4*>(et.stage);
+    if (et.lane == 0) bulk_wait_group_read<0>();  // the previous box has left the staging buffer
+    __syncwarp();
+    const int sw = et.lane & 7;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t* src = j < 4 ? &r0[8 * j] : &r1[8 * (j - 4)];
+      uint4 v;
+      if (sizeof(OutT) == 2 && std::is_same<OutT, __half>::value) {
+        v = make_uint4(pack_f16(__uint_as_float(src[0]), __uint_as_float(src[1])),
+                       pack_f16(__uint_as_float(src[2]), __uint_as_float(src[3])),
+                       pack_f16(__uint_as_float(src[4]), __uint_as_float(src[5])),
+                       pack_f16(__uint_as_float(src[6]), __uint_as_float(src[7])));
+      } else {
+        v = make_uint4(pack_bf16(__uint_as_float(src[0]), __uint_as_float(src[1])),
+                       pack_bf16(__uint_as_float(src[2]), __uint_as_float(src[3])),
+                       pack_bf16(__uint_as_float(src[4]), __uint_as_float(src[5])),
+                       pack_bf16(__uint_as_float(src[6]), __uint_as_float(src[7])));
+      }
+      stage[et.lane * 8 + (j ^ sw)] = v;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (et.lane == 0) {
+      tma_store_3d(map, et.stage, col0, row0, et.c.b);
+      bulk_commit_group();
+    }
   }
 
   __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape& s, volatile int*) {

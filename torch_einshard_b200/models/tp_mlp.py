@@ -1,7 +1,7 @@
 """Tensor-parallel MLP written with einshard formulas (the flagship benchmark model).
 
-    h   = einshard("b n c, h/tp c -> b n h/tp", x, w1)        column parallel
-    a   = silu(h)
+    a   = einshard("b n c, h/tp c -> b n h/tp", x, w1,        column parallel, SiLU
+                   activation="silu")                          in the GEMM's epilogue
     y_p = einshard("b n h/tp, c h/tp -> b n c // tp", a, w2)  row parallel, partial sums
     y   = einshard("b n c // tp -> b n c", y_p)                all-reduce over tp
 
@@ -17,7 +17,6 @@ the reference ships no model class.
 """
 
 import torch
-import torch.nn.functional as F
 
 from ..api import einshard
 
@@ -48,8 +47,7 @@ class TPMLP(torch.nn.Module):
 
     def forward(self, x):
         t = self.tp_dim
-        h = einshard(f"b n c, h/{t} c -> b n h/{t}", x, self.w1, mesh=self.mesh)
-        a = F.silu(h)
+        a = einshard(f"b n c, h/{t} c -> b n h/{t}", x, self.w1, mesh=self.mesh, activation="silu")
         if self.single_formula:
             return einshard(f"b n h/{t}, c h/{t} -> b n c", a, self.w2, mesh=self.mesh)
         y = einshard(f"b n h/{t}, c h/{t} -> b n c // {t}", a, self.w2, mesh=self.mesh)

@@ -70,15 +70,26 @@ def _prod(letters, size):
     return math.prod(size[c] for c in letters) if letters else 1
 
 
-def contract(equation, *operands):
+def _activate(z, activation):
+    if activation is None:
+        return z
+    if activation != "silu":
+        raise ValueError(f"unsupported activation {activation!r} (supported: 'silu')")
+    return gemm.silu(z)
+
+
+def contract(equation, *operands, activation=None):
+    """``torch.einsum(equation, *operands)``, optionally followed by an
+    elementwise ``activation`` ("silu"), which the native GEMM applies in its
+    epilogue."""
     if len(operands) != 2:
-        return torch.einsum(equation, *operands)
+        return _activate(torch.einsum(equation, *operands), activation)
     x, y = operands
     if not gemm.eligible(x, y):
-        return torch.einsum(equation, x, y)
+        return _activate(torch.einsum(equation, x, y), activation)
     plan = canonical_gemm(equation, tuple(x.shape), tuple(y.shape))
     if plan is None:
-        return torch.einsum(equation, x, y)
+        return _activate(torch.einsum(equation, x, y), activation)
     size = plan["size"]
     ex, ey, ez = plan["ex"], plan["ey"], plan["ez"]
     if plan["x_only"]:
@@ -90,10 +101,10 @@ def contract(equation, *operands):
     batch, rows, cols, red = plan["batch"], plan["rows"], plan["cols"], plan["red"]
     B, M, N, K = (_prod(batch, size), _prod(rows, size), _prod(cols, size), _prod(red, size))
     if K == 0 or M == 0 or N == 0 or B == 0:
-        return torch.einsum(equation, operands[0], operands[1])
+        return _activate(torch.einsum(equation, operands[0], operands[1]), activation)
     xv = x.permute([ex.index(c) for c in batch + rows + red]).reshape(B, M, K)
     yv = y.permute([ey.index(c) for c in batch + red + cols]).reshape(B, K, N)
-    z = gemm.matmul(xv, yv)
+    z = gemm.matmul(xv, yv, activation=activation)
     z = z.reshape([size[c] for c in batch + rows + cols])
     order = batch + rows + cols
     return z.permute([order.index(c) for c in ez])

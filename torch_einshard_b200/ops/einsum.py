@@ -119,8 +119,9 @@ def equation_for(shard, name_only=False):
     return f"{lhs}->{_letters(shard[2], table, name_only, allow_missing=False)}"
 
 
-def einsum(shard, *xs, name_only=False, sizes=None):
-    """Run the local contraction described by ``shard`` on ``xs``."""
+def einsum(shard, *xs, name_only=False, sizes=None, activation=None):
+    """Run the local contraction described by ``shard`` on ``xs``, optionally
+    followed by an elementwise ``activation`` (fused into the GEMM epilogue)."""
     binary = shard[1] is not None
     if not name_only:
         assert not getattr(shard[0], "partials", ()), "Local einsum does not support partial inputs"
@@ -134,5 +135,5 @@ def einsum(shard, *xs, name_only=False, sizes=None):
     if binary:
         lhs += "," + _letters(shard[1], table, name_only)
     rhs = _letters(shard[2], table, name_only, allow_missing=False)
-    output = contract(f"{lhs}->{rhs}", *xs)
+    output = contract(f"{lhs}->{rhs}", *xs, activation=activation)
     return output if name_only else pack_groups(output, shard[2])

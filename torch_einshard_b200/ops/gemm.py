@@ -14,7 +14,7 @@ import torch
 
 from . import _native
 
-__all__ = ["eligible", "matmul", "native_bmm"]
+__all__ = ["eligible", "matmul", "native_bmm", "silu"]
 
 _NATIVE_DTYPES = (torch.bfloat16, torch.float16)
 _ACTS = {None: 0, "silu": 1}
@@ -81,19 +81,69 @@ class _NativeMatmul(torch.autograd.Function):
     @staticmethod
     def backward(ctx, grad):
         a, b = ctx.saved_tensors
-        grad_a = native_bmm(grad, b.transpose(1, 2)) if ctx.needs_input_grad[0] else None
-        grad_b = None
-        if ctx.needs_input_grad[1]:
-            if b.stride(1) == 1 and b.size(1) > 1:
-                # b is a transposed view (e.g. a [out, in] weight): produce its gradient
-                # directly in that memory order, (dC^T A)^T, so no copy is needed later
-                grad_b = native_bmm(grad.transpose(1, 2), a).transpose(1, 2)
-            else:
-                grad_b = native_bmm(a.transpose(1, 2), grad)
-        return grad_a, grad_b
+        # a transposed-view b (e.g. an [out, in] weight) gets its gradient directly in
+        # that memory order, (dC^T A)^T, so no copy is needed later
+        return _grads(ctx, a, b, grad)
 
 
-def matmul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+def _grads(ctx, a, b, grad):
+    grad_a = native_bmm(grad, b.transpose(1, 2)) if ctx.needs_input_grad[0] else None
+    grad_b = None
+    if ctx.needs_input_grad[1]:
+        if b.stride(1) == 1 and b.size(1) > 1:
+            grad_b = native_bmm(grad.transpose(1, 2), a).transpose(1, 2)
+        else:
+            grad_b = native_bmm(a.transpose(1, 2), grad)
+    return grad_a, grad_b
+
+
+class _NativeMatmulSilu(torch.autograd.Function):
+    """silu(a @ b): the wide kernel writes the pre-activation H and silu(H) from
+    one pass over its accumulator; backward forms dH = dY * silu'(H) in one
+    elementwise pass and reuses the GEMM pair of the plain product."""
+
+    @staticmethod
+    def forward(ctx, a, b):
+        mod = _native.require()
+        a2, b2 = _prepare(a), _prepare(b)
+        out, pre = mod.gemm_silu(a2, b2, _native.error_word(a.device))
+        ctx.save_for_backward(a, b, pre)
+        return out
+
+    @staticmethod
+    def backward(ctx, grad):
+        a, b, pre = ctx.saved_tensors
+        dpre = _native.require().silu_backward(grad.contiguous(), pre)
+        return _grads(ctx, a, b, dpre)
+
+
+class _NativeSilu(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, h):
+        h = h.contiguous()
+        ctx.save_for_backward(h)
+        return _native.require().silu_forward(h)
+
+    @staticmethod
+    def backward(ctx, grad):
+        (h,) = ctx.saved_tensors
+        return _native.require().silu_backward(grad.contiguous(), h)
+
+
+def silu(t: torch.Tensor) -> torch.Tensor:
+    """SiLU on the native elementwise kernel for 16-bit CUDA tensors, else torch."""
+    if t.is_cuda and t.dtype in _NATIVE_DTYPES and _native.available():
+        return _NativeSilu.apply(t)
+    return torch.nn.functional.silu(t)
+
+
+def matmul(a: torch.Tensor, b: torch.Tensor, activation=None) -> torch.Tensor:
+    if activation == "silu":
+        if a.requires_grad or b.requires_grad:
+            return _NativeMatmulSilu.apply(a, b)
+        return _native.require().gemm_silu(_prepare(a), _prepare(b), _native.error_word(a.device))[0]
+    if activation is not None:
+        raise ValueError(f"unsupported activation {activation!r} (supported: 'silu')")
     if a.requires_grad or b.requires_grad:
         return _NativeMatmul.apply(a, b)
     return native_bmm(a, b)
