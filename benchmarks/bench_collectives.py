@@ -73,11 +73,11 @@ def main():
     import torch_einshard_b200 as es
     from torch.distributed.device_mesh import init_device_mesh
     from torch_einshard_b200.ops import _native
-    from torch_einshard_b200.parallel import native_comm
+    from torch_einshard_b200.parallel import symmetric
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     es.setup_native_comm(mesh)
     group = mesh["tp"].get_group()
-    comm = native_comm.communicator_for(group)
+    comm = symmetric.communicator_for(group)
     dtype = DTYPES[args.dtype]
     esize = torch.tensor([], dtype=dtype).element_size()
     sampler = ClockSampler(visible_gpu_indices(world)) if rank == 0 else None

@@ -40,8 +40,8 @@ def main():
     from torch.distributed.device_mesh import init_device_mesh
     mesh = init_device_mesh("cpu", (2, world // 2), mesh_dim_names=("dp", "sp"))
     sp = mesh["sp"].size()
-    a_shapes = [300, 250, 250, 224] if sp == 4 else es.helpers.compute_split_shapes(1024, sp)
-    b_shapes = es.helpers.compute_split_shapes(2048, 2)
+    a_shapes = [300, 250, 250, 224] if sp == 4 else es.compute_split_shapes(1024, sp)
+    b_shapes = es.compute_split_shapes(2048, 2)
     shapes = {"sp": {"a": a_shapes}, "dp": {"b": b_shapes}}
     g = torch.Generator().manual_seed(0)
     x = torch.randn(1024, 2048, generator=g)

@@ -73,7 +73,7 @@ def main():
     rank = dist.get_rank(group)
 
     rows = cfg["rows"] + 1
-    row_shapes = es.helpers.compute_split_shapes(rows, world)
+    row_shapes = es.compute_split_shapes(rows, world)
     x = torch.randn(rows, cfg["cols"], device=dev, dtype=dtype)
 
     def round_trip():
@@ -83,7 +83,7 @@ def main():
               extra={"global_shape": [rows, cfg["cols"]]})
 
     r, c = cfg["rows"], cfg["cols"]
-    rs, cs = es.helpers.compute_split_shapes(r, world), es.helpers.compute_split_shapes(c, world)
+    rs, cs = es.compute_split_shapes(r, world), es.compute_split_shapes(c, world)
     full = torch.randn(r, c, device=dev, dtype=dtype)
     xl = torch.split(full, rs, 0)[rank].contiguous()
     benchmark("distributed_repartition_axis_metadata",

@@ -44,11 +44,11 @@ def main():
     import torch_einshard_b200 as es
     from torch.distributed.device_mesh import init_device_mesh
     from torch_einshard_b200.ops import _native, fused_native, gemm
-    from torch_einshard_b200.parallel import native_comm, symmetric
+    from torch_einshard_b200.parallel import symmetric
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     es.setup_native_comm(mesh)
     group = mesh["tp"].get_group()
-    comm = native_comm.communicator_for(group)
+    comm = symmetric.communicator_for(group)
     k = args.h // world
     g = torch.Generator(device="cuda").manual_seed(rank)
     a = torch.randn(1, args.m, k, device="cuda", dtype=torch.bfloat16, generator=g)

@@ -16,9 +16,27 @@ for _key in dir(_pkg):
     if not _key.startswith("__"):
         globals()[_key] = getattr(_pkg, _key)
 
-for _name in ("helpers", "mappings", "grammar", "sharding", "symbolic", "families", "params", "einsum", "fft",
-              "halo", "conv", "roll", "mesh", "distributed"):
-    _module = sys.modules.get(f"torch_einshard_b200.{_name}") or importlib.import_module(f"torch_einshard_b200.{_name}")
+# reference module path -> the module here that implements it
+_PATHS = {
+    "helpers": "parallel.collectives",
+    "mappings": "parallel.mappings",
+    "grammar": "notation.parser",
+    "sharding": "notation.spec",
+    "families": "notation.families",
+    "symbolic": "plan",
+    "params": "params",
+    "einsum": "ops.einsum",
+    "fft": "ops.fft",
+    "halo": "ops.halo",
+    "conv": "ops.conv",
+    "roll": "ops.roll",
+    "mesh": "parallel.mesh",
+    "distributed": "parallel.executor",
+}
+for _name, _path in _PATHS.items():
+    _module = importlib.import_module(f"torch_einshard_b200.{_path}")
     sys.modules[f"{__name__}.{_name}"] = _module
+    globals()[_name] = _module
 
+del _path
 del _key, _name, _module

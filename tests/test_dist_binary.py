@@ -79,7 +79,7 @@ def _repartition_after_contraction(ctx):
     group = mesh["tp"].get_group()
     rank, P = dist.get_rank(group), dist.get_world_size(group)
     rows, cols = P * 2 + 1, P * 3 + 2
-    rs, cs = es.helpers.compute_split_shapes(rows, P), es.helpers.compute_split_shapes(cols, P)
+    rs, cs = es.compute_split_shapes(rows, P), es.compute_split_shapes(cols, P)
     x_full = torch.randn(rows, 4)
     y = torch.randn(4, cols, requires_grad=True)
     xs = _split(x_full, rs, 0, rank).clone().requires_grad_(True)
@@ -126,8 +126,8 @@ def _mesh2d(ctx):
     a, b, c = 64, 32, 16
     torch.manual_seed(0)
     xf, yf = torch.randn(a, b), torch.randn(b, c)
-    a_sh = es.helpers.compute_split_shapes(a, dist.get_world_size(sp))
-    b_sh = es.helpers.compute_split_shapes(b, dist.get_world_size(dp))
+    a_sh = es.compute_split_shapes(a, dist.get_world_size(sp))
+    b_sh = es.compute_split_shapes(b, dist.get_world_size(dp))
     xs = _split(_split(xf, a_sh, 0, dist.get_rank(sp)), b_sh, 1, dist.get_rank(dp)).contiguous()
     ys = _split(yf, b_sh, 0, dist.get_rank(dp)).contiguous()
     z = es.einshard("a/sp b/dp, b/dp c -> a/sp c", xs, ys, mesh=mesh, shapes={"sp": a_sh, "dp": b_sh})
@@ -153,8 +153,8 @@ def _mesh2d(ctx):
     q = torch.randn(2, 3, 8, 4)
     k = torch.randn(2, 3, 8, 4)
     P = dist.get_world_size(sp)
-    qs = _split(q, [8 // P] * P if 8 % P == 0 else es.helpers.compute_split_shapes(8, P), 2, dist.get_rank(sp))
-    ks = _split(k, [8 // P] * P if 8 % P == 0 else es.helpers.compute_split_shapes(8, P), 2, dist.get_rank(sp))
+    qs = _split(q, [8 // P] * P if 8 % P == 0 else es.compute_split_shapes(8, P), 2, dist.get_rank(sp))
+    ks = _split(k, [8 // P] * P if 8 % P == 0 else es.compute_split_shapes(8, P), 2, dist.get_rank(sp))
     s = es.einshard("b h q/sp d, b h k/sp d -> b h q/sp k", qs.contiguous(), ks.contiguous(), mesh=mesh)
     ref = torch.einsum("bhqd,bhkd->bhqk", q, k)
     assert_close(s, _split(ref, [8 // P] * P, 2, dist.get_rank(sp)), rtol=1e-4, atol=1e-5)

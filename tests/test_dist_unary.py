@@ -26,7 +26,7 @@ def _split_gather(ctx):
     group = mesh["dp"].get_group()
     rank, P = dist.get_rank(group), dist.get_world_size(group)
     rows = P * 2
-    shapes = es.helpers.compute_split_shapes(rows, P)
+    shapes = es.compute_split_shapes(rows, P)
     x = torch.randn(rows, 3, requires_grad=True)
     z = es.einshard("a b -> a/dp b", x, mesh=mesh, shapes=shapes)
     assert z.shape == (shapes[rank], 3)
@@ -49,7 +49,7 @@ def _split_gather(ctx):
     assert_close(z, _split(x, shapes, 1, rank).transpose(0, 1).contiguous())
 
     # uneven gather (BASELINE CPU config shape pattern)
-    uneven = es.helpers.compute_split_shapes(P * 3 + 1, P)
+    uneven = es.compute_split_shapes(P * 3 + 1, P)
     full = torch.randn(sum(uneven), 4)
     zz = es.einshard("a/dp c -> a c", _split(full, uneven, 0, rank).contiguous(), mesh=mesh, shapes=uneven)
     assert_close(zz, full)
@@ -64,8 +64,8 @@ def _repartition(ctx):
     group = mesh["dp"].get_group()
     rank, P = dist.get_rank(group), dist.get_world_size(group)
     for rows, cols in ((P * 2, P * 3), (P * 2 + 1, P * 3 + 2)):
-        rs = es.helpers.compute_split_shapes(rows, P)
-        cs = es.helpers.compute_split_shapes(cols, P)
+        rs = es.compute_split_shapes(rows, P)
+        cs = es.compute_split_shapes(cols, P)
         full = torch.randn(rows, cols)
         x = _split(full, rs, 0, rank).clone().requires_grad_(True)
         z = es.einshard("a/dp b -> a b/dp", x, mesh=mesh, shapes={"dp": {"a": rs, "b": cs}})
@@ -87,8 +87,8 @@ def _owner_swaps(ctx):
     mesh = ctx.mesh((2, ctx.world_size // 2), ("dp", "sp"))
     dp, sp = mesh["dp"].get_group(), mesh["sp"].get_group()
     rows = 16
-    dps = es.helpers.compute_split_shapes(rows, dist.get_world_size(dp))
-    sps = es.helpers.compute_split_shapes(rows, dist.get_world_size(sp))
+    dps = es.compute_split_shapes(rows, dist.get_world_size(dp))
+    sps = es.compute_split_shapes(rows, dist.get_world_size(sp))
     full = torch.randn(rows, 3)
     x = _split(full, dps, 0, dist.get_rank(dp)).clone()
     with pytest.warns(RuntimeWarning, match="gather/split fallback"):
@@ -98,7 +98,7 @@ def _owner_swaps(ctx):
     # (2, 2, 2) mesh: equal dims -> one owner swap
     mesh = ctx.mesh((2, 2, ctx.world_size // 4), ("dp", "sp", "tp"))
     dp, sp, tp = (mesh[n].get_group() for n in ("dp", "sp", "tp"))
-    shapes = es.helpers.compute_split_shapes(8, 2)
+    shapes = es.compute_split_shapes(8, 2)
     full = torch.randn(8, 3)
     x = _split(full, shapes, 0, dist.get_rank(dp)).clone().requires_grad_(True)
     z = es.einshard("a/dp b -> a/sp b", x, mesh=mesh, shapes={"dp": {"a": shapes}, "sp": {"a": shapes}})
@@ -108,7 +108,7 @@ def _owner_swaps(ctx):
     assert_close(x.grad, torch.ones_like(x))
 
     # swap plus an independent split
-    a_s, b_s = es.helpers.compute_split_shapes(5, 2), es.helpers.compute_split_shapes(7, dist.get_world_size(tp))
+    a_s, b_s = es.compute_split_shapes(5, 2), es.compute_split_shapes(7, dist.get_world_size(tp))
     full = torch.randn(5, 7)
     x = _split(full, a_s, 0, dist.get_rank(dp)).clone()
     z = es.einshard("a/dp b -> a/sp b/tp", x, mesh=mesh,
@@ -117,7 +117,7 @@ def _owner_swaps(ctx):
     assert [s.name for s in es.last_plan()] == ["owner_swap", "split_forward_allgather_backward"]
 
     # unchanged axis on an involved dim -> fallback
-    a_s, c_s = es.helpers.compute_split_shapes(5, 2), es.helpers.compute_split_shapes(7, 2)
+    a_s, c_s = es.compute_split_shapes(5, 2), es.compute_split_shapes(7, 2)
     full = torch.randn(5, 7, 3)
     x = _split(_split(full, a_s, 0, dist.get_rank(dp)), c_s, 1, dist.get_rank(sp)).clone()
     with pytest.warns(RuntimeWarning, match="gather/split fallback"):
@@ -129,7 +129,7 @@ def _owner_swaps(ctx):
     # multi-axis swap h/sp1 w/sp2 -> h/sp2 w/sp1
     mesh = ctx.mesh((ctx.world_size // 4, 2, 2), ("dp", "sp1", "sp2"))
     s1, s2 = mesh["sp1"].get_group(), mesh["sp2"].get_group()
-    hs, ws = es.helpers.compute_split_shapes(5, 2), es.helpers.compute_split_shapes(7, 2)
+    hs, ws = es.compute_split_shapes(5, 2), es.compute_split_shapes(7, 2)
     full = torch.randn(2, 5, 7, 3)
     x = _split(_split(full, hs, 1, dist.get_rank(s1)), ws, 2, dist.get_rank(s2)).clone().requires_grad_(True)
     z = es.einshard("b h/sp1 w/sp2 c -> b h/sp2 w/sp1 c", x, mesh=mesh,
@@ -161,7 +161,7 @@ def _partials(ctx):
     assert_close(x.grad, torch.ones_like(x) * P)
 
     rows = P * 2
-    shapes = es.helpers.compute_split_shapes(rows, P)
+    shapes = es.compute_split_shapes(rows, P)
     x = torch.full((rows, 3), float(rank + 1), requires_grad=True)
     z = es.einshard("a b // tp -> a/tp b", x, mesh=mesh, shapes=shapes)
     assert_close(z, _split(torch.full_like(x, total), shapes, 0, rank))

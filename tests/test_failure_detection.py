@@ -48,11 +48,11 @@ def _skip_one_allreduce(rank, world):
 
     import torch_einshard_b200 as es
     from torch_einshard_b200.ops import _native
-    from torch_einshard_b200.parallel import native_comm
+    from torch_einshard_b200.parallel import symmetric
 
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     assert es.setup_native_comm(mesh)
-    comm = native_comm.communicator_for(mesh["tp"].get_group())
+    comm = symmetric.communicator_for(mesh["tp"].get_group())
     x = torch.ones(1024, device="cuda")
     assert comm.all_reduce_(x)           # call 1: everyone
     comm.check_health()

@@ -27,12 +27,12 @@ def _body(rank, world):
     import torch_einshard_b200 as es
     from torch_einshard_b200.models.tp_mlp import TPMLP
     from torch_einshard_b200.ops import _native, fused_native
-    from torch_einshard_b200.parallel import native_comm
+    from torch_einshard_b200.parallel import symmetric
 
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     assert es.setup_native_comm(mesh)
     group = mesh["tp"].get_group()
-    comm = native_comm.communicator_for(group)
+    comm = symmetric.communicator_for(group)
     assert comm is not None and comm.nvls, "no NVLS multicast heap"
     g = torch.Generator(device="cuda").manual_seed(7 + rank)
 
@@ -75,9 +75,9 @@ def _body(rank, world):
 
     fused = run()
     assert [s.name for s in es.last_plan()] == ["rank_local_einsum", "allreduce_forward_identity_backward"]
-    native_comm.disable()
+    symmetric.disable()
     plain = run()
-    native_comm._state["enabled"] = True
+    symmetric._state["enabled"] = True
     for got, want in zip(fused, plain):
         scale = want.abs().max().item() + 1e-3
         assert (got - want).abs().max().item() <= 3e-2 * scale

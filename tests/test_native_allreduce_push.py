@@ -19,11 +19,11 @@ def _push(rank, world):
 
     import torch_einshard_b200 as es
     from torch_einshard_b200.ops import _native
-    from torch_einshard_b200.parallel import native_comm, symmetric
+    from torch_einshard_b200.parallel import symmetric
 
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     assert es.setup_native_comm(mesh)
-    comm = native_comm.communicator_for(mesh["tp"].get_group())
+    comm = symmetric.communicator_for(mesh["tp"].get_group())
     mod = _native.require()
     for dtype, n in [(torch.bfloat16, 8 * 7), (torch.float16, 4096 * 3 + 8), (torch.float32, 4 * 1001),
                      (torch.bfloat16, 1 << 20)]:

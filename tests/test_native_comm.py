@@ -18,19 +18,19 @@ def _collectives(rank, world):
     import torch_einshard_b200 as es
     from torch_einshard_b200.ops import _native
     from torch_einshard_b200.parallel import collectives as C
-    from torch_einshard_b200.parallel import native_comm
+    from torch_einshard_b200.parallel import symmetric
 
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     assert es.setup_native_comm(mesh)
     group = mesh["tp"].get_group()
-    assert native_comm.communicator_for(group) is not None
+    assert symmetric.communicator_for(group) is not None
 
     def ref(fn):
-        native_comm.disable()
+        symmetric.disable()
         try:
             return fn()
         finally:
-            native_comm._state["enabled"] = True
+            symmetric._state["enabled"] = True
 
     for dtype in (torch.bfloat16, torch.float32):
         x = torch.randn(3, 1000 + 8 * rank * 0, 24, device="cuda", dtype=dtype) * (rank + 1)

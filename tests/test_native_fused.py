@@ -18,13 +18,13 @@ def _fused(rank, world):
     import torch_einshard_b200 as es
     from torch_einshard_b200.ops import _native, fused_native, gemm
     from torch_einshard_b200.ops.fused_native import gemm_allreduce
-    from torch_einshard_b200.parallel import native_comm
+    from torch_einshard_b200.parallel import symmetric
     from torch_einshard_b200.models.tp_mlp import TPMLP
 
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     assert es.setup_native_comm(mesh)
     group = mesh["tp"].get_group()
-    comm = native_comm.communicator_for(group)
+    comm = symmetric.communicator_for(group)
 
     # raw fused kernel: ragged shapes, repeated calls (epochs), both operand layouts
     for (m, n, k) in [(256, 512, 128), (300, 700, 136), (1024, 2048, 512)]:
@@ -70,13 +70,13 @@ def _fused(rank, world):
         runs.append((y.detach().float(), xi.grad.float(), model.w1.grad.float(), model.w2.grad.float()))
     fused_native._MAX_FUSED_EPILOGUE_RANKS = 0
 
-    native_comm.disable()
+    symmetric.disable()
     x2 = x.detach().clone().requires_grad_(True)
     model.w1.grad = model.w2.grad = None
     y2 = model(x2)
     y2.backward(dy)
     want = (y2.detach().float(), x2.grad.float(), model.w1.grad.float(), model.w2.grad.float())
-    native_comm._state["enabled"] = True
+    symmetric._state["enabled"] = True
     for got in runs:
         for g, w in zip(got, want):
             scale = w.abs().max().item() + 1e-3
@@ -103,12 +103,12 @@ def _sequence_parallel(rank, world):
 
     import torch_einshard_b200 as es
     from torch_einshard_b200.ops import _native, fused_native
-    from torch_einshard_b200.parallel import native_comm
+    from torch_einshard_b200.parallel import symmetric
 
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     assert es.setup_native_comm(mesh)
     group = mesh["tp"].get_group()
-    comm = native_comm.communicator_for(group)
+    comm = symmetric.communicator_for(group)
 
     # raw fused GEMM + reduce-scatter of row segments
     torch.manual_seed(1)
@@ -163,9 +163,9 @@ def _sequence_parallel(rank, world):
     fused_native._MAX_FUSED_EPILOGUE_RANKS = 0
     assert p1 == ["allgather_forward_reducescatter_backward", "rank_local_einsum"], p1
     assert p2 == ["rank_local_einsum", "reducescatter_forward_allgather_backward"], p2
-    native_comm.disable()
+    symmetric.disable()
     want, q1, q2 = run()
-    native_comm._state["enabled"] = True
+    symmetric._state["enabled"] = True
     assert (p1, p2) == (q1, q2)
     for g, w in zip(got, want):
         scale = w.abs().max().item() + 1e-3

@@ -3,9 +3,9 @@
 import pytest
 
 import torch_einshard_b200 as es
-from torch_einshard_b200.grammar import parse_sharding, sharding
+from torch_einshard_b200.notation.parser import parse_sharding, sharding
 from torch_einshard_b200.notation.families import cached_expand_axis_families, expand_family_mapping
-from torch_einshard_b200.sharding import Axis, AxisGroup, EllipsisAxis, GradAnnotation, InitSyncAnnotation
+from torch_einshard_b200.notation.spec import Axis, AxisGroup, EllipsisAxis, GradAnnotation, InitSyncAnnotation
 
 
 def test_partials_single_and_list():

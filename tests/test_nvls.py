@@ -26,12 +26,12 @@ def _body(rank, world):
 
     import torch_einshard_b200 as es
     from torch_einshard_b200.ops import _native
-    from torch_einshard_b200.parallel import native_comm
+    from torch_einshard_b200.parallel import symmetric
 
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     assert es.setup_native_comm(mesh)
     group = mesh["tp"].get_group()
-    comm = native_comm.communicator_for(group)
+    comm = symmetric.communicator_for(group)
     assert comm is not None
     assert comm.nvls, "the heap has no NVLS multicast mapping on this machine"
     g = torch.Generator(device="cuda").manual_seed(100 + rank)

@@ -118,7 +118,7 @@ def _dist_roll_halo(ctx):
     group = mesh["dp"].get_group()
     rank, P = dist.get_rank(group), dist.get_world_size(group)
     for rows, shift in ((P * 3, 2), (P * 3, -2), (P * 3 + 1, -3), (P * 3, 3)):
-        shapes = es.helpers.compute_split_shapes(rows, P)
+        shapes = es.compute_split_shapes(rows, P)
         full = torch.randn(rows, 5)
         x = _split(full, shapes, 0, rank).clone().requires_grad_(True)
         z = es.einroll("a/dp b", x, {"a": shift}, mesh=mesh, shapes=shapes)
@@ -134,7 +134,7 @@ def _dist_roll_halo(ctx):
     # halos over uneven shards, including halos wider than a shard
     for boundary in ("constant", "periodic", "replicate"):
         for left, right in ((1, 1), (2, 0), (4, 5)):
-            shapes = es.helpers.compute_split_shapes(P * 3 + 2, P)
+            shapes = es.compute_split_shapes(P * 3 + 2, P)
             full = torch.randn(sum(shapes), 3)
             x = _split(full, shapes, 0, rank).clone().requires_grad_(True)
             z = es.einhalo("h/dp c", x, {"h": (left, right)}, boundary=boundary, fill=-2.0, mesh=mesh,
@@ -171,7 +171,7 @@ def _dist_conv_window(ctx):
     mesh = ctx.mesh((2, ctx.world_size // 2), ("sp_h", "sp_w"))
     hg, wg = mesh["sp_h"].get_group(), mesh["sp_w"].get_group()
     H, W = 9, 2 * dist.get_world_size(wg) + 1
-    hs, ws = es.helpers.compute_split_shapes(H, 2), es.helpers.compute_split_shapes(W, dist.get_world_size(wg))
+    hs, ws = es.compute_split_shapes(H, 2), es.compute_split_shapes(W, dist.get_world_size(wg))
     img = torch.randn(2, H, W, 3)
     weight = torch.randn(4, 3, 3, 3)
     local = _split(_split(img, hs, 1, dist.get_rank(hg)), ws, 2, dist.get_rank(wg)).contiguous()
@@ -195,7 +195,7 @@ def _dist_fft(ctx):
     group = mesh["tp"].get_group()
     rank, P = dist.get_rank(group), dist.get_world_size(group)
     size = P * P * 3
-    shapes = es.helpers.compute_split_shapes(size, P)
+    shapes = es.compute_split_shapes(size, P)
     full = torch.randn(2, size, dtype=torch.complex64)
     x = _split(full, shapes, 1, rank).contiguous().requires_grad_(True)
     for inverse in (False, True):
@@ -217,8 +217,8 @@ def _dist_fft(ctx):
     # slab layout (transform axes trade the mesh dim): b x/tp y -> b kx ky/tp
     X, Y = 2 * P, 3 * P
     vol = torch.randn(2, X, Y, dtype=torch.complex64)
-    xs_ = es.helpers.compute_split_shapes(X, P)
-    ys_ = es.helpers.compute_split_shapes(Y, P)
+    xs_ = es.compute_split_shapes(X, P)
+    ys_ = es.compute_split_shapes(Y, P)
     slab = _split(vol, xs_, 1, rank).contiguous()
     z = es.einfft("b x/tp y -> b kx ky/tp", slab, axes={"x": "kx", "y": "ky"}, mesh=mesh,
                   shapes={"tp": {"x": xs_, "ky": ys_}})

@@ -130,7 +130,7 @@ def _dist_params(ctx):
     p = nn.Parameter(torch.zeros(3, 4))
     es.register_parameter_layout(p, "o/sp c", mesh=mesh2d)
     meta = es.param_shard_metadata(p, (10, 4), mesh2d)
-    sizes = es.helpers.compute_split_shapes(10, dist.get_world_size(sp))
+    sizes = es.compute_split_shapes(10, dist.get_world_size(sp))
     start = sum(sizes[:dist.get_rank(sp)])
     assert meta.local_slices == (slice(start, start + sizes[dist.get_rank(sp)]), slice(None))
     assert meta.local_shape == (sizes[dist.get_rank(sp)], 4) and meta.shard_dims == ("sp",)
@@ -138,7 +138,7 @@ def _dist_params(ctx):
     es.register_parameter_layout(q, "o/dp-sp c", mesh=wrapped)
     size = dist.get_world_size(wrapped["dp-sp"].get_group())
     rank = dist.get_rank(wrapped["dp-sp"].get_group())
-    chunks = es.helpers.compute_split_shapes(16, size)
+    chunks = es.compute_split_shapes(16, size)
     assert es.param_local_slices(q, (16, 4), wrapped)[0] == slice(sum(chunks[:rank]), sum(chunks[:rank + 1]))
 
     # init sync broadcasts from group rank 0 of every replicated mesh dim

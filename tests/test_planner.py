@@ -3,8 +3,8 @@ model, policies and execution tracing."""
 
 import pytest
 
-from torch_einshard_b200.grammar import parse_sharding
-from torch_einshard_b200.symbolic import (
+from torch_einshard_b200.notation.parser import parse_sharding
+from torch_einshard_b200.plan import (
     ExecutionPlan,
     PlanPolicy,
     PlanStep,

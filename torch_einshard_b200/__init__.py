@@ -18,7 +18,8 @@ from .ops.halo import einhalo, einwindow
 from .ops.roll import einroll
 from .parallel.executor import distributed_1d
 from .parallel.mesh import CompoundDeviceMesh, wrap_mesh
-from .parallel.setup import setup_native_comm
+from .parallel.collectives import compute_split_shapes, compute_split_shapes_for_factors, init_process_group, resolve_split_shapes
+from .parallel.symmetric import setup_native_comm, teardown_native_comm
 from .params import (
     NativeGradReductionHandle,
     ParameterGradComm,
@@ -66,19 +67,6 @@ from .plan.state import TensorState
 from .plan.trace import ExecutionPlan, last_alternatives, last_candidates, last_plan, set_last_plan
 from .plan.transitions import build_binary_transition_plan, build_unary_transition_plan
 from .api import einshard, einshard_like, local_operation
-from . import helpers, mappings, grammar, sharding, symbolic, families  # noqa: F401  (module aliases)
 
 __version__ = "0.1.0"
 
-# Module paths of the reference package (``torch_einshard.fft``, ``.einsum``, ...)
-# name the implementation modules here, so code and tests that patch
-# ``<package>.fft._distributed_fft_1d_no_autograd`` and the like keep working.
-import sys as _sys
-
-from .ops import conv as _conv_mod, einsum as _einsum_mod, fft as _fft_mod, halo as _halo_mod, roll as _roll_mod
-from .parallel import executor as _executor_mod, mesh as _mesh_mod
-
-for _alias, _module in (("fft", _fft_mod), ("halo", _halo_mod), ("conv", _conv_mod), ("roll", _roll_mod),
-                        ("einsum", _einsum_mod), ("distributed", _executor_mod), ("mesh", _mesh_mod)):
-    _sys.modules.setdefault(f"{__name__}.{_alias}", _module)
-del _alias, _module

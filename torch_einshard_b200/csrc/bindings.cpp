@@ -836,6 +836,21 @@ void wait_probe_noalloc_status(const at::Tensor& flag, int64_t target, int64_t t
   TORCH_CHECK(rc == 0, "einshard wait_probe_noalloc_status: launch failed (", rc, ")");
 }
 
+// out = x (contiguous) rolled by shifts[d] along every dim d, one kernel.
+void roll_copy(const at::Tensor& x, at::Tensor out, std::vector<int64_t> shifts) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && out.is_contiguous() && out.sizes() == x.sizes() &&
+                  out.scalar_type() == x.scalar_type() && (int64_t)shifts.size() == x.dim() &&
+                  x.dim() >= 1 && x.dim() <= es::kCopyMaxRank + 1,
+              "einshard roll: contiguous tensors of equal shape, one shift per dim");
+  const c10::cuda::CUDAGuard guard(x.device());
+  std::vector<long long> size(x.sizes().begin(), x.sizes().end()), shift(shifts.begin(), shifts.end());
+  const int rc = es::roll_copy(x.data_ptr(), out.data_ptr(), static_cast<int>(x.element_size()),
+                               static_cast<int>(x.dim()), size.data(), shift.data(), num_sms(x.get_device()),
+                               at::cuda::getCurrentCUDAStream());
+  TORCH_CHECK(rc == 0, "einshard roll: launch failed (", rc, ")");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
 // out (contiguous) = view (any strides, rank <= 8), one gather kernel.
 void strided_copy(const at::Tensor& view, at::Tensor out) {
   TORCH_CHECK(view.is_cuda() && out.is_cuda() && out.is_contiguous() && out.sizes() == view.sizes() &&
@@ -926,6 +941,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
   m.def("conv2d_wgrad", &conv2d_wgrad, "weight gradient of the implicit-GEMM conv (split-K tcgen05, fp32 out)");
   m.def("conv2d_implicit", &conv2d_implicit, "implicit-GEMM NHWC conv2d on tcgen05 (stride 1)");
+  m.def("roll_copy", &roll_copy, "cyclic roll along several dims in one kernel");
   m.def("gemm_silu", &gemm_silu, "(silu(a @ b), a @ b), fused on the wide kernel when it runs the GEMM");
   m.def("silu_forward", &silu_forward, "elementwise silu");
   m.def("silu_backward", &silu_backward, "grad * silu'(h)");

@@ -171,6 +171,98 @@ int strided_gather(const void* src, void* dst, int esize, int rank, const long l
   return static_cast<int>(cudaGetLastError());
 }
 
+// ------------------------------------------------------------------ cyclic roll
+
+namespace {
+
+// dst = src rolled along several dims at once.  The tensor is viewed as
+// [lead dims ..., n, tail]: every rolled dim is a lead dim or n (the last
+// rolled dim), tail is the product of the dims after it, moved as one block of
+// `tail` units.  Output position (lead index i, c, t) reads source position
+// ((i_d - shift_d) mod size_d, (c - shift_n) mod n, t).
+struct RollGeom {
+  int rank;                       // lead dims, outermost first
+  long long size[kCopyMaxRank];
+  long long shift[kCopyMaxRank];  // in [0, size)
+  long long n, shift_n;           // the last rolled dim
+  long long tail;                 // units per block
+  long long total;                // units of the tensor
+};
+
+template <typename U>
+__global__ void __launch_bounds__(256) roll_kernel(const U* __restrict__ src, U* __restrict__ dst, RollGeom g) {
+  const long long nth = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < g.total; i += nth) {
+    const long long t = i % g.tail;
+    long long q = i / g.tail;
+    const long long c = q % g.n;
+    q /= g.n;
+    long long sc = c - g.shift_n;
+    if (sc < 0) sc += g.n;
+    long long srow = 0, mult = 1;
+#pragma unroll
+    for (int d = kCopyMaxRank - 1; d >= 0; --d) {
+      if (d < g.rank) {
+        const long long id = q % g.size[d];
+        q /= g.size[d];
+        long long sd = id - g.shift[d];
+        if (sd < 0) sd += g.size[d];
+        srow += sd * mult;
+        mult *= g.size[d];
+      }
+    }
+    dst[i] = src[(srow * g.n + sc) * g.tail + t];
+  }
+}
+
+}  // namespace
+
+int roll_copy(const void* src, void* dst, int esize, int rank, const long long* size, const long long* shift,
+              int num_sms, cudaStream_t stream) {
+  if (rank < 1 || rank > kCopyMaxRank + 1) return -1;
+  int last = -1;
+  for (int d = 0; d < rank; ++d)
+    if (shift[d] % size[d] != 0) last = d;
+  long long total_elems = 1;
+  for (int d = 0; d < rank; ++d) total_elems *= size[d];
+  if (total_elems == 0) return 0;
+  if (last < 0) {  // nothing moves
+    return static_cast<int>(cudaMemcpyAsync(dst, src, total_elems * esize, cudaMemcpyDeviceToDevice, stream));
+  }
+  RollGeom g;
+  long long tail = 1;
+  for (int d = last + 1; d < rank; ++d) tail *= size[d];
+  g.rank = last;
+  for (int d = 0; d < last; ++d) {
+    g.size[d] = size[d];
+    g.shift[d] = ((shift[d] % size[d]) + size[d]) % size[d];
+  }
+  g.n = size[last];
+  g.shift_n = ((shift[last] % size[last]) + size[last]) % size[last];
+  const bool aligned = ((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0;
+  int unit_bytes = esize;
+  for (int u : {16, 8, 4}) {
+    if (u > esize && (tail * esize) % u == 0 && aligned) {
+      unit_bytes = u;
+      break;
+    }
+  }
+  g.tail = tail * esize / unit_bytes;
+  g.total = total_elems * esize / unit_bytes;
+  const long long want = (g.total + 255) / 256;
+  const long long cap = static_cast<long long>(num_sms > 0 ? num_sms : 148) * 16;
+  const unsigned nb = static_cast<unsigned>(want < 1 ? 1 : (want > cap ? cap : want));
+  switch (unit_bytes) {
+    case 16: roll_kernel<uint4><<<nb, 256, 0, stream>>>(static_cast<const uint4*>(src), static_cast<uint4*>(dst), g); break;
+    case 8: roll_kernel<uint2><<<nb, 256, 0, stream>>>(static_cast<const uint2*>(src), static_cast<uint2*>(dst), g); break;
+    case 4: roll_kernel<uint32_t><<<nb, 256, 0, stream>>>(static_cast<const uint32_t*>(src), static_cast<uint32_t*>(dst), g); break;
+    case 2: roll_kernel<uint16_t><<<nb, 256, 0, stream>>>(static_cast<const uint16_t*>(src), static_cast<uint16_t*>(dst), g); break;
+    case 1: roll_kernel<uint8_t><<<nb, 256, 0, stream>>>(static_cast<const uint8_t*>(src), static_cast<uint8_t*>(dst), g); break;
+    default: return -1;
+  }
+  return static_cast<int>(cudaGetLastError());
+}
+
 // ------------------------------------------------------------------ bounded-wait probe
 
 namespace {

@@ -1,18 +1,32 @@
 """``einconv``: halo exchange followed by a same-length convolution.
 
-Validates the named-axis formula (one input channel axis, one output channel
-axis, local weight/kernel axes, stride 1, groups 1, padding that preserves the
-spatial length), exchanges halos of the sharded spatial axes and runs the
-convolution with zero padding on the haloed tensor.  ``checkpoint`` selects
-activation checkpointing: ``"full"`` (default: halo + conv recomputed in
-backward), ``"conv"`` (only the convolution), or off.  Contract of
-``src/torch_einshard/conv.py:64-210``.
+A call is handled in three stages.
 
-The 2-D bf16/fp16 CUDA case with a 3x3-style odd kernel runs as an implicit
-GEMM on the tcgen05 kernel (``ops.conv_native``): each kernel tap is one GEMM
-over shifted views of the haloed NHWC input, accumulated in fp32, so no
-im2col tensor is materialised.  Other cases use ``torch.nn.functional.conv*d``.
+1. Analysis (``_Analysis``): the named-axis formula, the windows mapping and the
+   numeric arguments are reduced to roles: batch axes, spatial (window source)
+   axes, kernel (window) axes, one input and one output channel axis, plus the
+   per-axis padding.  The checks form one ordered rule table (``_RULES``); the
+   first rule that fails raises.  The table keeps the reference's error types,
+   texts and order (user code and tests match them): one input channel axis,
+   one output channel axis, local weight and channel axes, stride 1, groups 1,
+   padding that preserves every spatial length.
+2. Layout (``_Layout``): the permutations that bring the operands into the
+   order the chosen kernel reads.  The native implicit-GEMM kernel
+   (``csrc/conv.cu``, tcgen05, no im2col) reads channels-last operands:
+   input [batch, spatial..., C], weight [O, taps..., C] and writes
+   [batch, spatial..., O]; ``torch.nn.functional.conv{1,2,3}d`` (every case
+   outside the native envelope) reads channels-first ones.  Local spatial axes
+   with a zero boundary are padded by the native kernel itself (TMA zero fill),
+   so no padded copy of the input is made for them; every other axis gets its
+   halo (``ops/halo.py``) first.
+3. Execution with the checkpoint mode: ``"full"`` (default; halo and conv
+   recomputed in backward), ``"conv"`` (only the convolution) or off.
+
+Contract of ``src/torch_einshard/conv.py:64-210``.
 """
+
+from dataclasses import dataclass
+from functools import cached_property
 
 import torch.nn.functional as F
 from torch.utils.checkpoint import checkpoint as torch_checkpoint
@@ -20,42 +34,206 @@ from torch.utils.checkpoint import checkpoint as torch_checkpoint
 from ..notation.families import cached_expand_axis_families, expand_family_mapping
 from ..notation.parser import parse_sharding
 from ..notation.spec import EllipsisAxis
+from . import conv_impl
 from .halo import halo_tensor, normalize_halo
 
 __all__ = ["einconv"]
+
+_TORCH_CONV = {1: F.conv1d, 2: F.conv2d, 3: F.conv3d}
 
 
 def _axes(spec):
     return spec.axes if hasattr(spec, "axes") else spec
 
 
-def _names(axes, *, label):
-    names = []
-    for axis in axes:
-        if isinstance(axis, EllipsisAxis):
-            raise NotImplementedError(f"einconv does not support ellipsis axes in {label}")
-        if not hasattr(axis, "name"):
-            raise NotImplementedError(f"einconv does not support factored axes in {label}")
-        if axis.name in names:
-            raise ValueError(f"Axis {axis.name!r} appears more than once in {label}")
-        names.append(axis.name)
-    return names
-
-
-def _per_dim(value, ndim, *, label):
-    if isinstance(value, int):
-        return (value,) * ndim
-    values = tuple(value)
+def _per_dim(value, ndim, label):
+    values = (value,) * ndim if isinstance(value, int) else tuple(value)
     if len(values) != ndim:
         raise ValueError(f"{label} must have {ndim} values")
     return values
 
 
-def _conv_fn(ndim):
-    try:
-        return {1: F.conv1d, 2: F.conv2d, 3: F.conv3d}[ndim]
-    except KeyError:
-        raise ValueError("einconv supports 1D, 2D, and 3D convolutions") from None
+class _Analysis:
+    """Roles of every axis of an einconv call, derived on demand (the rules
+    below read them in order, so a property is only computed once the rules
+    before it have passed)."""
+
+    def __init__(self, specs, windows, weight, padding, stride, dilation, groups, families):
+        self.in_spec, self.w_spec, self.out_spec = specs
+        self.windows, self.weight = windows, weight
+        self.padding, self.stride_arg, self.dilation_arg = padding, stride, dilation
+        self.groups, self.families = groups, families
+
+    def names(self, spec, label):
+        seen = []
+        for axis in _axes(spec):
+            if isinstance(axis, EllipsisAxis):
+                raise NotImplementedError(f"einconv does not support ellipsis axes in {label}")
+            if not hasattr(axis, "name"):
+                raise NotImplementedError(f"einconv does not support factored axes in {label}")
+            if axis.name in seen:
+                raise ValueError(f"Axis {axis.name!r} appears more than once in {label}")
+            seen.append(axis.name)
+        return seen
+
+    @cached_property
+    def in_names(self):
+        return self.names(self.in_spec, "input")
+
+    @cached_property
+    def w_names(self):
+        return self.names(self.w_spec, "weight")
+
+    @cached_property
+    def out_names(self):
+        return self.names(self.out_spec, "output")
+
+    @property
+    def spatial(self):
+        return list(self.windows)
+
+    @property
+    def kernel(self):
+        return list(self.windows.values())
+
+    def axis(self, spec, name):
+        return {a.name: a for a in _axes(spec)}[name]
+
+    @cached_property
+    def cin_candidates(self):
+        return [n for n in self.in_names if n in self.w_names and n not in self.spatial and n not in self.out_names]
+
+    @cached_property
+    def cout_candidates(self):
+        return [n for n in self.w_names if n in self.out_names and n not in self.in_names]
+
+    @property
+    def cin(self):
+        return self.cin_candidates[0]
+
+    @property
+    def cout(self):
+        return self.cout_candidates[0]
+
+    @cached_property
+    def ndim(self):
+        return len(self.spatial)
+
+    @cached_property
+    def stride(self):
+        return _per_dim(self.stride_arg, self.ndim, "stride")
+
+    @cached_property
+    def dilation(self):
+        return _per_dim(self.dilation_arg, self.ndim, "dilation")
+
+    @cached_property
+    def pads(self):
+        """Padding per spatial axis as given (an int or a (left, right) pair)."""
+        kdims = [self.w_names.index(n) for n in self.kernel]
+        if self.padding is None:
+            pads = []
+            for kd, dil in zip(kdims, self.dilation):
+                span = dil * (self.weight.shape[kd] - 1)
+                if span % 2:
+                    raise ValueError("Default einconv padding requires odd effective kernel sizes")
+                pads.append(span // 2)
+            return tuple(pads)
+        pads = expand_family_mapping(self.padding, self.families, label="Padding")
+        if not isinstance(pads, dict):
+            return _per_dim(pads, self.ndim, "padding")
+        unknown = set(pads) - set(self.spatial)
+        if unknown:
+            raise ValueError(f"Padding axis {sorted(unknown)[0]!r} has no matching window")
+        missing = [n for n in self.spatial if n not in pads]
+        if missing:
+            raise ValueError(f"Missing padding for window source axis {missing[0]!r}")
+        return tuple(pads[n] for n in self.spatial)
+
+
+def _first(items):
+    return items[0] if items else None
+
+
+# Ordered rule table: (condition that must hold, error raised when it does not).
+# Each condition may itself raise (name checks, per-dim lengths, padding forms).
+_RULES = (
+    (lambda a: a.w_spec is not None, lambda a: ValueError("einconv expects a binary sharding expression")),
+    (lambda a: not (a.in_spec.partials or a.w_spec.partials or a.out_spec.partials),
+     lambda a: ValueError("einconv does not support partial tensor specs")),
+    (lambda a: a.groups == 1, lambda a: NotImplementedError("einconv currently supports only groups=1")),
+    # the name checks raise their own errors (ellipsis, factored, repeated axes)
+    (lambda a: (a.in_names, a.w_names, a.out_names) is not None, None),
+    (lambda a: a.ndim in (1, 2, 3), lambda a: ValueError("einconv supports 1D, 2D, and 3D convolutions")),
+    (lambda a: len(set(a.kernel)) == len(a.kernel), lambda a: ValueError("Window axes must be distinct")),
+    (lambda a: _first([n for n in a.spatial if n not in a.in_names]) is None,
+     lambda a: ValueError(f"Window source axis {_first([n for n in a.spatial if n not in a.in_names])!r} "
+                          "is not present in the input")),
+    (lambda a: _first([n for n in a.kernel if n not in a.w_names]) is None,
+     lambda a: ValueError(f"Window axis {_first([n for n in a.kernel if n not in a.w_names])!r} "
+                          "is not present in the weight")),
+    (lambda a: not any(n in a.in_names or n in a.out_names for n in a.kernel),
+     lambda a: ValueError("Window axes must be weight-only axes")),
+    (lambda a: all(axis.local() for axis in _axes(a.w_spec)), lambda a: ValueError("einconv weight axes must be local")),
+    (lambda a: all(a.axis(a.out_spec, x.name) == x for x in _axes(a.in_spec) if x.name in a.out_names),
+     lambda a: ValueError("einconv output must preserve input axis sharding")),
+    (lambda a: len(a.cin_candidates) == 1, lambda a: ValueError("einconv expects exactly one input channel axis")),
+    (lambda a: a.axis(a.in_spec, a.cin).local(), lambda a: ValueError("einconv input channel axis must be local")),
+    (lambda a: len(a.cout_candidates) == 1, lambda a: ValueError("einconv expects exactly one output channel axis")),
+    (lambda a: a.axis(a.out_spec, a.cout).local(), lambda a: ValueError("einconv output channel axis must be local")),
+    (lambda a: _first([n for n in a.w_names if n not in {a.cout, a.cin, *a.kernel}]) is None,
+     lambda a: ValueError(f"Unexpected weight axis {_first([n for n in a.w_names if n not in {a.cout, a.cin, *a.kernel}])!r}")),
+    (lambda a: set(a.out_names) == (set(a.in_names) - {a.cin}) | {a.cout},
+     lambda a: ValueError("einconv output axes must be input axes with the channel axis replaced by the output "
+                          "channel axis")),
+    (lambda a: a.stride is not None and a.dilation is not None and all(s == 1 for s in a.stride),
+     lambda a: NotImplementedError("einconv currently supports only stride=1")),
+)
+
+
+def _preserving(a):
+    """Raise unless every spatial axis keeps its length (left + right = dilated span)."""
+    for name, pad, kd, dil in zip(a.spatial, a.pads, [a.w_names.index(n) for n in a.kernel], a.dilation):
+        left, right = normalize_halo(pad)
+        expected = dil * (a.weight.shape[kd] - 1)
+        if left + right != expected:
+            raise ValueError(
+                f"Padding for axis {name!r} must preserve the spatial length; "
+                f"got left + right = {left + right}, expected {expected}"
+            )
+
+
+def _validate(a):
+    for holds, error in _RULES:
+        if not holds(a):
+            raise error(a)
+    _preserving(a)
+
+
+@dataclass
+class _Layout:
+    """Operand and result permutations of one einconv call."""
+
+    batch: list
+    spatial: list
+    kernel: list
+    cin: str
+    cout: str
+    in_names: list
+    w_names: list
+    out_names: list
+
+    def x_order(self, channels_last):
+        order = self.batch + self.spatial + [self.cin] if channels_last else self.batch + [self.cin] + self.spatial
+        return [self.in_names.index(n) for n in order]
+
+    def w_order(self, channels_last):
+        order = [self.cout] + self.kernel + [self.cin] if channels_last else [self.cout, self.cin] + self.kernel
+        return [self.w_names.index(n) for n in order]
+
+    def out_order(self, channels_last):
+        produced = self.batch + self.spatial + [self.cout] if channels_last else self.batch + [self.cout] + self.spatial
+        return [produced.index(n) for n in self.out_names]
 
 
 def _mesh_dim_size(mesh, dim):
@@ -63,6 +241,24 @@ def _mesh_dim_size(mesh, dim):
         return mesh[dim].size()
     except Exception:  # noqa: BLE001 - compound or unknown names: not treated as trivial
         return 0
+
+
+def _kernel_padded_axes(a, x, mesh, boundary, fill):
+    """Spatial axes whose symmetric zero padding the native kernel applies
+    itself: local axes (and axes sharded over a one-rank mesh dim, which have
+    no neighbours), when the boundary is a zero constant."""
+    if boundary != "constant" or fill != 0:
+        return {}
+    if not conv_impl.kernel_padding_ok(x, a.weight, x.shape[a.in_names.index(a.cin)], a.spatial, a.dilation):
+        return {}
+    pads = {}
+    for name, pad in zip(a.spatial, a.pads):
+        left, right = normalize_halo(pad)
+        axis = a.axis(a.in_spec, name)
+        alone = not axis.local() and mesh is not None and _mesh_dim_size(mesh, axis.shard_dim) == 1
+        if (axis.local() or alone) and left == right:
+            pads[name] = left
+    return pads
 
 
 def _checkpointed(function, tensors, mode, use_reentrant):
@@ -79,139 +275,36 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
     """Sharding-aware halo exchange followed by a convolution."""
     shard, _ = cached_expand_axis_families(shard, families=families)
     windows = expand_family_mapping(windows, families, label="Window")
-    in_spec, w_spec, out_spec = parse_sharding(shard)
-    if w_spec is None:
-        raise ValueError("einconv expects a binary sharding expression")
-    if in_spec.partials or w_spec.partials or out_spec.partials:
-        raise ValueError("einconv does not support partial tensor specs")
-    if groups != 1:
-        raise NotImplementedError("einconv currently supports only groups=1")
+    a = _Analysis(parse_sharding(shard), windows, weight, padding, stride, dilation, groups, families)
+    _validate(a)
+    layout = _Layout([n for n in a.in_names if n not in a.spatial and n != a.cin], a.spatial, a.kernel, a.cin,
+                     a.cout, a.in_names, a.w_names, a.out_names)
+    kernel_pads = _kernel_padded_axes(a, x, mesh, boundary, fill)
+    exchanged = {n: p for n, p in zip(a.spatial, a.pads) if n not in kernel_pads}
+    halo_args = dict(mesh=mesh, shapes=shapes, boundary=boundary, fill=fill)
 
-    in_axes, w_axes, out_axes = _axes(in_spec), _axes(w_spec), _axes(out_spec)
-    in_names = _names(in_axes, label="input")
-    w_names = _names(w_axes, label="weight")
-    out_names = _names(out_axes, label="output")
-    spatial = list(windows.keys())
-    kernel = list(windows.values())
-    if len(spatial) not in (1, 2, 3):
-        raise ValueError("einconv supports 1D, 2D, and 3D convolutions")
-    if len(set(kernel)) != len(kernel):
-        raise ValueError("Window axes must be distinct")
-    missing = [n for n in spatial if n not in in_names]
-    if missing:
-        raise ValueError(f"Window source axis {missing[0]!r} is not present in the input")
-    missing = [n for n in kernel if n not in w_names]
-    if missing:
-        raise ValueError(f"Window axis {missing[0]!r} is not present in the weight")
-    if any(n in in_names or n in out_names for n in kernel):
-        raise ValueError("Window axes must be weight-only axes")
-    if not all(axis.local() for axis in w_axes):
-        raise ValueError("einconv weight axes must be local")
-    out_by = {a.name: a for a in out_axes}
-    for axis in in_axes:
-        if axis.name in out_by and out_by[axis.name] != axis:
-            raise ValueError("einconv output must preserve input axis sharding")
-    shared = [n for n in in_names if n in w_names and n not in spatial]
-    in_channels = [n for n in shared if n not in out_names]
-    if len(in_channels) != 1:
-        raise ValueError("einconv expects exactly one input channel axis")
-    cin = in_channels[0]
-    if not in_axes[in_names.index(cin)].local():
-        raise ValueError("einconv input channel axis must be local")
-    out_channels = [n for n in w_names if n in out_names and n not in in_names]
-    if len(out_channels) != 1:
-        raise ValueError("einconv expects exactly one output channel axis")
-    cout = out_channels[0]
-    if not out_by[cout].local():
-        raise ValueError("einconv output channel axis must be local")
-    extra = [n for n in w_names if n not in {cout, cin, *kernel}]
-    if extra:
-        raise ValueError(f"Unexpected weight axis {extra[0]!r}")
-    if set(out_names) != (set(in_names) - {cin}) | {cout}:
-        raise ValueError("einconv output axes must be input axes with the channel axis replaced by the output channel axis")
+    def conv(xa, wa, ba=None):
+        out = conv_impl.try_conv(xa, wa, ba, a.in_names, a.w_names, a.out_names, a.spatial, a.kernel, a.cin, a.cout,
+                                 a.dilation, kernel_pads)
+        if out is not None:
+            return out
+        if kernel_pads:  # the torch path pads through the halo builder instead
+            xa = halo_tensor(a.in_spec, xa, kernel_pads, **halo_args)
+        xc = xa.permute(layout.x_order(False)).contiguous()
+        lead = xc.shape[:len(layout.batch)]
+        xc = xc.reshape((-1, *xc.shape[len(layout.batch):]))
+        wc = wa.permute(layout.w_order(False)).contiguous()
+        out = _TORCH_CONV[a.ndim](xc, wc, ba, stride=a.stride, padding=0, dilation=a.dilation, groups=groups)
+        return out.reshape((*lead, *out.shape[1:])).permute(layout.out_order(False)).contiguous()
 
-    ndim = len(spatial)
-    stride = _per_dim(stride, ndim, label="stride")
-    dilation = _per_dim(dilation, ndim, label="dilation")
-    if any(s != 1 for s in stride):
-        raise NotImplementedError("einconv currently supports only stride=1")
-    kdims = tuple(w_names.index(n) for n in kernel)
-    if padding is None:
-        pads = []
-        for kd, dil in zip(kdims, dilation):
-            span = dil * (weight.shape[kd] - 1)
-            if span % 2:
-                raise ValueError("Default einconv padding requires odd effective kernel sizes")
-            pads.append(span // 2)
-        pads = tuple(pads)
-    else:
-        pads = expand_family_mapping(padding, families, label="Padding")
-        if isinstance(pads, dict):
-            unknown = set(pads) - set(spatial)
-            if unknown:
-                raise ValueError(f"Padding axis {sorted(unknown)[0]!r} has no matching window")
-            missing = [n for n in spatial if n not in pads]
-            if missing:
-                raise ValueError(f"Missing padding for window source axis {missing[0]!r}")
-            pads = tuple(pads[n] for n in spatial)
-        else:
-            pads = _per_dim(pads, ndim, label="padding")
-    for name, pad, kd, dil in zip(spatial, pads, kdims, dilation):
-        left, right = normalize_halo(pad)
-        expected = dil * (weight.shape[kd] - 1)
-        if left + right != expected:
-            raise ValueError(
-                f"Padding for axis {name!r} must preserve the spatial length; "
-                f"got left + right = {left + right}, expected {expected}"
-            )
-
-    halos = dict(zip(spatial, pads))
-    conv = _conv_fn(ndim)
-    batch = [n for n in in_names if n not in spatial and n != cin]
-    x_perm = [in_names.index(n) for n in batch + [cin] + spatial]
-    w_perm = [w_names.index(n) for n in [cout, cin] + kernel]
-    conv_out = batch + [cout] + spatial
-    out_perm = [conv_out.index(n) for n in out_names]
-
-    from . import conv_native
-    # Local spatial axes with a zero boundary are padded by the native kernel itself
-    # (TMA zero fill), so no padded copy of the input is made for them.
-    kernel_pads = {}
-    if conv_native.kernel_padding_ok(x, weight, x.shape[in_names.index(cin)], spatial, dilation) and \
-            boundary == "constant" and fill == 0:
-        for name in spatial:
-            left, right = normalize_halo(halos[name])
-            axis = in_axes[in_names.index(name)]
-            # an axis sharded over a one-rank mesh dim has no neighbours: its halo is the zero boundary
-            alone = not axis.local() and mesh is not None and _mesh_dim_size(mesh, axis.shard_dim) == 1
-            if (axis.local() or alone) and left == right:
-                kernel_pads[name] = left
-    other_halos = {n: h for n, h in halos.items() if n not in kernel_pads}
-
-    def run_conv(xa, wa, ba=None):
-        native = conv_native.try_conv(xa, wa, ba, in_names, w_names, out_names, spatial, kernel, cin, cout,
-                                      dilation, kernel_pads)
-        if native is not None:
-            return native
-        if kernel_pads:
-            xa = halo_tensor(in_spec, xa, kernel_pads, mesh=mesh, shapes=shapes, boundary=boundary, fill=fill)
-        xc = xa.permute(x_perm).contiguous()
-        lead = xc.shape[:len(batch)]
-        xc = xc.reshape((-1, xc.shape[len(batch)], *xc.shape[len(batch) + 1:]))
-        wc = wa.permute(w_perm).contiguous()
-        out = conv(xc, wc, ba, stride=stride, padding=0, dilation=dilation, groups=groups)
-        out = out.reshape((*lead, *out.shape[1:]))
-        return out.permute(out_perm).contiguous()
-
-    def run_full(xa, wa, *maybe_bias):
-        ba = maybe_bias[0] if maybe_bias else None
-        haloed = halo_tensor(in_spec, xa, other_halos, mesh=mesh, shapes=shapes, boundary=boundary, fill=fill)
+    def halo_then_conv(xa, wa, *maybe_bias):
+        haloed = halo_tensor(a.in_spec, xa, exchanged, **halo_args)
+        args = (haloed, wa, *maybe_bias)
         if checkpoint == "conv":
-            args = (haloed, wa) if ba is None else (haloed, wa, ba)
-            return _checkpointed(lambda *a: run_conv(*a), args, "conv", use_reentrant)
-        return run_conv(haloed, wa, ba)
+            return _checkpointed(conv, args, "conv", use_reentrant)
+        return conv(*args)
 
     tensors = (x, weight) if bias is None else (x, weight, bias)
     if checkpoint == "conv":
-        return run_full(*tensors)
-    return _checkpointed(lambda *a: run_full(*a), tensors, checkpoint, use_reentrant)
+        return halo_then_conv(*tensors)
+    return _checkpointed(halo_then_conv, tensors, checkpoint, use_reentrant)

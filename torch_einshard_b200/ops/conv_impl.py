@@ -20,7 +20,7 @@ import torch
 
 from . import _native
 
-__all__ = ["conv2d_nhwc", "conv2d_native"]
+__all__ = ["conv2d_nhwc", "conv2d_native", "try_conv", "kernel_padding_ok"]
 
 
 def _run(mod, x, w, bias, ph, pw):
@@ -97,3 +97,23 @@ def conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, ker
     out = out.reshape(*lead, *out.shape[1:])
     produced = batch + list(spatial) + [cout]
     return out.permute([produced.index(n) for n in out_names]).contiguous()
+
+
+def try_conv(x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation, pads=None):
+    """The native implicit-GEMM convolution of einconv's named-axis call, or
+    None outside its envelope (not CUDA bf16/fp16, not 2-D, dilation != 1,
+    channel counts the TMA boxes cannot address); einconv then uses
+    ``torch.nn.functional``."""
+    mod = _native.module()
+    if mod is None or not hasattr(mod, "conv2d_implicit") or not x.is_cuda:
+        return None
+    return conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation,
+                       pads)
+
+
+def kernel_padding_ok(x, weight, cin_size, spatial, dilation):
+    """True when the native kernel would run and can zero-pad by itself."""
+    mod = _native.module()
+    if mod is None or not hasattr(mod, "conv2d_implicit") or not x.is_cuda:
+        return False
+    return supported(x, weight.dtype, cin_size, len(spatial), dilation)

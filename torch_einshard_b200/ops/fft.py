@@ -20,7 +20,7 @@ Semantics, error texts and ``explain`` payloads follow
 ``src/torch_einshard/fft.py:16-895``.  The four-step decomposition is the
 standard Cooley-Tukey split ``k = k2 + P*k1``, ``n = q*L + m``.
 Local FFTs of CUDA complex64 tensors run on the native Stockham kernels when
-the extension provides them (``ops.fft_native``), else ``torch.fft``.
+the extension provides them (``ops/fft_impl.py``), else ``torch.fft``.
 """
 
 import math
@@ -99,8 +99,8 @@ def _group(mesh, dim):
 def _local_fft(x, dim, inverse, scale=1.0):
     """``scale`` times the unnormalised DFT along ``dim`` (inverse without the 1/n).
     The native kernel folds the scale into its stores."""
-    from . import fft_native
-    out = fft_native.try_fft(x, dim, inverse, scale)
+    from . import fft_impl
+    out = fft_impl.try_fft(x, dim, inverse, scale)
     if out is not None:
         return out
     out = torch.fft.ifft(x, dim=dim, norm="forward") if inverse else torch.fft.fft(x, dim=dim)
@@ -148,8 +148,8 @@ def _exchange_blocks(z, group, send_block, out_shape, recv_view):
     peer p lands in ``recv_view(out, p)``."""
     size, rank = dist.get_world_size(group), dist.get_rank(group)
     out = z.new_empty(out_shape)
-    from ..parallel import native_comm
-    comm = native_comm.communicator_for(group) if z.is_cuda else None
+    from ..parallel import symmetric
+    comm = symmetric.communicator_for(group) if z.is_cuda else None
     if comm is not None and comm.block_exchange(z, send_block, out, recv_view):
         return out
     ops, landing = [], []
@@ -547,9 +547,9 @@ def _run_slab_native(z, current, tmap, plan, *, inverse, scale):
     P = len(plan["src_shapes"])
     if len(set(plan["src_shapes"])) != 1 or len(set(plan["dst_shapes"])) != 1:
         return None
-    from ..parallel import native_comm
+    from ..parallel import symmetric
     from . import fft_impl
-    comm = native_comm.workspace_for(plan["group"], z.numel() * z.element_size())
+    comm = symmetric.workspace_for(plan["group"], z.numel() * z.element_size())
     pre = [_dim(current, s) for s in tmap if s != plan["src"]]
     if not fft_impl.slab_eligible(z, comm, plan["src_dim"], plan["dst_dim"], P, pre, ()):
         return None

@@ -20,8 +20,9 @@ import math
 import torch
 
 from . import _native
+from .native_ops import local_roll
 
-__all__ = ["supported_length", "fft_c2c", "slab_fft", "rfft_native", "irfft_native"]
+__all__ = ["supported_length", "fft_c2c", "try_fft", "slab_fft", "rfft_native", "irfft_native"]
 
 _MAX_LOG = 10
 _TWIDDLES = {}
@@ -213,7 +214,7 @@ def rfft_native(x, dim):
     xm = x.movedim(dim, -1).contiguous()
     z = torch.view_as_complex(xm.reshape(*xm.shape[:-1], n // 2, 2))
     Z = fft_c2c(mod, z, z.dim() - 1, False)
-    Zc = torch.conj(torch.roll(torch.flip(Z, dims=(-1,)), 1, dims=-1))  # conj Z[-k mod n/2]
+    Zc = torch.conj(local_roll(torch.flip(Z, dims=(-1,)), {Z.dim() - 1: 1}))  # conj Z[-k mod n/2]
     even = (Z + Zc) * 0.5
     odd = (Z - Zc) * (-0.5j)
     w = _half_twiddles(n, x.device)
@@ -239,3 +240,16 @@ def irfft_native(X, n, dim):
     Z = (even + 1j * odd).contiguous()
     z = fft_c2c(mod, Z, Z.dim() - 1, True, scale=2.0)
     return torch.view_as_real(z).reshape(*z.shape[:-1], n).movedim(-1, dim)
+
+
+def try_fft(x, dim, inverse, scale=1.0):
+    """Native FFT along one axis of a CUDA complex tensor, or None when the
+    kernels do not cover the call (not CUDA complex64, length not a supported
+    power of two); the caller then uses ``torch.fft``.  Replaces the
+    reference's ``torch.fft`` calls (``src/torch_einshard/fft.py:202-205``)."""
+    if not x.is_cuda:
+        return None
+    mod = _native.module()
+    if mod is None or not hasattr(mod, "fft_c2c"):
+        return None
+    return fft_c2c(mod, x, dim, inverse, scale)

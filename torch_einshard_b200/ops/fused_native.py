@@ -1,17 +1,30 @@
-"""Native fused contraction + all-reduce paths (installed by ``setup_native_comm``).
+"""Fused contraction + collective paths of the binary executor.
 
-Provides the fusion descriptors consumed by :mod:`.fused`:
+``provider(executor)`` inspects a binary plan while the native communicators
+are active (``setup_native_comm``) and returns a fusion descriptor when one of
+the patterns below applies (CUDA bf16 operands, a native communicator for the
+group); otherwise ``None`` and the executor runs the unfused steps.  Fuses the
+planner steps ``rank_local_einsum`` + ``allreduce_forward_identity_backward`` /
+``reducescatter_forward_allgather_backward`` and
+``allgather_forward_reducescatter_backward`` + ``rank_local_einsum``
+(``src/torch_einshard/mappings.py:169-187``,
+``src/torch_einshard/distributed.py:84-620``):
 
-* ``gemm_allreduce``  - forward ``AR(A @ B)`` runs as one kernel: the tcgen05
-  GEMM tiles are reduced over NVLink as they finish (``csrc/gemm_ar.cu``).
+* ``gemm_allreduce``  - forward ``AR(A @ B)`` runs as one launch: the wide
+  tcgen05 GEMM writes its output units into the symmetric heap and reducer
+  clusters of the same launch sum each unit in the NVSwitch as soon as every
+  rank produced it (``csrc/gemm_nvls.cu``; on heaps without multicast, the
+  older epilogue kernels ``csrc/gemm_ar.cu`` / ``gemm_push.cu`` on request).
   Backward needs no communication (the all-reduce's adjoint is the identity):
   ``dA = dC @ B^T`` and ``dB = A^T @ dC`` on the plain native GEMM.
 * ``dgrad_allreduce`` - forward is the plain GEMM; in backward the gradient of
   the replicated operand, which must be all-reduced over the group, is
-  computed by the fused kernel.
+  computed by the same fused kernel.
+* ``gemm_reducescatter`` / ``allgather_gemm`` - the row reduce-scatter epilogue
+  and the all-gather fused into the GEMM's operand loads (``csrc/gemm_ag.cu``).
 
-Both apply to two-operand contractions that canonicalise to a single
-(batch-free) GEMM of CUDA bf16 tensors whose output fits the symmetric buffer.
+All apply to two-operand contractions that canonicalise to a single
+(batch-free) GEMM of CUDA bf16 tensors.
 
 Fuses the reference's ``mappings.py:169-187`` collectives with the contraction
 of ``einsum.py:132``.
@@ -20,7 +33,7 @@ of ``einsum.py:132``.
 import torch
 import torch.distributed as dist
 
-from . import _native, fused
+from . import _native
 from .contraction import canonical_gemm
 from .einsum import equation_for
 from .gemm import _prepare, native_bmm
@@ -29,8 +42,8 @@ __all__ = ["install", "gemm_allreduce", "gemm_reducescatter", "gemm_allgather"]
 
 
 def _comm(group):
-    from ..parallel import native_comm
-    return native_comm.communicator_for(group)
+    from ..parallel import symmetric
+    return symmetric.communicator_for(group)
 
 
 def gemm_allreduce(comm, a, b):
@@ -149,8 +162,8 @@ class _AllGatherGemm(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, a_local, b, comm, seg, shard):
-        from ..parallel import native_comm
-        ws = native_comm.workspace_for(comm.group, a_local.numel() * a_local.element_size())
+        from ..parallel import symmetric
+        ws = symmetric.workspace_for(comm.group, a_local.numel() * a_local.element_size())
         if ws is not None and _ag_fits(ws, a_local, seg, shard):
             comm = ws
             out, a_full = gemm_allgather(comm, a_local, b, seg, shard)
@@ -187,9 +200,9 @@ def gemm_allreduce_nvls(comm, a, b):
     writes its output units into the symmetric heap and reducer clusters of the
     same launch sum each unit through the NVSwitch as soon as every rank has
     produced it (``csrc/gemm_nvls.cu``).  None when the group has no NVLS heap."""
-    from ..parallel import native_comm
+    from ..parallel import symmetric
     m, n = a.shape[1], b.shape[2]
-    ws = native_comm.workspace_for(comm.group, m * n * 2)
+    ws = symmetric.workspace_for(comm.group, m * n * 2)
     if ws is None or not ws.nvls or ws.broken:
         return None
     mod = _native.require()
@@ -539,6 +552,3 @@ def provider(executor):
                 return _Fusion("dgrad_allreduce", operand)
     return None
 
-
-def install():
-    fused.register_fusion_provider(provider)

@@ -133,8 +133,8 @@ class _HaloExchange(torch.autograd.Function):
         table = halo_intervals(shapes, left, right, periodic=periodic)
         length = shapes[rank] + left + right if periodic else sum(p[3] for p in table[rank])
         ctx.saved = (group, dim, shapes, left, right, periodic, tuple(x.shape))
-        from ..parallel import native_comm
-        comm = native_comm.communicator_for(group) if x.is_cuda else None
+        from ..parallel import symmetric
+        comm = symmetric.communicator_for(group) if x.is_cuda else None
         if comm is not None:
             out = comm.halo_gather(x.contiguous(), dim, table, length, shapes)
             if out is not None:
@@ -169,8 +169,8 @@ class _HaloExchange(torch.autograd.Function):
         group, dim, shapes, left, right, periodic, in_shape = ctx.saved
         rank = dist.get_rank(group)
         table = halo_intervals(shapes, left, right, periodic=periodic)
-        from ..parallel import native_comm
-        comm = native_comm.communicator_for(group) if grad.is_cuda else None
+        from ..parallel import symmetric
+        comm = symmetric.communicator_for(group) if grad.is_cuda else None
         if comm is not None:
             out = comm.halo_scatter_add(grad.contiguous(), dim, table, in_shape)
             if out is not None:

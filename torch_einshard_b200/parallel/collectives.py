@@ -9,7 +9,7 @@ between mesh coordinates.
 
 Backend choice, per call: CUDA tensors on a group that has a native
 communicator (peer-mapped symmetric buffers over NVLink, see
-:mod:`.native_comm`) run the sm_100a copy/reduce kernels; everything else
+:mod:`.symmetric`) run the sm_100a copy/reduce kernels; everything else
 (CPU/gloo, groups without peer access, oversize messages) runs through
 ``torch.distributed``.  Both paths compute the same values.
 """
@@ -61,8 +61,8 @@ def init_process_group(backend, use_cuda):
 def _native(group, tensor):
     if not tensor.is_cuda:
         return None
-    from . import native_comm
-    return native_comm.communicator_for(group)
+    from . import symmetric
+    return symmetric.communicator_for(group)
 
 
 def split_offsets(shapes):
@@ -236,8 +236,8 @@ def owner_swap(input, mesh, source_shard_dims, dest_shard_dims, output_shape):
     if send_rank == me and recv_rank == me:
         return input.contiguous()
     output = input.new_empty(output_shape)
-    from . import native_comm
-    comm = native_comm.world_communicator() if input.is_cuda else None
+    from . import symmetric
+    comm = symmetric.world_communicator() if input.is_cuda else None
     if comm is not None and comm.send_recv(input.contiguous(), send_rank, output, recv_rank):
         return output
     ops = [
@@ -308,7 +308,8 @@ def roll_sharded(input, group, dim, shift, shapes):
     total = sum(shapes)
     shift = shift % total
     if size == 1:
-        return torch.roll(input, shifts=shift, dims=dim)
+        from ..ops.native_ops import local_roll
+        return local_roll(input, {dim % input.dim(): shift})
     if shift == 0:
         return input
     if input.shape[dim] != shapes[rank]:

@@ -115,6 +115,17 @@ def distributed_1d(shard, *xs, mesh, shapes, policy=None):
 _MESH_SIZES = {}  # id(mesh) -> (weakref to the mesh, {dim name: size})
 
 
+
+def _binary_fusion(executor):
+    """A fused compute + collective kernel for this binary plan (see
+    ``ops/fused_native.py:provider``), or None: only while the native
+    communicators are active (``setup_native_comm``)."""
+    from . import symmetric
+    if not symmetric.enabled():
+        return None
+    from ..ops import fused_native
+    return fused_native.provider(executor)
+
 class BinaryExecutor:
     def __init__(self, shard, x, y, mesh, shapes, policy):
         self.plan = ExecutionPlan()
@@ -345,8 +356,7 @@ class BinaryExecutor:
                 if candidate.name == "alltoall_repartition":
                     plan.consider(candidate, status="rejected", reason="runtime split-shape validation failed")
 
-        from ..ops import fused
-        fuse = fused.binary_fusion(self)
+        fuse = _binary_fusion(self)
         deferred0 = [] if fuse is not None and fuse.kind == "dgrad_allreduce" and fuse.operand == 0 else None
         deferred1 = [] if fuse is not None and fuse.kind == "dgrad_allreduce" and fuse.operand == 1 else None
         if fuse is not None and fuse.kind == "allgather_gemm":

@@ -9,7 +9,7 @@ as ``src/torch_einshard/mesh.py:15-103``.
 
 On NVSwitch systems every rank subset has uniform bandwidth, so a compound
 group is only a rank list; the native communicator for it is created on first
-use by :mod:`.native_comm`.
+use by :mod:`.symmetric`.
 """
 
 from itertools import product

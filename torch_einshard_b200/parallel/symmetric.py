@@ -39,9 +39,9 @@ import torch
 import torch.distributed as dist
 
 from ..ops import _native
-from . import native_comm
 
-__all__ = ["Communicator", "activate", "deactivate", "communicator_for_group"]
+__all__ = ["Communicator", "activate", "deactivate", "communicator_for_group", "communicator_for", "workspace_for",
+           "world_communicator", "enabled", "disable", "setup_native_comm", "teardown_native_comm"]
 
 _DEFAULT_MB = int(os.environ.get("EINSHARD_SYMM_MB", "64"))
 # Block count of every NVLS collective on a heap (the per-block counters are
@@ -585,18 +585,58 @@ def activate(mesh=None):
         return False
     for group in _mesh_groups(mesh):
         communicator_for_group(group)
-    native_comm.enable(lambda group: _COMMS.get(_group_key(group)) if group is not None else None,
-                       lambda group, nbytes: workspace_for_group(group, nbytes) if group is not None else None)
-    _install_fusions()
+    _state["enabled"] = True
     return True
 
 
-def _install_fusions():
-    try:
-        from ..ops import fused_native
-        fused_native.install()
-    except ImportError:
-        pass
+# ------------------------------------------------------------------ lookup used by the collective helpers
+
+_state = {"enabled": False}
+
+
+def enabled() -> bool:
+    """Whether the native communicators are active (``setup_native_comm``)."""
+    return _state["enabled"]
+
+
+def disable():
+    """Route every collective to torch.distributed again (the heaps stay)."""
+    _state["enabled"] = False
+
+
+def communicator_for(group):
+    """The native communicator of ``group``, or None (not active, not eligible)."""
+    if not _state["enabled"] or group is None:
+        return None
+    return _COMMS.get(_group_key(group))
+
+
+def workspace_for(group, nbytes):
+    """A communicator of ``group`` whose symmetric region holds ``nbytes``
+    (collective: every member asks with the same size), or None."""
+    if not _state["enabled"] or group is None:
+        return None
+    return workspace_for_group(group, nbytes)
+
+
+def world_communicator():
+    return communicator_for(dist.group.WORLD) if _state["enabled"] else None
+
+
+def setup_native_comm(mesh=None, *, enable=True):
+    """Create the native NVLink communicators for every group of ``mesh`` (and
+    the world group): CUDA + NCCL process groups only.  Collective over every
+    rank.  Returns True when the native path is active; on CPU / gloo it does
+    nothing and returns False.  No reference counterpart (the reference only
+    uses ``torch.distributed``)."""
+    if not enable or not torch.cuda.is_available() or not dist.is_initialized():
+        return False
+    return activate(mesh)
+
+
+def teardown_native_comm():
+    """Free every symmetric heap (collective while the process group lives)."""
+    deactivate()
 
 
 def _all_comms():
@@ -606,7 +646,7 @@ def _all_comms():
 def deactivate():
     """Free every heap.  With the process group still initialised this is a
     collective close (synchronise, barrier, free); otherwise see _release_at_exit."""
-    native_comm.disable()
+    disable()
     if dist.is_initialized():
         for comm in _all_comms():
             if not comm.closed:

@@ -267,8 +267,8 @@ def _allreduce_mean(buffer, group, divisor):
     one fused reduce+divide kernel over NVLink; otherwise NCCL/gloo followed
     by an in-place divide.
     """
-    from ..parallel import native_comm
-    comm = native_comm.communicator_for(group) if buffer.is_cuda else None
+    from ..parallel import symmetric
+    comm = symmetric.communicator_for(group) if buffer.is_cuda else None
     if comm is not None and comm.all_reduce_div_(buffer, divisor):
         future = torch.futures.Future()
         future.set_result(buffer)
