@@ -10,8 +10,10 @@ Prints one JSON line on rank 0.  ``value`` is whole-job TFLOP/s from CUDA
 events around exactly K steps (barrier + synchronize on both sides, max over
 ranks).  Inputs (x: 512 MiB bf16 per rank) are larger than the 126 MB L2, so
 no explicit flush is needed between steps.  ``e2e`` repeats the measurement
-end to end: each step copies its input from pinned host memory and reads the
-loss back to the host.
+end to end through the public API: each rank copies its b/tp slice of the
+step's input from pinned host memory, the step gathers x with
+``einshard("b/tp n c -> b n c")`` (both arms, each with its own framework), and
+the loss is read back to the host.
 """
 
 import argparse
@@ -85,20 +87,20 @@ def build_native(cfg, world, rank):
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     es.setup_native_comm(mesh)
     model = TPMLP(cfg["c"], cfg["h"], mesh, device="cuda")
-    return es, model
+    return es, model, mesh
 
 
 def build_reference(cfg, world, rank):
     ref = os.path.join(HERE, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref, "torch_einshard")):
-        return None, "reference is not installed under baseline/_ref"
+        return None, "reference is not installed under baseline/_ref", None
     sys.path.insert(0, ref)
     shim = os.path.join(HERE, "baseline", "parsley_shim")
     sys.path.insert(0, shim)
     try:
         import torch_einshard as es  # noqa: F401
     except Exception as error:  # noqa: BLE001
-        return None, f"reference import failed: {error!r}"
+        return None, f"reference import failed: {error!r}", None
     from torch.distributed.device_mesh import init_device_mesh
     import torch.nn.functional as F
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
@@ -119,7 +121,7 @@ def build_reference(cfg, world, rank):
             y = es.einshard("b n h/tp, c h/tp -> b n c // tp", F.silu(h), self.w2, mesh=mesh)
             return es.einshard("b n c // tp -> b n c", y, mesh=mesh)
 
-    return es, RefMLP()
+    return es, RefMLP(), mesh
 
 
 def native_launches(impl):
@@ -139,14 +141,14 @@ def main():
     if args.small:
         cfg = dict(b=2, n=512, c=1024, h=4096)
     if args.impl == "reference":
-        es, model = build_reference(cfg, world, rank)
+        es, model, mesh = build_reference(cfg, world, rank)
         if es is None:
             if rank == 0:
                 print(json.dumps({"impl": "reference", "unavailable": model}), flush=True)
             dist.destroy_process_group()
             return
     else:
-        es, model = build_native(cfg, world, rank)
+        es, model, mesh = build_native(cfg, world, rank)
 
     torch.manual_seed(0)
     b, n, c, h = cfg["b"], cfg["n"], cfg["c"], cfg["h"]
@@ -188,9 +190,14 @@ def main():
                                             max_name_column_width=90), file=sys.stderr, flush=True)
 
     # ---------------------------------------------------------------- end to end
-    host_x = torch.randn(b, n, c, dtype=torch.bfloat16).pin_memory()
+    # Each rank loads only its b/tp slice of the step's input from pinned host
+    # memory (one step ahead, on a side stream), and the step gathers the full x
+    # over NVLink through the framework's own API ("b/tp n c -> b n c"): the job
+    # reads every input byte from the host once, not once per rank.
+    b_local = b // world if b % world == 0 else b
+    host_x = torch.randn(b_local, n, c, dtype=torch.bfloat16).pin_memory()
     copy_stream = torch.cuda.Stream()
-    bufs = [torch.empty(b, n, c, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
+    bufs = [torch.empty(b_local, n, c, device="cuda", dtype=torch.bfloat16) for _ in range(2)]
     ready = [torch.cuda.Event() for _ in range(2)]
     losses = []
 
@@ -204,7 +211,8 @@ def main():
         xin = bufs[i % 2].requires_grad_(True)
         for p in model.parameters():
             p.grad = None
-        y = model(xin)
+        xfull = xin if b_local == b else es.einshard("b/tp n c -> b n c", xin, mesh=mesh)
+        y = model(xfull)
         loss = y.float().square().mean()
         loss.backward()
         xin.grad = None
@@ -262,6 +270,9 @@ def main():
                 "h2d_bytes_per_step": host_x.numel() * host_x.element_size(),
                 "d2h_bytes_per_step": 4,
                 "ms_per_step": round(e2e_ms / args.steps, 4),
+                "input": ("per rank: its b/tp slice of x copied from pinned host memory, then gathered "
+                          "with einshard('b/tp n c -> b n c'); bytes are per rank") if b_local != b else
+                         "x copied from pinned host memory",
             },
             "gpu_launches": launches,
             "impl": args.impl,

@@ -67,19 +67,35 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 // Wait for the phase with the given parity.  Returns false when the CTA-wide
 // abort flag is raised or the timeout expires (then the abort flag and the
 // global error word are set).
+// try_wait with a suspend-time hint: the thread may sleep in hardware until the
+// phase completes or about `hint_ns` pass, instead of polling (fewer issued
+// instructions while a warp waits, for instance a whole tile).
+constexpr uint32_t kMbarSuspendNs = 200000;  // 0.2 ms per try
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int* err, int code) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > ES_WAIT_TIMEOUT_NS) {
-        *abort_flag = 1;
-        if (err) atomicCAS(err, 0, code);
-        return false;
-      }
+  for (;;) {
+    // each try may park the thread until the phase completes (bounded by the hint),
+    // so the abort flag and the deadline are checked on every round
+    if (mbar_try_wait_suspend(bar, parity, kMbarSuspendNs)) return true;
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > ES_WAIT_TIMEOUT_NS) {
+      *abort_flag = 1;
+      if (err) atomicCAS(err, 0, code);
+      return false;
     }
   }
 }
