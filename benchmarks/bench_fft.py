@@ -28,7 +28,7 @@ import torch.distributed as dist
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
-from common import peaks  # noqa: E402
+from common import ClockSampler, peaks, visible_gpu_indices  # noqa: E402
 
 NVLINK_GBS = 770.0  # measured peer copy per direction on this machine class
 
@@ -86,6 +86,9 @@ def main():
             z = es.einshard("b x ky/sp kz -> b x/sp ky kz", z, mesh=mesh, shapes=shapes)
             return es.einfft("b x/sp ky kz -> b x/sp y z", z, {"ky": "y", "kz": "z"}, inverse=True, mesh=mesh)
 
+    sampler = ClockSampler(visible_gpu_indices(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
     with torch.no_grad():
         out = step()
         err = ((out - x).abs().max() / x.abs().max()).item()
@@ -94,11 +97,15 @@ def main():
         dist.barrier()
         torch.cuda.synchronize()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if sampler:
+            sampler.mark_start()
         t0.record()
         for _ in range(args.steps):
             step()
         t1.record()
         torch.cuda.synchronize()
+        if sampler:
+            sampler.mark_end()
         dist.barrier()
     ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device="cuda", dtype=torch.float64)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
@@ -112,7 +119,7 @@ def main():
                           "higher_is_better": False, "n_gpus": world, "impl": args.impl,
                           "config": {"shape": [1, nx, n, n], "dtype": "complex64", "layout": "b x/sp y z <-> b kx ky/sp kz",
                                      "l2": "inputs larger than L2; no flush"},
-                          "roundtrip_rel_err": err, "roofline_ms": round(roofline_ms, 3),
+                          "clocks": sampler.stop() if sampler else None, "roundtrip_rel_err": err, "roofline_ms": round(roofline_ms, 3),
                           "roofline_frac": round(roofline_ms / ms, 3),
                           "roofline_of": f"{peaks()['source']} hbm_gbs; NVLink 770 GB/s"}), flush=True)
     dist.destroy_process_group()

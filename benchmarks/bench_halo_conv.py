@@ -28,7 +28,7 @@ import torch.distributed as dist
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
-from common import peaks  # noqa: E402
+from common import ClockSampler, peaks, visible_gpu_indices  # noqa: E402
 
 MESHES = {1: (1, 1), 2: (2, 1), 4: (2, 2), 8: (2, 4)}
 
@@ -94,6 +94,9 @@ def main():
                                {"h": 1, "w": 1}, mesh=mesh, shapes=shapes)
             return es.einshard("b h w kh kw c, kh kw c o -> b h w o", win, w)
 
+    sampler = ClockSampler(visible_gpu_indices(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
     with torch.no_grad():
         for _ in range(args.warmup):
             y = step()
@@ -101,11 +104,15 @@ def main():
         dist.barrier()
         torch.cuda.synchronize()
         t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        if sampler:
+            sampler.mark_start()
         t0.record()
         for _ in range(args.steps):
             step()
         t1.record()
         torch.cuda.synchronize()
+        if sampler:
+            sampler.mark_end()
         dist.barrier()
     ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device="cuda", dtype=torch.float64)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
@@ -115,7 +122,7 @@ def main():
     if rank == 0:
         print(json.dumps({"metric": "halo-conv ms (forward)", "value": round(ms, 3), "unit": "ms",
                           "higher_is_better": False, "n_gpus": world, "impl": args.impl, "path": args.path,
-                          "tflops_all_gpus": round(tflops, 1),
+                          "clocks": sampler.stop() if sampler else None, "tflops_all_gpus": round(tflops, 1),
                           "roofline_frac": round(tflops / world / peaks()["bf16_tflops"], 3),
                           "roofline_of": f"{peaks()['source']} bf16_tflops per GPU",
                           "config": {"b": B, "h": H, "w": W, "c": C, "o": O, "mesh": [mh, mw], "h_split": hs,

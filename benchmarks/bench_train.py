@@ -33,6 +33,8 @@ import torch.utils.checkpoint
 from torch.nn.parallel import DistributedDataParallel
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+from common import ClockSampler, visible_gpu_indices  # noqa: E402
 MESHES = {1: (1, 1), 2: (2, 1), 4: (2, 2), 8: (2, 4)}
 
 
@@ -177,17 +179,25 @@ def main():
         opt.zero_grad(set_to_none=True)
         return loss
 
+    sampler = ClockSampler(visible_gpu_indices(world)) if rank == 0 else None
+    if sampler:
+        sampler.start()
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     dist.barrier()
     t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark_start()
     t0.record()
     losses = []
     for _ in range(args.steps):
         losses.append(step().detach())
     t1.record()
     torch.cuda.synchronize()
+    if sampler:
+        sampler.mark_end()
+    clocks = sampler.stop() if sampler else None
     dist.barrier()
     ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device="cuda", dtype=torch.float64)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
@@ -208,7 +218,7 @@ def main():
         print(json.dumps({"metric": "train tok/s", "value": round(tok_s, 1), "unit": "tokens/s",
                           "higher_is_better": True, "n_gpus": world, "impl": args.impl, "ms_per_step": round(ms, 2),
                           "model_tflops_all_gpus": round(tok_s * flops_per_token(cfg) / 1e12, 1),
-                          "loss": round(float(losses[-1].item()), 4), "activation_checkpointing": checkpoint,
+                          "loss": round(float(losses[-1].item()), 4), "clocks": clocks, "activation_checkpointing": checkpoint,
                           "config": {"layers": cfg.layers, "d": cfg.d, "heads": cfg.heads, "mlp": cfg.mlp,
                                      "vocab": cfg.vocab, "seq_len": cfg.seq, "batch_per_dp": cfg.batch,
                                      "mesh": [dp, tp], "dtype": "bf16", "optimizer": "AdamW (fused)",
