@@ -2,7 +2,7 @@
 
 Covers all-reduce below and above the one-shot/two-shot switch, an odd byte
 count, a tensor larger than the default heap (the heap grows and the
-all-reduce runs in pieces), the three dtypes with and without scaling,
+all-reduce runs in pieces), the three dtypes with and without scaling, broadcasts from every rank,
 all-gather and reduce-scatter with uneven shards along inner and outer
 dimensions (vector and byte paths), many collectives in a row (the per-block
 counters), and NVLS collectives interleaved with the copy-protocol kernels on
@@ -82,6 +82,13 @@ def _body(rank, world):
             want = nccl_sum(full).narrow(dim, sum(shapes[:rank]), shapes[rank])
             t = 2e-2 if dtype == torch.bfloat16 else 1e-5
             torch.testing.assert_close(got, want, rtol=t, atol=t * world)
+
+    # broadcast from each rank (NVLS: the source multicasts, every rank copies out)
+    for src in range(world):
+        for n in (5, 4096 + 3, 3 << 20):
+            t = torch.full((n,), float(rank + 10), device="cuda", dtype=torch.bfloat16)
+            assert comm.broadcast_(t, src)
+            assert torch.all(t == float(src + 10))
 
     # many collectives in a row, alternating with the copy protocol on the same heap
     rs = [3 + p for p in range(world)]

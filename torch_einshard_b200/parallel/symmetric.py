@@ -318,9 +318,27 @@ class Communicator:
         return self.all_reduce_(t, 1.0 / float(divisor))
 
     def broadcast_(self, t, src):
+        """In place: every rank's ``t`` becomes the group rank ``src``'s.  With
+        multicast, the source writes each byte once through the switch into
+        every rank's heap (an all-gather in which only the source has a shard)
+        and every rank copies it out; otherwise peers pull the staged tensor."""
         if self.broken or not t.is_contiguous():
             return False
         n = t.numel()
+        if self.nvls and n > 0:
+            lens = [n if q == src else 0 for q in range(self.size)]
+            comm = self._nvls_workspace(1, 1, t.element_size(), lens)
+            if comm is not None:
+                flat = t.view(-1)
+                if flat.data_ptr() % 16:
+                    tmp = flat.clone()
+                    self.broadcast_(tmp, src)
+                    flat.copy_(tmp)
+                    return True
+                mine = flat if self.rank == src else flat[:0]
+                comm.enter("nvls")
+                comm.mod.nvls_all_gather(comm.cid, mine, flat, 1, 1, lens, comm.err)
+                return True
         box = make_box([n], [1], 0, [1], 0, src, t.element_size())
         stage = t if self.rank == src else None
         return self._copy(stage, t, [box])

@@ -167,11 +167,19 @@ def init_params_(module, mesh, *, sync=None, sharded=None, mesh_dim_names=(), so
 
 
 def sync_param_(param, state, mesh):
-    """Broadcast ``param`` from group rank 0 over each ``init_sync`` group."""
+    """Broadcast ``param`` from group rank 0 over each ``init_sync`` group
+    (reference ``src/torch_einshard/params.py:880-887``).  CUDA parameters on a
+    group with a native communicator take the NVLS broadcast (rank 0 writes the
+    tensor once through the switch into every rank's heap); otherwise
+    ``torch.distributed.broadcast``."""
+    from ..parallel import symmetric
     state = _require_state_object(state)
     for name in state.shared:
         group = mesh_group(mesh, name)
         if dist.get_world_size(group) == 1:
+            continue
+        comm = symmetric.communicator_for(group) if param.is_cuda else None
+        if comm is not None and param.data.is_contiguous() and comm.broadcast_(param.data, 0):
             continue
         dist.broadcast(param.data, src=dist.get_global_rank(group, 0), group=group)
     return param
