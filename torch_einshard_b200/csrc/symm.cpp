@@ -211,6 +211,7 @@ std::string symm_prepare(SymmHeap& h, size_t bytes, int device, const std::strin
   h.want_mc = want_mc && mc_api();
   const size_t g = symm_granularity(device, size, h.want_mc);
   if (g == 0) return "cuMemGetAllocationGranularity failed";
+  h.granularity = g;
   h.bytes = (bytes + g - 1) / g * g;
   CUmemAllocationProp p = mem_prop(device);
   CUresult r = d.MemCreate(&h.local, h.bytes, &p, 0);
@@ -312,7 +313,7 @@ std::string symm_exchange(SymmHeap& h, double timeout_s) {
     return err;
   }
   // map every rank's allocation: rank p at uc_base + p * bytes
-  CUresult r = d.AddressReserve(&h.uc_base, h.bytes * h.size, h.bytes, 0, 0);
+  CUresult r = d.AddressReserve(&h.uc_base, h.bytes * h.size, h.granularity, 0, 0);
   if (r != CUDA_SUCCESS) {
     h.uc_base = 0;
     return cu_err("cuMemAddressReserve", r);
@@ -364,7 +365,7 @@ std::string symm_bind(SymmHeap& h) {
 std::string symm_map_mc(SymmHeap& h) {
   const Driver& d = drv();
   if (!h.want_mc) return "";
-  CUresult r = d.AddressReserve(&h.mc_base, h.bytes, h.bytes, 0, 0);
+  CUresult r = d.AddressReserve(&h.mc_base, h.bytes, h.granularity, 0, 0);
   if (r != CUDA_SUCCESS) {
     h.mc_base = 0;
     return cu_err("cuMemAddressReserve (multicast)", r);

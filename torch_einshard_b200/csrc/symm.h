@@ -36,6 +36,7 @@ namespace es {
 struct SymmHeap {
   int rank = 0, size = 1, device = 0;
   size_t bytes = 0;            // per rank, multiple of the granularity
+  size_t granularity = 0;      // allocation granularity (a power of two): alignment of the mappings
   std::string tag;             // unique name of this heap's sockets
   bool want_mc = false;
   // this rank's allocation
