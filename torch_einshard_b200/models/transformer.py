@@ -6,8 +6,9 @@ Every block is Megatron-style over the ``tp`` mesh dimension:
     q    = einshard("b s d, e/tp d -> b s e/tp", x_t, wq)         column parallel (local)
     ...  causal attention on the local heads (torch SDPA / flash)
     o    = einshard("b s e/tp, d e/tp -> b s d", attn, wo)       row parallel: fused GEMM + all-reduce
-    h    = einshard("b s d, f/tp d -> b s f/tp", x_t, w_up)       column parallel
-    y    = einshard("b s f/tp, d f/tp -> b s d", silu(h), w_dn)  row parallel: fused GEMM + all-reduce
+    a    = einshard("b s d, f/tp d -> b s f/tp", x_t, w_up,       column parallel, SiLU in
+                    activation="silu")                            the GEMM's epilogue
+    y    = einshard("b s f/tp, d f/tp -> b s d", a, w_dn)        row parallel: fused GEMM + all-reduce
 
 Data parallelism over ``dp`` uses PyTorch DDP with
 :func:`register_grad_reduction_hook_`: the hook averages every bucket over
@@ -87,8 +88,8 @@ class _Block(torch.nn.Module):
         attn = attn.transpose(1, 2).reshape(b, s, self.local_heads * self.head_dim)
         x = x + einshard("b s e/tp, d e/tp -> b s d", attn, self.wo, mesh=mesh)
         h = einshard("b s d -> b s d // tp", self.ln2(x), mesh=mesh)
-        up = einshard("b s d, f/tp d -> b s f/tp", h, self.w_up, mesh=mesh)
-        return x + einshard("b s f/tp, d f/tp -> b s d", F.silu(up), self.w_dn, mesh=mesh)
+        act = einshard("b s d, f/tp d -> b s f/tp", h, self.w_up, mesh=mesh, activation="silu")
+        return x + einshard("b s f/tp, d f/tp -> b s d", act, self.w_dn, mesh=mesh)
 
 
 class TPTransformer(torch.nn.Module):
