@@ -352,7 +352,8 @@ void comm_all_reduce_push(int64_t id, at::Tensor buf, double scale, int64_t nblo
 
 // boxes: list of (src_rank, (d0,d1,d2,d3), src_off, dst_off, (s0,s1,s2), (t0,t1,t2)) in bytes for offsets/strides
 void comm_copy(int64_t id, at::Tensor src, int64_t stage_bytes, at::Tensor dst, py::list boxes, int64_t esize,
-               bool reduce, bool accumulate, double scale, bool sequential, int64_t nblocks, const at::Tensor& err) {
+               bool reduce, bool accumulate, double scale, bool sequential, int64_t nblocks, const at::Tensor& err,
+               c10::optional<at::Tensor> local) {
   HostComm& hc = comm_ref(id);
   TORCH_CHECK(hc.open, "einshard comm: not connected");
   TORCH_CHECK((size_t)stage_bytes <= hc.data_bytes, "einshard comm copy: staging exceeds buffer");
@@ -388,7 +389,8 @@ void comm_copy(int64_t id, at::Tensor src, int64_t stage_bytes, at::Tensor dst, 
   const int rc = reduce ? es::comm_stage_and_reduce(d, sp, stage_bytes, 0, dst.data_ptr(), plan, static_cast<int>(nblocks),
                                                     at::cuda::getCurrentCUDAStream())
                         : es::comm_stage_and_copy(d, sp, stage_bytes, 0, dst.data_ptr(), plan, static_cast<int>(nblocks),
-                                                  at::cuda::getCurrentCUDAStream());
+                                                  at::cuda::getCurrentCUDAStream(),
+                                                  local.has_value() ? local->data_ptr() : nullptr);
   TORCH_CHECK(rc == 0, "einshard comm copy: launch failed (", rc, ")");
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
@@ -937,7 +939,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("nvls_reduce_scatter", &nvls_reduce_scatter, "reduce-scatter along a dimension through the NVSwitch");
   m.def("comm_all_reduce", &comm_all_reduce, "two-shot NVLink all-reduce in place");
   m.def("comm_all_reduce_push", &comm_all_reduce_push, "two-shot NVLink all-reduce in place, stores only");
-  m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)");
+  m.def("comm_copy", &comm_copy, "stage + pull strided boxes from peers (copy, accumulate or reduce)",
+        py::arg("id"), py::arg("src"), py::arg("stage_bytes"), py::arg("dst"), py::arg("boxes"), py::arg("esize"),
+        py::arg("reduce"), py::arg("accumulate"), py::arg("scale"), py::arg("sequential"), py::arg("nblocks"),
+        py::arg("err"), py::arg("local") = py::none());
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
   m.def("conv2d_wgrad", &conv2d_wgrad, "weight gradient of the implicit-GEMM conv (split-K tcgen05, fp32 out)");
   m.def("conv2d_implicit", &conv2d_implicit, "implicit-GEMM NHWC conv2d on tcgen05 (stride 1)");

@@ -185,8 +185,10 @@ __device__ void acc_copy_box(const uint8_t* sbase, uint8_t* dbase, const CopyBox
 
 // ------------------------------------------------------------------ kernels
 
+// src: the bytes staged into this rank's region; local: what boxes with
+// src_rank < 0 read (this rank's own data, which need not be staged).
 __global__ void __launch_bounds__(512) k_stage_and_run(CommDev c, const void* src, size_t nbytes, size_t stage_off,
-                                                       void* dst, CopyPlan plan, int reduce) {
+                                                       void* dst, CopyPlan plan, int reduce, const void* local) {
   uint32_t bars = 0;
   const uint32_t nb = gridDim.x;
   // peers must be done reading our data region from the previous op
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(512) k_stage_and_run(CommDev c, const void* sr
     if (reduce) {
       reduce_box(c, d, b, plan);
     } else {
-      const uint8_t* s = b.src_rank < 0 ? reinterpret_cast<const uint8_t*>(src)
+      const uint8_t* s = b.src_rank < 0 ? reinterpret_cast<const uint8_t*>(local)
                                         : reinterpret_cast<const uint8_t*>(c.data[b.src_rank]);
       if (plan.accumulate)
         acc_copy_box(s, d, b, plan);
@@ -414,14 +416,15 @@ static int launch_coop(const void* fn, int nblocks, void** args, cudaStream_t st
 }
 
 int comm_stage_and_copy(const CommDev& c, const void* src, size_t nbytes, size_t stage_off, void* dst,
-                        const CopyPlan& plan, int nblocks, cudaStream_t stream) {
+                        const CopyPlan& plan, int nblocks, cudaStream_t stream, const void* local) {
   CommDev cc = c;
   const void* s = src;
   size_t n = nbytes, off = stage_off;
   void* d = dst;
   CopyPlan p = plan;
   int reduce = 0;
-  void* args[] = {&cc, &s, &n, &off, &d, &p, &reduce};
+  const void* l = local != nullptr ? local : src;
+  void* args[] = {&cc, &s, &n, &off, &d, &p, &reduce, &l};
   return launch_coop(reinterpret_cast<const void*>(k_stage_and_run), nblocks, args, stream);
 }
 
@@ -433,7 +436,8 @@ int comm_stage_and_reduce(const CommDev& c, const void* src, size_t nbytes, size
   void* d = dst;
   CopyPlan p = plan;
   int reduce = 1;
-  void* args[] = {&cc, &s, &n, &off, &d, &p, &reduce};
+  const void* l = src;
+  void* args[] = {&cc, &s, &n, &off, &d, &p, &reduce, &l};
   return launch_coop(reinterpret_cast<const void*>(k_stage_and_run), nblocks, args, stream);
 }
 

@@ -68,8 +68,10 @@ struct CopyPlan {
 // Stage `nbytes` of `src` into this rank's data region at `stage_off`, publish
 // it, then run `plan` (copies from peers' staged data into `dst`).  With
 // nbytes == 0 nothing is staged (the plan may read regions staged earlier).
+// Boxes with src_rank < 0 read from `local` (default: `src`), so a rank's own
+// pieces need not pass through its region.
 int comm_stage_and_copy(const CommDev& c, const void* src, size_t nbytes, size_t stage_off, void* dst,
-                        const CopyPlan& plan, int nblocks, cudaStream_t stream);
+                        const CopyPlan& plan, int nblocks, cudaStream_t stream, const void* local = nullptr);
 // Same, but the plan's boxes are summed over all ranks (box src_rank ignored).
 int comm_stage_and_reduce(const CommDev& c, const void* src, size_t nbytes, size_t stage_off, void* dst,
                           const CopyPlan& plan, int nblocks, cudaStream_t stream);

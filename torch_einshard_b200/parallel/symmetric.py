@@ -140,6 +140,83 @@ def _view_geometry(view, base):
     return view.storage_offset() - base.storage_offset(), list(view.stride())
 
 
+def _sent_pieces(table, src):
+    """The halo pieces rank ``src`` sends, in packing order (by destination,
+    then table order): (dst, (out_off, src, src_off, n))."""
+    return [(dst, piece) for dst, pieces in enumerate(table) for piece in pieces if piece[1] == src and dst != src]
+
+
+def halo_gather_plan(rank, x_shape, dim, table, length, esize):
+    """Host plan of ``Communicator.halo_gather`` on rank ``rank``: the slabs
+    (offset, rows along ``dim``) it packs into its staged buffer, the copy
+    boxes that build its haloed shard (rank -1: from the local input; a peer:
+    from that peer's packed buffer) and the haloed shape.  Every rank derives
+    every peer's packing from the same table, so no offsets are exchanged."""
+    out_shape = list(x_shape)
+    out_shape[dim] = length
+    out_strides = _contig_strides(out_shape)
+    x_strides = _contig_strides(list(x_shape))
+    send = [(piece[2], piece[3]) for _, piece in _sent_pieces(table, rank)]
+    boxes = []
+    for out_off, src, src_off, n in table[rank]:
+        shape = list(x_shape)
+        shape[dim] = n
+        if src == rank:
+            boxes.append(make_box(shape, x_strides, src_off * x_strides[dim], out_strides, out_off * out_strides[dim],
+                                  -1, esize))
+            continue
+        packed = _sent_pieces(table, src)
+        before = 0
+        for dst, piece in packed:
+            if dst == rank and piece == (out_off, src, src_off, n):
+                break
+            before += piece[3]
+        packed_shape = list(x_shape)
+        packed_shape[dim] = sum(piece[3] for _, piece in packed)
+        pstrides = _contig_strides(packed_shape)
+        boxes.append(make_box(shape, pstrides, before * pstrides[dim], out_strides, out_off * out_strides[dim], src,
+                              esize))
+    return send, boxes, out_shape
+
+
+def halo_scatter_plan(rank, size, grad_shape, dim, table, in_shape, esize):
+    """Host plan of ``Communicator.halo_scatter_add`` on rank ``rank``: the
+    ghost slabs of its gradient (offset, rows) it packs and returns to their
+    owners, and the accumulate boxes: its own rows from the local gradient
+    (rank -1), the rows peers return from their packed buffers."""
+    in_strides = _contig_strides(list(in_shape))
+    g_strides = _contig_strides(list(grad_shape))
+
+    def returns(q):
+        return [p for p in table[q] if p[1] != q]
+
+    send = [(p[0], p[3]) for p in returns(rank)]
+    boxes = []
+    for out_off, src, src_off, n in table[rank]:
+        if src != rank:
+            continue
+        shape = list(in_shape)
+        shape[dim] = n
+        boxes.append(make_box(shape, g_strides, out_off * g_strides[dim], in_strides, src_off * in_strides[dim], -1,
+                              esize))
+    for q in range(size):
+        if q == rank:
+            continue
+        packed = returns(q)
+        packed_shape = list(in_shape)
+        packed_shape[dim] = sum(p[3] for p in packed)
+        pstrides = _contig_strides(packed_shape)
+        before = 0
+        for out_off, src, src_off, n in packed:
+            if src == rank:
+                shape = list(in_shape)
+                shape[dim] = n
+                boxes.append(make_box(shape, pstrides, before * pstrides[dim], in_strides, src_off * in_strides[dim],
+                                      q, esize))
+            before += n
+    return send, boxes
+
+
 class Communicator:
     def __init__(self, group, data_bytes):
         self.mod = _native.require()
@@ -222,7 +299,10 @@ class Communicator:
     def _blocks(self, nbytes):
         return int(max(8, min(self.sms, nbytes // (512 * 1024) + 8)))
 
-    def _copy(self, stage, out, boxes, *, reduce=False, accumulate=False, scale=1.0, sequential=False):
+    def _copy(self, stage, out, boxes, *, reduce=False, accumulate=False, scale=1.0, sequential=False, local=None):
+        """Stage ``stage`` in this rank's region, then run the boxes into ``out``:
+        a box with a peer rank reads that peer's staged bytes, a box with rank
+        -1 reads ``local`` (default: ``stage``)."""
         boxes = [b for b in boxes if b != "empty"]
         if any(b is None for b in boxes) or len(boxes) > 16:
             return False
@@ -233,8 +313,9 @@ class Communicator:
         dummy = stage if stage is not None else out
         esize = out.element_size()
         self.enter("copy")
+        work = max(stage_bytes, out.numel() * esize)
         self.mod.comm_copy(self.cid, dummy, stage_bytes, out, boxes, esize, reduce, accumulate, float(scale),
-                           sequential, self._blocks(max(stage_bytes, out.numel() * esize)), self.err)
+                           sequential, self._blocks(work), self.err, local)
         return True
 
     # -- health -------------------------------------------------------------
@@ -465,43 +546,29 @@ class Communicator:
         return out if self._copy(x, out, boxes) else None
 
     def halo_gather(self, x, dim, table, length, shapes):
+        """Haloed shard: this rank's own rows come straight from ``x``; the
+        rows peers hold come from a small staged buffer on each peer that packs
+        only the slabs it sends (never the whole shard)."""
         if self.broken:
             return None
         x = x.contiguous()
-        out_shape = list(x.shape)
-        out_shape[dim] = length
+        send, boxes, out_shape = halo_gather_plan(self.rank, list(x.shape), dim, table, length, x.element_size())
         out = x.new_empty(out_shape)
-        out_strides = _contig_strides(out_shape)
-        boxes = []
-        for out_off, src, src_off, n in table[self.rank]:
-            src_shape = list(x.shape)
-            src_shape[dim] = shapes[src]
-            src_strides = _contig_strides(src_shape)
-            shape = list(src_shape)
-            shape[dim] = n
-            boxes.append(make_box(shape, src_strides, src_off * src_strides[dim], out_strides,
-                                  out_off * out_strides[dim], src, x.element_size()))
-        return out if self._copy(x, out, boxes) else None
+        stage = torch.cat([x.narrow(dim, off, n) for off, n in send], dim) if send else None
+        return out if self._copy(stage, out, boxes, local=x) else None
 
     def halo_scatter_add(self, grad, dim, table, in_shape):
+        """Adjoint of halo_gather: this rank's own rows of ``grad`` add into the
+        result straight from ``grad``; the ghost rows go back to their owners
+        through a staged buffer that packs only the slabs this rank returns."""
         if self.broken or grad.dtype not in (torch.bfloat16, torch.float16, torch.float32):
             return None
         grad = grad.contiguous()
+        send, boxes = halo_scatter_plan(self.rank, self.size, list(grad.shape), dim, table, list(in_shape),
+                                        grad.element_size())
         grad_in = grad.new_zeros(in_shape)
-        in_strides = _contig_strides(list(in_shape))
-        boxes = []
-        for dst, pieces in enumerate(table):
-            g_shape = list(grad.shape)
-            g_shape[dim] = sum(p[3] for p in pieces)
-            g_strides = _contig_strides(g_shape)
-            for out_off, src, src_off, n in pieces:
-                if src != self.rank:
-                    continue
-                shape = list(g_shape)
-                shape[dim] = n
-                boxes.append(make_box(shape, g_strides, out_off * g_strides[dim], in_strides,
-                                      src_off * in_strides[dim], dst, grad.element_size()))
-        ok = self._copy(grad, grad_in, boxes, accumulate=True, sequential=True)
+        stage = torch.cat([grad.narrow(dim, off, n) for off, n in send], dim) if send else None
+        ok = self._copy(stage, grad_in, boxes, accumulate=True, sequential=True, local=grad)
         return grad_in if ok else None
 
     def block_exchange(self, z, send_block, out, recv_view):
