@@ -1,0 +1,103 @@
+"""Native halo exchange (staged boundary slabs over NVLink) on 2+ GPUs against
+the same halo built from the full tensor: uneven shards, a halo wider than a
+neighbour's shard, periodic and constant boundaries, forward and the adjoint
+scatter-add, and einconv over a sharded spatial axis against a local conv of
+the full input."""
+
+import pytest
+import torch
+
+pytestmark = [pytest.mark.gpu, pytest.mark.multigpu]
+
+if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+    pytest.skip("needs 2 or more CUDA devices", allow_module_level=True)
+
+from gpu_harness import run_gpus  # noqa: E402
+
+
+def _body(rank, world):
+    import torch.distributed as dist
+    import torch.nn.functional as F
+    from torch.distributed.device_mesh import init_device_mesh
+
+    import torch_einshard_b200 as es
+    from torch_einshard_b200.ops import _native
+    from torch_einshard_b200.parallel import symmetric
+
+    mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("sp",))
+    assert es.setup_native_comm(mesh)
+    calls = []
+    comm = symmetric.communicator_for(mesh["sp"].get_group())
+    real = comm.halo_gather
+
+    def spy(*a, **k):
+        out = real(*a, **k)
+        calls.append(out is not None)
+        return out
+    comm.halo_gather = spy
+
+    shapes = [3 + 2 * p for p in range(world)]
+    offs = [sum(shapes[:p]) for p in range(world)]
+    total = sum(shapes)
+    torch.manual_seed(11)
+    full = torch.randn(2, total, 5, device="cuda", dtype=torch.float32)
+    mine = full[:, offs[rank]:offs[rank] + shapes[rank]].contiguous().requires_grad_(True)
+    for left, right, boundary in ((1, 1, "constant"), (2, 4, "periodic"), (4, 1, "constant")):
+        got = es.einhalo("b h/sp c", mine, {"h": (left, right)}, boundary=boundary, mesh=mesh,
+                         shapes={"sp": shapes})
+        rows = torch.arange(offs[rank] - left, offs[rank] + shapes[rank] + right, device="cuda")
+        if boundary == "periodic":
+            want = full[:, rows % total]
+        else:
+            want = F.pad(full, (0, 0, left, right))[:, rows + left]
+        torch.testing.assert_close(got, want)
+        g = torch.randn_like(got)
+        (grad,) = torch.autograd.grad(got, mine, g)
+        # the adjoint on the full tensor: every haloed element's gradient returns to its owner
+        full_g = torch.zeros_like(full)
+        sizes = torch.tensor([g.shape[1]], device="cuda")
+        all_sizes = [torch.zeros_like(sizes) for _ in range(world)]
+        dist.all_gather(all_sizes, sizes)
+        for p in range(world):
+            piece = torch.empty(2, int(all_sizes[p].item()), 5, device="cuda")
+            if p == rank:
+                piece.copy_(g)
+            dist.broadcast(piece, p)
+            rows = torch.arange(offs[p] - left, offs[p] + shapes[p] + right, device="cuda")
+            if boundary == "periodic":
+                full_g.index_add_(1, rows % total, piece)
+            else:
+                keep = (rows >= 0) & (rows < total)
+                full_g.index_add_(1, rows[keep], piece[:, keep])
+        torch.testing.assert_close(grad, full_g[:, offs[rank]:offs[rank] + shapes[rank]], rtol=1e-5, atol=1e-5)
+    assert calls and all(calls), "the native halo exchange declined"
+
+    # einconv over a sharded spatial axis (bf16, native implicit-GEMM conv)
+    H, W, C, O = 8 * world, 16, 64, 64
+    x = torch.randn(2, H, W, C, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(3, 3, C, O, device="cuda", dtype=torch.bfloat16) * 0.05
+    dist.broadcast(x, 0)
+    dist.broadcast(w, 0)
+    hs = [H // world] * world
+    xl = x[:, rank * hs[0]:(rank + 1) * hs[0]].contiguous()
+    got = es.einconv("b h/sp w c, kh kw c o -> b h/sp w o", xl, w, {"h": "kh", "w": "kw"}, mesh=mesh,
+                     shapes={"sp": hs}, checkpoint=None)
+    ref = F.conv2d(x.float().permute(0, 3, 1, 2), w.float().permute(3, 2, 0, 1), padding=1).permute(0, 2, 3, 1)
+    ref = ref[:, rank * hs[0]:(rank + 1) * hs[0]]
+    assert (got.float() - ref).abs().max().item() <= 3e-2 * (ref.abs().max().item() + 1)
+    torch.cuda.synchronize()
+    _native.check_errors()
+
+
+def test_native_halo_2gpus():
+    run_gpus(_body, 2, timeout=300)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 4, reason="needs 4 GPUs")
+def test_native_halo_4gpus():
+    run_gpus(_body, 4, timeout=300)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 8, reason="needs 8 GPUs")
+def test_native_halo_8gpus():
+    run_gpus(_body, 8, timeout=300)
