@@ -40,16 +40,16 @@ DX = PlanStep("identity_forward_allreduce_backward", ("tp",))
 
 @pytest.mark.parametrize("size", [2, 4, 8])
 def test_nvls_groups_fuse_the_allreduce_by_default(ranks, monkeypatch, size):
-    """With a multicast heap, the row-parallel GEMM + all-reduce and the
-    replicated operand's gradient all-reduce run as the fused NVLS kernel at
-    every group size; the reduce-scatter output keeps the unfused steps."""
+    """With a multicast heap, the row-parallel GEMM + all-reduce, the replicated
+    operand's gradient all-reduce and the row reduce-scatter output run as the
+    fused NVLS kernel at every group size."""
     ranks(size, nvls=True)
     monkeypatch.setattr(fn, "_MAX_FUSED_EPILOGUE_RANKS", 0)
     monkeypatch.setattr(fn, "_FUSED_NVLS", True)
     assert fn.provider(executor(output_steps=[AR])).kind == "gemm_allreduce"
     f = fn.provider(executor(input0_steps=[DX]))
     assert f.kind == "dgrad_allreduce" and f.operand == 0
-    assert fn.provider(executor(output_steps=[RS])) is None
+    assert fn.provider(executor(output_steps=[RS])).kind == "gemm_reducescatter"
 
 
 def test_nvls_fusion_can_be_switched_off(ranks, monkeypatch):

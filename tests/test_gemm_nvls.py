@@ -5,8 +5,8 @@ all-reduced by NCCL, on 2, 4 and 8 GPUs.
 Ragged shapes (rows and columns that end inside a unit), both operand
 layouts, calls of alternating shapes on one heap (the per-unit epochs), the
 fused call between NVLS collectives and copy-protocol kernels on the same heap,
-and the TP-MLP through the public API (forward and backward) against the
-unfused NCCL path.
+the reduce-scatter mode (row segments), and the TP-MLP through the public API
+(forward and backward) against the unfused NCCL path.
 """
 
 import pytest
@@ -58,6 +58,17 @@ def _body(rank, world):
             assert comm.all_reduce_(x) and torch.all(x == world * (world - 1) / 2)
             part = torch.randn(3, 2 * world, 5, device="cuda", generator=g)
             assert comm.all_to_all(part, 0, 1, [3] * world, [2] * world) is not None
+    # reduce-scatter mode: each rank keeps its rows of every segment
+    for m, n, k, seg in [(1024 * world, 1024, 256, 64 * world), (256 * world, 520, 136, 32 * world)]:
+        a = torch.randn(1, m, k, device="cuda", dtype=torch.bfloat16, generator=g)
+        b = torch.randn(1, n, k, device="cuda", dtype=torch.bfloat16, generator=g).transpose(1, 2)
+        shard = seg // world
+        got = fused_native.gemm_reducescatter_nvls(comm, a, b, seg, shard)
+        want = a.float() @ b.float()
+        dist.all_reduce(want, group=group)
+        want = want.reshape(1, m // seg, seg, n)[:, :, rank * shard:(rank + 1) * shard].reshape(1, m // world, n)
+        scale = want.abs().max().item() + 1.0
+        assert (got.float() - want).abs().max().item() <= 2e-2 * scale, (m, n, k, seg)
     torch.cuda.synchronize()
     _native.check_errors()
 

@@ -505,6 +505,9 @@ void nvls_reduce_scatter(int64_t id, const at::Tensor& in, at::Tensor out, int64
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
+void launch_gemm_nvls(HostComm& hc, const es::GemmArgs& g, int64_t reducer_clusters, int64_t red_warps, int64_t seg,
+                      int64_t shard);
+
 // out (every rank) = sum over the communicator's ranks of (a @ b): the wide GEMM
 // and an NVLS all-reduce of its output units in one launch (gemm_nvls.cu).
 void gemm_allreduce_nvls(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out,
@@ -518,8 +521,13 @@ void gemm_allreduce_nvls(int64_t id, const at::Tensor& a, const at::Tensor& b, a
   es::GemmArgs g = gemm_args(a, b, out, 0, err);
   TORCH_CHECK(g.N % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
               "einshard fused gemm+NVLS all-reduce: N must be a multiple of 8");
-  TORCH_CHECK((size_t)g.M * g.N * 2 <= hc.data_bytes, "einshard fused gemm+NVLS all-reduce: heap too small");
-  TORCH_CHECK(es::gemm_nvls_units(g.M, g.N) <= es::kNvlsMaxUnits, "einshard fused gemm+NVLS all-reduce: too many units");
+  launch_gemm_nvls(hc, g, reducer_clusters, red_warps, 0, 0);
+}
+
+void launch_gemm_nvls(HostComm& hc, const es::GemmArgs& g, int64_t reducer_clusters, int64_t red_warps, int64_t seg,
+                      int64_t shard) {
+  TORCH_CHECK((size_t)g.M * g.N * 2 <= hc.data_bytes, "einshard fused gemm+NVLS: heap too small");
+  TORCH_CHECK(es::gemm_nvls_units(g.M, g.N) <= es::kNvlsMaxUnits, "einshard fused gemm+NVLS: too many units");
   es::NvlsGemmJob j;
   j.heap_uc = static_cast<char*>(hc.local) + es::kFlagBytes;
   j.heap_mc = static_cast<char*>(hc.mc) + es::kFlagBytes;
@@ -532,10 +540,37 @@ void gemm_allreduce_nvls(int64_t id, const at::Tensor& a, const at::Tensor& b, a
   j.epoch = static_cast<uint32_t>(++hc.tile_epoch);
   j.reducer_clusters = static_cast<int>(reducer_clusters);
   j.red_warps = static_cast<int>(red_warps);
+  j.seg = static_cast<int>(seg);
+  j.shard = static_cast<int>(shard);
   j.timeout_ns = g_wait_timeout_ns;
   const int rc = es::gemm_nvls_allreduce_launch(g, j, at::cuda::getCurrentCUDAStream());
-  TORCH_CHECK(rc == 0, "einshard fused gemm+NVLS all-reduce: launch failed (", rc, ")");
+  TORCH_CHECK(rc == 0, "einshard fused gemm+NVLS: launch failed (", rc, ")");
   g_launches.fetch_add(1, std::memory_order_relaxed);
+}
+
+// out (this rank's rows) = reduce-scatter over the communicator's ranks of
+// (a @ b) along row segments: rows [seg i + rank shard, + shard) of every
+// segment i; the wide GEMM and the NVLS reduction in one launch.
+void gemm_reducescatter_nvls(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out, int64_t seg,
+                             int64_t shard, int64_t reducer_clusters, int64_t red_warps, const at::Tensor& err) {
+  HostComm& hc = comm_ref(id);
+  TORCH_CHECK(hc.open && hc.mc != nullptr, "einshard fused gemm+NVLS reduce-scatter: no multicast mapping");
+  TORCH_CHECK(a.size(0) == 1 && a.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16 &&
+                  out.is_contiguous() && out.dim() == 3 && out.size(1) * hc.size == a.size(1) && out.size(2) == b.size(2),
+              "einshard fused gemm+NVLS reduce-scatter: bf16, batch 1, contiguous [1, M / P, N] output");
+  TORCH_CHECK(seg > 0 && shard * hc.size == seg && shard % 32 == 0 && a.size(1) % seg == 0,
+              "einshard fused gemm+NVLS reduce-scatter: segments of P x (multiple of 32) rows");
+  const c10::cuda::CUDAGuard guard(a.device());
+  es::GemmArgs g = gemm_operand_args(a, b, 0, err);
+  g.C = out.data_ptr();
+  g.out_dtype = es::kDtypeBF16;
+  g.ldc = out.stride(1);
+  g.c_batch_stride = out.stride(0);
+  const char* why = es::check_gemm_args(g);
+  TORCH_CHECK(why == nullptr, "einshard fused gemm+NVLS reduce-scatter: ", why ? why : "");
+  TORCH_CHECK(g.N % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
+              "einshard fused gemm+NVLS reduce-scatter: N must be a multiple of 8");
+  launch_gemm_nvls(hc, g, reducer_clusters, red_warps, seg, shard);
 }
 
 // out = all-reduce over the communicator's ranks of (a @ b); one fused kernel.
@@ -931,6 +966,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_finish", &symm_finish, "phase 4: map the multicast object, zero the flags");
   m.def("comm_destroy", &comm_destroy, "unmap and free");
   m.def("comm_has_multicast", &comm_has_multicast, "whether the communicator has an NVLS multicast mapping");
+  m.def("gemm_reducescatter_nvls", &gemm_reducescatter_nvls,
+        "wide GEMM whose output row segments are reduce-scattered through the NVSwitch in the same launch");
   m.def("gemm_allreduce_nvls", &gemm_allreduce_nvls,
         "wide GEMM whose output units are all-reduced through the NVSwitch in the same launch");
   m.def("nvls_quiesce", &nvls_quiesce, "wait until every rank completed this heap's NVLS collectives");

@@ -94,11 +94,19 @@ __device__ __forceinline__ void unit_origin(const GemmShape& s, long long u, int
 
 // Epilogue of the GEMM clusters: the plain TMA-store epilogue into the heap,
 // then the unit's ready word on its owner.
+// Owner of a unit: all-reduce (seg == 0): u mod P; reduce-scatter: the rank
+// whose rows the unit holds (rows [seg i + p shard, seg i + (p + 1) shard) are
+// rank p's; shard is a multiple of the 32-row unit height).
+__device__ __forceinline__ int unit_owner(long long u, int row0, int size, int seg, int shard) {
+  return seg ? (row0 % seg) / shard : static_cast<int>(u % size);
+}
+
 struct PartialEpilogue {
   StoreEpilogue<__nv_bfloat16> store;
   uint64_t ready[kMaxRanks];  // each rank's ready[0][0] (peer-mapped)
   int rank, size;
   uint32_t epoch;
+  int seg, shard;             // reduce-scatter row segments (seg == 0: all-reduce)
 
   __device__ __forceinline__ void setup(int*, const GemmShape&) {}
   __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
@@ -110,7 +118,7 @@ struct PartialEpilogue {
       bulk_wait_group<0>();        // the unit's TMA stores have completed
       fence_proxy_async_global();  // ... and are ordered before generic-proxy accesses
       fence_acq_rel_sys();
-      const int owner = static_cast<int>(u % size);
+      const int owner = unit_owner(u, et.c.m0 + et.q * 32, size, seg, shard);
       st_release_sys_u32(reinterpret_cast<uint32_t*>(ready[owner]) + u * size + rank, epoch);
     }
     __syncwarp();
@@ -131,11 +139,54 @@ struct ReduceJob {
   uint32_t epoch;
   int clusters;        // reducer clusters at the front of the grid
   int red_warps;       // warps of each reducer CTA that reduce; the others copy out
+  int seg, shard;      // reduce-scatter (seg > 0): out holds this rank's rows only, [M / P][ldo]
   int* err;
   uint64_t timeout_ns;
 };
 
 constexpr int kRowsInFlight = 16;
+
+// Reduce and copy-out roles of the first job.clusters clusters.
+// One unit owned by this rank: wait until every rank's partial is in its heap,
+// sum it in the switch, then either multicast the sum back into every rank's
+// heap (all-reduce) or store it into this rank's rows of the output
+// (reduce-scatter), and multicast reduced[u] = epoch.  False on a timeout.
+__device__ __forceinline__ bool reduce_unit(const ReduceJob& j, const GemmShape& s, long long u, int row0, int col0,
+                                            int lane) {
+  bool ok = true;
+  if (lane < j.size) ok = wait_epoch(j.ready + u * j.size + lane, j.epoch, j.timeout_ns);
+  if (!__all_sync(0xffffffffu, ok)) {
+    if (lane == 0) atomicCAS(j.err, 0, kErrWaitPeerFlag);
+    return false;
+  }
+  const int col = col0 + lane * 8;
+  const int rows = es_min(32, s.M - row0);
+  if (col < s.N) {
+    for (int r0 = 0; r0 < rows; r0 += kRowsInFlight) {
+      uint4 v[kRowsInFlight];
+#pragma unroll
+      for (int i = 0; i < kRowsInFlight; ++i)
+        if (r0 + i < rows) v[i] = ld_reduce_bf16x8(j.mc + ((row0 + r0 + i) * j.ldh + col) * 2);
+#pragma unroll
+      for (int i = 0; i < kRowsInFlight; ++i) {
+        if (r0 + i >= rows) continue;
+        const long long row = row0 + r0 + i;
+        if (j.seg) {
+          const long long local = (row / j.seg) * j.shard + (row % j.seg) - static_cast<long long>(j.rank) * j.shard;
+          *reinterpret_cast<uint4*>(j.out + (local * j.ldo + col) * 2) = v[i];
+        } else {
+          mc_st16(j.mc + (row * j.ldh + col) * 2, v[i]);
+        }
+      }
+    }
+  }
+  __syncwarp();
+  if (lane == 0) {
+    fence_acq_rel_sys();
+    mc_st_release_u32(j.reduced_mc + u, j.epoch);
+  }
+  return true;
+}
 
 // Reduce and copy-out roles of the first job.clusters clusters.
 __device__ void reducer_role(const ReduceJob& j, const GemmShape& s, int cta, int ncta) {
@@ -145,38 +196,43 @@ __device__ void reducer_role(const ReduceJob& j, const GemmShape& s, int cta, in
   if (warp < j.red_warps) {
     const long long gw = static_cast<long long>(cta) * j.red_warps + warp;
     const long long W = static_cast<long long>(ncta) * j.red_warps;
-    for (long long k = gw;; k += W) {
-      const long long u = j.rank + k * j.size;
-      if (u >= j.units) break;
-      int row0, col0;
-      unit_origin(s, u, &row0, &col0);
-      if (row0 >= s.M || col0 >= s.N) continue;
-      bool ok = true;
-      if (lane < j.size) ok = wait_epoch(j.ready + u * j.size + lane, j.epoch, j.timeout_ns);
-      if (!__all_sync(0xffffffffu, ok)) {
-        if (lane == 0) atomicCAS(j.err, 0, kErrWaitPeerFlag);
-        return;
+    if (!j.seg) {
+      for (long long k = gw;; k += W) {
+        const long long u = j.rank + k * j.size;
+        if (u >= j.units) break;
+        int row0, col0;
+        unit_origin(s, u, &row0, &col0);
+        if (row0 >= s.M || col0 >= s.N) continue;
+        if (!reduce_unit(j, s, u, row0, col0, lane)) return;
       }
-      const int col = col0 + lane * 8;
-      const int rows = es_min(32, s.M - row0);
-      if (col < s.N) {
-        for (int r0 = 0; r0 < rows; r0 += kRowsInFlight) {
-          uint4 v[kRowsInFlight];
-#pragma unroll
-          for (int i = 0; i < kRowsInFlight; ++i)
-            if (r0 + i < rows) v[i] = ld_reduce_bf16x8(j.mc + ((row0 + r0 + i) * j.ldh + col) * 2);
-#pragma unroll
-          for (int i = 0; i < kRowsInFlight; ++i)
-            if (r0 + i < rows) mc_st16(j.mc + ((row0 + r0 + i) * j.ldh + col) * 2, v[i]);
+    } else {
+      // the units whose rows this rank owns, in unit order, found 32 at a time
+      long long k = 0;
+      for (long long base = 0; base < j.units; base += 32) {
+        const long long u = base + lane;
+        int row0 = 0, col0 = 0;
+        bool mine = false;
+        if (u < j.units) {
+          unit_origin(s, u, &row0, &col0);
+          mine = row0 < s.M && col0 < s.N && unit_owner(u, row0, j.size, j.seg, j.shard) == j.rank;
         }
-      }
-      __syncwarp();
-      if (lane == 0) {
-        fence_acq_rel_sys();
-        mc_st_release_u32(j.reduced_mc + u, j.epoch);
+        unsigned m = __ballot_sync(0xffffffffu, mine);
+        while (m) {
+          const int bit = __ffs(m) - 1;
+          m &= m - 1;
+          if (k % W == gw) {
+            int r0, c0;
+            unit_origin(s, base + bit, &r0, &c0);
+            if (!reduce_unit(j, s, base + bit, r0, c0, lane)) return;
+          }
+          ++k;
+        }
       }
     }
   } else {
+    // every unit: wait until its owner reduced it, then (all-reduce) copy the sum
+    // from the heap into the output; when these waits end, no peer touches this
+    // rank's heap for the call any more
     const int ncw = nwarps - j.red_warps;
     const long long gw = static_cast<long long>(cta) * ncw + (warp - j.red_warps);
     const long long W = static_cast<long long>(ncta) * ncw;
@@ -190,6 +246,7 @@ __device__ void reducer_role(const ReduceJob& j, const GemmShape& s, int cta, in
         if (lane == 0) atomicCAS(j.err, 0, kErrWaitPeerFlag);
         return;
       }
+      if (j.seg) continue;
       const int col = col0 + lane * 8;
       const int rows = es_min(32, s.M - row0);
       if (col < s.N) {
@@ -234,6 +291,8 @@ int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& nj, cudaStr
   const long long units = gemm_nvls_units(g.M, g.N);
   if (units > kNvlsMaxUnits || nj.reducer_clusters < 1 || nj.red_warps < 1 || nj.red_warps >= kThreads3 / 32)
     return static_cast<int>(cudaErrorInvalidValue);
+  if (nj.seg && (nj.shard % 32 != 0 || nj.shard * nj.size != nj.seg || g.M % nj.seg != 0))
+    return static_cast<int>(cudaErrorInvalidValue);
   CUtensorMap ma, mb, mc, mw;
   make_operand_maps(g, &ma, &mb, true);
   // the partial product goes to the heap (row pitch N), not to the output tensor
@@ -261,6 +320,8 @@ int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& nj, cudaStr
   epi.rank = nj.rank;
   epi.size = nj.size;
   epi.epoch = nj.epoch;
+  epi.seg = nj.seg;
+  epi.shard = nj.shard;
   ReduceJob job;
   job.uc = static_cast<uint8_t*>(nj.heap_uc);
   job.mc = static_cast<uint8_t*>(nj.heap_mc);
@@ -276,6 +337,8 @@ int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& nj, cudaStr
   job.epoch = nj.epoch;
   job.clusters = nj.reducer_clusters;
   job.red_warps = nj.red_warps;
+  job.seg = nj.seg;
+  job.shard = nj.shard;
   job.err = g.err;
   job.timeout_ns = nj.timeout_ns;
 

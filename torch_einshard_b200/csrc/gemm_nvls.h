@@ -19,12 +19,14 @@ struct NvlsGemmJob {
   uint32_t epoch = 1;            // this call's number on the heap (>= 1, same on every rank)
   int reducer_clusters = 4;      // CTA pairs that reduce and copy out
   int red_warps = 3;             // of the 10 warps of each reducer CTA, how many reduce
+  int seg = 0, shard = 0;        // reduce-scatter: rows [seg i + p shard, + shard) go to rank p (seg 0: all-reduce)
   uint64_t timeout_ns = 4000000000ull;
 };
 
 // Units (32 x 256 output blocks) of an M x N product on the wide kernel's tiles.
 long long gemm_nvls_units(int M, int N);
-// g.C / g.ldc: the output tensor (every rank gets the sum); g.err: error word.
+// g.C / g.ldc: the output tensor (all-reduce: every rank gets the whole sum;
+// reduce-scatter: this rank's rows, [M / P][ldc]); g.err: error word.
 int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& job, cudaStream_t stream);
 
 }  // namespace es

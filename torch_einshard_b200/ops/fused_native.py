@@ -141,9 +141,7 @@ class _GemmReduceScatter(torch.autograd.Function):
     def forward(ctx, a, b, comm, seg, shard):
         ctx.save_for_backward(a, b)
         ctx.args = (comm, seg, shard)
-        if _rs_fits(comm, a.shape[1], b.shape[2], seg, shard):
-            return gemm_reducescatter(comm, a, b, seg, shard)
-        return _scatter_rows(comm, native_bmm(a, b), seg, shard)
+        return _reducescatter(comm, a, b, seg, shard)
 
     @staticmethod
     def backward(ctx, grad):
@@ -180,11 +178,7 @@ class _AllGatherGemm(torch.autograd.Function):
         comm, seg, shard = ctx.args
         ga = gb = None
         if ctx.needs_input_grad[0]:
-            bt = b.transpose(1, 2)
-            if _rs_fits(comm, grad.shape[1], bt.shape[2], seg, shard):
-                ga = gemm_reducescatter(comm, grad, bt, seg, shard)
-            else:
-                ga = _scatter_rows(comm, native_bmm(grad, bt), seg, shard)
+            ga = _reducescatter(comm, grad, b.transpose(1, 2), seg, shard)
         if ctx.needs_input_grad[1]:
             gb = _grad_b(a_full, b, grad)
         return ga, gb, None, None, None
@@ -212,6 +206,42 @@ def gemm_allreduce_nvls(comm, a, b):
     mod.gemm_allreduce_nvls(ws.cid, a, b, out, _NVLS_REDUCER_CLUSTERS, _NVLS_REDUCE_WARPS,
                             _native.error_word(a.device))
     return out
+
+
+def gemm_reducescatter_nvls(comm, a, b, seg, shard):
+    """This rank's row segments of ``sum over ranks of a @ b`` in one launch:
+    the wide GEMM writes its output units into the symmetric heap and each
+    unit's owner (the rank whose rows it holds) sums it in the NVSwitch and
+    stores it into its output.  None when the group has no NVLS heap."""
+    from ..parallel import symmetric
+    m, n = a.shape[1], b.shape[2]
+    ws = symmetric.workspace_for(comm.group, m * n * 2)
+    if ws is None or not ws.nvls or ws.broken:
+        return None
+    mod = _native.require()
+    a, b = _prepare(a), _prepare(b)
+    out = torch.empty((1, m // comm.size, n), dtype=torch.bfloat16, device=a.device)
+    ws.enter("tile")
+    mod.gemm_reducescatter_nvls(ws.cid, a, b, out, seg, shard, _NVLS_REDUCER_CLUSTERS, _NVLS_REDUCE_WARPS,
+                                _native.error_word(a.device))
+    return out
+
+
+def _nvls_rs_fits(comm, a, b, seg, shard):
+    return (_nvls_fits(comm, a, b) and seg > 0 and shard % 32 == 0 and shard * comm.size == seg
+            and a.shape[1] % seg == 0)
+
+
+def _reducescatter(comm, a, b, seg, shard):
+    """Row reduce-scatter of a @ b: the fused NVLS kernel, else the older fused
+    epilogue, else the GEMM followed by the collective."""
+    if _nvls_rs_fits(comm, a, b, seg, shard):
+        out = gemm_reducescatter_nvls(comm, a, b, seg, shard)
+        if out is not None:
+            return out
+    if _fusable(comm, _MAX_FUSED_EPILOGUE_RANKS) and _rs_fits(comm, a.shape[1], b.shape[2], seg, shard):
+        return gemm_reducescatter(comm, a, b, seg, shard)
+    return _scatter_rows(comm, native_bmm(a, b), seg, shard)
 
 
 def _nvls_fits(comm, a, b):
@@ -524,7 +554,8 @@ def provider(executor):
     if (len(out_steps) == 1 and out_steps[0].name == "reducescatter_forward_allgather_backward"
             and not tp.input0_steps and not tp.input1_steps):
         name, dim = out_steps[0].args
-        if _fusable(_comm(executor.group(dim)), _MAX_FUSED_EPILOGUE_RANKS):
+        comm = _comm(executor.group(dim))
+        if _nvls_comm(comm) or _fusable(comm, _MAX_FUSED_EPILOGUE_RANKS):
             return _Fusion("gemm_reducescatter", axis=name)
         return None
     if (not out_steps and len(tp.input0_steps) == 1 and not tp.input1_steps
