@@ -76,6 +76,7 @@ def main():
     from torch_einshard_b200.parallel import symmetric
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     es.setup_native_comm(mesh)
+    symmetric._NVLS_AR_MIN_RANKS = 1  # time the native kernels at every group size
     group = mesh["tp"].get_group()
     comm = symmetric.communicator_for(group)
     dtype = DTYPES[args.dtype]

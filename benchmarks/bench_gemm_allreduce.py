@@ -36,6 +36,9 @@ def main():
     p.add_argument("--iters", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--arms", default="fused,gemm+nvls,gemm+nccl,torch+nccl")
+    p.add_argument("--reducers", default="", help="comma list of reducer CTA-pair counts to time the fused arm with "
+                                                   "(arms fused-R<n>); empty: the default")
+    p.add_argument("--reduce-warps", type=int, default=0, help="reduce warps per reducer CTA (0: default)")
     args = p.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -47,6 +50,7 @@ def main():
     from torch_einshard_b200.parallel import symmetric
     mesh = init_device_mesh("cuda", (world,), mesh_dim_names=("tp",))
     es.setup_native_comm(mesh)
+    symmetric._NVLS_AR_MIN_RANKS = 1  # time the native kernels at every group size
     group = mesh["tp"].get_group()
     comm = symmetric.communicator_for(group)
     k = args.h // world
@@ -73,6 +77,15 @@ def main():
         return out
 
     arms = {"fused": fused, "gemm+nvls": gemm_nvls, "gemm+nccl": gemm_nccl, "torch+nccl": torch_nccl}
+    if args.reduce_warps:
+        fused_native._NVLS_REDUCE_WARPS = args.reduce_warps
+    names = args.arms.split(",")
+    for r in [int(v) for v in args.reducers.split(",") if v]:
+        def fused_r(r=r):
+            fused_native._NVLS_REDUCER_CLUSTERS = r
+            return fused_native.gemm_allreduce_nvls(comm, a, b)
+        arms[f"fused-R{r}"] = fused_r
+        names.append(f"fused-R{r}")
     sampler = ClockSampler(visible_gpu_indices(world)) if rank == 0 else None
     if sampler:
         sampler.start()
@@ -84,8 +97,8 @@ def main():
     t_link = (9.0 / 8.0 if world > 1 else 0.0) * out_bytes / 770e9 * 1e3
     roof = max(t_compute, t_link)
     results = {}
-    for name in args.arms.split(","):
-        if comm is None and name in ("fused", "gemm+nvls"):
+    for name in names:
+        if comm is None and (name.startswith("fused") or name == "gemm+nvls"):
             continue
         fn = arms[name]
         for _ in range(args.warmup):

@@ -98,13 +98,19 @@ def test_nvls_heaps_take_every_size(size, monkeypatch):
     comm.nvls = True
     small = torch.zeros(symmetric._NVLS_ONE_SHOT_MAX // 2, dtype=torch.bfloat16)
     large = torch.zeros(8 << 20, dtype=torch.bfloat16)       # 16 MiB
-    assert comm.all_reduce_(small, 0.5) and comm.all_reduce_(large)
-    assert comm.mod.calls == [("nvls1", symmetric._NVLS_ONE_SHOT_MAX, 0.5), ("nvls2", 16 << 20, 1.0)]
+    assert comm.all_reduce_(small, 0.5)
+    if size < symmetric._NVLS_AR_MIN_RANKS:
+        # a two-shot NVLS all-reduce moves more bytes than a ring at 2 ranks: NCCL takes it
+        assert not comm.all_reduce_(large)
+        assert comm.mod.calls == [("nvls1", symmetric._NVLS_ONE_SHOT_MAX, 0.5)]
+    else:
+        assert comm.all_reduce_(large)
+        assert comm.mod.calls == [("nvls1", symmetric._NVLS_ONE_SHOT_MAX, 0.5), ("nvls2", 16 << 20, 1.0)]
 
 
 def test_nvls_pieces_when_larger_than_the_workspace(monkeypatch):
     monkeypatch.delenv("EINSHARD_FAULT_INJECT", raising=False)
-    comm = make_comm(2, capacity=4 << 20)
+    comm = make_comm(4, capacity=4 << 20)
     comm.nvls = True
     monkeypatch.setattr(symmetric, "workspace_for_group", lambda group, nbytes: comm)
     comm.group = None

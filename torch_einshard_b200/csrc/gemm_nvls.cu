@@ -144,7 +144,7 @@ struct ReduceJob {
   uint64_t timeout_ns;
 };
 
-constexpr int kRowsInFlight = 16;
+constexpr int kRowsInFlight = 32;  // a whole unit (16 KB per warp) in flight
 
 // Reduce and copy-out roles of the first job.clusters clusters.
 // One unit owned by this rank: wait until every rank's partial is in its heap,
@@ -162,21 +162,32 @@ __device__ __forceinline__ bool reduce_unit(const ReduceJob& j, const GemmShape&
   const int col = col0 + lane * 8;
   const int rows = es_min(32, s.M - row0);
   if (col < s.N) {
+    // the unit's rows: heap row pitch ldh; in reduce-scatter mode a 32-row unit
+    // lies inside one owner's shard, so its output rows are consecutive too
+    const long long pitch = j.ldh * 2;
+    const uint8_t* src = j.mc + (static_cast<long long>(row0) * j.ldh + col) * 2;
+    uint8_t* dst;
+    long long dpitch;
+    if (j.seg) {
+      const long long local = (row0 / j.seg) * j.shard + (row0 % j.seg) - static_cast<long long>(j.rank) * j.shard;
+      dst = j.out + (local * j.ldo + col) * 2;
+      dpitch = j.ldo * 2;
+    } else {
+      dst = j.mc + (static_cast<long long>(row0) * j.ldh + col) * 2;
+      dpitch = pitch;
+    }
     for (int r0 = 0; r0 < rows; r0 += kRowsInFlight) {
       uint4 v[kRowsInFlight];
 #pragma unroll
       for (int i = 0; i < kRowsInFlight; ++i)
-        if (r0 + i < rows) v[i] = ld_reduce_bf16x8(j.mc + ((row0 + r0 + i) * j.ldh + col) * 2);
+        if (r0 + i < rows) v[i] = ld_reduce_bf16x8(src + (r0 + i) * pitch);
 #pragma unroll
       for (int i = 0; i < kRowsInFlight; ++i) {
         if (r0 + i >= rows) continue;
-        const long long row = row0 + r0 + i;
-        if (j.seg) {
-          const long long local = (row / j.seg) * j.shard + (row % j.seg) - static_cast<long long>(j.rank) * j.shard;
-          *reinterpret_cast<uint4*>(j.out + (local * j.ldo + col) * 2) = v[i];
-        } else {
-          mc_st16(j.mc + (row * j.ldh + col) * 2, v[i]);
-        }
+        if (j.seg)
+          *reinterpret_cast<uint4*>(dst + (r0 + i) * dpitch) = v[i];
+        else
+          mc_st16(dst + (r0 + i) * dpitch, v[i]);
       }
     }
   }
@@ -250,15 +261,17 @@ __device__ void reducer_role(const ReduceJob& j, const GemmShape& s, int cta, in
       const int col = col0 + lane * 8;
       const int rows = es_min(32, s.M - row0);
       if (col < s.N) {
+        const uint8_t* src = j.uc + (static_cast<long long>(row0) * j.ldh + col) * 2;
+        uint8_t* dst = j.out + (static_cast<long long>(row0) * j.ldo + col) * 2;
+        const long long sp = j.ldh * 2, dp = j.ldo * 2;
         for (int r0 = 0; r0 < rows; r0 += kRowsInFlight) {
           uint4 v[kRowsInFlight];
 #pragma unroll
           for (int i = 0; i < kRowsInFlight; ++i)
-            if (r0 + i < rows)
-              v[i] = *reinterpret_cast<const uint4*>(j.uc + ((row0 + r0 + i) * j.ldh + col) * 2);
+            if (r0 + i < rows) v[i] = *reinterpret_cast<const uint4*>(src + (r0 + i) * sp);
 #pragma unroll
           for (int i = 0; i < kRowsInFlight; ++i)
-            if (r0 + i < rows) *reinterpret_cast<uint4*>(j.out + ((row0 + r0 + i) * j.ldo + col) * 2) = v[i];
+            if (r0 + i < rows) *reinterpret_cast<uint4*>(dst + (r0 + i) * dp) = v[i];
         }
       }
     }

@@ -15,7 +15,7 @@ namespace es {
 namespace {
 
 constexpr int kNvlsThreads = 512;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 8;  // 16-byte units in flight per thread
 
 // ---------------------------------------------------------------- multimem wrappers
 
@@ -161,6 +161,27 @@ __device__ __forceinline__ void store_unit(uint8_t* dst, long long u, long long 
   for (long long i = o; i < n; ++i) dst[i] = b[i - o];
 }
 
+// Per-thread loop over units [u0, u1) of this block with kUnroll units in
+// flight: each round loads kUnroll units (block-strided) through `ld`, then
+// stores them through `st`.
+template <class Ld, class St>
+__device__ __forceinline__ void unit_loop(long long u0, long long u1, Ld ld, St st) {
+  const long long step = blockDim.x;
+  for (long long base = u0 + threadIdx.x; base < u1; base += step * kUnroll) {
+    uint4 v[kUnroll];
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) {
+      const long long u = base + j * step;
+      if (u < u1) v[j] = ld(u);
+    }
+#pragma unroll
+    for (int j = 0; j < kUnroll; ++j) {
+      const long long u = base + j * step;
+      if (u < u1) st(u, v[j]);
+    }
+  }
+}
+
 // ---------------------------------------------------------------- all-reduce
 
 template <int DT>
@@ -172,10 +193,11 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_all_reduce(NvlsDev d, con
   long long u0, u1;
   unit_range(units, &u0, &u1);
   if (!block_wait(d, kNvlsSeq + b, P * static_cast<uint32_t>(d.epoch - 1))) return;
-  if (in != nullptr) {
-    for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x)
-      *reinterpret_cast<uint4*>(d.uc + u * 16) = load_unit(in, u, nbytes);
-  }
+  uint8_t* uc = d.uc;
+  const uint8_t* mc = d.mc;
+  if (in != nullptr)
+    unit_loop(u0, u1, [&](long long u) { return load_unit(in, u, nbytes); },
+              [&](long long u, uint4 v) { *reinterpret_cast<uint4*>(uc + u * 16) = v; });
   block_signal(d, kNvlsReady + b);
   if (!block_wait(d, kNvlsReady + b, P * static_cast<uint32_t>(d.epoch))) return;
   const bool scaled = scale != 1.0f;
@@ -183,39 +205,16 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_all_reduce(NvlsDev d, con
     const long long len = u1 - u0;
     const long long s0 = u0 + len * d.rank / d.size;
     const long long s1 = u0 + len * (d.rank + 1) / d.size;
-    for (long long u = s0 + threadIdx.x; u < s1; u += static_cast<long long>(blockDim.x) * kUnroll) {
-      uint4 v[kUnroll];
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const long long w = u + static_cast<long long>(j) * blockDim.x;
-        if (w < s1) v[j] = mm_ld_reduce<DT>(d.mc + w * 16);
-      }
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const long long w = u + static_cast<long long>(j) * blockDim.x;
-        if (w < s1) mm_st(d.mc + w * 16, scaled ? scale16<DT>(v[j], scale) : v[j]);
-      }
-    }
+    unit_loop(s0, s1, [&](long long u) { return mm_ld_reduce<DT>(mc + u * 16); },
+              [&](long long u, uint4 v) { mm_st(d.mc + u * 16, scaled ? scale16<DT>(v, scale) : v); });
     block_signal(d, kNvlsSeq + b);
     if (!block_wait(d, kNvlsSeq + b, P * static_cast<uint32_t>(d.epoch))) return;
-    if (out != nullptr) {
-      for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x)
-        store_unit(out, u, nbytes, *reinterpret_cast<const uint4*>(d.uc + u * 16));
-    }
+    if (out != nullptr)
+      unit_loop(u0, u1, [&](long long u) { return *reinterpret_cast<const uint4*>(uc + u * 16); },
+                [&](long long u, uint4 v) { store_unit(out, u, nbytes, v); });
   } else {
-    for (long long u = u0 + threadIdx.x; u < u1; u += static_cast<long long>(blockDim.x) * kUnroll) {
-      uint4 v[kUnroll];
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const long long w = u + static_cast<long long>(j) * blockDim.x;
-        if (w < u1) v[j] = mm_ld_reduce<DT>(d.mc + w * 16);
-      }
-#pragma unroll
-      for (int j = 0; j < kUnroll; ++j) {
-        const long long w = u + static_cast<long long>(j) * blockDim.x;
-        if (w < u1) store_unit(out, w, nbytes, scaled ? scale16<DT>(v[j], scale) : v[j]);
-      }
-    }
+    unit_loop(u0, u1, [&](long long u) { return mm_ld_reduce<DT>(mc + u * 16); },
+              [&](long long u, uint4 v) { store_unit(out, u, nbytes, scaled ? scale16<DT>(v, scale) : v); });
     block_signal(d, kNvlsSeq + b);
   }
 }
@@ -245,7 +244,8 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_all_gather(NvlsDev d, con
     long long u0, u1;
     unit_range((n + 15) / 16, &u0, &u1);
     uint8_t* dst = d.mc + L.region[d.rank];
-    for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x) mm_st(dst + u * 16, load_unit(in, u, n));
+    unit_loop(u0, u1, [&](long long u) { return load_unit(in, u, n); },
+              [&](long long u, uint4 v) { mm_st(dst + u * 16, v); });
   }
   block_signal(d, kNvlsReady + b);
   if (!block_wait(d, kNvlsReady + b, P * static_cast<uint32_t>(d.epoch))) return;
@@ -255,8 +255,8 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_all_gather(NvlsDev d, con
     unit_range((n + 15) / 16, &u0, &u1);
     const uint8_t* src = d.uc + L.region[q];
     if (strided_units_ok(L, q, out)) {
-      for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x)
-        *reinterpret_cast<uint4*>(out + full_offset(L, q, u * 16)) = *reinterpret_cast<const uint4*>(src + u * 16);
+      unit_loop(u0, u1, [&](long long u) { return *reinterpret_cast<const uint4*>(src + u * 16); },
+                [&](long long u, uint4 v) { *reinterpret_cast<uint4*>(out + full_offset(L, q, u * 16)) = v; });
     } else {
       const long long e = u1 * 16 < n ? u1 * 16 : n;
       for (long long i = u0 * 16 + threadIdx.x; i < e; i += blockDim.x) out[full_offset(L, q, i)] = src[i];
@@ -277,11 +277,12 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_reduce_scatter(NvlsDev d,
     unit_range((n + 15) / 16, &u0, &u1);
     uint8_t* dst = d.uc + L.region[q];
     if (strided_units_ok(L, q, in)) {
-      for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
-        const long long o = u * 16;
-        *reinterpret_cast<uint4*>(dst + o) = o + 16 <= n ? *reinterpret_cast<const uint4*>(in + full_offset(L, q, o))
-                                                         : make_uint4(0, 0, 0, 0);
-      }
+      unit_loop(u0, u1,
+                [&](long long u) {
+                  const long long o = u * 16;
+                  return o + 16 <= n ? *reinterpret_cast<const uint4*>(in + full_offset(L, q, o)) : make_uint4(0, 0, 0, 0);
+                },
+                [&](long long u, uint4 v) { *reinterpret_cast<uint4*>(dst + u * 16) = v; });
     } else {
       for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
         uint4 v = make_uint4(0, 0, 0, 0);
@@ -299,10 +300,8 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_reduce_scatter(NvlsDev d,
     unit_range((n + 15) / 16, &u0, &u1);
     const uint8_t* src = d.mc + L.region[d.rank];
     const bool scaled = scale != 1.0f;
-    for (long long u = u0 + threadIdx.x; u < u1; u += blockDim.x) {
-      const uint4 v = mm_ld_reduce<DT>(src + u * 16);
-      store_unit(out, u, n, scaled ? scale16<DT>(v, scale) : v);
-    }
+    unit_loop(u0, u1, [&](long long u) { return mm_ld_reduce<DT>(src + u * 16); },
+              [&](long long u, uint4 v) { store_unit(out, u, n, scaled ? scale16<DT>(v, scale) : v); });
   }
   block_signal(d, kNvlsSeq + b);
 }

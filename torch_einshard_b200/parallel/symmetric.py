@@ -45,8 +45,15 @@ __all__ = ["Communicator", "activate", "deactivate", "communicator_for_group", "
 
 _DEFAULT_MB = int(os.environ.get("EINSHARD_SYMM_MB", "64"))
 # Block count of every NVLS collective on a heap (the per-block counters are
-# shared by all collectives of the heap, so it is fixed when the heap is made).
-_NVLS_BLOCKS = int(os.environ.get("EINSHARD_NVLS_BLOCKS", "32"))
+# shared by all collectives of the heap, so it is fixed when the heap is made);
+# 0: two per SM, which keeps enough 16-byte loads and multimem operations in
+# flight to reach the link rate (32 blocks measured 150 GB/s for a 512 MiB
+# all-reduce on 2 ranks, a third of NCCL).
+_NVLS_BLOCKS = int(os.environ.get("EINSHARD_NVLS_BLOCKS", "0"))
+# A two-shot NVLS all-reduce moves N (1 + 1/P) bytes over each GPU's links
+# against 2 N (P - 1) / P for a ring: more at P = 2, less from P = 4 on.  Below
+# this group size, all-reduces of _NCCL_AR_MIN_BYTES and more go to NCCL.
+_NVLS_AR_MIN_RANKS = int(os.environ.get("EINSHARD_NVLS_AR_MIN_RANKS", "4"))
 _NVLS = os.environ.get("EINSHARD_NVLS", "1") not in ("0", "")
 # Without multicast: 512 MiB all-reduce at 8 ranks on B200, the two-shot copy
 # kernel 2.19 ms, NCCL 1.34 ms; NCCL takes the buffers of this size and more.
@@ -77,12 +84,21 @@ def _unique_tag(group):
     return tag[0]
 
 
+def _nvls_blocks(group, device):
+    """The heap's NVLS block count, the same on every rank (minimum over ranks)."""
+    want = _NVLS_BLOCKS or 2 * torch.cuda.get_device_properties(device).multi_processor_count
+    t = torch.tensor([min(1024, max(1, want))], dtype=torch.int32, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN, group=group)
+    return int(t.item())
+
+
 def _create_heap(mod, group, data_bytes, device, want_mc):
     """Collective creation of a heap communicator; its id, or None when any
     rank failed (then no rank keeps one)."""
     rank, size = dist.get_rank(group), dist.get_world_size(group)
+    blocks = _nvls_blocks(group, device)
     tag = _unique_tag(group)
-    cid, err = mod.symm_prepare(int(data_bytes), device, tag, rank, size, bool(want_mc), _NVLS_BLOCKS)
+    cid, err = mod.symm_prepare(int(data_bytes), device, tag, rank, size, bool(want_mc), blocks)
     phases = (lambda: mod.symm_exchange(cid, 120.0), lambda: mod.symm_bind(cid), lambda: mod.symm_finish(cid))
     errors = [err]
     ok = _agree(group, err == "")
@@ -350,7 +366,7 @@ class Communicator:
         nbytes = t.numel() * t.element_size()
         if nbytes == 0:
             return True
-        if self.nvls:
+        if self.nvls and (self.size >= _NVLS_AR_MIN_RANKS or nbytes < _NCCL_AR_MIN_BYTES):
             return self._nvls_all_reduce(t, scale)
         if nbytes >= _NCCL_AR_MIN_BYTES:
             # without multicast, measured on 2 ranks (bf16): NCCL 0.026 / 0.056 / 0.28 / 0.99 ms
