@@ -138,7 +138,7 @@ struct ReduceJob {
   int rank, size;
   uint32_t epoch;
   int clusters;        // reducer clusters at the front of the grid
-  int red_warps;       // warps of each reducer CTA that reduce; the others copy out
+  int red_warps;       // unused (warp 0 of a reducer CTA copies out, the others reduce)
   int seg, shard;      // reduce-scatter (seg > 0): out holds this rank's rows only, [M / P][ldo]
   int* err;
   uint64_t timeout_ns;
@@ -146,7 +146,6 @@ struct ReduceJob {
 
 constexpr int kRowsInFlight = 32;  // a whole unit (16 KB per warp) in flight
 
-// Reduce and copy-out roles of the first job.clusters clusters.
 // One unit owned by this rank: wait until every rank's partial is in its heap,
 // sum it in the switch, then either multicast the sum back into every rank's
 // heap (all-reduce) or store it into this rank's rows of the output
@@ -199,81 +198,119 @@ __device__ __forceinline__ bool reduce_unit(const ReduceJob& j, const GemmShape&
   return true;
 }
 
-// Reduce and copy-out roles of the first job.clusters clusters.
-__device__ void reducer_role(const ReduceJob& j, const GemmShape& s, int cta, int ncta) {
+constexpr int kCopySlots = 8;            // 16 KB units in flight per reducer CTA's copy warp
+constexpr int kUnitBytes = 32 * kBN * 2;  // 32 rows x 256 columns of bf16
+
+// Copy warp of a reducer CTA (lane 0 drives the TMA engine): for the units
+// u = cta, cta + ncta, ... it waits until the unit's owner reduced it, then
+// (all-reduce) moves it from the heap to the output through shared memory with
+// TMA bulk tensor copies, up to kCopySlots units in flight; in reduce-scatter
+// mode it only waits.  When it returns, every peer's access to this rank's
+// heap for the call is over.
+__device__ void copy_role(const ReduceJob& j, const GemmShape& s, const CUtensorMap* tm_heap,
+                          const CUtensorMap* tm_out, int cta, int ncta) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(ring + kCopySlots * kUnitBytes);
+  if ((threadIdx.x & 31) != 0) return;
+  for (int i = 0; i < kCopySlots; ++i) mbar_init(&bars[i], 1);
+  fence_mbar_init();
+  const bool copy = j.seg == 0;
+  long long issued = 0, stored = 0;  // unit counts along u = cta + k ncta (in-range units only)
+  int pending_row[kCopySlots], pending_col[kCopySlots];
+  long long next = cta;
+  int dummy_abort = 0;
+  for (;;) {
+    // issue loads while slots are free
+    while (copy ? issued - stored < kCopySlots : true) {
+      int row0 = 0, col0 = 0;
+      while (next < j.units) {
+        unit_origin(s, next, &row0, &col0);
+        if (row0 < s.M && col0 < s.N) break;
+        next += ncta;
+      }
+      if (next >= j.units) break;
+      if (!wait_epoch(j.reduced + next, j.epoch, j.timeout_ns)) {
+        atomicCAS(j.err, 0, kErrWaitPeerFlag);
+        bulk_wait_group<0>();
+        return;
+      }
+      next += ncta;
+      if (!copy) continue;
+      fence_proxy_async_global();  // the sums arrived as generic stores; the TMA load is an async-proxy read
+      const int slot = static_cast<int>(issued % kCopySlots);
+      if (issued >= kCopySlots) bulk_wait_group_read<0>();  // the slot's last store has read its bytes
+      uint8_t* buf = ring + slot * kUnitBytes;
+      mbar_arrive_expect_tx(&bars[slot], kUnitBytes);
+#pragma unroll
+      for (int b = 0; b < kBN / 64; ++b) tma_load_3d(buf + b * 4096, tm_heap, &bars[slot], col0 + 64 * b, row0, 0);
+      pending_row[slot] = row0;
+      pending_col[slot] = col0;
+      ++issued;
+    }
+    if (!copy || stored == issued) break;
+    // store the oldest loaded unit
+    const int slot = static_cast<int>(stored % kCopySlots);
+    const uint32_t parity = static_cast<uint32_t>((stored / kCopySlots) & 1);
+    if (!mbar_wait(&bars[slot], parity, &dummy_abort, j.err, kErrWaitFull)) {
+      bulk_wait_group<0>();
+      return;
+    }
+    uint8_t* buf = ring + slot * kUnitBytes;
+#pragma unroll
+    for (int b = 0; b < kBN / 64; ++b)
+      tma_store_3d(tm_out, buf + b * 4096, pending_col[slot] + 64 * b, pending_row[slot], 0);
+    bulk_commit_group();
+    ++stored;
+  }
+  bulk_wait_group<0>();
+}
+
+// Reduce and copy-out roles of the first job.clusters clusters: warp 0 copies
+// out (copy_role), the other warps reduce the units this rank owns.
+__device__ void reducer_role(const ReduceJob& j, const GemmShape& s, const CUtensorMap* tm_heap,
+                             const CUtensorMap* tm_out, int cta, int ncta) {
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
-  if (warp < j.red_warps) {
-    const long long gw = static_cast<long long>(cta) * j.red_warps + warp;
-    const long long W = static_cast<long long>(ncta) * j.red_warps;
-    if (!j.seg) {
-      for (long long k = gw;; k += W) {
-        const long long u = j.rank + k * j.size;
-        if (u >= j.units) break;
-        int row0, col0;
-        unit_origin(s, u, &row0, &col0);
-        if (row0 >= s.M || col0 >= s.N) continue;
-        if (!reduce_unit(j, s, u, row0, col0, lane)) return;
-      }
-    } else {
-      // the units whose rows this rank owns, in unit order, found 32 at a time
-      long long k = 0;
-      for (long long base = 0; base < j.units; base += 32) {
-        const long long u = base + lane;
-        int row0 = 0, col0 = 0;
-        bool mine = false;
-        if (u < j.units) {
-          unit_origin(s, u, &row0, &col0);
-          mine = row0 < s.M && col0 < s.N && unit_owner(u, row0, j.size, j.seg, j.shard) == j.rank;
-        }
-        unsigned m = __ballot_sync(0xffffffffu, mine);
-        while (m) {
-          const int bit = __ffs(m) - 1;
-          m &= m - 1;
-          if (k % W == gw) {
-            int r0, c0;
-            unit_origin(s, base + bit, &r0, &c0);
-            if (!reduce_unit(j, s, base + bit, r0, c0, lane)) return;
-          }
-          ++k;
-        }
-      }
-    }
-  } else {
-    // every unit: wait until its owner reduced it, then (all-reduce) copy the sum
-    // from the heap into the output; when these waits end, no peer touches this
-    // rank's heap for the call any more
-    const int ncw = nwarps - j.red_warps;
-    const long long gw = static_cast<long long>(cta) * ncw + (warp - j.red_warps);
-    const long long W = static_cast<long long>(ncta) * ncw;
-    for (long long u = gw; u < j.units; u += W) {
+  if (warp == 0) {
+    copy_role(j, s, tm_heap, tm_out, cta, ncta);
+    return;
+  }
+  const int red_warps = nwarps - 1;
+  const long long gw = static_cast<long long>(cta) * red_warps + (warp - 1);
+  const long long W = static_cast<long long>(ncta) * red_warps;
+  if (!j.seg) {
+    for (long long k = gw;; k += W) {
+      const long long u = j.rank + k * j.size;
+      if (u >= j.units) break;
       int row0, col0;
       unit_origin(s, u, &row0, &col0);
       if (row0 >= s.M || col0 >= s.N) continue;
-      bool ok = true;
-      if (lane == 0) ok = wait_epoch(j.reduced + u, j.epoch, j.timeout_ns);
-      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) {
-        if (lane == 0) atomicCAS(j.err, 0, kErrWaitPeerFlag);
-        return;
+      if (!reduce_unit(j, s, u, row0, col0, lane)) return;
+    }
+    return;
+  }
+  // reduce-scatter: the units whose rows this rank owns, in unit order, found 32 at a time
+  long long k = 0;
+  for (long long base = 0; base < j.units; base += 32) {
+    const long long u = base + lane;
+    int row0 = 0, col0 = 0;
+    bool mine = false;
+    if (u < j.units) {
+      unit_origin(s, u, &row0, &col0);
+      mine = row0 < s.M && col0 < s.N && unit_owner(u, row0, j.size, j.seg, j.shard) == j.rank;
+    }
+    unsigned m = __ballot_sync(0xffffffffu, mine);
+    while (m) {
+      const int bit = __ffs(m) - 1;
+      m &= m - 1;
+      if (k % W == gw) {
+        int r0, c0;
+        unit_origin(s, base + bit, &r0, &c0);
+        if (!reduce_unit(j, s, base + bit, r0, c0, lane)) return;
       }
-      if (j.seg) continue;
-      const int col = col0 + lane * 8;
-      const int rows = es_min(32, s.M - row0);
-      if (col < s.N) {
-        const uint8_t* src = j.uc + (static_cast<long long>(row0) * j.ldh + col) * 2;
-        uint8_t* dst = j.out + (static_cast<long long>(row0) * j.ldo + col) * 2;
-        const long long sp = j.ldh * 2, dp = j.ldo * 2;
-        for (int r0 = 0; r0 < rows; r0 += kRowsInFlight) {
-          uint4 v[kRowsInFlight];
-#pragma unroll
-          for (int i = 0; i < kRowsInFlight; ++i)
-            if (r0 + i < rows) v[i] = *reinterpret_cast<const uint4*>(src + (r0 + i) * sp);
-#pragma unroll
-          for (int i = 0; i < kRowsInFlight; ++i)
-            if (r0 + i < rows) *reinterpret_cast<uint4*>(dst + (r0 + i) * dp) = v[i];
-        }
-      }
+      ++k;
     }
   }
 }
@@ -284,7 +321,7 @@ __global__ void __launch_bounds__(kThreads3, 1)
                         const GemmShape shp, PartialEpilogue epi, const ReduceJob job) {
   const int cluster = static_cast<int>(cluster_id_x());
   if (cluster < job.clusters) {
-    reducer_role(job, shp, cluster * 2 + static_cast<int>(cluster_ctarank()), job.clusters * 2);
+    reducer_role(job, shp, &tmC, &tmW, cluster * 2 + static_cast<int>(cluster_ctarank()), job.clusters * 2);
     return;
   }
   gemm_tc3_body(tmA, tmB, tmC, tmW, shp, epi, NoGather{}, cluster - job.clusters,
@@ -314,7 +351,9 @@ int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& nj, cudaStr
   gh.ldc = g.N;
   gh.c_batch_stride = 0;
   if (!make_output_map(gh, false, &mc)) return static_cast<int>(cudaErrorInvalidValue);
+  // the output map (all-reduce copy-out target) travels in the stream-K workspace slot
   memset(&mw, 0, sizeof(mw));
+  if (nj.seg == 0 && !make_output_map(g, false, &mw)) return static_cast<int>(cudaErrorInvalidValue);
   GemmShape s = make_shape(g);
   s.num_m = (g.M + 2 * kBM - 1) / (2 * kBM);
   s.num_n = (g.N + kBN3 - 1) / kBN3;
