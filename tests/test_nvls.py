@@ -38,9 +38,10 @@ def _body(rank, world):
     g = torch.Generator(device="cuda").manual_seed(100 + rank)
 
     def nccl_sum(x, scale=1.0):
-        y = x.clone()
+        """The fp32 sum over ranks (the oracle: a bf16 ring rounds at every step)."""
+        y = x.float()
         dist.all_reduce(y, group=group)
-        return y * scale if scale != 1.0 else y
+        return (y * scale if scale != 1.0 else y)
 
     tol = {torch.bfloat16: 2e-2, torch.float16: 5e-3, torch.float32: 1e-5}
     sizes = [8, 500, 128 << 10, (1 << 20) + 9, 3 << 20]
@@ -50,17 +51,17 @@ def _body(rank, world):
             want = nccl_sum(x)
             got = x.clone()
             assert comm.all_reduce_(got)
-            torch.testing.assert_close(got, want, rtol=tol[dtype], atol=tol[dtype] * world)
+            torch.testing.assert_close(got.float(), want, rtol=tol[dtype], atol=tol[dtype] * world)
         x = torch.randn(4096, 33, device="cuda", dtype=dtype, generator=g)
         got = x.clone()
         assert comm.all_reduce_(got, 1.0 / world)
-        torch.testing.assert_close(got, nccl_sum(x, 1.0 / world), rtol=tol[dtype], atol=tol[dtype])
+        torch.testing.assert_close(got.float(), nccl_sum(x, 1.0 / world), rtol=tol[dtype], atol=tol[dtype])
 
     # larger than the default heap: grows the group's workspace, runs in pieces
     big = torch.randn(80 << 20, device="cuda", dtype=torch.bfloat16, generator=g)
     want = nccl_sum(big)
     assert comm.all_reduce_(big)
-    torch.testing.assert_close(big, want, rtol=2e-2, atol=2e-2 * world)
+    torch.testing.assert_close(big.float(), want, rtol=2e-2, atol=2e-2 * world)
 
     # uneven all-gather / reduce-scatter along an inner (byte path) and the outer dimension
     for dtype in (torch.bfloat16, torch.float32):
@@ -82,7 +83,7 @@ def _body(rank, world):
             got = comm.reduce_scatter(full, dim, shapes)
             want = nccl_sum(full).narrow(dim, sum(shapes[:rank]), shapes[rank])
             t = 2e-2 if dtype == torch.bfloat16 else 1e-5
-            torch.testing.assert_close(got, want, rtol=t, atol=t * world)
+            torch.testing.assert_close(got.float(), want, rtol=t, atol=t * want.abs().max().item())
 
     # broadcast from each rank (NVLS: the source multicasts, every rank copies out)
     for src in range(world):

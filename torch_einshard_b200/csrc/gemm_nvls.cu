@@ -72,10 +72,15 @@ __device__ __forceinline__ uint32_t ld_acquire_sys_u32(const uint32_t* p) {
 }
 
 // Bounded wait of one thread until *p >= target (epochs, wrap-safe).
+// Polls back off with __nanosleep (doubling up to 1 us) so waiting reducer
+// warps issue few instructions and draw little power next to the GEMM.
 __device__ __forceinline__ bool wait_epoch(const uint32_t* p, uint32_t target, uint64_t timeout_ns) {
   if (static_cast<int>(ld_acquire_sys_u32(p) - target) >= 0) return true;
   const uint64_t t0 = global_timer_ns();
+  uint32_t nap = 32;
   while (static_cast<int>(ld_acquire_sys_u32(p) - target) < 0) {
+    __nanosleep(nap);
+    if (nap < 1024) nap <<= 1;
     if (global_timer_ns() - t0 > timeout_ns) return false;
   }
   return true;

@@ -113,7 +113,10 @@ __device__ __forceinline__ bool block_wait(const NvlsDev& d, int slot, uint32_t 
     const uint32_t* f = d.flags + slot;
     if (static_cast<int>(ld_acquire_sys_u32(f) - target) < 0) {
       const uint64_t t0 = global_timer_ns();
+      uint32_t nap = 32;
       while (static_cast<int>(ld_acquire_sys_u32(f) - target) < 0) {
+        __nanosleep(nap);
+        if (nap < 512) nap <<= 1;
         if (global_timer_ns() - t0 > d.timeout_ns) {
           atomicCAS(d.err, 0, kErrWaitPeerFlag);
           ok = false;

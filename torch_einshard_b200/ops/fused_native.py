@@ -523,7 +523,7 @@ import os
 _FUSED_NVLS = os.environ.get("EINSHARD_FUSED_NVLS", "1") not in ("0", "")
 # reducer CTA pairs at the front of the fused launch, and how many of each reducer
 # CTA's 10 warps reduce (the others copy reduced units into the output)
-_NVLS_REDUCER_CLUSTERS = int(os.environ.get("EINSHARD_NVLS_REDUCER_CLUSTERS", "8"))
+_NVLS_REDUCER_CLUSTERS = int(os.environ.get("EINSHARD_NVLS_REDUCER_CLUSTERS", "12"))
 _NVLS_REDUCE_WARPS = int(os.environ.get("EINSHARD_NVLS_REDUCE_WARPS", "3"))
 _MAX_FUSED_EPILOGUE_RANKS = int(os.environ.get("EINSHARD_FUSED_EPILOGUE_MAX_RANKS", "0"))
 _MAX_FUSED_GATHER_RANKS = int(os.environ.get("EINSHARD_FUSED_GATHER_MAX_RANKS", "2"))
