@@ -37,8 +37,8 @@ def main():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--arms", default="fused,gemm+nvls,gemm+nccl,torch+nccl")
     p.add_argument("--reducers", default="", help="comma list of reducer CTA-pair counts to time the fused arm with "
-                                                   "(arms fused-R<n>); empty: the default")
-    p.add_argument("--reduce-warps", type=int, default=0, help="reduce warps per reducer CTA (0: default)")
+                                                   "(arms fused-R<n>; 0 = overlap mode); empty: the default")
+    p.add_argument("--lags", default="", help="comma list of overlap-mode lags (arms fused-L<n>; 0 = auto)")
     args = p.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -77,8 +77,6 @@ def main():
         return out
 
     arms = {"fused": fused, "gemm+nvls": gemm_nvls, "gemm+nccl": gemm_nccl, "torch+nccl": torch_nccl}
-    if args.reduce_warps:
-        fused_native._NVLS_REDUCE_WARPS = args.reduce_warps
     names = args.arms.split(",")
     for r in [int(v) for v in args.reducers.split(",") if v]:
         def fused_r(r=r):
@@ -86,6 +84,13 @@ def main():
             return fused_native.gemm_allreduce_nvls(comm, a, b)
         arms[f"fused-R{r}"] = fused_r
         names.append(f"fused-R{r}")
+    for lag in [int(v) for v in args.lags.split(",") if v]:
+        def fused_l(lag=lag):
+            fused_native._NVLS_REDUCER_CLUSTERS = 0
+            fused_native._NVLS_LAG = lag
+            return fused_native.gemm_allreduce_nvls(comm, a, b)
+        arms[f"fused-L{lag}"] = fused_l
+        names.append(f"fused-L{lag}")
     sampler = ClockSampler(visible_gpu_indices(world)) if rank == 0 else None
     if sampler:
         sampler.start()

@@ -5,7 +5,9 @@ all-reduced by NCCL, on 2, 4 and 8 GPUs.
 Ragged shapes (rows and columns that end inside a unit), both operand
 layouts, calls of alternating shapes on one heap (the per-unit epochs), the
 fused call between NVLS collectives and copy-protocol kernels on the same heap,
-the reduce-scatter mode (row segments), and the TP-MLP through the public API
+the reduce-scatter mode (row segments), both reduction modes (dedicated
+reducer CTA pairs; the GEMM's epilogue warps with several lags, the product
+spanning more than one wave of CTA pairs), and the TP-MLP through the public API
 (forward and backward) against the unfused NCCL path.
 """
 
@@ -35,6 +37,7 @@ def _body(rank, world):
     comm = symmetric.communicator_for(group)
     assert comm is not None and comm.nvls, "no NVLS multicast heap"
     g = torch.Generator(device="cuda").manual_seed(7 + rank)
+    defaults = fused_native._NVLS_REDUCER_CLUSTERS, fused_native._NVLS_LAG
 
     def check(a, b):
         got = fused_native.gemm_allreduce_nvls(comm, a, b)
@@ -45,8 +48,13 @@ def _body(rank, world):
         err = (got.float() - want).abs().max().item()
         assert err <= 2e-2 * scale, (tuple(a.shape), tuple(b.shape), err, scale)
 
-    shapes = [(512, 1024, 256), (300, 712, 136), (2048, 4096, 1024), (256, 512, 64), (777, 1032, 320)]
-    for _ in range(2):
+    shapes = [(512, 1024, 256), (300, 712, 136), (2048, 4096, 1024), (256, 512, 64), (777, 1032, 320),
+              (4096, 4096, 256)]
+    # (reducer CTA pairs, lag): dedicated reducers, and overlap mode (the GEMM's
+    # epilogue warps reduce) with the automatic lag and lags inside one wave
+    modes = [(12, 0), (0, 0), (0, 1), (0, 5)]
+    for rep in range(2 * len(modes)):
+        fused_native._NVLS_REDUCER_CLUSTERS, fused_native._NVLS_LAG = modes[rep % len(modes)]
         for m, n, k in shapes:
             a = torch.randn(1, m, k, device="cuda", dtype=torch.bfloat16, generator=g)
             b_kn = torch.randn(1, k, n, device="cuda", dtype=torch.bfloat16, generator=g)
@@ -59,7 +67,9 @@ def _body(rank, world):
             part = torch.randn(3, 2 * world, 5, device="cuda", generator=g)
             assert comm.all_to_all(part, 0, 1, [3] * world, [2] * world) is not None
     # reduce-scatter mode: each rank keeps its rows of every segment
-    for m, n, k, seg in [(1024 * world, 1024, 256, 64 * world), (256 * world, 520, 136, 32 * world)]:
+    for (reducers, lag), (m, n, k, seg) in [(md, sh) for md in modes for sh in
+                                            [(1024 * world, 1024, 256, 64 * world), (256 * world, 520, 136, 32 * world)]]:
+        fused_native._NVLS_REDUCER_CLUSTERS, fused_native._NVLS_LAG = reducers, lag
         a = torch.randn(1, m, k, device="cuda", dtype=torch.bfloat16, generator=g)
         b = torch.randn(1, n, k, device="cuda", dtype=torch.bfloat16, generator=g).transpose(1, 2)
         shard = seg // world
@@ -71,6 +81,7 @@ def _body(rank, world):
         assert (got.float() - want).abs().max().item() <= 2e-2 * scale, (m, n, k, seg)
     torch.cuda.synchronize()
     _native.check_errors()
+    fused_native._NVLS_REDUCER_CLUSTERS, fused_native._NVLS_LAG = defaults
 
     # the TP-MLP through the public API: fused NVLS path against NCCL only
     model = TPMLP(1024, 4096, mesh, device="cuda")

@@ -505,13 +505,13 @@ void nvls_reduce_scatter(int64_t id, const at::Tensor& in, at::Tensor out, int64
   g_launches.fetch_add(1, std::memory_order_relaxed);
 }
 
-void launch_gemm_nvls(HostComm& hc, const es::GemmArgs& g, int64_t reducer_clusters, int64_t red_warps, int64_t seg,
+void launch_gemm_nvls(HostComm& hc, const es::GemmArgs& g, int64_t reducer_clusters, int64_t lag, int64_t seg,
                       int64_t shard);
 
 // out (every rank) = sum over the communicator's ranks of (a @ b): the wide GEMM
 // and an NVLS all-reduce of its output units in one launch (gemm_nvls.cu).
 void gemm_allreduce_nvls(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out,
-                         int64_t reducer_clusters, int64_t red_warps, const at::Tensor& err) {
+                         int64_t reducer_clusters, int64_t lag, const at::Tensor& err) {
   HostComm& hc = comm_ref(id);
   TORCH_CHECK(hc.open && hc.mc != nullptr, "einshard fused gemm+NVLS all-reduce: no multicast mapping");
   TORCH_CHECK(a.size(0) == 1 && out.scalar_type() == at::kBFloat16 && a.scalar_type() == at::kBFloat16 &&
@@ -521,10 +521,10 @@ void gemm_allreduce_nvls(int64_t id, const at::Tensor& a, const at::Tensor& b, a
   es::GemmArgs g = gemm_args(a, b, out, 0, err);
   TORCH_CHECK(g.N % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
               "einshard fused gemm+NVLS all-reduce: N must be a multiple of 8");
-  launch_gemm_nvls(hc, g, reducer_clusters, red_warps, 0, 0);
+  launch_gemm_nvls(hc, g, reducer_clusters, lag, 0, 0);
 }
 
-void launch_gemm_nvls(HostComm& hc, const es::GemmArgs& g, int64_t reducer_clusters, int64_t red_warps, int64_t seg,
+void launch_gemm_nvls(HostComm& hc, const es::GemmArgs& g, int64_t reducer_clusters, int64_t lag, int64_t seg,
                       int64_t shard) {
   TORCH_CHECK((size_t)g.M * g.N * 2 <= hc.data_bytes, "einshard fused gemm+NVLS: heap too small");
   TORCH_CHECK(es::gemm_nvls_units(g.M, g.N) <= es::kNvlsMaxUnits, "einshard fused gemm+NVLS: too many units");
@@ -539,7 +539,7 @@ void launch_gemm_nvls(HostComm& hc, const es::GemmArgs& g, int64_t reducer_clust
   j.size = hc.size;
   j.epoch = static_cast<uint32_t>(++hc.tile_epoch);
   j.reducer_clusters = static_cast<int>(reducer_clusters);
-  j.red_warps = static_cast<int>(red_warps);
+  j.lag = static_cast<int>(lag);
   j.seg = static_cast<int>(seg);
   j.shard = static_cast<int>(shard);
   j.timeout_ns = g_wait_timeout_ns;
@@ -552,7 +552,7 @@ void launch_gemm_nvls(HostComm& hc, const es::GemmArgs& g, int64_t reducer_clust
 // (a @ b) along row segments: rows [seg i + rank shard, + shard) of every
 // segment i; the wide GEMM and the NVLS reduction in one launch.
 void gemm_reducescatter_nvls(int64_t id, const at::Tensor& a, const at::Tensor& b, at::Tensor out, int64_t seg,
-                             int64_t shard, int64_t reducer_clusters, int64_t red_warps, const at::Tensor& err) {
+                             int64_t shard, int64_t reducer_clusters, int64_t lag, const at::Tensor& err) {
   HostComm& hc = comm_ref(id);
   TORCH_CHECK(hc.open && hc.mc != nullptr, "einshard fused gemm+NVLS reduce-scatter: no multicast mapping");
   TORCH_CHECK(a.size(0) == 1 && a.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16 &&
@@ -570,7 +570,7 @@ void gemm_reducescatter_nvls(int64_t id, const at::Tensor& a, const at::Tensor& 
   TORCH_CHECK(why == nullptr, "einshard fused gemm+NVLS reduce-scatter: ", why ? why : "");
   TORCH_CHECK(g.N % 8 == 0 && (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0,
               "einshard fused gemm+NVLS reduce-scatter: N must be a multiple of 8");
-  launch_gemm_nvls(hc, g, reducer_clusters, red_warps, seg, shard);
+  launch_gemm_nvls(hc, g, reducer_clusters, lag, seg, shard);
 }
 
 // out = all-reduce over the communicator's ranks of (a @ b); one fused kernel.

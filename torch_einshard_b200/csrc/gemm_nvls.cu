@@ -97,39 +97,12 @@ __device__ __forceinline__ void unit_origin(const GemmShape& s, long long u, int
   *col0 = c.n0 + half * kBN;
 }
 
-// Epilogue of the GEMM clusters: the plain TMA-store epilogue into the heap,
-// then the unit's ready word on its owner.
 // Owner of a unit: all-reduce (seg == 0): u mod P; reduce-scatter: the rank
 // whose rows the unit holds (rows [seg i + p shard, seg i + (p + 1) shard) are
 // rank p's; shard is a multiple of the 32-row unit height).
 __device__ __forceinline__ int unit_owner(long long u, int row0, int size, int seg, int shard) {
   return seg ? (row0 % seg) / shard : static_cast<int>(u % size);
 }
-
-struct PartialEpilogue {
-  StoreEpilogue<__nv_bfloat16> store;
-  uint64_t ready[kMaxRanks];  // each rank's ready[0][0] (peer-mapped)
-  int rank, size;
-  uint32_t epoch;
-  int seg, shard;             // reduce-scatter row segments (seg == 0: all-reduce)
-
-  __device__ __forceinline__ void setup(int*, const GemmShape&) {}
-  __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
-  __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape& s, volatile int* abort_flag) {
-    store.tile(et, s, abort_flag);
-    const int half = (et.c.n0 / kBN) & 1;
-    const long long u = static_cast<long long>(et.t) * 8 + half * 4 + et.q;
-    if (et.lane == 0) {
-      bulk_wait_group<0>();        // the unit's TMA stores have completed
-      fence_proxy_async_global();  // ... and are ordered before generic-proxy accesses
-      fence_acq_rel_sys();
-      const int owner = unit_owner(u, et.c.m0 + et.q * 32, size, seg, shard);
-      st_release_sys_u32(reinterpret_cast<uint32_t*>(ready[owner]) + u * size + rank, epoch);
-    }
-    __syncwarp();
-    return true;
-  }
-};
 
 struct ReduceJob {
   uint8_t* uc;         // this rank's partial / reduced C in the heap, bf16 [M][ldh]
@@ -143,18 +116,18 @@ struct ReduceJob {
   int rank, size;
   uint32_t epoch;
   int clusters;        // reducer clusters at the front of the grid
-  int red_warps;       // unused (warp 0 of a reducer CTA copies out, the others reduce)
   int seg, shard;      // reduce-scatter (seg > 0): out holds this rank's rows only, [M / P][ldo]
   int* err;
   uint64_t timeout_ns;
 };
 
-constexpr int kRowsInFlight = 32;  // a whole unit (16 KB per warp) in flight
+constexpr int kRowsInFlight = 32;  // reducer warps: a whole unit (16 KB per warp) in flight
 
 // One unit owned by this rank: wait until every rank's partial is in its heap,
 // sum it in the switch, then either multicast the sum back into every rank's
 // heap (all-reduce) or store it into this rank's rows of the output
 // (reduce-scatter), and multicast reduced[u] = epoch.  False on a timeout.
+template <int kRows = kRowsInFlight>
 __device__ __forceinline__ bool reduce_unit(const ReduceJob& j, const GemmShape& s, long long u, int row0, int col0,
                                             int lane) {
   bool ok = true;
@@ -180,13 +153,13 @@ __device__ __forceinline__ bool reduce_unit(const ReduceJob& j, const GemmShape&
       dst = j.mc + (static_cast<long long>(row0) * j.ldh + col) * 2;
       dpitch = pitch;
     }
-    for (int r0 = 0; r0 < rows; r0 += kRowsInFlight) {
-      uint4 v[kRowsInFlight];
+    for (int r0 = 0; r0 < rows; r0 += kRows) {
+      uint4 v[kRows];
 #pragma unroll
-      for (int i = 0; i < kRowsInFlight; ++i)
+      for (int i = 0; i < kRows; ++i)
         if (r0 + i < rows) v[i] = ld_reduce_bf16x8(src + (r0 + i) * pitch);
 #pragma unroll
-      for (int i = 0; i < kRowsInFlight; ++i) {
+      for (int i = 0; i < kRows; ++i) {
         if (r0 + i >= rows) continue;
         if (j.seg)
           *reinterpret_cast<uint4*>(dst + (r0 + i) * dpitch) = v[i];
@@ -202,6 +175,104 @@ __device__ __forceinline__ bool reduce_unit(const ReduceJob& j, const GemmShape&
   }
   return true;
 }
+
+constexpr int kCopyRowsInFlight = 16;
+
+// Copy-out of one reduced unit by one warp through registers: wait until the
+// unit's owner stored the sum into this rank's heap (reduced[u] = epoch), then
+// move it to the output (all-reduce) or only wait (reduce-scatter: the owner
+// stored its rows itself).  Loads bypass L1 (the sums arrived from the switch).
+__device__ __forceinline__ bool copy_unit(const ReduceJob& j, const GemmShape& s, long long u, int lane) {
+  int row0, col0;
+  unit_origin(s, u, &row0, &col0);
+  if (row0 >= s.M || col0 >= s.N) return true;
+  bool ok = true;
+  if (lane == 0) ok = wait_epoch(j.reduced + u, j.epoch, j.timeout_ns);
+  if (!__shfl_sync(0xffffffffu, ok, 0)) {
+    if (lane == 0) atomicCAS(j.err, 0, kErrWaitPeerFlag);
+    return false;
+  }
+  if (j.seg) return true;
+  const int col = col0 + lane * 8;
+  if (col >= s.N) return true;
+  const int rows = es_min(32, s.M - row0);
+  const uint4* src = reinterpret_cast<const uint4*>(j.uc + (static_cast<long long>(row0) * j.ldh + col) * 2);
+  uint4* dst = reinterpret_cast<uint4*>(j.out + (static_cast<long long>(row0) * j.ldo + col) * 2);
+  const long long sp = j.ldh / 8, dp = j.ldo / 8;  // row pitches in uint4
+  for (int r0 = 0; r0 < rows; r0 += kCopyRowsInFlight) {
+    uint4 v[kCopyRowsInFlight];
+#pragma unroll
+    for (int i = 0; i < kCopyRowsInFlight; ++i)
+      if (r0 + i < rows) v[i] = __ldcg(src + (r0 + i) * sp);
+#pragma unroll
+    for (int i = 0; i < kCopyRowsInFlight; ++i)
+      if (r0 + i < rows) dst[(r0 + i) * dp] = v[i];
+  }
+  return true;
+}
+
+// Epilogue of the GEMM clusters: the plain TMA-store epilogue into the heap,
+// then the unit's ready word on its owner.
+struct PartialEpilogue {
+  StoreEpilogue<__nv_bfloat16> store;
+  ReduceJob job;              // overlap mode: what the epilogue warps reduce and copy out
+  int lag;                    // overlap mode: slot p reduces tile p - lag, copies out tile p - 2 lag (0: off)
+  int tiles;                  // pair tiles of the product
+  uint64_t ready[kMaxRanks];  // each rank's ready[0][0] (peer-mapped)
+  int rank, size;
+  uint32_t epoch;
+  int seg, shard;             // reduce-scatter row segments (seg == 0: all-reduce)
+
+  __device__ __forceinline__ void setup(int*, const GemmShape&) {}
+  __device__ __forceinline__ void finish(const GemmShape&, volatile int*) {}
+  __device__ __forceinline__ bool tile(const EpiTile& et, const GemmShape& s, volatile int* abort_flag) {
+    store.tile(et, s, abort_flag);
+    const int half = (et.c.n0 / kBN) & 1;
+    const long long u = static_cast<long long>(et.t) * 8 + half * 4 + et.q;
+    if (et.lane == 0) {
+      bulk_wait_group<0>();        // the unit's TMA stores have completed
+      fence_proxy_async_global();  // ... and are ordered before generic-proxy accesses
+      fence_acq_rel_sys();
+      const int owner = unit_owner(u, et.c.m0 + et.q * 32, size, seg, shard);
+      st_release_sys_u32(reinterpret_cast<uint32_t*>(ready[owner]) + u * size + rank, epoch);
+    }
+    __syncwarp();
+    return true;
+  }
+
+  // Overlap mode (one tile per cluster, lag > 0): before waiting for its own
+  // accumulator, the pair's 16 epilogue warps reduce the units of tile
+  // slot - lag that this rank owns (warp w: the w-th of them) and copy out
+  // unit w of tile slot - 2 lag.  Both tiles belong to clusters that started
+  // earlier, so the waits point backwards in launch order; the last 2 lag
+  // slots are clusters without a tile.
+  __device__ __forceinline__ void overlap(int slot, int cta, int ewarp, int lane, const GemmShape& s) {
+    if (lag != 0) overlap_slot(slot, cta, ewarp, lane, s);
+  }
+  // out of line: the epilogue loop's registers are saved once per tile rather
+  // than squeezed under the 168-register cap of 10-warp blocks
+  __device__ __noinline__ void overlap_slot(int slot, int cta, int ewarp, int lane, const GemmShape& s) const {
+    if (*reinterpret_cast<volatile int*>(job.err) != 0) return;  // a wait of this call already gave up
+    const int w = cta * kEpiWarps3 + ewarp;
+    const int t = slot - lag;
+    if (t >= 0 && t < tiles) {
+      int k = 0;
+      for (int i = 0; i < 16; ++i) {
+        const long long u = static_cast<long long>(t) * 16 + i;
+        int row0, col0;
+        unit_origin(s, u, &row0, &col0);
+        if (row0 >= s.M || col0 >= s.N || unit_owner(u, row0, size, seg, shard) != rank) continue;
+        if (k++ == w) {
+          // 16 rows in flight: the epilogue warps keep their tile state live
+          if (!reduce_unit<16>(job, s, u, row0, col0, lane)) return;
+          break;
+        }
+      }
+    }
+    const int t2 = slot - 2 * lag;
+    if (t2 >= 0 && t2 < tiles) copy_unit(job, s, static_cast<long long>(t2) * 16 + w, lane);
+  }
+};
 
 constexpr int kCopySlots = 8;            // 16 KB units in flight per reducer CTA's copy warp
 constexpr int kUnitBytes = 32 * kBN * 2;  // 32 rows x 256 columns of bf16
@@ -344,7 +415,10 @@ int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& nj, cudaStr
   if (g.batch != 1 || g.out_dtype != kDtypeBF16 || g.dtype != kDtypeBF16 || g.N % 8 != 0 || g.act != 0)
     return static_cast<int>(cudaErrorInvalidValue);
   const long long units = gemm_nvls_units(g.M, g.N);
-  if (units > kNvlsMaxUnits || nj.reducer_clusters < 1 || nj.red_warps < 1 || nj.red_warps >= kThreads3 / 32)
+  if (units > kNvlsMaxUnits || nj.reducer_clusters < 0 || nj.lag < 0)
+    return static_cast<int>(cudaErrorInvalidValue);
+  // overlap mode (no reducer clusters): register copy-out, 16-byte rows
+  if (nj.reducer_clusters == 0 && (reinterpret_cast<uintptr_t>(g.C) % 16 != 0 || g.ldc % 8 != 0))
     return static_cast<int>(cudaErrorInvalidValue);
   if (nj.seg && (nj.shard % 32 != 0 || nj.shard * nj.size != nj.seg || g.M % nj.seg != 0))
     return static_cast<int>(cudaErrorInvalidValue);
@@ -393,11 +467,19 @@ int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& nj, cudaStr
   job.size = nj.size;
   job.epoch = nj.epoch;
   job.clusters = nj.reducer_clusters;
-  job.red_warps = nj.red_warps;
   job.seg = nj.seg;
   job.shard = nj.shard;
   job.err = g.err;
   job.timeout_ns = nj.timeout_ns;
+  const int pairs = s.num_m * s.num_n;
+  epi.job = job;
+  epi.tiles = pairs;
+  epi.lag = 0;
+  if (nj.reducer_clusters == 0) {
+    // one tile per cluster; slot p reduces tile p - lag: with lag = the pairs
+    // resident at once, tile p - lag finished about when cluster p started
+    epi.lag = es_min(pairs, nj.lag > 0 ? nj.lag : g.num_sms / 2);
+  }
 
   auto kernel = gemm_nvls_ar_kernel;
   static unsigned long long attr_set = 0;
@@ -407,11 +489,11 @@ int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& nj, cudaStr
     cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmem3Bytes);
     attr_set |= 1ull << dev;
   }
-  const int pairs = s.num_m * s.num_n;
   const bool persistent = g.persistent > 0 || (g.persistent < 0 && s.num_kb <= 32);
   int gemm_clusters = g.num_sms / 2 - nj.reducer_clusters;
   if (gemm_clusters < 1) return static_cast<int>(cudaErrorInvalidValue);
   if (pairs < gemm_clusters || !persistent) gemm_clusters = pairs;
+  if (epi.lag > 0) gemm_clusters = pairs + 2 * epi.lag;  // the last 2 lag slots hold no tile
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2 * (gemm_clusters + nj.reducer_clusters));
   cfg.blockDim = dim3(kThreads3);

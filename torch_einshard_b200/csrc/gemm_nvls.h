@@ -17,8 +17,9 @@ struct NvlsGemmJob {
   uint32_t* reduced_mc = nullptr;
   int rank = 0, size = 1;
   uint32_t epoch = 1;            // this call's number on the heap (>= 1, same on every rank)
-  int reducer_clusters = 4;      // CTA pairs that reduce and copy out
-  int red_warps = 3;             // of the 10 warps of each reducer CTA, how many reduce
+  int reducer_clusters = 4;      // CTA pairs that reduce and copy out (0: overlap mode, the GEMM's
+                                 // epilogue warps reduce and copy out during later tiles' mainloops)
+  int lag = 0;                   // overlap mode: tiles between a tile and its reduction (0: auto)
   int seg = 0, shard = 0;        // reduce-scatter: rows [seg i + p shard, + shard) go to rank p (seg 0: all-reduce)
   uint64_t timeout_ns = 4000000000ull;
 };

@@ -30,6 +30,9 @@
 // a plain launch limited to sk_first tiles.
 #pragma once
 
+#include <type_traits>
+#include <utility>
+
 #include "gemm_tc.cuh"
 
 namespace es {
@@ -162,6 +165,21 @@ struct NoGather {
   __device__ __forceinline__ void copy(int, int, volatile int*) const {}
   __device__ __forceinline__ void finish(bool) const {}
 };
+
+// Optional epilogue-policy hook `overlap(slot, cta, ewarp, lane, shape)`:
+// work the epilogue warps do for schedule slot `slot` (the cluster index)
+// before they wait for the accumulator, i.e. overlapped with the slot's
+// mainloop; clusters with no tile call it once.  Policies without it do nothing.
+template <class E, class = void>
+struct HasOverlap : std::false_type {};
+template <class E>
+struct HasOverlap<E, std::void_t<decltype(std::declval<E&>().overlap(0, 0, 0, 0, std::declval<const GemmShape&>()))>>
+    : std::true_type {};
+
+template <class Epi>
+__device__ __forceinline__ void epilogue_overlap(Epi& epi, int slot, int cta, int ewarp, int lane, const GemmShape& s) {
+  if constexpr (HasOverlap<Epi>::value) epi.overlap(slot, cta, ewarp, lane, s);
+}
 
 // The kernel body, for `nclusters` clusters of which this is number `cluster`
 // (kernels that give some clusters another role run it with offset indices).
@@ -334,11 +352,15 @@ __device__ __forceinline__ void gemm_tc3_body(const CUtensorMap& tmA, const CUte
     const int q = warp & 3;           // TMEM lane quadrant this warp may access
     const int half = (warp - 2) >> 2;  // 256-column half of the tile
     uint32_t tc = 0;
+    bool any_tile = false;
     TileCoord ce;
     int pidx, kb0, kb1;
     SegIter seg = seg_begin(shp, cluster);
     for (; seg_next(shp, cluster, nclusters, static_cast<int>(rank), seg, &ce, &pidx, &kb0, &kb1); ++tc) {
+      any_tile = true;
       ce.m0 = gather.map_m0(ce.m0);
+      // work the policy overlaps with this tile's mainloop (while the accumulator fills)
+      epilogue_overlap(epi, cluster, static_cast<int>(rank), warp - 2, lane, shp);
       if (!mbar_wait_sleepy(&st->tfull_[0], tc & 1u, abort_flag, shp.err, kErrWaitTmemFull, shp.sleep_ns)) break;
       tc_fence_after();
       EpiTile et;
@@ -361,6 +383,7 @@ __device__ __forceinline__ void gemm_tc3_body(const CUtensorMap& tmA, const CUte
         break;
       }
     }
+    if (!any_tile) epilogue_overlap(epi, cluster, static_cast<int>(rank), warp - 2, lane, shp);  // clusters without a tile
     epi.finish(shp, abort_flag);
     if (lane == 0) bulk_wait_group<0>();  // every TMA store of this warp has landed
   }

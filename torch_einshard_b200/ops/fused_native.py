@@ -203,7 +203,7 @@ def gemm_allreduce_nvls(comm, a, b):
     a, b = _prepare(a), _prepare(b)
     out = torch.empty((1, m, n), dtype=torch.bfloat16, device=a.device)
     ws.enter("tile")
-    mod.gemm_allreduce_nvls(ws.cid, a, b, out, _NVLS_REDUCER_CLUSTERS, _NVLS_REDUCE_WARPS,
+    mod.gemm_allreduce_nvls(ws.cid, a, b, out, _NVLS_REDUCER_CLUSTERS, _NVLS_LAG,
                             _native.error_word(a.device))
     return out
 
@@ -222,7 +222,7 @@ def gemm_reducescatter_nvls(comm, a, b, seg, shard):
     a, b = _prepare(a), _prepare(b)
     out = torch.empty((1, m // comm.size, n), dtype=torch.bfloat16, device=a.device)
     ws.enter("tile")
-    mod.gemm_reducescatter_nvls(ws.cid, a, b, out, seg, shard, _NVLS_REDUCER_CLUSTERS, _NVLS_REDUCE_WARPS,
+    mod.gemm_reducescatter_nvls(ws.cid, a, b, out, seg, shard, _NVLS_REDUCER_CLUSTERS, _NVLS_LAG,
                                 _native.error_word(a.device))
     return out
 
@@ -521,10 +521,13 @@ class _Fusion:
 import os
 
 _FUSED_NVLS = os.environ.get("EINSHARD_FUSED_NVLS", "1") not in ("0", "")
-# reducer CTA pairs at the front of the fused launch, and how many of each reducer
-# CTA's 10 warps reduce (the others copy reduced units into the output)
+# Who reduces in the fused launch: 0 = the GEMM's own epilogue warps, while
+# later tiles' mainloops run (overlap mode, every SM computes); n > 0 = n CTA
+# pairs at the front of the launch that only reduce and copy out.  _NVLS_LAG:
+# overlap mode's distance in tiles between a tile and its reduction (0: the
+# number of CTA pairs resident at once).
 _NVLS_REDUCER_CLUSTERS = int(os.environ.get("EINSHARD_NVLS_REDUCER_CLUSTERS", "12"))
-_NVLS_REDUCE_WARPS = int(os.environ.get("EINSHARD_NVLS_REDUCE_WARPS", "3"))
+_NVLS_LAG = int(os.environ.get("EINSHARD_NVLS_LAG", "0"))
 _MAX_FUSED_EPILOGUE_RANKS = int(os.environ.get("EINSHARD_FUSED_EPILOGUE_MAX_RANKS", "0"))
 _MAX_FUSED_GATHER_RANKS = int(os.environ.get("EINSHARD_FUSED_GATHER_MAX_RANKS", "2"))
 # Row-parallel all-reduce overlapped with the GEMM in this many row pieces (0: off,
