@@ -1,4 +1,6 @@
-"""Implicit-GEMM conv2d (tcgen05, NHWC) against an fp32 PyTorch reference."""
+"""Implicit-GEMM conv2d (tcgen05, NHWC) against an fp32 PyTorch reference:
+both forward kernels (the CTA-pair kernel with resident weights and the
+weights-streaming kernel), per-side zero padding, backward."""
 
 import pytest
 import torch
@@ -26,8 +28,12 @@ def _close(got, want, tol=2e-2):
 
 
 @pytest.mark.parametrize("B,H,W,C,O,K", [(1, 8, 8, 64, 128, 3), (2, 17, 300, 64, 96, 3), (1, 5, 513, 128, 128, 1),
-                                         (3, 9, 40, 192, 256, 5), (1, 4, 4, 64, 8, 3)])
-def test_conv_forward(B, H, W, C, O, K):
+                                         (3, 9, 40, 192, 256, 5), (1, 4, 4, 64, 8, 3),
+                                         (2, 40, 1000, 128, 128, 3), (1, 10, 70, 64, 256, 7)])
+@pytest.mark.parametrize("kernel", [0, 1])
+def test_conv_forward(B, H, W, C, O, K, kernel, monkeypatch):
+    from torch_einshard_b200.ops import conv_impl
+    monkeypatch.setattr(conv_impl, "_KERNEL", kernel)
     torch.manual_seed(0)
     x = torch.randn(B, H, W, C, device="cuda", dtype=torch.bfloat16)
     w = (torch.randn(O, K, K, C, device="cuda") * 0.05).to(torch.bfloat16)
@@ -125,10 +131,37 @@ def test_conv_weight_gradient_native(B, H, W, C, O, KH, KW, ph, pw):
     Ho, Wo = H + 2 * ph - KH + 1, W + 2 * pw - KW + 1
     dy = torch.randn(B, Ho, Wo, O, device="cuda", dtype=torch.bfloat16)
     dw = torch.empty(O, KH, KW, C, device="cuda", dtype=torch.float32)
-    mod.conv2d_wgrad(x, dy, dw, ph, pw, _native.error_word(x.device))
+    mod.conv2d_wgrad(x, dy, dw, ph, pw, -1, -1, _native.error_word(x.device))
     torch.cuda.synchronize()
     _native.check_errors()
     ref = torch.nn.grad.conv2d_weight(x.float().permute(0, 3, 1, 2), (O, C, KH, KW), dy.float().permute(0, 3, 1, 2),
                                       padding=(ph, pw)).permute(0, 2, 3, 1)
     scale = ref.abs().max().item()
     assert (dw - ref).abs().max().item() <= 1e-4 * scale + 1e-3, (dw - ref).abs().max().item()
+
+
+@pytest.mark.parametrize("kernel", [0, 1])
+@pytest.mark.parametrize("ph,pw", [((1, 0), (0, 1)), ((0, 2), (2, 0)), ((1, 1), (0, 0))])
+def test_conv_per_side_padding_forward_backward(ph, pw, kernel, monkeypatch):
+    """Zero padding that differs per side (the global edge of a sharded axis)."""
+    from torch_einshard_b200.ops import conv_impl
+    monkeypatch.setattr(conv_impl, "_KERNEL", kernel)
+    torch.manual_seed(4)
+    x = torch.randn(2, 11, 300, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(128, 3, 3, 64, device="cuda") * 0.05).to(torch.bfloat16).requires_grad_(True)
+    bias = torch.randn(128, device="cuda", requires_grad=True)
+    y = conv2d_native(x, w, bias, ph, pw)
+    assert y.shape == (2, 11 + sum(ph) - 2, 300 + sum(pw) - 2, 128)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().float().requires_grad_(True)
+    br = bias.detach().clone().requires_grad_(True)
+    xp = F.pad(xr.permute(0, 3, 1, 2), (pw[0], pw[1], ph[0], ph[1]))
+    yr = F.conv2d(xp, wr.permute(0, 3, 1, 2), br).permute(0, 2, 3, 1)
+    yr.backward(g.float())
+    _close(y, yr)
+    _close(x.grad, xr.grad)
+    _close(w.grad, wr.grad)
+    _close(bias.grad, br.grad, tol=1e-3)
+    _native.check_errors()

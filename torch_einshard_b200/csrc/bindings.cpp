@@ -808,8 +808,11 @@ void fft_slab(int64_t id, at::Tensor out, int64_t n, int64_t A, int64_t B, int64
 // ------------------------------------------------------------------ convolution
 
 // out[B, Hout, Wout, O] = conv2d(x[B, Hin, Win, C], w[O, KH, KW, C]) + bias, zero padding (ph, pw).
+// out = conv(x, w) + bias with zero padding (ph, ph_hi) rows and (pw, pw_hi)
+// columns (hi < 0: the same as lo); kernel 0 picks the CTA-pair kernel with
+// resident weights where it fits, 1 forces conv.cu's kernel.
 void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor& bias, at::Tensor out, int64_t ph,
-                     int64_t pw, const at::Tensor& err) {
+                     int64_t pw, int64_t ph_hi, int64_t pw_hi, int64_t kernel, const at::Tensor& err) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda() && x.dim() == 4 && w.dim() == 4 && out.dim() == 4,
               "einshard conv: 4-D CUDA tensors required");
   TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "einshard conv: contiguous NHWC required");
@@ -839,10 +842,13 @@ void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
   a.err = err.data_ptr<int>();
   a.num_sms = num_sms(x.get_device());
   a.persistent = g_small_persistent;
+  a.ph_hi = static_cast<int>(ph_hi);
+  a.pw_hi = static_cast<int>(pw_hi);
+  a.kernel = static_cast<int>(kernel);
   const char* why = es::check_conv_args(a);
   TORCH_CHECK(why == nullptr, "einshard conv: ", why ? why : "");
-  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
-  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  const int Hout = es::conv_hout(a);
+  const int Wout = es::conv_wout(a);
   TORCH_CHECK(out.size(0) == a.B && out.size(1) == Hout && out.size(2) == Wout && out.size(3) == a.O,
               "einshard conv: output shape");
   const c10::cuda::CUDAGuard guard(x.device());
@@ -917,8 +923,8 @@ int64_t comm_data_bytes(int64_t id) { return static_cast<int64_t>(comm_ref(id).d
 
 // dw (fp32 [O][KH][KW][C], zeroed here) = weight gradient of the implicit-GEMM
 // conv with input x [B][Hin][Win][C], output gradient dy [B][Hout][Wout][O].
-void conv2d_wgrad(const at::Tensor& x, const at::Tensor& dy, at::Tensor dw, int64_t ph, int64_t pw,
-                  const at::Tensor& err) {
+void conv2d_wgrad(const at::Tensor& x, const at::Tensor& dy, at::Tensor dw, int64_t ph, int64_t pw, int64_t ph_hi,
+                  int64_t pw_hi, const at::Tensor& err) {
   TORCH_CHECK(x.is_cuda() && dy.is_cuda() && dw.is_cuda() && x.dim() == 4 && dy.dim() == 4 && dw.dim() == 4,
               "einshard conv wgrad: 4-D CUDA tensors required");
   TORCH_CHECK(x.is_contiguous() && dy.is_contiguous() && dw.is_contiguous(), "einshard conv wgrad: contiguous required");
@@ -939,13 +945,15 @@ void conv2d_wgrad(const at::Tensor& x, const at::Tensor& dy, at::Tensor dw, int6
   a.KW = dw.size(2);
   a.ph = static_cast<int>(ph);
   a.pw = static_cast<int>(pw);
+  a.ph_hi = static_cast<int>(ph_hi);
+  a.pw_hi = static_cast<int>(pw_hi);
   a.err = err.data_ptr<int>();
   a.num_sms = num_sms(x.get_device());
   TORCH_CHECK(dw.size(3) == a.C, "einshard conv wgrad: channel mismatch");
   const char* why = es::check_conv_wgrad_args(a);
   TORCH_CHECK(why == nullptr, "einshard conv wgrad: ", why ? why : "");
-  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
-  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  const int Hout = es::conv_hout(a);
+  const int Wout = es::conv_wout(a);
   TORCH_CHECK(dy.size(0) == a.B && dy.size(1) == Hout && dy.size(2) == Wout && dy.size(3) == a.O,
               "einshard conv wgrad: output-gradient shape");
   const c10::cuda::CUDAGuard guard(x.device());

@@ -154,8 +154,8 @@ int launch(const ConvArgs& a, cudaStream_t stream) {
   const uint32_t box[4] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(kBN), 1, 1};
   const CUtensorMap mb = make_tmap_nd(a.x, dt, 4, dims, strides, box);
 
-  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
-  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  const int Hout = conv_hout(a);
+  const int Wout = conv_wout(a);
   const int Wv = (Wout + kBN - 1) / kBN * kBN;
   GemmShape s;
   s.M = a.O;
@@ -280,9 +280,9 @@ const char* check_conv_wgrad_args(const ConvWgradArgs& a) {
   if (a.B <= 0 || a.Hin <= 0 || a.Win <= 0 || a.C <= 0 || a.O <= 0 || a.KH <= 0 || a.KW <= 0)
     return "empty convolution";
   if (a.C % 64 || a.O % 64) return "input and output channels must be multiples of 64";
-  if (a.ph < 0 || a.pw < 0) return "negative padding";
-  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
-  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  if (a.ph < 0 || a.pw < 0 || a.ph_hi < -1 || a.pw_hi < -1) return "negative padding";
+  const int Hout = conv_hout(a);
+  const int Wout = conv_wout(a);
   if (Hout <= 0 || Wout <= 0) return "empty output";
   if ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.dy) | reinterpret_cast<uintptr_t>(a.dw)) & 15)
     return "operands not 16-byte aligned";
@@ -295,8 +295,8 @@ int conv_wgrad_launch(const ConvWgradArgs& a, cudaStream_t stream) {
   if (check_conv_wgrad_args(a)) return -1;
   const CUtensorMapDataType dt = a.dtype == kDtypeBF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
                                                       : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
-  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  const int Hout = conv_hout(a);
+  const int Wout = conv_wout(a);
   const int N = a.KH * a.KW * a.C;
   // A: dY (O, Wout, Hout, B), box 64 channels x 64 columns (MN-major: channels contiguous)
   const uint64_t ady[4] = {static_cast<uint64_t>(a.O), static_cast<uint64_t>(Wout), static_cast<uint64_t>(Hout),
@@ -362,9 +362,9 @@ const char* check_conv_args(const ConvArgs& a) {
   if (a.B <= 0 || a.Hin <= 0 || a.Win <= 0 || a.C <= 0 || a.O <= 0 || a.KH <= 0 || a.KW <= 0)
     return "empty convolution";
   if (a.C % kBK) return "input channels must be a multiple of 64";
-  if (a.ph < 0 || a.pw < 0) return "negative padding";
-  const int Hout = a.Hin + 2 * a.ph - a.KH + 1;
-  const int Wout = a.Win + 2 * a.pw - a.KW + 1;
+  if (a.ph < 0 || a.pw < 0 || a.ph_hi < -1 || a.pw_hi < -1) return "negative padding";
+  const int Hout = conv_hout(a);
+  const int Wout = conv_wout(a);
   if (Hout <= 0 || Wout <= 0) return "empty output";
   if ((reinterpret_cast<uintptr_t>(a.x) | reinterpret_cast<uintptr_t>(a.w)) & 15) return "operands not 16-byte aligned";
   const long long n = static_cast<long long>(a.B) * Hout * ((Wout + kBN - 1) / kBN) * kBN;
@@ -374,6 +374,7 @@ const char* check_conv_args(const ConvArgs& a) {
 
 int conv_launch(const ConvArgs& a, cudaStream_t stream) {
   if (check_conv_args(a)) return -1;
+  if (a.kernel == 0 && conv_pair_eligible(a)) return conv_pair_launch(a, stream);
   return a.dtype == kDtypeBF16 ? launch<__nv_bfloat16>(a, stream) : launch<__half>(a, stream);
 }
 

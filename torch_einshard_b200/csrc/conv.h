@@ -11,17 +11,31 @@ struct ConvArgs {
   const void* x = nullptr;     // [B][Hin][Win][C]
   const void* w = nullptr;     // [O][KH][KW][C]
   const float* bias = nullptr; // [O] or null
-  void* out = nullptr;         // [B][Hout][Wout][O], Hout = Hin + 2 ph - KH + 1
+  void* out = nullptr;         // [B][Hout][Wout][O], Hout = Hin + ph + ph_hi - KH + 1
   int dtype = kDtypeBF16;      // x, w and out share it
   int B = 0, Hin = 0, Win = 0, C = 0, O = 0, KH = 0, KW = 0;
-  int ph = 0, pw = 0;          // zero padding on each side
+  int ph = 0, pw = 0;          // zero padding before the first row / column
+  int ph_hi = -1, pw_hi = -1;  // zero padding after the last (-1: the same as before)
   int* err = nullptr;
   int num_sms = 148;
   int persistent = 1;          // 1 persistent CTAs (default), 0 one tile per CTA (tuning)
+  int kernel = 0;              // 0 auto (the pair kernel with resident weights where it fits), 1 conv.cu's kernel
 };
+
+template <class Args>
+inline int conv_hout(const Args& a) {
+  return a.Hin + a.ph + (a.ph_hi < 0 ? a.ph : a.ph_hi) - a.KH + 1;
+}
+template <class Args>
+inline int conv_wout(const Args& a) {
+  return a.Win + a.pw + (a.pw_hi < 0 ? a.pw : a.pw_hi) - a.KW + 1;
+}
 
 const char* check_conv_args(const ConvArgs& a);
 int conv_launch(const ConvArgs& a, cudaStream_t stream);
+// The CTA-pair kernel with the weights resident in shared memory (conv_pair.cu).
+bool conv_pair_eligible(const ConvArgs& a);
+int conv_pair_launch(const ConvArgs& a, cudaStream_t stream);
 
 // Weight gradient of conv_launch's convolution: dw[o][kh][kw][c] (fp32, must be
 // zero on entry) += sum over output pixels of dy[b][h][w][o] * x[b][h+kh-ph][w+kw-pw][c].
@@ -32,6 +46,7 @@ struct ConvWgradArgs {
   int dtype = kDtypeBF16;      // x and dy share it
   int B = 0, Hin = 0, Win = 0, C = 0, O = 0, KH = 0, KW = 0;
   int ph = 0, pw = 0;
+  int ph_hi = -1, pw_hi = -1;
   int* err = nullptr;
   int num_sms = 148;
 };

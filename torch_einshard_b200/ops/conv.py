@@ -35,7 +35,7 @@ from ..notation.families import cached_expand_axis_families, expand_family_mappi
 from ..notation.parser import parse_sharding
 from ..notation.spec import EllipsisAxis
 from . import conv_impl
-from .halo import halo_tensor, normalize_halo
+from .halo import halo_tensor, halo_tensor_unpadded, normalize_halo, pad_dim
 
 __all__ = ["einconv"]
 
@@ -244,9 +244,9 @@ def _mesh_dim_size(mesh, dim):
 
 
 def _kernel_padded_axes(a, x, mesh, boundary, fill):
-    """Spatial axes whose symmetric zero padding the native kernel applies
-    itself: local axes (and axes sharded over a one-rank mesh dim, which have
-    no neighbours), when the boundary is a zero constant."""
+    """Spatial axes whose zero padding (before, after) the native kernel
+    applies itself: local axes (and axes sharded over a one-rank mesh dim,
+    which have no neighbours), when the boundary is a zero constant."""
     if boundary != "constant" or fill != 0:
         return {}
     if not conv_impl.kernel_padding_ok(x, a.weight, x.shape[a.in_names.index(a.cin)], a.spatial, a.dilation):
@@ -256,8 +256,8 @@ def _kernel_padded_axes(a, x, mesh, boundary, fill):
         left, right = normalize_halo(pad)
         axis = a.axis(a.in_spec, name)
         alone = not axis.local() and mesh is not None and _mesh_dim_size(mesh, axis.shard_dim) == 1
-        if (axis.local() or alone) and left == right:
-            pads[name] = left
+        if axis.local() or alone:
+            pads[name] = (left, right)
     return pads
 
 
@@ -282,14 +282,19 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
     kernel_pads = _kernel_padded_axes(a, x, mesh, boundary, fill)
     exchanged = {n: p for n, p in zip(a.spatial, a.pads) if n not in kernel_pads}
     halo_args = dict(mesh=mesh, shapes=shapes, boundary=boundary, fill=fill)
+    # with a zero boundary the native kernel also supplies the fill at the
+    # global edges of sharded axes: the exchange adds only the neighbours' rows
+    edges_in_kernel = (bool(exchanged) and boundary == "constant" and fill == 0 and
+                       conv_impl.kernel_padding_ok(x, weight, x.shape[a.in_names.index(a.cin)], a.spatial, a.dilation))
+    pads = dict(kernel_pads)
 
     def conv(xa, wa, ba=None):
         out = conv_impl.try_conv(xa, wa, ba, a.in_names, a.w_names, a.out_names, a.spatial, a.kernel, a.cin, a.cout,
-                                 a.dilation, kernel_pads)
+                                 a.dilation, pads)
         if out is not None:
             return out
-        if kernel_pads:  # the torch path pads through the halo builder instead
-            xa = halo_tensor(a.in_spec, xa, kernel_pads, **halo_args)
+        for name, (lo, hi) in pads.items():  # the torch path pads explicitly
+            xa = pad_dim(xa, a.in_names.index(name), lo, hi, boundary="constant", fill=0)
         xc = xa.permute(layout.x_order(False)).contiguous()
         lead = xc.shape[:len(layout.batch)]
         xc = xc.reshape((-1, *xc.shape[len(layout.batch):]))
@@ -298,7 +303,11 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
         return out.reshape((*lead, *out.shape[1:])).permute(layout.out_order(False)).contiguous()
 
     def halo_then_conv(xa, wa, *maybe_bias):
-        haloed = halo_tensor(a.in_spec, xa, exchanged, **halo_args)
+        if edges_in_kernel:
+            haloed, edges = halo_tensor_unpadded(a.in_spec, xa, exchanged, mesh=mesh, shapes=shapes)
+            pads.update(edges)
+        else:
+            haloed = halo_tensor(a.in_spec, xa, exchanged, **halo_args)
         args = (haloed, wa, *maybe_bias)
         if checkpoint == "conv":
             return _checkpointed(conv, args, "conv", use_reentrant)

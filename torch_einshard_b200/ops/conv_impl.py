@@ -5,9 +5,16 @@ here on), so the forward is a valid convolution.  Tensors are brought to NHWC
 (batch axes flattened), weights to [O][KH][KW][C]; the kernel reads the input
 windows straight from the NHWC tensor with shifted TMA boxes (no im2col).
 
-Backward: the input gradient runs on the same kernel as a full correlation of
-dY with the flipped, channel-transposed weights (zero padding KH-1, KW-1 done
-by the TMA zero fill); the weight gradient runs on the split-K implicit-GEMM
+Zero padding may differ per side (``pads`` values are ``p`` or ``(lo, hi)``):
+the einconv path pads only where a sharded axis has no neighbour (the global
+edge) and lets the kernel read zeros there.  Where the weights fit in shared
+memory the forward runs on the CTA-pair kernel with resident weights
+(``csrc/conv_pair.cu``), else on the weights-streaming kernel (``csrc/conv.cu``;
+``EINSHARD_CONV_KERNEL=1`` forces it).
+
+Backward: the input gradient runs on the same kernels as a full correlation of
+dY with the flipped, channel-transposed weights (zero padding KH-1-lo, KH-1-hi
+done by the TMA zero fill); the weight gradient runs on the split-K implicit-GEMM
 kernel (``_C.conv2d_wgrad``: dY and the shifted input windows as MN-major
 operands, fp32 partial tiles added atomically) when both channel counts are
 multiples of 64, else ``torch.nn.grad.conv2d_weight``; the bias gradient is a
@@ -16,20 +23,35 @@ reduction.
 Replaces the reference's ``F.conv2d`` call in ``einconv`` (``src/torch_einshard/conv.py:48-52``).
 """
 
+import os
+
 import torch
 
 from . import _native
 
 __all__ = ["conv2d_nhwc", "conv2d_native", "try_conv", "kernel_padding_ok"]
 
+_KERNEL = int(os.environ.get("EINSHARD_CONV_KERNEL", "0"))
+
+
+def _lohi(p):
+    return (int(p[0]), int(p[1])) if isinstance(p, (tuple, list)) else (int(p), int(p))
+
 
 def _run(mod, x, w, bias, ph, pw):
+    """ph, pw: (lo, hi) zero padding of the rows and the columns."""
     B, H, W, _ = x.shape
     O, KH, KW, _ = w.shape
-    out = torch.empty(B, H + 2 * ph - KH + 1, W + 2 * pw - KW + 1, O, dtype=x.dtype, device=x.device)
+    out = torch.empty(B, H + ph[0] + ph[1] - KH + 1, W + pw[0] + pw[1] - KW + 1, O, dtype=x.dtype, device=x.device)
     b = bias if bias is not None else torch.empty(0, dtype=torch.float32, device=x.device)
-    mod.conv2d_implicit(x, w, b, out, ph, pw, _native.error_word(x.device))
+    mod.conv2d_implicit(x, w, b, out, ph[0], pw[0], ph[1], pw[1], _KERNEL, _native.error_word(x.device))
     return out
+
+
+def _torch_pads(ph, pw):
+    """F.pad / conv padding for the torch fallbacks: symmetric pads as conv padding,
+    asymmetric ones as an explicit F.pad of the NCHW input."""
+    return (ph[0], pw[0]) if ph[0] == ph[1] and pw[0] == pw[1] else None
 
 
 class _Conv2dNHWC(torch.autograd.Function):
@@ -48,21 +70,31 @@ class _Conv2dNHWC(torch.autograd.Function):
         gx = gw = gb = None
         O, KH, KW, C = w.shape
         ph, pw = ctx.pad
+        sym = _torch_pads(ph, pw)
+        xt = x.permute(0, 3, 1, 2)
+        if sym is None and not (O % 64 == 0 and KH - 1 >= max(ph) and KW - 1 >= max(pw)):
+            # the torch fallbacks take symmetric padding only: pad the input explicitly
+            xt = torch.nn.functional.pad(xt, (pw[0], pw[1], ph[0], ph[1]))
+            sym = (0, 0)
         if ctx.needs_input_grad[0]:
-            if O % 64 == 0:
+            if O % 64 == 0 and KH - 1 >= max(ph) and KW - 1 >= max(pw):
                 # full correlation with the flipped, channel-transposed kernel, cropped by the padding
                 wt = w.flip(1, 2).permute(3, 1, 2, 0).contiguous()  # [C][KH][KW][O]
-                gx = _run(_native.require(), grad, wt, None, KH - 1 - ph, KW - 1 - pw)
+                gx = _run(_native.require(), grad, wt, None, (KH - 1 - ph[0], KH - 1 - ph[1]),
+                          (KW - 1 - pw[0], KW - 1 - pw[1]))
             else:
-                gx = torch.nn.grad.conv2d_input(x.permute(0, 3, 1, 2).shape, w.permute(0, 3, 1, 2),
-                                                grad.permute(0, 3, 1, 2), padding=(ph, pw)).permute(0, 2, 3, 1)
+                gx = torch.nn.grad.conv2d_input(xt.shape, w.permute(0, 3, 1, 2), grad.permute(0, 3, 1, 2),
+                                                padding=sym)
+                if xt.shape[2:] != x.shape[1:3]:
+                    gx = gx[:, :, ph[0]:ph[0] + x.shape[1], pw[0]:pw[0] + x.shape[2]]
+                gx = gx.permute(0, 2, 3, 1)
         if ctx.needs_input_grad[1] and O % 64 == 0:
             dw = torch.empty(O, KH, KW, C, dtype=torch.float32, device=x.device)
-            _native.require().conv2d_wgrad(x, grad, dw, ph, pw, _native.error_word(x.device))
+            _native.require().conv2d_wgrad(x, grad, dw, ph[0], pw[0], ph[1], pw[1], _native.error_word(x.device))
             gw = dw.to(w.dtype)
         elif ctx.needs_input_grad[1]:
-            gw = torch.nn.grad.conv2d_weight(x.permute(0, 3, 1, 2), w.permute(0, 3, 1, 2).shape,
-                                             grad.permute(0, 3, 1, 2), padding=(ph, pw)).permute(0, 2, 3, 1)
+            gw = torch.nn.grad.conv2d_weight(xt, w.permute(0, 3, 1, 2).shape, grad.permute(0, 3, 1, 2),
+                                             padding=sym).permute(0, 2, 3, 1)
         if ctx.has_bias and ctx.needs_input_grad[2]:
             gb = grad.float().sum(dim=(0, 1, 2)).to(ctx.bias_dtype)
         return gx, gw, gb, None, None
@@ -74,8 +106,9 @@ def supported(x, w_dtype, cin_size, ndim, dilation):
 
 
 def conv2d_native(x, w, bias=None, ph=0, pw=0):
-    """NHWC conv2d with zero padding (ph, pw): x [B, H, W, C], w [O, KH, KW, C] ->
-    [B, H + 2 ph - KH + 1, W + 2 pw - KW + 1, O]."""
+    """NHWC conv2d with zero padding ph, pw (``p`` or ``(lo, hi)``): x [B, H, W, C],
+    w [O, KH, KW, C] -> [B, H + lo + hi - KH + 1, W + lo + hi - KW + 1, O]."""
+    ph, pw = _lohi(ph), _lohi(pw)
     x, w = x.contiguous(), w.contiguous()
     if torch.is_grad_enabled() and (x.requires_grad or w.requires_grad or (bias is not None and bias.requires_grad)):
         return _Conv2dNHWC.apply(x, w, bias, ph, pw)
@@ -84,7 +117,7 @@ def conv2d_native(x, w, bias=None, ph=0, pw=0):
 
 def conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, kernel, cin, cout, dilation,
                 pads=None):
-    """``pads``: {spatial name: symmetric zero padding done by the kernel (TMA zero fill)}."""
+    """``pads``: {spatial name: zero padding ``p`` or ``(lo, hi)`` done by the kernel (TMA zero fill)}."""
     if not weight.is_cuda or not supported(x, weight.dtype, x.shape[in_names.index(cin)], len(spatial), dilation):
         return None
     pads = pads or {}

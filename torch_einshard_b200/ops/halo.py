@@ -204,6 +204,14 @@ class _HaloExchange(torch.autograd.Function):
 
 
 def _sharded_halo(x, axis, dim, left, right, *, mesh, shapes, boundary, fill):
+    z, lo, hi = _sharded_halo_unpadded(x, axis, dim, left, right, mesh=mesh, shapes=shapes, boundary=boundary)
+    return pad_dim(z, dim, lo, hi, boundary=boundary, fill=fill) if lo or hi else z
+
+
+def _sharded_halo_unpadded(x, axis, dim, left, right, *, mesh, shapes, boundary):
+    """The exchanged part of a sharded halo: this rank's rows plus the ghost
+    rows its neighbours hold, and how many rows of boundary fill are missing
+    before and after them (the global edges)."""
     if mesh is None:
         raise ValueError("Sharded einhalo axes require mesh")
     group = mesh[axis.shard_dim].get_group()
@@ -219,13 +227,13 @@ def _sharded_halo(x, axis, dim, left, right, *, mesh, shapes, boundary, fill):
     if boundary == "periodic":
         if total == 0:
             raise ValueError("Cannot periodic-pad an empty axis")
-        return _HaloExchange.apply(x, group, dim, split, left, right, True)
+        return _HaloExchange.apply(x, group, dim, split, left, right, True), 0, 0
     if boundary not in ("constant", "replicate"):
         raise ValueError(f"Unsupported halo boundary {boundary!r}")
     start, local = sum(split[:rank]), split[rank]
     lo, hi = max(0, start - left), min(total, start + local + right)
     z = _HaloExchange.apply(x, group, dim, split, left, right, False)
-    return pad_dim(z, dim, lo - (start - left), (start + local + right) - hi, boundary=boundary, fill=fill)
+    return z, lo - (start - left), (start + local + right) - hi
 
 
 def _check_axes(axes):
@@ -258,6 +266,30 @@ def halo_tensor(spec, x, halos, *, mesh=None, shapes=None, boundary="constant", 
         else:
             z = _sharded_halo(z, axis, dim, left, right, mesh=mesh, shapes=shapes, boundary=boundary, fill=fill)
     return z
+
+
+def halo_tensor_unpadded(spec, x, halos, *, mesh=None, shapes=None):
+    """Zero-boundary halo for a consumer that zero-pads by itself (the native
+    conv's TMA fill): sharded axes get their neighbours' ghost rows, and the
+    fill that ``halo_tensor`` would add (local axes, global edges of sharded
+    axes) is returned as {axis name: (before, after)} instead of copied in."""
+    axes = _axes(spec)
+    _check_axes(axes)
+    pads = {}
+    z = x
+    for dim, axis in enumerate(axes):
+        if axis.name not in halos:
+            continue
+        left, right = normalize_halo(halos[axis.name])
+        if left == 0 and right == 0:
+            continue
+        if axis.local():
+            pads[axis.name] = (left, right)
+            continue
+        z, lo, hi = _sharded_halo_unpadded(z, axis, dim, left, right, mesh=mesh, shapes=shapes, boundary="constant")
+        if lo or hi:
+            pads[axis.name] = (lo, hi)
+    return z, pads
 
 
 def einhalo(shard, x, halos, *, boundary="constant", fill=0, mesh=None, shapes=None, families=None):
