@@ -39,6 +39,9 @@ def main():
     p.add_argument("--reducers", default="", help="comma list of reducer CTA-pair counts to time the fused arm with "
                                                    "(arms fused-R<n>; 0 = overlap mode); empty: the default")
     p.add_argument("--lags", default="", help="comma list of overlap-mode lags (arms fused-L<n>; 0 = auto)")
+    p.add_argument("--solo", action="store_true",
+                   help="one process: run the fused kernel over a one-rank NVLS heap (the multimem traffic still "
+                        "goes through the switch), so that ncu can profile it on one GPU")
     args = p.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -53,12 +56,20 @@ def main():
     symmetric._NVLS_AR_MIN_RANKS = 1  # time the native kernels at every group size
     group = mesh["tp"].get_group()
     comm = symmetric.communicator_for(group)
+    if args.solo and world == 1:
+        # one-rank groups get no communicator by default; build one for profiling
+        comm = symmetric.Communicator(group, args.m * args.n * 2 + (64 << 20))
+        symmetric._COMMS[symmetric._group_key(group)] = comm
+        symmetric._state["enabled"] = True
     k = args.h // world
     g = torch.Generator(device="cuda").manual_seed(rank)
     a = torch.randn(1, args.m, k, device="cuda", dtype=torch.bfloat16, generator=g)
     b = torch.randn(1, args.n, k, device="cuda", dtype=torch.bfloat16, generator=g).transpose(1, 2)
 
+    default_mode = fused_native._NVLS_REDUCER_CLUSTERS, fused_native._NVLS_LAG
+
     def fused():
+        fused_native._NVLS_REDUCER_CLUSTERS, fused_native._NVLS_LAG = default_mode
         return fused_native.gemm_allreduce_nvls(comm, a, b)
 
     def gemm_nvls():
@@ -80,7 +91,7 @@ def main():
     names = args.arms.split(",")
     for r in [int(v) for v in args.reducers.split(",") if v]:
         def fused_r(r=r):
-            fused_native._NVLS_REDUCER_CLUSTERS = r
+            fused_native._NVLS_REDUCER_CLUSTERS, fused_native._NVLS_LAG = r, default_mode[1]
             return fused_native.gemm_allreduce_nvls(comm, a, b)
         arms[f"fused-R{r}"] = fused_r
         names.append(f"fused-R{r}")
@@ -102,23 +113,24 @@ def main():
     t_link = (9.0 / 8.0 if world > 1 else 0.0) * out_bytes / 770e9 * 1e3
     roof = max(t_compute, t_link)
     results = {}
+    names = [n for n in names if comm is not None or not (n.startswith("fused") or n == "gemm+nvls")]
     for name in names:
-        if comm is None and (name.startswith("fused") or name == "gemm+nvls"):
-            continue
-        fn = arms[name]
         for _ in range(args.warmup):
-            fn()
-        torch.cuda.synchronize()
-        dist.barrier()
-        times = []
-        for _ in range(args.iters):
+            arms[name]()
+    torch.cuda.synchronize()
+    dist.barrier()
+    # arms interleaved call by call, so that clock and power drift reach every arm alike
+    times = {name: [] for name in names}
+    for _ in range(args.iters):
+        for name in names:
             s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             s.record()
-            fn()
+            arms[name]()
             e.record()
             torch.cuda.synchronize()
-            times.append(s.elapsed_time(e))
-        med = torch.tensor([statistics.median(times)], dtype=torch.float64, device="cuda")
+            times[name].append(s.elapsed_time(e))
+    for name in names:
+        med = torch.tensor([statistics.median(times[name])], dtype=torch.float64, device="cuda")
         dist.all_reduce(med, op=dist.ReduceOp.MAX)
         results[name] = float(med.item())
     # numerics of the fused call against the unfused native path
