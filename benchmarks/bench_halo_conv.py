@@ -49,6 +49,9 @@ def main():
     p.add_argument("--hw", type=int, default=2048)
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--breakdown", action="store_true",
+                   help="after the timed steps, one more step under torch.profiler: every rank's kernels with their "
+                        "device time, one JSON line per rank (not a timing run)")
     args = p.parse_args()
     if "RANK" not in os.environ:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT="29631", RANK="0", WORLD_SIZE="1", LOCAL_RANK="0")
@@ -114,6 +117,26 @@ def main():
         if sampler:
             sampler.mark_end()
         dist.barrier()
+    if args.breakdown:
+        from torch.profiler import ProfilerActivity, profile
+        with torch.no_grad(), profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+        kernels = {}
+        for ev in prof.events():
+            if ev.device_type.name == "CUDA":
+                k = kernels.setdefault(ev.name[:90], [0, 0.0])
+                k[0] += 1
+                k[1] += ev.device_time_total / 1e3
+        top = sorted(kernels.items(), key=lambda kv: -kv[1][1])[:12]
+        line = json.dumps({"breakdown_rank": rank, "mesh_rank": [rh, rw],
+                           "kernels_ms": [[name, n, round(t, 3)] for name, (n, t) in top],
+                           "total_ms": round(sum(t for _, t in kernels.values()), 3)})
+        lines = [None] * world
+        dist.all_gather_object(lines, line)
+        if rank == 0:
+            for entry in lines:
+                print(entry, flush=True)
     ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device="cuda", dtype=torch.float64)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = ms.item()
