@@ -845,6 +845,7 @@ void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
   a.ph_hi = static_cast<int>(ph_hi);
   a.pw_hi = static_cast<int>(pw_hi);
   a.kernel = static_cast<int>(kernel);
+  a.prof = g_prof;
   const char* why = es::check_conv_args(a);
   TORCH_CHECK(why == nullptr, "einshard conv: ", why ? why : "");
   const int Hout = es::conv_hout(a);
@@ -1013,8 +1014,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_gemm_group_m", [](int64_t v) { g_group_m = static_cast<int>(v); }, "raster group height (0 default)");
   m.def("set_gemm_split", [](int64_t v) { g_split = static_cast<int>(v); }, "wide-kernel cluster split (0/1/2)");
   m.def("set_gemm_profile", [](const at::Tensor& t) {
-        g_prof = t.numel() >= 3 ? reinterpret_cast<unsigned long long*>(t.data_ptr()) : nullptr;
-      }, "int64 CUDA tensor of >= 3 wait-cycle counters for the wide GEMM (empty tensor: off)");
+        g_prof = t.numel() >= 8 ? reinterpret_cast<unsigned long long*>(t.data_ptr()) : nullptr;
+      }, "int64 CUDA tensor of >= 8 wait-cycle counters for the wide GEMM and the pair conv (empty tensor: off)");
   m.def("set_gemm_persistent", [](int64_t v) { g_persistent = static_cast<int>(v); }, "wide kernel: 1 persistent, 0 one tile per cluster, -1 by K");
   m.def("set_small_persistent", [](int64_t v) { g_small_persistent = static_cast<int>(v); },
         "1-SM GEMM and conv: 1 persistent CTAs, 0 one tile per CTA");

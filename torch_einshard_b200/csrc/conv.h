@@ -20,6 +20,7 @@ struct ConvArgs {
   int num_sms = 148;
   int persistent = 1;          // 1 persistent CTAs (default), 0 one tile per CTA (tuning)
   int kernel = 0;              // 0 auto (the pair kernel with resident weights where it fits), 1 conv.cu's kernel
+  unsigned long long* prof = nullptr;  // pair kernel: wait-cycle counters (tuning), null when off
 };
 
 template <class Args>

@@ -83,6 +83,11 @@ struct PairShape {
   int tmem_cols;
   int in_bf16;
   int* err;
+  // optional wait-cycle counters: [0] MMA-warp cycles, [1] of them waiting for a
+  // filled stage, [2] waiting for a free accumulator, [3] producer cycles,
+  // [4] of them waiting for a free stage, [5] epilogue cycles waiting for a
+  // full accumulator (warp 2 of each CTA), [6] epilogue cycles in all
+  unsigned long long* prof;
 };
 
 __device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* map, uint32_t bar_cluster_addr, int c0,
@@ -92,6 +97,27 @@ __device__ __forceinline__ void tma_load_4d_pair(void* dst, const CUtensorMap* m
       " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar_cluster_addr)
       : "memory");
+}
+
+// The KW x 4 MMAs of one (kh, channel block) stage.  `ad`: descriptor of the
+// stage's input box; `bd`: descriptor of tap (kh, 0)'s weight sub-tile; `bstep`:
+// descriptor units (16 B) between the taps' sub-tiles.  Descriptors advance by
+// plain adds of the start-address field (kw rows = kw x 8 units, a K16 step = 2
+// units), so the single issuing thread spends a few instructions per MMA: at
+// N = 128 an M = 256 MMA keeps the tensor pipe busy for only 64 cycles.
+template <int KWc>
+__device__ __forceinline__ void issue_stage(uint32_t d_tmem, uint64_t ad, uint64_t bd, uint32_t bstep, int kw_n,
+                                            uint32_t idesc, uint32_t& accum) {
+#pragma unroll
+  for (int kw = 0; kw < (KWc > 0 ? KWc : 9); ++kw) {
+    if (KWc == 0 && kw >= kw_n) break;
+#pragma unroll
+    for (int k = 0; k < kBK / kUmmaK; ++k) {
+      umma_f16_pair(d_tmem, ad + static_cast<uint64_t>(kw * 8 + k * 2),
+                    bd + static_cast<uint64_t>(kw * bstep + k * 2), idesc, accum);
+      accum = 1u;
+    }
+  }
 }
 
 // Pixel tile p of output-channel tile `ot` -> image, output row, first column of this CTA.
@@ -161,6 +187,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
     uint32_t it = 0;
+    long long p_wait = 0;
+    const long long p_start = clock64();
     if (lane == 0) {
       const uint32_t wbar = map_to_cta(&st->wfull, 0);
       if (leader) mbar_arrive_expect_tx(&st->wfull, 2u * static_cast<uint32_t>(nsub * wsub));
@@ -176,7 +204,9 @@ __global__ void __launch_bounds__(kPThreads, 1)
         for (int cb = 0; cb < s.cblocks; ++cb, ++it) {
           const int stg = it % kPStages;
           const uint32_t ph = (it / kPStages) & 1u;
+          const long long t_w = s.prof ? clock64() : 0;
           if (!mbar_wait_lane0(&st->empty[stg], ph ^ 1u, abort_flag, s.err, kErrWaitEmpty)) goto producer_done;
+          if (s.prof) p_wait += clock64() - t_w;
           if (lane == 0) {
             if (leader) mbar_arrive_expect_tx(&st->full[stg], 2u * static_cast<uint32_t>(abytes));
             tma_load_4d_pair(sA + stg * kAStage, &tmX, full_leader0 + stg * 8, cb * kBK, pt.w0 - s.pw,
@@ -188,6 +218,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
   producer_done:
     __syncwarp();
+    if (s.prof && lane == 0) {
+      atomicAdd(&s.prof[3], static_cast<unsigned long long>(clock64() - p_start));
+      atomicAdd(&s.prof[4], static_cast<unsigned long long>(p_wait));
+    }
     if (*abort_flag && leader && lane == 0) {
       // loads in flight must land before the CTA exits (bounded waits)
       int dummy_abort = 0;
@@ -202,36 +236,39 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // ------------------------------------------------------------ MMA issuer (leader CTA)
     if (leader) {
       const uint32_t idesc = umma_idesc_f16(2 * kCtaPx, s.otile, s.in_bf16, 0, 0);
-      const uint32_t a0 = smem_u32(sA);
-      const uint32_t w0 = smem_u32(sW);
+      const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA), 16u, 1024u);
+      const uint64_t wdesc0 = umma_desc_sw128(smem_u32(sW), 16u, 1024u);
+      const uint32_t bstep = static_cast<uint32_t>(s.cblocks * wsub) >> 4;
       uint32_t it = 0, tc = 0;
       bool issued_any = false;
+      long long w_full = 0, w_empty = 0;
+      const long long m_start = clock64();
       if (!mbar_wait_lane0(&st->wfull, 0, abort_flag, s.err, kErrWaitFull)) goto mma_done;
       for (int p = first; p < s.ptiles; p += per_ot, ++tc) {
         const uint32_t acc = tc & 1u;
         const uint32_t aph = (tc >> 1) & 1u;
+        const long long t_e = s.prof ? clock64() : 0;
         if (!mbar_wait_lane0(&st->tempty[acc], aph ^ 1u, abort_flag, s.err, kErrWaitTmemEmpty)) goto mma_done;
+        if (s.prof) w_empty += clock64() - t_e;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * s.otile;
+        uint32_t accum = 0u;  // the tile's first MMA overwrites the accumulator
         for (int kh = 0; kh < s.KH; ++kh) {
           for (int cb = 0; cb < s.cblocks; ++cb, ++it) {
             const int stg = it % kPStages;
             const uint32_t ph = (it / kPStages) & 1u;
+            const long long t_f = s.prof ? clock64() : 0;
             if (!mbar_wait_lane0(&st->full[stg], ph, abort_flag, s.err, kErrWaitFull)) goto mma_done;
+            if (s.prof) w_full += clock64() - t_f;
             tc_fence_after();
             if (lane == 0) {
-              const uint32_t a_addr = a0 + stg * kAStage;
-              for (int kw = 0; kw < s.KW; ++kw) {
-                const uint32_t b_addr = w0 + ((kh * s.KW + kw) * s.cblocks + cb) * wsub;
-#pragma unroll
-                for (int k = 0; k < kBK / kUmmaK; ++k) {
-                  // the tap's operand starts kw pixel rows into the box
-                  const uint64_t ad = umma_desc_sw128(a_addr + kw * 128 + k * 32, 16u, 1024u);
-                  const uint64_t bd = umma_desc_sw128(b_addr + k * 32, 16u, 1024u);
-                  const uint32_t accum = (kh | cb | kw | k) != 0 ? 1u : 0u;
-                  umma_f16_pair(d_tmem, ad, bd, idesc, accum);
-                }
-              }
+              // tap kw's operand starts kw pixel rows into the box
+              const uint64_t ad = adesc0 + static_cast<uint64_t>((stg * kAStage) >> 4);
+              const uint64_t bd = wdesc0 + static_cast<uint64_t>(((kh * s.KW * s.cblocks + cb) * wsub) >> 4);
+              if (s.KW == 3)
+                issue_stage<3>(d_tmem, ad, bd, bstep, 3, idesc, accum);
+              else
+                issue_stage<0>(d_tmem, ad, bd, bstep, s.KW, idesc, accum);
               umma_commit_pair_mc(&st->empty[stg], 0x3);
               *reinterpret_cast<volatile int*>(&st->consumed) = static_cast<int>(it + 1);
             }
@@ -244,6 +281,11 @@ __global__ void __launch_bounds__(kPThreads, 1)
       }
     mma_done:
       __syncwarp();
+      if (s.prof && lane == 0) {
+        atomicAdd(&s.prof[0], static_cast<unsigned long long>(clock64() - m_start));
+        atomicAdd(&s.prof[1], static_cast<unsigned long long>(w_full));
+        atomicAdd(&s.prof[2], static_cast<unsigned long long>(w_empty));
+      }
       if (*abort_flag && issued_any && lane == 0) {
         umma_commit_pair_mc(&st->drain, 0x1);
         int dummy_abort = 0;
@@ -254,10 +296,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // ------------------------------------------------------------ epilogue (both CTAs, 4 warps)
     const int q = warp & 3;
     uint32_t tc = 0;
+    long long e_wait = 0;
+    const long long e_start = clock64();
     for (int p = first; p < s.ptiles; p += per_ot, ++tc) {
       const uint32_t acc = tc & 1u;
       const uint32_t aph = (tc >> 1) & 1u;
+      const long long t_t = s.prof ? clock64() : 0;
       if (!mbar_wait_sleepy(&st->tfull[acc], aph, abort_flag, s.err, kErrWaitTmemFull, 64)) break;
+      if (s.prof) e_wait += clock64() - t_t;
       tc_fence_after();
       const PixTile pt = pix_tile(s, p, static_cast<int>(rank));
       const int w = pt.w0 + q * 32 + lane;
@@ -278,6 +324,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(tempty_leader0 + acc * 8);
+    }
+    if (s.prof && warp == 2 && lane == 0) {
+      atomicAdd(&s.prof[5], static_cast<unsigned long long>(e_wait));
+      atomicAdd(&s.prof[6], static_cast<unsigned long long>(clock64() - e_start));
     }
   }
 
@@ -324,6 +374,7 @@ int launch_pair(const ConvArgs& a, int otile, cudaStream_t stream) {
   s.tmem_cols = 2 * otile < 32 ? 32 : 2 * otile;
   s.in_bf16 = a.dtype == kDtypeBF16 ? 1 : 0;
   s.err = a.err;
+  s.prof = a.prof;
   // X: NHWC input, dims (C, Win, Hin, B), box 64 channels x arows pixels
   const uint64_t dims[4] = {static_cast<uint64_t>(a.C), static_cast<uint64_t>(a.Win), static_cast<uint64_t>(a.Hin),
                             static_cast<uint64_t>(a.B)};
