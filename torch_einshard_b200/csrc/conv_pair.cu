@@ -28,7 +28,7 @@
 //
 // Warps (192 threads): 0 TMA producer, 1 MMA issuer (leader CTA) + TMEM owner,
 // 2..5 epilogue (TMEM lane quadrant warp % 4: one pixel per thread, its otile
-// channels as contiguous 16-byte stores).  Two TMEM accumulators of otile
+// channels as contiguous 32-byte stores).  Two TMEM accumulators of otile
 // columns: the epilogue of tile i overlaps the MMAs of tile i + 1.  Every wait
 // is bounded (ptx.cuh); a timed-out kernel records a code, drains its own
 // copies, frees TMEM and returns.
@@ -82,6 +82,7 @@ struct PairShape {
   int arows;          // rows of each A box (128 + KW - 1 rounded up to 8)
   int tmem_cols;
   int in_bf16;
+  int v8;             // output 32-byte aligned: 256-bit stores
   int* err;
   // optional wait-cycle counters: [0] MMA-warp cycles, [1] of them waiting for a
   // filled stage, [2] waiting for a free accumulator, [3] producer cycles,
@@ -118,6 +119,24 @@ __device__ __forceinline__ void issue_stage(uint32_t d_tmem, uint64_t ad, uint64
       accum = 1u;
     }
   }
+}
+
+// 32 fp32 values -> 32 bf16/fp16 at p (32-byte aligned) as two 256-bit stores:
+// every store writes whole 32-byte sectors.
+template <typename OutT>
+__device__ __forceinline__ void store32_v8(OutT* p, const uint32_t (&r)[32]) {
+  uint32_t w[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const float a = __uint_as_float(r[2 * i]), b = __uint_as_float(r[2 * i + 1]);
+    w[i] = std::is_same<OutT, __nv_bfloat16>::value ? pack_bf16(a, b) : pack_f16(a, b);
+  }
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p + 16 * h), "r"(w[8 * h]),
+                 "r"(w[8 * h + 1]), "r"(w[8 * h + 2]), "r"(w[8 * h + 3]), "r"(w[8 * h + 4]), "r"(w[8 * h + 5]),
+                 "r"(w[8 * h + 6]), "r"(w[8 * h + 7])
+                 : "memory");
 }
 
 // Pixel tile p of output-channel tile `ot` -> image, output row, first column of this CTA.
@@ -234,7 +253,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader CTA)
-    if (leader) {
+    // one thread runs the whole loop: no warp-wide votes between stages
+    if (leader && lane == 0) {
       const uint32_t idesc = umma_idesc_f16(2 * kCtaPx, s.otile, s.in_bf16, 0, 0);
       const uint64_t adesc0 = umma_desc_sw128(smem_u32(sA), 16u, 1024u);
       const uint64_t wdesc0 = umma_desc_sw128(smem_u32(sW), 16u, 1024u);
@@ -243,12 +263,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
       bool issued_any = false;
       long long w_full = 0, w_empty = 0;
       const long long m_start = clock64();
-      if (!mbar_wait_lane0(&st->wfull, 0, abort_flag, s.err, kErrWaitFull)) goto mma_done;
+      if (!mbar_wait(&st->wfull, 0, abort_flag, s.err, kErrWaitFull)) goto mma_done;
       for (int p = first; p < s.ptiles; p += per_ot, ++tc) {
         const uint32_t acc = tc & 1u;
         const uint32_t aph = (tc >> 1) & 1u;
         const long long t_e = s.prof ? clock64() : 0;
-        if (!mbar_wait_lane0(&st->tempty[acc], aph ^ 1u, abort_flag, s.err, kErrWaitTmemEmpty)) goto mma_done;
+        if (!mbar_wait(&st->tempty[acc], aph ^ 1u, abort_flag, s.err, kErrWaitTmemEmpty)) goto mma_done;
         if (s.prof) w_empty += clock64() - t_e;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * s.otile;
@@ -258,40 +278,36 @@ __global__ void __launch_bounds__(kPThreads, 1)
             const int stg = it % kPStages;
             const uint32_t ph = (it / kPStages) & 1u;
             const long long t_f = s.prof ? clock64() : 0;
-            if (!mbar_wait_lane0(&st->full[stg], ph, abort_flag, s.err, kErrWaitFull)) goto mma_done;
+            if (!mbar_wait(&st->full[stg], ph, abort_flag, s.err, kErrWaitFull)) goto mma_done;
             if (s.prof) w_full += clock64() - t_f;
             tc_fence_after();
-            if (lane == 0) {
-              // tap kw's operand starts kw pixel rows into the box
-              const uint64_t ad = adesc0 + static_cast<uint64_t>((stg * kAStage) >> 4);
-              const uint64_t bd = wdesc0 + static_cast<uint64_t>(((kh * s.KW * s.cblocks + cb) * wsub) >> 4);
-              if (s.KW == 3)
-                issue_stage<3>(d_tmem, ad, bd, bstep, 3, idesc, accum);
-              else
-                issue_stage<0>(d_tmem, ad, bd, bstep, s.KW, idesc, accum);
-              umma_commit_pair_mc(&st->empty[stg], 0x3);
-              *reinterpret_cast<volatile int*>(&st->consumed) = static_cast<int>(it + 1);
-            }
+            // tap kw's operand starts kw pixel rows into the box
+            const uint64_t ad = adesc0 + static_cast<uint64_t>((stg * kAStage) >> 4);
+            const uint64_t bd = wdesc0 + static_cast<uint64_t>(((kh * s.KW * s.cblocks + cb) * wsub) >> 4);
+            if (s.KW == 3)
+              issue_stage<3>(d_tmem, ad, bd, bstep, 3, idesc, accum);
+            else
+              issue_stage<0>(d_tmem, ad, bd, bstep, s.KW, idesc, accum);
+            umma_commit_pair_mc(&st->empty[stg], 0x3);
+            *reinterpret_cast<volatile int*>(&st->consumed) = static_cast<int>(it + 1);
             issued_any = true;
-            __syncwarp();
           }
         }
-        if (lane == 0) umma_commit_pair_mc(&st->tfull[acc], 0x3);
-        __syncwarp();
+        umma_commit_pair_mc(&st->tfull[acc], 0x3);
       }
     mma_done:
-      __syncwarp();
-      if (s.prof && lane == 0) {
+      if (s.prof) {
         atomicAdd(&s.prof[0], static_cast<unsigned long long>(clock64() - m_start));
         atomicAdd(&s.prof[1], static_cast<unsigned long long>(w_full));
         atomicAdd(&s.prof[2], static_cast<unsigned long long>(w_empty));
       }
-      if (*abort_flag && issued_any && lane == 0) {
+      if (*abort_flag && issued_any) {
         umma_commit_pair_mc(&st->drain, 0x1);
         int dummy_abort = 0;
         mbar_wait(&st->drain, 0, &dummy_abort, nullptr, 0);
       }
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs, 4 warps)
     const int q = warp & 3;
@@ -319,7 +335,12 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) + __ldg(bsrc + i));
         }
-        if (valid) StoreOut<OutT>::store32(dst + ch, v, 0);
+        if (valid) {
+          if (s.v8)
+            store32_v8(dst + ch, v);
+          else
+            StoreOut<OutT>::store32(dst + ch, v, 0);
+        }
       }
       tc_fence_before();
       __syncwarp();
@@ -375,6 +396,7 @@ int launch_pair(const ConvArgs& a, int otile, cudaStream_t stream) {
   s.in_bf16 = a.dtype == kDtypeBF16 ? 1 : 0;
   s.err = a.err;
   s.prof = a.prof;
+  s.v8 = (reinterpret_cast<uintptr_t>(a.out) & 31) == 0 ? 1 : 0;
   // X: NHWC input, dims (C, Win, Hin, B), box 64 channels x arows pixels
   const uint64_t dims[4] = {static_cast<uint64_t>(a.C), static_cast<uint64_t>(a.Win), static_cast<uint64_t>(a.Hin),
                             static_cast<uint64_t>(a.B)};
