@@ -47,3 +47,17 @@ def test_local_roll_gradient_and_einroll():
     assert torch.equal(x.grad, torch.roll(g, shifts=(-2, 5), dims=(0, 2)))
     mod = _native.require()
     assert mod.launch_count() > 0
+
+
+def test_local_roll_of_lazy_conjugate_views():
+    """Lazy conjugate / negative views (autograd passes conj(grad) that way) are
+    rolled by value, forward and backward."""
+    from torch_einshard_b200.ops.native_ops import local_roll
+    z = torch.randn(3, 6, 5, dtype=torch.complex64, device="cuda")
+    for view in (z.conj(), torch.neg(z.conj()).conj()):
+        torch.testing.assert_close(local_roll(view, {1: 2, 2: -1}), torch.roll(view, (2, -1), (1, 2)))
+    zr = z.clone().requires_grad_(True)
+    zt = z.clone().requires_grad_(True)
+    local_roll(zr, {1: 1}).conj().abs().sum().backward()
+    torch.roll(zt, 1, 1).conj().abs().sum().backward()
+    torch.testing.assert_close(zr.grad, zt.grad)

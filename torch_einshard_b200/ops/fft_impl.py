@@ -49,7 +49,7 @@ def _eligible(x, dim):
 
 
 def _run(mod, x, dim, inverse, scale=1.0, out=None):
-    x = x.contiguous()
+    x = x.resolve_conj().resolve_neg().contiguous()  # the kernel reads raw memory
     if out is None:
         out = torch.empty_like(x, memory_format=torch.contiguous_format)
     mod.fft_c2c(x, out, dim, bool(inverse), twiddles(x.shape[dim], inverse, x.device), float(scale))

@@ -21,7 +21,7 @@ _MAX_RANK = 8
 
 def strided_copy(view: torch.Tensor):
     """Materialise an arbitrary strided view contiguously with one kernel."""
-    if not view.is_cuda or view.dim() > _MAX_RANK or view.numel() == 0:
+    if not view.is_cuda or view.dim() > _MAX_RANK or view.numel() == 0 or view.is_conj() or view.is_neg():
         return None
     mod = _native.module()
     if mod is None or not hasattr(mod, "strided_copy"):
@@ -43,7 +43,9 @@ class _LocalRoll(torch.autograd.Function):
 
 
 def _roll_native(x, shifts):
-    x = x.contiguous()
+    # the kernel moves raw memory: resolve lazy conjugate / negative views first
+    # (autograd hands conj(grad) of torch.conj to backward as such a view)
+    x = x.resolve_conj().resolve_neg().contiguous()
     out = torch.empty_like(x)
     _native.require().roll_copy(x, out, [int(s) for s in shifts])
     return out
