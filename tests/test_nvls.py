@@ -39,7 +39,7 @@ def _body(rank, world):
 
     def nccl_sum(x, scale=1.0):
         """The fp32 sum over ranks (the oracle: a bf16 ring rounds at every step)."""
-        y = x.float()
+        y = x.to(torch.float32, copy=True)  # never x itself: the input stays for the native call
         dist.all_reduce(y, group=group)
         return (y * scale if scale != 1.0 else y)
 

@@ -94,11 +94,42 @@ template <> struct UnitT<4> { using T = uint32_t; };
 template <> struct UnitT<2> { using T = uint16_t; };
 template <> struct UnitT<1> { using T = uint8_t; };
 
+// Work items of a box: (row, chunk of up to kChunkUnits units of the row).
+// Offsets are derived once per item, so long rows cost no per-unit index
+// arithmetic and rows shorter than a chunk are one item each.
+constexpr long long kChunkUnits = 2048;
+
 template <int U>
 __device__ void copy_box_units(const uint8_t* sbase, uint8_t* dbase, const CopyBox& b, int esize) {
   using T = typename UnitT<U>::T;
   const long long nu = (long long)b.dims[3] * esize / U;
-  const long long total = nu * b.dims[2] * b.dims[1] * b.dims[0];
+  const long long rows = (long long)b.dims[2] * b.dims[1] * b.dims[0];
+  if (nu >= 64) {
+    const long long nchunk = (nu + kChunkUnits - 1) / kChunkUnits;
+    for (long long item = blockIdx.x; item < rows * nchunk; item += gridDim.x) {
+      const long long r = item / nchunk;
+      const long long c0 = (item - r * nchunk) * kChunkUnits;
+      const long long c1 = c0 + kChunkUnits < nu ? c0 + kChunkUnits : nu;
+      const long long i2 = r % b.dims[2];
+      const long long q = r / b.dims[2];
+      const long long i1 = q % b.dims[1];
+      const long long i0 = q / b.dims[1];
+      const T* s = reinterpret_cast<const T*>(sbase + b.src_off + i0 * b.sstr[0] + i1 * b.sstr[1] + i2 * b.sstr[2]);
+      T* d = reinterpret_cast<T*>(dbase + b.dst_off + i0 * b.dstr[0] + i1 * b.dstr[1] + i2 * b.dstr[2]);
+      const long long step = blockDim.x;
+      for (long long u = c0 + threadIdx.x; u < c1; u += 4 * step) {
+        T v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (u + k * step < c1) v[k] = s[u + k * step];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (u + k * step < c1) d[u + k * step] = v[k];
+      }
+    }
+    return;
+  }
+  const long long total = nu * rows;
   const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   const long long nth = (long long)gridDim.x * blockDim.x;
   for (long long i = tid; i < total; i += nth) {
@@ -166,7 +197,28 @@ __device__ void reduce_box(const CommDev& c, uint8_t* dbase, const CopyBox& b, c
 __device__ void acc_copy_box(const uint8_t* sbase, uint8_t* dbase, const CopyBox& b, const CopyPlan& plan) {
   const int es_ = plan.esize;
   const long long n3 = b.dims[3];
-  const long long total = n3 * b.dims[2] * b.dims[1] * b.dims[0];
+  const long long rows = (long long)b.dims[2] * b.dims[1] * b.dims[0];
+  const long long nchunk = (n3 + kChunkUnits - 1) / kChunkUnits;
+  // items of (row, chunk) as in copy_box_units; short rows are spread over threads
+  if (n3 >= 64) {
+    for (long long item = blockIdx.x; item < rows * nchunk; item += gridDim.x) {
+      const long long r = item / nchunk;
+      const long long c0 = (item - r * nchunk) * kChunkUnits;
+      const long long c1 = c0 + kChunkUnits < n3 ? c0 + kChunkUnits : n3;
+      const long long i2 = r % b.dims[2];
+      const long long q = r / b.dims[2];
+      const long long i1 = q % b.dims[1];
+      const long long i0 = q / b.dims[1];
+      const uint8_t* s = sbase + b.src_off + i0 * b.sstr[0] + i1 * b.sstr[1] + i2 * b.sstr[2];
+      uint8_t* d = dbase + b.dst_off + i0 * b.dstr[0] + i1 * b.dstr[1] + i2 * b.dstr[2];
+      for (long long u = c0 + threadIdx.x; u < c1; u += blockDim.x) {
+        const float v = load_as_float(s + u * es_, plan.dtype) * plan.scale + load_as_float(d + u * es_, plan.dtype);
+        store_float(d + u * es_, plan.dtype, v);
+      }
+    }
+    return;
+  }
+  const long long total = n3 * rows;
   const long long tid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
   const long long nth = (long long)gridDim.x * blockDim.x;
   for (long long i = tid; i < total; i += nth) {
@@ -194,12 +246,27 @@ __global__ void __launch_bounds__(512) k_stage_and_run(CommDev c, const void* sr
   // peers must be done reading our data region from the previous op
   if (!wait_peers(c, kFlagDone, c.epoch - 1)) return;
   if (nbytes) copy_bytes(reinterpret_cast<uint8_t*>(c.data[c.rank]) + stage_off, src, nbytes);
+  uint8_t* d = reinterpret_cast<uint8_t*>(dst);
+  // boxes that read only this rank's own data need nothing from the peers: run
+  // them before waiting for the peers' staged data (a skew between ranks then
+  // overlaps the local copy)
+  if (!reduce) {
+    for (int i = 0; i < plan.nbox; ++i) {
+      const CopyBox& b = plan.box[i];
+      if (b.src_rank >= 0) continue;
+      if (plan.accumulate)
+        acc_copy_box(reinterpret_cast<const uint8_t*>(local), d, b, plan);
+      else
+        copy_box(reinterpret_cast<const uint8_t*>(local), d, b, plan.esize);
+      if (plan.sequential && !grid_barrier(c, c.bar_base + nb * ++bars)) return;
+    }
+  }
   if (!grid_barrier(c, c.bar_base + nb * ++bars)) return;
   publish(c, kFlagStaged);
   if (!wait_peers(c, kFlagStaged, c.epoch)) return;
-  uint8_t* d = reinterpret_cast<uint8_t*>(dst);
   for (int i = 0; i < plan.nbox; ++i) {
     const CopyBox& b = plan.box[i];
+    if (!reduce && b.src_rank < 0) continue;  // done above
     if (reduce) {
       reduce_box(c, d, b, plan);
     } else {

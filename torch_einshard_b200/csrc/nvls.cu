@@ -137,6 +137,25 @@ __device__ __forceinline__ void block_signal(const NvlsDev& d, int slot) {
   }
 }
 
+// End of a collective on this rank: the last block to finish adds 1 to the
+// done counter of every rank.  A collective starts only when done reaches
+// P x (epoch - 1), i.e. every block of every rank finished the previous one:
+// the per-block counters alone do not order two collectives whose bytes fall
+// to different blocks (the block of a byte depends on the collective's size),
+// so without this a late multicast store or reduction of the previous
+// collective could meet the next one's staging.
+__device__ __forceinline__ void block_done(const NvlsDev& d) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_acq_rel_sys();
+    const uint32_t n = atomicAdd(d.flags + kNvlsArrived, 1u) + 1u;
+    if (n == static_cast<uint32_t>(d.nblocks) * static_cast<uint32_t>(d.epoch)) {
+      fence_acq_rel_sys();
+      mm_red_add_release(d.mcflags + kNvlsDone, 1u);
+    }
+  }
+}
+
 __device__ __forceinline__ void unit_range(long long units, long long* u0, long long* u1) {
   const long long per = (units + gridDim.x - 1) / gridDim.x;
   const long long a = static_cast<long long>(blockIdx.x) * per;
@@ -195,7 +214,7 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_all_reduce(NvlsDev d, con
   const long long units = (nbytes + 15) / 16;
   long long u0, u1;
   unit_range(units, &u0, &u1);
-  if (!block_wait(d, kNvlsSeq + b, P * static_cast<uint32_t>(d.epoch - 1))) return;
+  if (!block_wait(d, kNvlsDone, P * static_cast<uint32_t>(d.epoch - 1))) return;
   uint8_t* uc = d.uc;
   const uint8_t* mc = d.mc;
   if (in != nullptr)
@@ -220,6 +239,7 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_all_reduce(NvlsDev d, con
               [&](long long u, uint4 v) { store_unit(out, u, nbytes, scaled ? scale16<DT>(v, scale) : v); });
     block_signal(d, kNvlsSeq + b);
   }
+  block_done(d);
 }
 
 // ---------------------------------------------------------------- all-gather / reduce-scatter
@@ -241,7 +261,7 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_all_gather(NvlsDev d, con
                                                                    ShardLayout L) {
   const int b = blockIdx.x;
   const uint32_t P = static_cast<uint32_t>(d.size);
-  if (!block_wait(d, kNvlsSeq + b, P * static_cast<uint32_t>(d.epoch - 1))) return;
+  if (!block_wait(d, kNvlsDone, P * static_cast<uint32_t>(d.epoch - 1))) return;
   {
     const long long n = L.outer * L.len[d.rank] * L.inner_bytes;
     long long u0, u1;
@@ -266,6 +286,7 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_all_gather(NvlsDev d, con
     }
   }
   block_signal(d, kNvlsSeq + b);
+  block_done(d);
 }
 
 template <int DT>
@@ -273,7 +294,7 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_reduce_scatter(NvlsDev d,
                                                                        ShardLayout L, float scale) {
   const int b = blockIdx.x;
   const uint32_t P = static_cast<uint32_t>(d.size);
-  if (!block_wait(d, kNvlsSeq + b, P * static_cast<uint32_t>(d.epoch - 1))) return;
+  if (!block_wait(d, kNvlsDone, P * static_cast<uint32_t>(d.epoch - 1))) return;
   for (int q = 0; q < d.size; ++q) {
     const long long n = L.outer * L.len[q] * L.inner_bytes;
     long long u0, u1;
@@ -307,16 +328,15 @@ __global__ void __launch_bounds__(kNvlsThreads) k_nvls_reduce_scatter(NvlsDev d,
               [&](long long u, uint4 v) { store_unit(out, u, n, scaled ? scale16<DT>(v, scale) : v); });
   }
   block_signal(d, kNvlsSeq + b);
+  block_done(d);
 }
 
 // Wait until every rank finished the NVLS collectives issued so far on this heap
-// (all per-block completion counters at P * epoch), before other kernels reuse
-// the data region.
+// (the done counter at P * epoch), before other kernels reuse the data region.
 __global__ void k_nvls_quiesce(NvlsDev d) {
-  const int b = threadIdx.x;
-  if (b >= d.nblocks) return;
+  if (threadIdx.x != 0) return;
   const uint32_t target = static_cast<uint32_t>(d.size) * static_cast<uint32_t>(d.epoch);
-  const uint32_t* f = d.flags + kNvlsSeq + b;
+  const uint32_t* f = d.flags + kNvlsDone;
   const uint64_t t0 = global_timer_ns();
   while (static_cast<int>(ld_acquire_sys_u32(f) - target) < 0) {
     if (global_timer_ns() - t0 > d.timeout_ns) {

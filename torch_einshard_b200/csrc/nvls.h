@@ -25,13 +25,15 @@ namespace es {
 constexpr int kNvlsReady = 262144;                 // word index: per-block ready counters
 constexpr int kNvlsSeq = kNvlsReady + 1024;        // per-block completion counters
 constexpr int kNvlsMaxBlocks = 1024;
+constexpr int kNvlsDone = kNvlsSeq + kNvlsMaxBlocks;  // collectives every rank has finished, x P (multicast adds)
+constexpr int kNvlsArrived = kNvlsDone + 1;          // this rank's blocks that finished a collective (local)
 // Fused GEMM + all-reduce (gemm_nvls.cu), per 32 x 256 output unit u:
 //   reduced[u]       - the epoch of the last call whose unit u is reduced (written by its owner, multicast)
 //   ready[u][q]      - on the owner of u: the epoch of rank q's last partial of unit u
 constexpr int kNvlsMaxUnits = 120000;
 constexpr int kTileReduced0 = 270336;                              // word index of reduced[0]
 constexpr int kTileReady0 = 393216;                                // word index of ready[0][0]
-static_assert(kNvlsSeq + kNvlsMaxBlocks <= kTileReduced0, "NVLS counters overlap the unit flags");
+static_assert(kNvlsArrived + 1 <= kTileReduced0, "NVLS counters overlap the unit flags");
 static_assert(kTileReduced0 + kNvlsMaxUnits <= kTileReady0, "unit flags overlap");
 static_assert(kTileReady0 + kNvlsMaxUnits * kMaxRanks <= static_cast<int>(kFlagBytes / 4),
               "NVLS flags exceed the flag area");
