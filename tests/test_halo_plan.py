@@ -104,3 +104,34 @@ def test_halo_plans_rebuild_the_haloed_shards_and_the_adjoint(shapes, left, righ
         got = np.frombuffer(_replay(plans[q], local, staged, out, accumulate=True).tobytes(),
                             dtype=np.float32).reshape(xs[q].shape)
         np.testing.assert_allclose(got, want_in[q], rtol=1e-6, atol=1e-6)
+
+
+@pytest.mark.parametrize("shapes,left,right,periodic,dim,others", CASES)
+def test_ghost_plans_rebuild_only_the_peers_rows(shapes, left, right, periodic, dim, others):
+    """halo_ghost_plan: every rank's G holds exactly the haloed shard's rows
+    that peers own (those above the shard, then those below), nothing of its own."""
+    from torch_einshard_b200.parallel.symmetric import halo_ghost_plan
+    size = len(shapes)
+    rng = np.random.default_rng(1)
+    xs = [rng.standard_normal([shapes[q] if o is None else o for o in others]).astype(np.float32) for q in range(size)]
+    table = halo_intervals(shapes, left, right, periodic=periodic)
+    plans, staged = {}, {}
+    for q in range(size):
+        length = shapes[q] + left + right if periodic else sum(p[3] for p in table[q])
+        plans[q] = halo_ghost_plan(q, list(xs[q].shape), dim, table, length, ESIZE)
+        send = plans[q][0] if plans[q] is not None else []
+        packed = (np.concatenate([np.take(xs[q], range(o, o + n), axis=dim) for o, n in send], axis=dim)
+                  if send else np.zeros(0, np.float32))
+        staged[q] = np.frombuffer(np.ascontiguousarray(packed).tobytes(), dtype=np.uint8)
+    for q in range(size):
+        if plans[q] is None:
+            continue
+        _, boxes, g_shape, gtop, gbot = plans[q]
+        out = np.zeros(int(np.prod(g_shape)) * ESIZE, dtype=np.uint8)
+        local = np.frombuffer(np.ascontiguousarray(xs[q]).tobytes(), dtype=np.uint8)
+        got = np.frombuffer(_replay(boxes, local, staged, out).tobytes(), dtype=np.float32).reshape(g_shape)
+        full = _pieces_tensor(xs, dim, table[q])
+        want = np.concatenate([np.take(full, range(0, gtop), axis=dim),
+                               np.take(full, range(full.shape[dim] - gbot, full.shape[dim]), axis=dim)], axis=dim)
+        np.testing.assert_array_equal(got, want)
+        assert g_shape[dim] == gtop + gbot

@@ -165,3 +165,33 @@ def test_conv_per_side_padding_forward_backward(ph, pw, kernel, monkeypatch):
     _close(w.grad, wr.grad)
     _close(bias.grad, br.grad, tol=1e-3)
     _native.check_errors()
+
+
+@pytest.mark.parametrize("gtop,gbot,ph", [(1, 1, (0, 0)), (1, 0, (0, 1)), (0, 2, (2, 0)), (2, 2, (0, 0))])
+def test_conv_ghost_rows_forward_backward(gtop, gbot, ph):
+    """Rows read from a separate ghost tensor above and below x (the halo of a
+    sharded axis) give the conv of the assembled input, forward and backward."""
+    from torch_einshard_b200.ops.conv_impl import conv2d_ghost_rows
+    torch.manual_seed(5)
+    B, H, W, C, O, K = 2, 9, 300, 64, 128, 5 if max(gtop, gbot) > 1 else 3
+    x = torch.randn(B, H, W, C, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    g = torch.randn(B, gtop + gbot, W, C, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(O, K, K, C, device="cuda") * 0.05).to(torch.bfloat16).requires_grad_(True)
+    bias = torch.randn(O, device="cuda", requires_grad=True)
+    pw = (K // 2, K // 2)
+    # ghosts are constants here: the adjoint keeps the shard's rows
+    y = conv2d_ghost_rows(x, g, gtop, gbot, lambda dv: dv[:, gtop:gtop + H], w, bias, ph, pw)
+    full = torch.cat([g[:, :gtop].float(), x.detach().float(), g[:, gtop:].float()], 1).requires_grad_(True)
+    wr = w.detach().float().requires_grad_(True)
+    br = bias.detach().clone().requires_grad_(True)
+    xp = F.pad(full.permute(0, 3, 1, 2), (pw[0], pw[1], ph[0], ph[1]))
+    yr = F.conv2d(xp, wr.permute(0, 3, 1, 2), br).permute(0, 2, 3, 1)
+    assert y.shape == yr.shape
+    _close(y, yr)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    yr.backward(gy.float())
+    _close(x.grad, full.grad[:, gtop:gtop + H])
+    _close(w.grad, wr.grad)
+    _close(bias.grad, br.grad, tol=1e-3)
+    _native.check_errors()

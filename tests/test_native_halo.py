@@ -80,11 +80,32 @@ def _body(rank, world):
     dist.broadcast(w, 0)
     hs = [H // world] * world
     xl = x[:, rank * hs[0]:(rank + 1) * hs[0]].contiguous()
-    got = es.einconv("b h/sp w c, kh kw c o -> b h/sp w o", xl, w, {"h": "kh", "w": "kw"}, mesh=mesh,
+    # forward and backward: the rows are sharded, so the conv reads the shard and
+    # its neighbours' ghost rows in place (no haloed copy)
+    ghost_calls = []
+    from torch_einshard_b200.ops import conv as conv_mod
+    real_ghosts = conv_mod.halo_ghost_rows
+    conv_mod.halo_ghost_rows = lambda *a, **k: ghost_calls.append(1) or real_ghosts(*a, **k)
+    xg = xl.clone().requires_grad_(True)
+    wg = w.clone().requires_grad_(True)
+    got = es.einconv("b h/sp w c, kh kw c o -> b h/sp w o", xg, wg, {"h": "kh", "w": "kw"}, mesh=mesh,
                      shapes={"sp": hs}, checkpoint=None)
-    ref = F.conv2d(x.float().permute(0, 3, 1, 2), w.float().permute(3, 2, 0, 1), padding=1).permute(0, 2, 3, 1)
-    ref = ref[:, rank * hs[0]:(rank + 1) * hs[0]]
-    assert (got.float() - ref).abs().max().item() <= 3e-2 * (ref.abs().max().item() + 1)
+    conv_mod.halo_ghost_rows = real_ghosts
+    assert ghost_calls, "the ghost-row conv path was not taken"
+    xr = x.float().requires_grad_(True)
+    wr = w.float().requires_grad_(True)
+    ref = F.conv2d(xr.permute(0, 3, 1, 2), wr.permute(3, 2, 0, 1), padding=1).permute(0, 2, 3, 1)
+    mine = ref[:, rank * hs[0]:(rank + 1) * hs[0]]
+    assert (got.float() - mine).abs().max().item() <= 3e-2 * (mine.abs().max().item() + 1)
+    gy = torch.randn(ref.shape, device="cuda", dtype=torch.bfloat16)
+    dist.broadcast(gy, 0)
+    got.backward(gy[:, rank * hs[0]:(rank + 1) * hs[0]])
+    ref.backward(gy.float())
+    want_dx = xr.grad[:, rank * hs[0]:(rank + 1) * hs[0]]
+    assert (xg.grad.float() - want_dx).abs().max().item() <= 3e-2 * (want_dx.abs().max().item() + 1)
+    dw = wg.grad.float()
+    dist.all_reduce(dw)  # each rank holds its shard's share of the weight gradient
+    assert (dw - wr.grad).abs().max().item() <= 3e-2 * (wr.grad.abs().max().item() + 1)
     torch.cuda.synchronize()
     _native.check_errors()
 

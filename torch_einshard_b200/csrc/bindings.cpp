@@ -811,8 +811,11 @@ void fft_slab(int64_t id, at::Tensor out, int64_t n, int64_t A, int64_t B, int64
 // out = conv(x, w) + bias with zero padding (ph, ph_hi) rows and (pw, pw_hi)
 // columns (hi < 0: the same as lo); kernel 0 picks the CTA-pair kernel with
 // resident weights where it fits, 1 forces conv.cu's kernel.
+// ghosts: empty, or [B][gtop + gbot][W][C] rows that continue x above and below
+// (the CTA-pair kernel reads them in place of a haloed copy of x).
 void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor& bias, at::Tensor out, int64_t ph,
-                     int64_t pw, int64_t ph_hi, int64_t pw_hi, int64_t kernel, const at::Tensor& err) {
+                     int64_t pw, int64_t ph_hi, int64_t pw_hi, int64_t kernel, const at::Tensor& ghosts, int64_t gtop,
+                     int64_t gbot, const at::Tensor& err) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda() && x.dim() == 4 && w.dim() == 4 && out.dim() == 4,
               "einshard conv: 4-D CUDA tensors required");
   TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "einshard conv: contiguous NHWC required");
@@ -846,6 +849,15 @@ void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
   a.pw_hi = static_cast<int>(pw_hi);
   a.kernel = static_cast<int>(kernel);
   a.prof = g_prof;
+  if (gtop + gbot > 0) {
+    TORCH_CHECK(ghosts.is_cuda() && ghosts.is_contiguous() && ghosts.dim() == 4 && ghosts.scalar_type() == x.scalar_type() &&
+                    ghosts.size(0) == x.size(0) && ghosts.size(1) == gtop + gbot && ghosts.size(2) == x.size(2) &&
+                    ghosts.size(3) == x.size(3) && gtop >= 0 && gbot >= 0,
+                "einshard conv: ghosts must be a contiguous [B, gtop + gbot, W, C] tensor like x");
+    a.ghosts = ghosts.data_ptr();
+    a.gtop = static_cast<int>(gtop);
+    a.gbot = static_cast<int>(gbot);
+  }
   const char* why = es::check_conv_args(a);
   TORCH_CHECK(why == nullptr, "einshard conv: ", why ? why : "");
   const int Hout = es::conv_hout(a);

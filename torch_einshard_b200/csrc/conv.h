@@ -21,11 +21,20 @@ struct ConvArgs {
   int persistent = 1;          // 1 persistent CTAs (default), 0 one tile per CTA (tuning)
   int kernel = 0;              // 0 auto (the pair kernel with resident weights where it fits), 1 conv.cu's kernel
   unsigned long long* prof = nullptr;  // pair kernel: wait-cycle counters (tuning), null when off
+  // ghost rows (pair kernel only): the input continues gtop rows above and
+  // gbot rows below x in ghosts [B][gtop + gbot][Win][C]; the zero padding
+  // ph / ph_hi lies beyond them
+  const void* ghosts = nullptr;
+  int gtop = 0, gbot = 0;
 };
+
+inline int conv_ghost_rows(const ConvArgs& a) { return a.gtop + a.gbot; }
+template <class Args>
+inline int conv_ghost_rows(const Args&) { return 0; }
 
 template <class Args>
 inline int conv_hout(const Args& a) {
-  return a.Hin + a.ph + (a.ph_hi < 0 ? a.ph : a.ph_hi) - a.KH + 1;
+  return a.Hin + conv_ghost_rows(a) + a.ph + (a.ph_hi < 0 ? a.ph : a.ph_hi) - a.KH + 1;
 }
 template <class Args>
 inline int conv_wout(const Args& a) {

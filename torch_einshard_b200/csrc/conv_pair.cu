@@ -26,6 +26,13 @@
 // zeros through TMA out-of-bounds fill; pads may differ per side (the caller
 // gives the offset and the output extent).
 //
+// Ghost rows (the halo of an image axis sharded over ranks): the input rows
+// may continue above and below the caller's tensor in a second, small tensor
+// G [B][gtop + gbot][W][C] (the neighbours' rows, exchanged beforehand).  A
+// tap row r < 0 reads G row r + gtop, a row r >= H reads G row gtop + r - H,
+// all others read the input itself, so the haloed input is never assembled in
+// memory.
+//
 // Warps (192 threads): 0 TMA producer, 1 MMA issuer (leader CTA) + TMEM owner,
 // 2..5 epilogue (TMEM lane quadrant warp % 4: one pixel per thread, its otile
 // channels as contiguous 32-byte stores).  Two TMEM accumulators of otile
@@ -80,6 +87,8 @@ struct PairShape {
   int ptiles;         // pixel tiles: B * Hout * wtiles
   int cblocks;        // C / 64
   int arows;          // rows of each A box (128 + KW - 1 rounded up to 8)
+  int rows_x;         // input rows per image in the input tensor
+  int gtop, gbot;     // ghost rows above and below it, in G (0: none)
   int tmem_cols;
   int in_bf16;
   int v8;             // output 32-byte aligned: 256-bit stores
@@ -152,6 +161,7 @@ __device__ __forceinline__ PixTile pix_tile(const PairShape& s, int p, int rank)
 template <typename OutT>
 __global__ void __launch_bounds__(kPThreads, 1)
     conv_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                     const __grid_constant__ CUtensorMap tmG,
                      const PairShape s, OutT* __restrict__ out, const float* __restrict__ bias) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -228,8 +238,18 @@ __global__ void __launch_bounds__(kPThreads, 1)
           if (s.prof) p_wait += clock64() - t_w;
           if (lane == 0) {
             if (leader) mbar_arrive_expect_tx(&st->full[stg], 2u * static_cast<uint32_t>(abytes));
-            tma_load_4d_pair(sA + stg * kAStage, &tmX, full_leader0 + stg * 8, cb * kBK, pt.w0 - s.pw,
-                             pt.h + kh - s.ph, pt.b);
+            // input row of this tap: the tensor itself, a ghost row, or zero fill
+            const int r = pt.h + kh - s.ph;
+            const CUtensorMap* map = &tmX;
+            int row = r;
+            if (r < 0 && r >= -s.gtop) {
+              map = &tmG;
+              row = r + s.gtop;
+            } else if (r >= s.rows_x && r < s.rows_x + s.gbot) {
+              map = &tmG;
+              row = s.gtop + r - s.rows_x;
+            }
+            tma_load_4d_pair(sA + stg * kAStage, map, full_leader0 + stg * 8, cb * kBK, pt.w0 - s.pw, row, pt.b);
           }
           __syncwarp();
         }
@@ -382,7 +402,10 @@ int launch_pair(const ConvArgs& a, int otile, cudaStream_t stream) {
   s.O = a.O;
   s.KH = a.KH;
   s.KW = a.KW;
-  s.ph = a.ph;
+  s.ph = a.ph + a.gtop;  // tap rows in the input tensor's coordinates
+  s.rows_x = a.Hin;
+  s.gtop = a.gtop;
+  s.gbot = a.gbot;
   s.pw = a.pw;
   s.Hout = conv_hout(a);
   s.Wout = conv_wout(a);
@@ -404,6 +427,14 @@ int launch_pair(const ConvArgs& a, int otile, cudaStream_t stream) {
                                static_cast<uint64_t>(a.Hin) * a.Win * a.C * 2};
   const uint32_t box[4] = {static_cast<uint32_t>(kBK), static_cast<uint32_t>(s.arows), 1, 1};
   const CUtensorMap mx = make_tmap_nd(a.x, dt, 4, dims, strides, box);
+  CUtensorMap mg = mx;
+  if (a.gtop + a.gbot > 0) {
+    const uint64_t gdims[4] = {static_cast<uint64_t>(a.C), static_cast<uint64_t>(a.Win),
+                               static_cast<uint64_t>(a.gtop + a.gbot), static_cast<uint64_t>(a.B)};
+    const uint64_t gstrides[3] = {static_cast<uint64_t>(a.C) * 2, static_cast<uint64_t>(a.Win) * a.C * 2,
+                                  static_cast<uint64_t>(a.gtop + a.gbot) * a.Win * a.C * 2};
+    mg = make_tmap_nd(a.ghosts, dt, 4, gdims, gstrides, box);
+  }
   // W: [O][K] (K-major), box 64 x otile / 2
   const CUtensorMap mw = make_tmap_3d(a.w, dt, 2, K, a.O, 1, K, static_cast<uint64_t>(K) * a.O, kBK,
                                       static_cast<uint32_t>(otile / 2));
@@ -428,12 +459,13 @@ int launch_pair(const ConvArgs& a, int otile, cudaStream_t stream) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return static_cast<int>(
-      cudaLaunchKernelEx(&cfg, kernel, mx, mw, s, reinterpret_cast<OutT*>(a.out), a.bias));
+      cudaLaunchKernelEx(&cfg, kernel, mx, mw, mg, s, reinterpret_cast<OutT*>(a.out), a.bias));
 }
 
 }  // namespace
 
 bool conv_pair_eligible(const ConvArgs& a) {
+  if (a.gtop + a.gbot > 0 && (a.ghosts == nullptr || (reinterpret_cast<uintptr_t>(a.ghosts) & 15) != 0)) return false;
   return a.C % kBK == 0 && a.KW >= 1 && a.KW <= 9 && a.O % 16 == 0 && a.num_sms >= 2 && pick_otile(a) > 0 &&
          (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && static_cast<long long>(a.C) * a.Win * 2 % 16 == 0;
 }

@@ -35,7 +35,7 @@ from ..notation.families import cached_expand_axis_families, expand_family_mappi
 from ..notation.parser import parse_sharding
 from ..notation.spec import EllipsisAxis
 from . import conv_impl
-from .halo import halo_tensor, halo_tensor_unpadded, normalize_halo, pad_dim
+from .halo import halo_ghost_rows, halo_tensor, halo_tensor_unpadded, normalize_halo, pad_dim
 
 __all__ = ["einconv"]
 
@@ -287,10 +287,20 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
     edges_in_kernel = (bool(exchanged) and boundary == "constant" and fill == 0 and
                        conv_impl.kernel_padding_ok(x, weight, x.shape[a.in_names.index(a.cin)], a.spatial, a.dilation))
     pads = dict(kernel_pads)
+    native_shape = groups == 1 and all(s == 1 for s in a.stride)  # the native kernels: stride 1, one group
+    # the first spatial axis (the NHWC rows) sharded: the pair conv reads the
+    # shard and its neighbours' rows in place, so no haloed copy is made along it
+    row = a.spatial[0]
+    ghost_rows = (edges_in_kernel and native_shape and a.ndim == 2 and row in exchanged and
+                  conv_impl.pair_kernel_fits(x.shape[a.in_names.index(a.cin)], weight.shape[a.w_names.index(a.cout)],
+                                             weight.shape[a.w_names.index(a.kernel[0])],
+                                             weight.shape[a.w_names.index(a.kernel[1])]))
 
     def conv(xa, wa, ba=None):
-        out = conv_impl.try_conv(xa, wa, ba, a.in_names, a.w_names, a.out_names, a.spatial, a.kernel, a.cin, a.cout,
-                                 a.dilation, pads)
+        out = None
+        if native_shape:
+            out = conv_impl.try_conv(xa, wa, ba, a.in_names, a.w_names, a.out_names, a.spatial, a.kernel, a.cin,
+                                     a.cout, a.dilation, pads)
         if out is not None:
             return out
         for name, (lo, hi) in pads.items():  # the torch path pads explicitly
@@ -303,6 +313,18 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
         return out.reshape((*lead, *out.shape[1:])).permute(layout.out_order(False)).contiguous()
 
     def halo_then_conv(xa, wa, *maybe_bias):
+        if ghost_rows:
+            others = {n: p for n, p in exchanged.items() if n != row}
+            za, edges = (halo_tensor_unpadded(a.in_spec, xa, others, mesh=mesh, shapes=shapes) if others
+                         else (xa, {}))
+            pads.update(edges)
+            left, right = normalize_halo(exchanged[row])
+            g, gtop, gbot, missing_lo, missing_hi, adjoint = halo_ghost_rows(
+                za, a.axis(a.in_spec, row), a.in_names.index(row), left, right, mesh=mesh, shapes=shapes)
+            pads[row] = (missing_lo, missing_hi)
+            return conv_impl.conv2d_nhwc_ghost_rows(za, g, gtop, gbot, adjoint, wa, maybe_bias[0] if maybe_bias else None,
+                                                    a.in_names, a.w_names, a.out_names, a.spatial, a.kernel, a.cin,
+                                                    a.cout, pads)
         if edges_in_kernel:
             haloed, edges = halo_tensor_unpadded(a.in_spec, xa, exchanged, mesh=mesh, shapes=shapes)
             pads.update(edges)

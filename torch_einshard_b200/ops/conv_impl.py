@@ -29,7 +29,8 @@ import torch
 
 from . import _native
 
-__all__ = ["conv2d_nhwc", "conv2d_native", "try_conv", "kernel_padding_ok"]
+__all__ = ["conv2d_nhwc", "conv2d_native", "conv2d_ghost_rows", "conv2d_nhwc_ghost_rows", "pair_kernel_fits",
+           "try_conv", "kernel_padding_ok"]
 
 _KERNEL = int(os.environ.get("EINSHARD_CONV_KERNEL", "0"))
 
@@ -38,14 +39,97 @@ def _lohi(p):
     return (int(p[0]), int(p[1])) if isinstance(p, (tuple, list)) else (int(p), int(p))
 
 
-def _run(mod, x, w, bias, ph, pw):
-    """ph, pw: (lo, hi) zero padding of the rows and the columns."""
+def _run(mod, x, w, bias, ph, pw, ghosts=None, gtop=0, gbot=0):
+    """ph, pw: (lo, hi) zero padding of the rows and the columns; ghosts: rows
+    that continue x above (gtop) and below (gbot), [B, gtop + gbot, W, C]."""
     B, H, W, _ = x.shape
     O, KH, KW, _ = w.shape
-    out = torch.empty(B, H + ph[0] + ph[1] - KH + 1, W + pw[0] + pw[1] - KW + 1, O, dtype=x.dtype, device=x.device)
+    Hv = H + gtop + gbot
+    out = torch.empty(B, Hv + ph[0] + ph[1] - KH + 1, W + pw[0] + pw[1] - KW + 1, O, dtype=x.dtype, device=x.device)
     b = bias if bias is not None else torch.empty(0, dtype=torch.float32, device=x.device)
-    mod.conv2d_implicit(x, w, b, out, ph[0], pw[0], ph[1], pw[1], _KERNEL, _native.error_word(x.device))
+    g = ghosts.contiguous() if ghosts is not None else torch.empty(0, dtype=x.dtype, device=x.device)
+    mod.conv2d_implicit(x, w, b, out, ph[0], pw[0], ph[1], pw[1], _KERNEL, g, gtop, gbot,
+                        _native.error_word(x.device))
     return out
+
+
+# Shared-memory budget of the CTA-pair kernel's resident weights (csrc/conv_pair.cu:
+# 227 KB per block less 4 input stages of 17 KB, alignment and barriers).
+_PAIR_WEIGHT_BYTES = 232448 - 1024 - 4 * 136 * 128 - 256
+
+
+def pair_kernel_fits(C, O, KH, KW):
+    """Whether the CTA-pair kernel (the only one that reads ghost rows) takes
+    this shape: channels as its boxes need, and some output-channel tile whose
+    weight slice fits in shared memory (the kernel's own choice, csrc/conv_pair.cu)."""
+    if C % 64 or O % 16 or KW > 9:
+        return False
+    return any(ot <= O and O % ot == 0 and KH * KW * (C // 64) * (ot // 2) * 128 <= _PAIR_WEIGHT_BYTES
+               for ot in (128, 64, 32, 16))
+
+
+class _Conv2dGhostRows(torch.autograd.Function):
+    """NHWC conv2d of the rows [ghosts above; x; ghosts below] without
+    assembling them: the pair kernel reads x and the ghost tensor in place.
+    Backward: the gradient of the whole haloed input from the flipped-kernel
+    conv, handed to ``adjoint`` (the halo exchange's adjoint, which returns the
+    ghost rows' share to their owners); the weight gradient over the haloed
+    input, assembled only here."""
+
+    @staticmethod
+    def forward(ctx, x, ghosts, w, bias, gtop, gbot, ph, pw, adjoint):
+        ctx.save_for_backward(x, ghosts, w)
+        ctx.meta = (gtop, gbot, ph, pw, adjoint)
+        ctx.has_bias = bias is not None
+        ctx.bias_dtype = bias.dtype if bias is not None else None
+        return _run(_native.require(), x, w, None if bias is None else bias.float().contiguous(), ph, pw,
+                    ghosts, gtop, gbot)
+
+    @staticmethod
+    def backward(ctx, grad):
+        x, g, w = ctx.saved_tensors
+        gtop, gbot, ph, pw, adjoint = ctx.meta
+        grad = grad.contiguous()
+        O, KH, KW, C = w.shape
+        gx = gw = gb = None
+        haloed = None
+
+        def assembled():
+            return torch.cat([g.narrow(1, 0, gtop), x, g.narrow(1, gtop, gbot)], 1)
+        native_dgrad = O % 64 == 0 and KH - 1 >= max(ph) and KW - 1 >= max(pw)
+        if ctx.needs_input_grad[0]:
+            if native_dgrad:
+                wt = w.flip(1, 2).permute(3, 1, 2, 0).contiguous()  # [C][KH][KW][O]
+                dv = _run(_native.require(), grad, wt, None, (KH - 1 - ph[0], KH - 1 - ph[1]),
+                          (KW - 1 - pw[0], KW - 1 - pw[1]))
+            else:
+                haloed = assembled()
+                xt = torch.nn.functional.pad(haloed.permute(0, 3, 1, 2), (pw[0], pw[1], ph[0], ph[1]))
+                dv = torch.nn.grad.conv2d_input(xt.shape, w.permute(0, 3, 1, 2), grad.permute(0, 3, 1, 2))
+                dv = dv[:, :, ph[0]:ph[0] + haloed.shape[1], pw[0]:pw[0] + haloed.shape[2]].permute(0, 2, 3, 1)
+            gx = adjoint(dv.contiguous())
+        if ctx.needs_input_grad[2]:
+            haloed = assembled() if haloed is None else haloed
+            if O % 64 == 0:
+                dw = torch.empty(O, KH, KW, C, dtype=torch.float32, device=x.device)
+                _native.require().conv2d_wgrad(haloed.contiguous(), grad, dw, ph[0], pw[0], ph[1], pw[1],
+                                               _native.error_word(x.device))
+                gw = dw.to(w.dtype)
+            else:
+                xt = torch.nn.functional.pad(haloed.permute(0, 3, 1, 2), (pw[0], pw[1], ph[0], ph[1]))
+                gw = torch.nn.grad.conv2d_weight(xt, w.permute(0, 3, 1, 2).shape,
+                                                 grad.permute(0, 3, 1, 2)).permute(0, 2, 3, 1)
+        if ctx.has_bias and ctx.needs_input_grad[3]:
+            gb = grad.float().sum(dim=(0, 1, 2)).to(ctx.bias_dtype)
+        return gx, None, gw, gb, None, None, None, None, None
+
+
+def conv2d_ghost_rows(x, ghosts, gtop, gbot, adjoint, w, bias=None, ph=0, pw=0):
+    """NHWC conv2d of [ghosts[:, :gtop]; x; ghosts[:, gtop:]] along the rows
+    with zero padding ph / pw beyond them, on the CTA-pair kernel."""
+    ph, pw = _lohi(ph), _lohi(pw)
+    x, w = x.contiguous(), w.contiguous()
+    return _Conv2dGhostRows.apply(x, ghosts.detach().contiguous(), w, bias, gtop, gbot, ph, pw, adjoint)
 
 
 def _torch_pads(ph, pw):
@@ -127,6 +211,30 @@ def conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, ker
     xn = xn.reshape(-1, *xn.shape[len(batch):])
     wn = weight.permute([w_names.index(n) for n in [cout] + list(kernel) + [cin]])
     out = conv2d_native(xn, wn, bias, pads.get(spatial[0], 0), pads.get(spatial[1], 0))
+    out = out.reshape(*lead, *out.shape[1:])
+    produced = batch + list(spatial) + [cout]
+    return out.permute([produced.index(n) for n in out_names]).contiguous()
+
+
+def conv2d_nhwc_ghost_rows(x, ghosts, gtop, gbot, adjoint, weight, bias, in_names, w_names, out_names, spatial,
+                           kernel, cin, cout, pads):
+    """einconv's named-axis call with ghost rows along ``spatial[0]`` (the NHWC
+    H axis): x and ghosts in ``in_names`` order; ``adjoint`` maps a gradient of
+    the haloed input (in ``in_names`` order) to x's gradient."""
+    batch = [n for n in in_names if n not in spatial and n != cin]
+    order = [in_names.index(n) for n in batch + list(spatial) + [cin]]
+    inverse = [order.index(d) for d in range(len(order))]
+    xn = x.permute(order)
+    lead = xn.shape[:len(batch)]
+    xn = xn.reshape(-1, *xn.shape[len(batch):])
+    gn = ghosts.permute(order).reshape(-1, *ghosts.permute(order).shape[len(batch):])
+
+    def adjoint_nhwc(dv):
+        d = adjoint(dv.reshape(*lead, *dv.shape[1:]).permute(inverse))
+        return d.permute(order).reshape(-1, *d.permute(order).shape[len(batch):])
+    wn = weight.permute([w_names.index(n) for n in [cout] + list(kernel) + [cin]])
+    out = conv2d_ghost_rows(xn, gn, gtop, gbot, adjoint_nhwc, wn, bias, pads.get(spatial[0], 0),
+                            pads.get(spatial[1], 0))
     out = out.reshape(*lead, *out.shape[1:])
     produced = batch + list(spatial) + [cout]
     return out.permute([produced.index(n) for n in out_names]).contiguous()

@@ -122,85 +122,94 @@ def _resized(x, dim, length):
     return x.new_empty(shape)
 
 
+def _halo_forward(x, group, dim, shapes, left, right, periodic):
+    """The haloed shard of x along ``dim`` (native staged exchange, else NCCL P2P)."""
+    size, rank = dist.get_world_size(group), dist.get_rank(group)
+    if len(shapes) != size:
+        raise ValueError(f"Error: passed shapes of size {len(shapes)} not equal to {size}")
+    if x.shape[dim] != shapes[rank]:
+        raise ValueError(f"Local tensor size {x.shape[dim]} does not match split shape {shapes[rank]}")
+    table = halo_intervals(shapes, left, right, periodic=periodic)
+    length = shapes[rank] + left + right if periodic else sum(p[3] for p in table[rank])
+    from ..parallel import symmetric
+    comm = symmetric.communicator_for(group) if x.is_cuda else None
+    if comm is not None:
+        out = comm.halo_gather(x.contiguous(), dim, table, length, shapes)
+        if out is not None:
+            return out
+    out = _resized(x, dim, length)
+    ops, landing, keep = [], [], []
+    for out_off, src, src_off, n in table[rank]:
+        target = out.narrow(dim, out_off, n)
+        if src == rank:
+            target.copy_(x.narrow(dim, src_off, n))
+            continue
+        incoming = torch.empty_like(target)
+        landing.append((incoming, target))
+        ops.append(dist.P2POp(dist.irecv, incoming, dist.get_global_rank(group, src), group))
+    for dst, pieces in enumerate(table):
+        if dst == rank:
+            continue
+        for _, src, src_off, n in pieces:
+            if src == rank:
+                outgoing = x.narrow(dim, src_off, n).contiguous()
+                keep.append(outgoing)
+                ops.append(dist.P2POp(dist.isend, outgoing, dist.get_global_rank(group, dst), group))
+    if ops:
+        for request in dist.batch_isend_irecv(ops):
+            request.wait()
+    for incoming, target in landing:
+        target.copy_(incoming)
+    return out.contiguous()
+
+
+def _halo_adjoint(grad, group, dim, shapes, left, right, periodic, in_shape):
+    """Adjoint of _halo_forward: every haloed row's gradient back to its owner, summed."""
+    rank = dist.get_rank(group)
+    table = halo_intervals(shapes, left, right, periodic=periodic)
+    from ..parallel import symmetric
+    comm = symmetric.communicator_for(group) if grad.is_cuda else None
+    if comm is not None:
+        out = comm.halo_scatter_add(grad.contiguous(), dim, table, in_shape)
+        if out is not None:
+            return out
+    grad_in = grad.new_zeros(in_shape)
+    ops, landing, keep = [], [], []
+    for out_off, src, src_off, n in table[rank]:
+        piece = grad.narrow(dim, out_off, n)
+        if src == rank:
+            grad_in.narrow(dim, src_off, n).add_(piece)
+            continue
+        outgoing = piece.contiguous()
+        keep.append(outgoing)
+        ops.append(dist.P2POp(dist.isend, outgoing, dist.get_global_rank(group, src), group))
+    for dst, pieces in enumerate(table):
+        if dst == rank:
+            continue
+        for _, src, src_off, n in pieces:
+            if src != rank:
+                continue
+            target = grad_in.narrow(dim, src_off, n)
+            incoming = torch.empty_like(target)
+            landing.append((incoming, target))
+            ops.append(dist.P2POp(dist.irecv, incoming, dist.get_global_rank(group, dst), group))
+    if ops:
+        for request in dist.batch_isend_irecv(ops):
+            request.wait()
+    for incoming, target in landing:
+        target.add_(incoming)
+    return grad_in
+
+
 class _HaloExchange(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, group, dim, shapes, left, right, periodic):
-        size, rank = dist.get_world_size(group), dist.get_rank(group)
-        if len(shapes) != size:
-            raise ValueError(f"Error: passed shapes of size {len(shapes)} not equal to {size}")
-        if x.shape[dim] != shapes[rank]:
-            raise ValueError(f"Local tensor size {x.shape[dim]} does not match split shape {shapes[rank]}")
-        table = halo_intervals(shapes, left, right, periodic=periodic)
-        length = shapes[rank] + left + right if periodic else sum(p[3] for p in table[rank])
         ctx.saved = (group, dim, shapes, left, right, periodic, tuple(x.shape))
-        from ..parallel import symmetric
-        comm = symmetric.communicator_for(group) if x.is_cuda else None
-        if comm is not None:
-            out = comm.halo_gather(x.contiguous(), dim, table, length, shapes)
-            if out is not None:
-                return out
-        out = _resized(x, dim, length)
-        ops, landing, keep = [], [], []
-        for out_off, src, src_off, n in table[rank]:
-            target = out.narrow(dim, out_off, n)
-            if src == rank:
-                target.copy_(x.narrow(dim, src_off, n))
-                continue
-            incoming = torch.empty_like(target)
-            landing.append((incoming, target))
-            ops.append(dist.P2POp(dist.irecv, incoming, dist.get_global_rank(group, src), group))
-        for dst, pieces in enumerate(table):
-            if dst == rank:
-                continue
-            for _, src, src_off, n in pieces:
-                if src == rank:
-                    outgoing = x.narrow(dim, src_off, n).contiguous()
-                    keep.append(outgoing)
-                    ops.append(dist.P2POp(dist.isend, outgoing, dist.get_global_rank(group, dst), group))
-        if ops:
-            for request in dist.batch_isend_irecv(ops):
-                request.wait()
-        for incoming, target in landing:
-            target.copy_(incoming)
-        return out.contiguous()
+        return _halo_forward(x, group, dim, shapes, left, right, periodic)
 
     @staticmethod
     def backward(ctx, grad):
-        group, dim, shapes, left, right, periodic, in_shape = ctx.saved
-        rank = dist.get_rank(group)
-        table = halo_intervals(shapes, left, right, periodic=periodic)
-        from ..parallel import symmetric
-        comm = symmetric.communicator_for(group) if grad.is_cuda else None
-        if comm is not None:
-            out = comm.halo_scatter_add(grad.contiguous(), dim, table, in_shape)
-            if out is not None:
-                return out, None, None, None, None, None, None
-        grad_in = grad.new_zeros(in_shape)
-        ops, landing, keep = [], [], []
-        for out_off, src, src_off, n in table[rank]:
-            piece = grad.narrow(dim, out_off, n)
-            if src == rank:
-                grad_in.narrow(dim, src_off, n).add_(piece)
-                continue
-            outgoing = piece.contiguous()
-            keep.append(outgoing)
-            ops.append(dist.P2POp(dist.isend, outgoing, dist.get_global_rank(group, src), group))
-        for dst, pieces in enumerate(table):
-            if dst == rank:
-                continue
-            for _, src, src_off, n in pieces:
-                if src != rank:
-                    continue
-                target = grad_in.narrow(dim, src_off, n)
-                incoming = torch.empty_like(target)
-                landing.append((incoming, target))
-                ops.append(dist.P2POp(dist.irecv, incoming, dist.get_global_rank(group, dst), group))
-        if ops:
-            for request in dist.batch_isend_irecv(ops):
-                request.wait()
-        for incoming, target in landing:
-            target.add_(incoming)
-        return grad_in, None, None, None, None, None, None
+        return _halo_adjoint(grad, *ctx.saved), None, None, None, None, None, None
 
 
 def _sharded_halo(x, axis, dim, left, right, *, mesh, shapes, boundary, fill):
@@ -234,6 +243,46 @@ def _sharded_halo_unpadded(x, axis, dim, left, right, *, mesh, shapes, boundary)
     lo, hi = max(0, start - left), min(total, start + local + right)
     z = _HaloExchange.apply(x, group, dim, split, left, right, False)
     return z, lo - (start - left), (start + local + right) - hi
+
+
+def halo_ghost_rows(x, axis, dim, left, right, *, mesh, shapes):
+    """Zero-boundary halo of a sharded axis for a consumer that reads the
+    shard and its neighbours' rows in place (the pair conv's ghost rows):
+    returns (G, gtop, gbot, missing_lo, missing_hi, adjoint).  G holds the
+    gtop rows above the shard and the gbot rows below it along ``dim`` (only
+    the rows peers own; the shard is not copied), missing_lo / missing_hi the
+    zero rows beyond the global edges, and adjoint(dv) maps the gradient of
+    the haloed shard (gtop + shard + gbot rows) back to the shard's gradient."""
+    if mesh is None:
+        raise ValueError("Sharded einhalo axes require mesh")
+    group = mesh[axis.shard_dim].get_group()
+    size, rank = dist.get_world_size(group), dist.get_rank(group)
+    split = resolve_split_shapes(shapes, axis.shard_dim, axis.name, group)
+    if split is None:
+        split = [x.shape[dim]] * size
+    if x.shape[dim] != split[rank]:
+        raise ValueError(
+            f"Local tensor size {x.shape[dim]} does not match split shape {split[rank]} for axis {axis.name!r}"
+        )
+    total, start, local = sum(split), sum(split[:rank]), split[rank]
+    lo, hi = max(0, start - left), min(total, start + local + right)
+    table = halo_intervals(split, left, right, periodic=False)
+    length = sum(p[3] for p in table[rank])
+    from ..parallel import symmetric
+    comm = symmetric.communicator_for(group) if x.is_cuda else None
+    got = comm.halo_ghosts(x, dim, table, length) if comm is not None else None
+    if got is None:
+        full = _halo_forward(x, group, dim, split, left, right, False)
+        gtop, gbot = start - lo, hi - (start + local)
+        g = torch.cat([full.narrow(dim, 0, gtop), full.narrow(dim, gtop + local, gbot)], dim)
+    else:
+        g, gtop, gbot = got
+    in_shape = tuple(x.shape)
+
+    def adjoint(dv):
+        return _halo_adjoint(dv, group, dim, split, left, right, False, in_shape)
+
+    return g, gtop, gbot, lo - (start - left), (start + local + right) - hi, adjoint
 
 
 def _check_axes(axes):

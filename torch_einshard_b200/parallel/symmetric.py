@@ -195,6 +195,29 @@ def halo_gather_plan(rank, x_shape, dim, table, length, esize):
     return send, boxes, out_shape
 
 
+def halo_ghost_plan(rank, x_shape, dim, table, length, esize):
+    """Plan of ``Communicator.halo_ghosts``: only the rows this rank's haloed
+    shard takes from peers, as one tensor G whose first ``gtop`` rows (along
+    ``dim``) lie above the shard and the other ``gbot`` below it.  Returns
+    (send, boxes, G shape, gtop, gbot), or None when the shard's own rows are
+    not exactly one piece (a periodic halo wider than the group)."""
+    pieces = table[rank]
+    own = [i for i, p in enumerate(pieces) if p[1] == rank]
+    if len(own) != 1:
+        return None
+    k = own[0]
+    local_n = pieces[k][3]
+    mine = [(p[0] if i < k else p[0] - local_n, p[1], p[2], p[3]) for i, p in enumerate(pieces) if i != k]
+    gtop = sum(p[3] for p in pieces[:k])
+    gbot = sum(p[3] for p in pieces[k + 1:])
+    # only this rank's entry changes: every peer packs from its own unchanged
+    # table in the same order, so the packed offsets agree
+    ghost_table = list(table)
+    ghost_table[rank] = mine
+    send, boxes, g_shape = halo_gather_plan(rank, x_shape, dim, ghost_table, length - local_n, esize)
+    return send, boxes, g_shape, gtop, gbot
+
+
 def halo_scatter_plan(rank, size, grad_shape, dim, table, in_shape, esize):
     """Host plan of ``Communicator.halo_scatter_add`` on rank ``rank``: the
     ghost slabs of its gradient (offset, rows) it packs and returns to their
@@ -572,6 +595,26 @@ class Communicator:
         out = x.new_empty(out_shape)
         stage = torch.cat([x.narrow(dim, off, n) for off, n in send], dim) if send else None
         return out if self._copy(stage, out, boxes, local=x) else None
+
+    def halo_ghosts(self, x, dim, table, length):
+        """The rows of this rank's haloed shard that peers hold, without the
+        shard itself: (G, gtop, gbot) with G's first gtop rows along ``dim``
+        above the shard and the next gbot below it (``halo_ghost_plan``), or
+        None.  A consumer that reads x and G in place (the pair conv) needs no
+        haloed copy of x."""
+        if self.broken:
+            return None
+        x = x.contiguous()
+        plan = halo_ghost_plan(self.rank, list(x.shape), dim, table, length, x.element_size())
+        if plan is None:
+            return None
+        send, boxes, g_shape, gtop, gbot = plan
+        g = x.new_empty(g_shape)
+        stage = torch.cat([x.narrow(dim, off, n) for off, n in send], dim) if send else None
+        # collective: every rank launches the staged copy, with or without boxes
+        if not self._copy(stage, g, boxes, local=x):
+            return None
+        return g, gtop, gbot
 
     def halo_scatter_add(self, grad, dim, table, in_shape):
         """Adjoint of halo_gather: this rank's own rows of ``grad`` add into the
