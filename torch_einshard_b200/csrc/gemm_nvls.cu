@@ -476,9 +476,11 @@ int gemm_nvls_allreduce_launch(const GemmArgs& g, const NvlsGemmJob& nj, cudaStr
   epi.tiles = pairs;
   epi.lag = 0;
   if (nj.reducer_clusters == 0) {
-    // one tile per cluster; slot p reduces tile p - lag: with lag = the pairs
-    // resident at once, tile p - lag finished about when cluster p started
-    epi.lag = es_min(pairs, nj.lag > 0 ? nj.lag : g.num_sms / 2);
+    // one tile per cluster; slot p reduces tile p - lag.  Two waves of
+    // resident pairs: tile p - lag finished a wave before cluster p started on
+    // this rank, which leaves a wave of slack for ranks running behind (2 GPUs:
+    // 6.58 ms at lag 148 against 6.74 at 74, 6.27 at 37 and 9.30 at 16)
+    epi.lag = es_min(pairs, nj.lag > 0 ? nj.lag : g.num_sms);
   }
 
   auto kernel = gemm_nvls_ar_kernel;

@@ -524,8 +524,8 @@ _FUSED_NVLS = os.environ.get("EINSHARD_FUSED_NVLS", "1") not in ("0", "")
 # Who reduces in the fused launch: 0 = the GEMM's own epilogue warps, while
 # later tiles' mainloops run (overlap mode, every SM computes); n > 0 = n CTA
 # pairs at the front of the launch that only reduce and copy out.  _NVLS_LAG:
-# overlap mode's distance in tiles between a tile and its reduction (0: the
-# number of CTA pairs resident at once).
+# overlap mode's distance in tiles between a tile and its reduction (0: two
+# waves of resident CTA pairs).
 _NVLS_REDUCER_CLUSTERS = int(os.environ.get("EINSHARD_NVLS_REDUCER_CLUSTERS", "0"))
 _NVLS_LAG = int(os.environ.get("EINSHARD_NVLS_LAG", "0"))
 _MAX_FUSED_EPILOGUE_RANKS = int(os.environ.get("EINSHARD_FUSED_EPILOGUE_MAX_RANKS", "0"))
