@@ -40,6 +40,9 @@ def main():
     p.add_argument("--nx", type=int, default=0, help="length of the x axis (default n); smaller for profiling")
     p.add_argument("--steps", type=int, default=5)
     p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--breakdown", action="store_true",
+                   help="after the timed steps, one more step under torch.profiler: rank 0's kernels with their "
+                        "device time (not a timing run)")
     args = p.parse_args()
     if "RANK" not in os.environ:
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT="29611", RANK="0", WORLD_SIZE="1", LOCAL_RANK="0")
@@ -107,6 +110,17 @@ def main():
         if sampler:
             sampler.mark_end()
         dist.barrier()
+    if args.breakdown:
+        from torch.profiler import ProfilerActivity, profile
+        with torch.no_grad(), profile(activities=[ProfilerActivity.CUDA]) as prof:
+            step()
+            torch.cuda.synchronize()
+        kernels = []
+        for ev in prof.events():
+            if ev.device_type.name == "CUDA":
+                kernels.append([ev.name[:80], round(ev.device_time_total / 1e3, 3)])
+        if rank == 0:
+            print(json.dumps({"breakdown_rank": rank, "kernels_ms_in_order": kernels[:40]}), flush=True)
     ms = torch.tensor([t0.elapsed_time(t1) / args.steps], device="cuda", dtype=torch.float64)
     dist.all_reduce(ms, op=dist.ReduceOp.MAX)
     ms = ms.item()
