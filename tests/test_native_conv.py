@@ -195,3 +195,25 @@ def test_conv_ghost_rows_forward_backward(gtop, gbot, ph):
     _close(w.grad, wr.grad)
     _close(bias.grad, br.grad, tol=1e-3)
     _native.check_errors()
+
+
+@pytest.mark.parametrize("gl,gr,gtop,gbot,ph,pw", [(1, 1, 1, 1, (0, 0), (0, 0)), (1, 0, 0, 1, (1, 0), (0, 1)),
+                                                   (0, 1, 0, 0, (1, 1), (1, 0))])
+def test_conv_ghost_2d_native(gl, gr, gtop, gbot, ph, pw):
+    """The two-axis ghost conv on the native kernels (wider ghost rows, output
+    column ranges, transposed strips) against a conv of the assembled input."""
+    from torch_einshard_b200.ops.conv_impl import conv2d_ghost_2d
+    torch.manual_seed(6)
+    B, H, W, C, O = 2, 20, 300, 64, 128
+    full = torch.randn(B, gtop + H + gbot, gl + W + gr, C, device="cuda", dtype=torch.bfloat16)
+    x = full[:, gtop:gtop + H, gl:gl + W].contiguous()
+    cols = torch.cat([full[:, gtop:gtop + H, :gl], full[:, gtop:gtop + H, gl + W:]], 2).contiguous()
+    ghosts = torch.cat([full[:, :gtop], full[:, gtop + H:]], 1).contiguous() if gtop + gbot else None
+    w = (torch.randn(O, 3, 3, C, device="cuda") * 0.05).to(torch.bfloat16)
+    bias = torch.randn(O, device="cuda")
+    got = conv2d_ghost_2d(x, ghosts, gtop, gbot, cols, gl, gr, w, bias, ph, pw)
+    xp = F.pad(full.float().permute(0, 3, 1, 2), (pw[0], pw[1], ph[0], ph[1]))
+    want = F.conv2d(xp, w.float().permute(0, 3, 1, 2), bias).permute(0, 2, 3, 1)
+    assert got.shape == want.shape
+    _close(got, want)
+    _native.check_errors()

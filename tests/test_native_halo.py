@@ -106,6 +106,25 @@ def _body(rank, world):
     dw = wg.grad.float()
     dist.all_reduce(dw)  # each rank holds its shard's share of the weight gradient
     assert (dw - wr.grad).abs().max().item() <= 3e-2 * (wr.grad.abs().max().item() + 1)
+
+    # inference with the second image axis sharded: ghost columns exchanged as a
+    # thin tensor, interior conv plus transposed edge strips (no haloed copy)
+    cols_calls = []
+    real_2d = conv_mod.conv_impl.conv2d_ghost_2d
+    conv_mod.conv_impl.conv2d_ghost_2d = lambda *a, **k: cols_calls.append(1) or real_2d(*a, **k)
+    Wd = 32 * world
+    xw = torch.randn(2, 12, Wd, C, device="cuda", dtype=torch.bfloat16)
+    dist.broadcast(xw, 0)
+    ws_ = [Wd // world] * world
+    xwl = xw[:, :, rank * ws_[0]:(rank + 1) * ws_[0]].contiguous()
+    with torch.no_grad():
+        got = es.einconv("b h w/sp c, kh kw c o -> b h w/sp o", xwl, w, {"h": "kh", "w": "kw"}, mesh=mesh,
+                         shapes={"sp": ws_}, checkpoint=None)
+    conv_mod.conv_impl.conv2d_ghost_2d = real_2d
+    assert cols_calls, "the two-axis ghost conv path was not taken"
+    ref = F.conv2d(xw.float().permute(0, 3, 1, 2), w.float().permute(3, 2, 0, 1), padding=1).permute(0, 2, 3, 1)
+    ref = ref[:, :, rank * ws_[0]:(rank + 1) * ws_[0]]
+    assert (got.float() - ref).abs().max().item() <= 3e-2 * (ref.abs().max().item() + 1)
     torch.cuda.synchronize()
     _native.check_errors()
 

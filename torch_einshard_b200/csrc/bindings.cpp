@@ -813,9 +813,12 @@ void fft_slab(int64_t id, at::Tensor out, int64_t n, int64_t A, int64_t B, int64
 // resident weights where it fits, 1 forces conv.cu's kernel.
 // ghosts: empty, or [B][gtop + gbot][W][C] rows that continue x above and below
 // (the CTA-pair kernel reads them in place of a haloed copy of x).
+// ghost_wpitch / ghost_w0: ghost rows wider than x, x's columns from ghost_w0;
+// out_w0: the computed columns go to columns out_w0 .. of out (whose width
+// may exceed the conv's; 0 with out as wide as the conv: the whole output).
 void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor& bias, at::Tensor out, int64_t ph,
                      int64_t pw, int64_t ph_hi, int64_t pw_hi, int64_t kernel, const at::Tensor& ghosts, int64_t gtop,
-                     int64_t gbot, const at::Tensor& err) {
+                     int64_t gbot, int64_t ghost_w0, int64_t out_w0, const at::Tensor& err) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda() && x.dim() == 4 && w.dim() == 4 && out.dim() == 4,
               "einshard conv: 4-D CUDA tensors required");
   TORCH_CHECK(x.is_contiguous() && w.is_contiguous() && out.is_contiguous(), "einshard conv: contiguous NHWC required");
@@ -851,18 +854,28 @@ void conv2d_implicit(const at::Tensor& x, const at::Tensor& w, const at::Tensor&
   a.prof = g_prof;
   if (gtop + gbot > 0) {
     TORCH_CHECK(ghosts.is_cuda() && ghosts.is_contiguous() && ghosts.dim() == 4 && ghosts.scalar_type() == x.scalar_type() &&
-                    ghosts.size(0) == x.size(0) && ghosts.size(1) == gtop + gbot && ghosts.size(2) == x.size(2) &&
+                    ghosts.size(0) == x.size(0) && ghosts.size(1) == gtop + gbot && ghosts.size(2) >= x.size(2) &&
                     ghosts.size(3) == x.size(3) && gtop >= 0 && gbot >= 0,
                 "einshard conv: ghosts must be a contiguous [B, gtop + gbot, W, C] tensor like x");
     a.ghosts = ghosts.data_ptr();
     a.gtop = static_cast<int>(gtop);
     a.gbot = static_cast<int>(gbot);
   }
+  if (gtop + gbot > 0) {
+    TORCH_CHECK(ghost_w0 >= 0 && ghost_w0 + x.size(2) <= ghosts.size(2), "einshard conv: ghost column range");
+    a.ghost_wpitch = static_cast<int>(ghosts.size(2));
+    a.ghost_w0 = static_cast<int>(ghost_w0);
+  }
   const char* why = es::check_conv_args(a);
   TORCH_CHECK(why == nullptr, "einshard conv: ", why ? why : "");
   const int Hout = es::conv_hout(a);
   const int Wout = es::conv_wout(a);
-  TORCH_CHECK(out.size(0) == a.B && out.size(1) == Hout && out.size(2) == Wout && out.size(3) == a.O,
+  if (out.size(2) != Wout || out_w0 != 0) {  // the conv fills columns out_w0 .. out_w0 + Wout of out
+    TORCH_CHECK(out_w0 >= 0 && out_w0 + Wout <= out.size(2), "einshard conv: output column range");
+    a.out_wpitch = static_cast<int>(out.size(2));
+    a.out_w0 = static_cast<int>(out_w0);
+  }
+  TORCH_CHECK(out.size(0) == a.B && out.size(1) == Hout && out.size(2) >= Wout && out.size(3) == a.O,
               "einshard conv: output shape");
   const c10::cuda::CUDAGuard guard(x.device());
   const int rc = es::conv_launch(a, at::cuda::getCurrentCUDAStream());

@@ -374,7 +374,8 @@ const char* check_conv_args(const ConvArgs& a) {
 
 int conv_launch(const ConvArgs& a, cudaStream_t stream) {
   if (check_conv_args(a)) return -1;
-  if (a.gtop + a.gbot > 0) return conv_pair_eligible(a) ? conv_pair_launch(a, stream) : -1;  // ghosts: pair kernel only
+  if (a.gtop + a.gbot > 0 || a.out_wpitch > 0)  // ghosts and column ranges: pair kernel only
+    return conv_pair_eligible(a) ? conv_pair_launch(a, stream) : -1;
   if (a.kernel == 0 && conv_pair_eligible(a)) return conv_pair_launch(a, stream);
   return a.dtype == kDtypeBF16 ? launch<__nv_bfloat16>(a, stream) : launch<__half>(a, stream);
 }

@@ -26,6 +26,10 @@ struct ConvArgs {
   // ph / ph_hi lies beyond them
   const void* ghosts = nullptr;
   int gtop = 0, gbot = 0;
+  int ghost_wpitch = 0, ghost_w0 = 0;  // ghost rows of ghost_wpitch pixels (0: Win), x's columns from ghost_w0
+  // output rows of out_wpitch pixels (0: Wout), the computed columns written from
+  // column out_w0 on (pair kernel only): a conv that fills a column range of out
+  int out_wpitch = 0, out_w0 = 0;
 };
 
 inline int conv_ghost_rows(const ConvArgs& a) { return a.gtop + a.gbot; }

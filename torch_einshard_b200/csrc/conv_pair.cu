@@ -81,6 +81,7 @@ struct PairShape {
   int B, C, O, KH, KW;
   int ph, pw;         // input offset of output pixel (0, 0) is (-ph, -pw)
   int Hout, Wout;
+  int out_wpitch, out_w0;  // output rows hold out_wpitch pixels; computed column w goes to w + out_w0
   int otile;          // output channels per tile (MMA N), multiple of 16
   int n_otiles;       // O / otile
   int wtiles;         // pair tiles per output row
@@ -344,7 +345,8 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const PixTile pt = pix_tile(s, p, static_cast<int>(rank));
       const int w = pt.w0 + q * 32 + lane;
       const bool valid = w < s.Wout;
-      OutT* dst = out + ((static_cast<long long>(pt.b) * s.Hout + pt.h) * s.Wout + w) * s.O + ot * s.otile;
+      OutT* dst = out + ((static_cast<long long>(pt.b) * s.Hout + pt.h) * s.out_wpitch + w + s.out_w0) * s.O +
+                  ot * s.otile;
       const uint32_t taddr = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + acc * s.otile;
       for (int ch = 0; ch < s.otile; ch += 32) {
         uint32_t v[32];
@@ -409,6 +411,8 @@ int launch_pair(const ConvArgs& a, int otile, cudaStream_t stream) {
   s.pw = a.pw;
   s.Hout = conv_hout(a);
   s.Wout = conv_wout(a);
+  s.out_wpitch = a.out_wpitch > 0 ? a.out_wpitch : s.Wout;
+  s.out_w0 = a.out_w0;
   s.otile = otile;
   s.n_otiles = a.O / otile;
   s.wtiles = (s.Wout + kPairPx - 1) / kPairPx;
@@ -429,11 +433,15 @@ int launch_pair(const ConvArgs& a, int otile, cudaStream_t stream) {
   const CUtensorMap mx = make_tmap_nd(a.x, dt, 4, dims, strides, box);
   CUtensorMap mg = mx;
   if (a.gtop + a.gbot > 0) {
+    // the ghost rows may be wider than x (ghost_wpitch pixels per row); x's
+    // columns start at pixel ghost_w0 of each ghost row
+    const int gp = a.ghost_wpitch > 0 ? a.ghost_wpitch : a.Win;
     const uint64_t gdims[4] = {static_cast<uint64_t>(a.C), static_cast<uint64_t>(a.Win),
                                static_cast<uint64_t>(a.gtop + a.gbot), static_cast<uint64_t>(a.B)};
-    const uint64_t gstrides[3] = {static_cast<uint64_t>(a.C) * 2, static_cast<uint64_t>(a.Win) * a.C * 2,
-                                  static_cast<uint64_t>(a.gtop + a.gbot) * a.Win * a.C * 2};
-    mg = make_tmap_nd(a.ghosts, dt, 4, gdims, gstrides, box);
+    const uint64_t gstrides[3] = {static_cast<uint64_t>(a.C) * 2, static_cast<uint64_t>(gp) * a.C * 2,
+                                  static_cast<uint64_t>(a.gtop + a.gbot) * gp * a.C * 2};
+    const void* gbase = static_cast<const uint8_t*>(a.ghosts) + static_cast<size_t>(a.ghost_w0) * a.C * 2;
+    mg = make_tmap_nd(gbase, dt, 4, gdims, gstrides, box);
   }
   // W: [O][K] (K-major), box 64 x otile / 2
   const CUtensorMap mw = make_tmap_3d(a.w, dt, 2, K, a.O, 1, K, static_cast<uint64_t>(K) * a.O, kBK,
@@ -466,6 +474,7 @@ int launch_pair(const ConvArgs& a, int otile, cudaStream_t stream) {
 
 bool conv_pair_eligible(const ConvArgs& a) {
   if (a.gtop + a.gbot > 0 && (a.ghosts == nullptr || (reinterpret_cast<uintptr_t>(a.ghosts) & 15) != 0)) return false;
+  if (a.out_wpitch > 0 && a.out_w0 + conv_wout(a) > a.out_wpitch) return false;
   return a.C % kBK == 0 && a.KW >= 1 && a.KW <= 9 && a.O % 16 == 0 && a.num_sms >= 2 && pick_otile(a) > 0 &&
          (reinterpret_cast<uintptr_t>(a.out) & 15) == 0 && static_cast<long long>(a.C) * a.Win * 2 % 16 == 0;
 }

@@ -39,16 +39,20 @@ def _lohi(p):
     return (int(p[0]), int(p[1])) if isinstance(p, (tuple, list)) else (int(p), int(p))
 
 
-def _run(mod, x, w, bias, ph, pw, ghosts=None, gtop=0, gbot=0):
+def _run(mod, x, w, bias, ph, pw, ghosts=None, gtop=0, gbot=0, ghost_w0=0, out=None, out_w0=0):
     """ph, pw: (lo, hi) zero padding of the rows and the columns; ghosts: rows
-    that continue x above (gtop) and below (gbot), [B, gtop + gbot, W, C]."""
+    that continue x above (gtop) and below (gbot), [B, gtop + gbot, Wg, C] with
+    x's columns at ghost_w0 .. ghost_w0 + W; out: write the result into
+    columns out_w0 .. of this (wider) tensor instead of a new one."""
     B, H, W, _ = x.shape
     O, KH, KW, _ = w.shape
     Hv = H + gtop + gbot
-    out = torch.empty(B, Hv + ph[0] + ph[1] - KH + 1, W + pw[0] + pw[1] - KW + 1, O, dtype=x.dtype, device=x.device)
+    Ho, Wo = Hv + ph[0] + ph[1] - KH + 1, W + pw[0] + pw[1] - KW + 1
+    if out is None:
+        out = torch.empty(B, Ho, Wo, O, dtype=x.dtype, device=x.device)
     b = bias if bias is not None else torch.empty(0, dtype=torch.float32, device=x.device)
     g = ghosts.contiguous() if ghosts is not None else torch.empty(0, dtype=x.dtype, device=x.device)
-    mod.conv2d_implicit(x, w, b, out, ph[0], pw[0], ph[1], pw[1], _KERNEL, g, gtop, gbot,
+    mod.conv2d_implicit(x, w, b, out, ph[0], pw[0], ph[1], pw[1], _KERNEL, g, gtop, gbot, ghost_w0, out_w0,
                         _native.error_word(x.device))
     return out
 
@@ -214,6 +218,51 @@ def conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, ker
     out = out.reshape(*lead, *out.shape[1:])
     produced = batch + list(spatial) + [cout]
     return out.permute([produced.index(n) for n in out_names]).contiguous()
+
+
+def conv2d_ghost_2d(x, ghosts, gtop, gbot, cols, gl, gr, w, bias, ph, pw, run=None):
+    """Inference conv of a shard haloed along both image axes, without
+    assembling the haloed shard.  x [B, H, W, C]; ghosts [B, gtop + gbot,
+    gl + W + gr, C]: the rows above / below, including the corners; cols
+    [B, H, gl + gr, C]: the columns left / right of x; ph / pw: zero padding
+    beyond the ghosts.  The interior columns are one conv over x with ghost
+    rows, written into its column range of the output; the P = gl + pw[0]
+    left and Q = gr + pw[1] right output columns come from thin strips of the
+    haloed input (KW - 1 + ghost columns wide), convolved transposed so that
+    their long axis runs along the kernel's 256-pixel tiles.  ``run``: the
+    conv of ``_run``'s contract (default: the native kernels)."""
+    run = run or (lambda *a, **k: _run(_native.require(), *a, **k))
+    B, H, W, C = x.shape
+    O, KH, KW, _ = w.shape
+    Hv = H + gtop + gbot
+    Ho, Wo = Hv + ph[0] + ph[1] - KH + 1, gl + W + gr + pw[0] + pw[1] - KW + 1
+    P, Q = gl + pw[0], gr + pw[1]
+    bias32 = None if bias is None else bias.float().contiguous()
+    out = torch.empty(B, Ho, Wo, O, dtype=x.dtype, device=x.device)
+    run(x, w, bias32, ph, (0, 0), ghosts if gtop + gbot else None, gtop, gbot, gl, out, P)
+
+    def strip(c0, c1):
+        """Columns [c0, c1) of the haloed input (x's column 0 at index 0), all rows."""
+        parts = []
+        if c0 < 0:
+            parts.append(cols.narrow(2, gl + c0, min(c1, 0) - c0))
+        if c1 > 0 and c0 < W:
+            parts.append(x.narrow(2, max(c0, 0), min(c1, W) - max(c0, 0)))
+        if c1 > W:
+            parts.append(cols.narrow(2, gl + max(c0, W) - W, c1 - max(c0, W)))
+        mid = torch.cat(parts, 2)
+        if gtop + gbot == 0:
+            return mid
+        g = ghosts.narrow(2, gl + c0, c1 - c0)
+        return torch.cat([g.narrow(1, 0, gtop), mid, g.narrow(1, gtop, gbot)], 1)
+    wt = w.transpose(1, 2).contiguous()  # [O][KW][KH][C]: the strips run transposed
+    if P > 0:
+        s = strip(-gl, KW - 1).transpose(1, 2).contiguous()
+        out[:, :, :P] = run(s, wt, bias32, (pw[0], 0), ph).transpose(1, 2)
+    if Q > 0:
+        s = strip(W - KW + 1, W + gr).transpose(1, 2).contiguous()
+        out[:, :, Wo - Q:] = run(s, wt, bias32, (0, pw[1]), ph).transpose(1, 2)
+    return out
 
 
 def conv2d_nhwc_ghost_rows(x, ghosts, gtop, gbot, adjoint, weight, bias, in_names, w_names, out_names, spatial,

@@ -245,14 +245,17 @@ def _sharded_halo_unpadded(x, axis, dim, left, right, *, mesh, shapes, boundary)
     return z, lo - (start - left), (start + local + right) - hi
 
 
-def halo_ghost_rows(x, axis, dim, left, right, *, mesh, shapes):
+def halo_ghost_rows(x, axis, dim, left, right, *, mesh, shapes, slab=None, shape=None):
     """Zero-boundary halo of a sharded axis for a consumer that reads the
     shard and its neighbours' rows in place (the pair conv's ghost rows):
     returns (G, gtop, gbot, missing_lo, missing_hi, adjoint).  G holds the
     gtop rows above the shard and the gbot rows below it along ``dim`` (only
     the rows peers own; the shard is not copied), missing_lo / missing_hi the
     zero rows beyond the global edges, and adjoint(dv) maps the gradient of
-    the haloed shard (gtop + shard + gbot rows) back to the shard's gradient."""
+    the haloed shard (gtop + shard + gbot rows) back to the shard's gradient.
+    ``slab(off, n)`` / ``shape``: exchange the rows of a tensor of that shape
+    that is never assembled (only the sent rows are built)."""
+    shape = list(x.shape) if shape is None else list(shape)
     if mesh is None:
         raise ValueError("Sharded einhalo axes require mesh")
     group = mesh[axis.shard_dim].get_group()
@@ -260,9 +263,9 @@ def halo_ghost_rows(x, axis, dim, left, right, *, mesh, shapes):
     split = resolve_split_shapes(shapes, axis.shard_dim, axis.name, group)
     if split is None:
         split = [x.shape[dim]] * size
-    if x.shape[dim] != split[rank]:
+    if shape[dim] != split[rank]:
         raise ValueError(
-            f"Local tensor size {x.shape[dim]} does not match split shape {split[rank]} for axis {axis.name!r}"
+            f"Local tensor size {shape[dim]} does not match split shape {split[rank]} for axis {axis.name!r}"
         )
     total, start, local = sum(split), sum(split[:rank]), split[rank]
     lo, hi = max(0, start - left), min(total, start + local + right)
@@ -270,14 +273,15 @@ def halo_ghost_rows(x, axis, dim, left, right, *, mesh, shapes):
     length = sum(p[3] for p in table[rank])
     from ..parallel import symmetric
     comm = symmetric.communicator_for(group) if x.is_cuda else None
-    got = comm.halo_ghosts(x, dim, table, length) if comm is not None else None
+    got = comm.halo_ghosts(x, dim, table, length, slab=slab, shape=shape) if comm is not None else None
     if got is None:
-        full = _halo_forward(x, group, dim, split, left, right, False)
+        whole = x if slab is None else slab(0, shape[dim])
+        full = _halo_forward(whole, group, dim, split, left, right, False)
         gtop, gbot = start - lo, hi - (start + local)
         g = torch.cat([full.narrow(dim, 0, gtop), full.narrow(dim, gtop + local, gbot)], dim)
     else:
         g, gtop, gbot = got
-    in_shape = tuple(x.shape)
+    in_shape = tuple(shape)
 
     def adjoint(dv):
         return _halo_adjoint(dv, group, dim, split, left, right, False, in_shape)

@@ -596,21 +596,25 @@ class Communicator:
         stage = torch.cat([x.narrow(dim, off, n) for off, n in send], dim) if send else None
         return out if self._copy(stage, out, boxes, local=x) else None
 
-    def halo_ghosts(self, x, dim, table, length):
+    def halo_ghosts(self, x, dim, table, length, slab=None, shape=None):
         """The rows of this rank's haloed shard that peers hold, without the
         shard itself: (G, gtop, gbot) with G's first gtop rows along ``dim``
         above the shard and the next gbot below it (``halo_ghost_plan``), or
         None.  A consumer that reads x and G in place (the pair conv) needs no
-        haloed copy of x."""
+        haloed copy of x.  ``slab(off, n)`` / ``shape``: the rows of a tensor
+        of that shape that is never assembled (x with ghost columns on both
+        sides); only the rows this rank sends are built."""
         if self.broken:
             return None
         x = x.contiguous()
-        plan = halo_ghost_plan(self.rank, list(x.shape), dim, table, length, x.element_size())
+        shape = list(x.shape) if shape is None else list(shape)
+        plan = halo_ghost_plan(self.rank, shape, dim, table, length, x.element_size())
         if plan is None:
             return None
         send, boxes, g_shape, gtop, gbot = plan
         g = x.new_empty(g_shape)
-        stage = torch.cat([x.narrow(dim, off, n) for off, n in send], dim) if send else None
+        rows = slab if slab is not None else (lambda off, n: x.narrow(dim, off, n))
+        stage = torch.cat([rows(off, n) for off, n in send], dim) if send else None
         # collective: every rank launches the staged copy, with or without boxes
         if not self._copy(stage, g, boxes, local=x):
             return None
