@@ -4,7 +4,8 @@ strips equal a conv of the assembled haloed input, for ghost columns and rows
 of any width and zero padding on either side; on 4 gloo ranks (mesh 2 x 2) the
 ghost exchanges (columns of x, then rows of the column-haloed tensor that is
 never assembled, corners included) feed it the rows and columns a conv of the
-full tensor uses.  The conv itself is a torch stand-in with the native
+full tensor uses, and the training form's gradients (through the exchanges'
+adjoints) equal the full conv's.  The conv itself is a torch stand-in with the native
 kernel's contract (ghost rows, output column range)."""
 
 import pytest
@@ -77,6 +78,33 @@ def _mesh_body(ctx):
     want = _torch_run(full, w, None, (1, 1), (1, 1))
     want = want[:, sum(hs[:rh]):sum(hs[:rh + 1]), sum(ws[:rw]):sum(ws[:rw + 1])]
     torch.testing.assert_close(got, want, rtol=1e-5, atol=1e-5)
+
+    # training: the gradient of the haloed input goes back through the row
+    # exchange's adjoint, then the column exchange's
+    from torch_einshard_b200.ops.conv_impl import conv2d_ghost_2d_train
+    _, _, _, _, _, adjoint_cols = halo_ghost_rows(x, axes["w"], 2, 1, 1, mesh=mesh, shapes=shapes)
+    _, _, _, _, _, adjoint_rows = halo_ghost_rows(x, axes["h"], 1, 1, 1, mesh=mesh, shapes=shapes, slab=slab,
+                                                  shape=vshape)
+    xg = x.clone().requires_grad_(True)
+    wg = w.clone().requires_grad_(True)
+    bias = torch.randn(O, requires_grad=True)
+    y = conv2d_ghost_2d_train(xg, g, gtop, gbot, cols, gl, gr, lambda dv: adjoint_cols(adjoint_rows(dv)), wg, bias,
+                              (mlo, mhi), (zl, zr), run=_torch_run)
+    fullg = full.clone().requires_grad_(True)
+    wr = w.clone().requires_grad_(True)
+    br = bias.detach().clone().requires_grad_(True)
+    yr = _torch_run(fullg, wr, br, (1, 1), (1, 1))
+    dy_full = torch.randn_like(yr)  # the same on every rank (seeded)
+    rows = slice(sum(hs[:rh]), sum(hs[:rh + 1]))
+    colsl = slice(sum(ws[:rw]), sum(ws[:rw + 1]))
+    y.backward(dy_full[:, rows, colsl])
+    yr.backward(dy_full)
+    torch.testing.assert_close(xg.grad, fullg.grad[:, rows, colsl], rtol=1e-4, atol=1e-4)
+    dw, db = wg.grad.clone(), bias.grad.clone()
+    torch.distributed.all_reduce(dw)
+    torch.distributed.all_reduce(db)
+    torch.testing.assert_close(dw, wr.grad, rtol=1e-4, atol=1e-4)
+    torch.testing.assert_close(db, br.grad, rtol=1e-4, atol=1e-4)
 
 
 def test_ghost_exchanges_on_a_2x2_mesh_feed_the_decomposition():

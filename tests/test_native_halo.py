@@ -2,7 +2,9 @@
 the same halo built from the full tensor: uneven shards, a halo wider than a
 neighbour's shard, periodic and constant boundaries, forward and the adjoint
 scatter-add, and einconv over a sharded spatial axis against a local conv of
-the full input."""
+the full input: the first image axis sharded (ghost rows read in place, with
+gradients) and the second (ghost columns, interior conv plus transposed edge
+strips, inference and with gradients)."""
 
 import pytest
 import torch
@@ -125,6 +127,23 @@ def _body(rank, world):
     ref = F.conv2d(xw.float().permute(0, 3, 1, 2), w.float().permute(3, 2, 0, 1), padding=1).permute(0, 2, 3, 1)
     ref = ref[:, :, rank * ws_[0]:(rank + 1) * ws_[0]]
     assert (got.float() - ref).abs().max().item() <= 3e-2 * (ref.abs().max().item() + 1)
+    # the same with gradients: back through the column exchange's adjoint
+    xwg = xwl.clone().requires_grad_(True)
+    wwg = w.clone().requires_grad_(True)
+    got = es.einconv("b h w/sp c, kh kw c o -> b h w/sp o", xwg, wwg, {"h": "kh", "w": "kw"}, mesh=mesh,
+                     shapes={"sp": ws_}, checkpoint=None)
+    xr = xw.float().requires_grad_(True)
+    wr = w.float().requires_grad_(True)
+    ref = F.conv2d(xr.permute(0, 3, 1, 2), wr.permute(3, 2, 0, 1), padding=1).permute(0, 2, 3, 1)
+    gy = torch.randn(ref.shape, device="cuda", dtype=torch.bfloat16)
+    dist.broadcast(gy, 0)
+    got.backward(gy[:, :, rank * ws_[0]:(rank + 1) * ws_[0]])
+    ref.backward(gy.float())
+    want_dx = xr.grad[:, :, rank * ws_[0]:(rank + 1) * ws_[0]]
+    assert (xwg.grad.float() - want_dx).abs().max().item() <= 3e-2 * (want_dx.abs().max().item() + 1)
+    dw = wwg.grad.float()
+    dist.all_reduce(dw)
+    assert (dw - wr.grad).abs().max().item() <= 3e-2 * (wr.grad.abs().max().item() + 1)
     torch.cuda.synchronize()
     _native.check_errors()
 

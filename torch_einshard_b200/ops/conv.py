@@ -297,14 +297,13 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
                                              weight.shape[a.w_names.index(a.kernel[0])],
                                              weight.shape[a.w_names.index(a.kernel[1])]))
 
-    # inference with the second image axis sharded too (channels-last input):
-    # ghost columns and ghost rows (with the corners) are exchanged as thin
-    # tensors and the conv runs as an interior part plus two transposed strips
-    # (conv_impl.conv2d_ghost_2d), so no haloed copy of the shard is made
+    # the second image axis sharded too (channels-last input): ghost columns
+    # and ghost rows (with the corners) are exchanged as thin tensors and the
+    # conv runs as an interior part plus two transposed strips
+    # (conv_impl.conv2d_ghost_2d_train), so no haloed copy of the shard is made
     col = a.spatial[1] if a.ndim == 2 else None
-    grads = torch.is_grad_enabled() and any(t is not None and t.requires_grad for t in (x, weight, bias))
     ghost_cols = (ghost_rows or (edges_in_kernel and native_shape and a.ndim == 2 and row in kernel_pads)) and (
-        not grads and col in exchanged and a.in_names[-3:] == [row, col, a.cin] and
+        col in exchanged and a.in_names[-3:] == [row, col, a.cin] and
         x.shape[a.in_names.index(col)] >= weight.shape[a.w_names.index(a.kernel[1])] and
         conv_impl.pair_kernel_fits(x.shape[a.in_names.index(a.cin)], weight.shape[a.w_names.index(a.cout)],
                                    weight.shape[a.w_names.index(a.kernel[0])],
@@ -313,8 +312,9 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
     def ghost_2d(xa, wa, ba):
         dim_h, dim_w = a.in_names.index(row), a.in_names.index(col)
         lw, rw = normalize_halo(exchanged[col])
-        cols_g, gl, gr, zl, zr, _ = halo_ghost_rows(xa, a.axis(a.in_spec, col), dim_w, lw, rw, mesh=mesh,
-                                                     shapes=shapes)
+        cols_g, gl, gr, zl, zr, adjoint_cols = halo_ghost_rows(xa, a.axis(a.in_spec, col), dim_w, lw, rw,
+                                                                mesh=mesh, shapes=shapes)
+        adjoint_rows = None
         if row in exchanged:
             lh, rh = normalize_halo(exchanged[row])
             vshape = list(xa.shape)
@@ -323,16 +323,22 @@ def einconv(shard, x, weight, windows, *, bias=None, padding=None, stride=1, dil
             def slab(off, n):  # rows of [ghost columns left | x | ghost columns right]
                 c = cols_g.narrow(dim_h, off, n)
                 return torch.cat([c.narrow(dim_w, 0, gl), xa.narrow(dim_h, off, n), c.narrow(dim_w, gl, gr)], dim_w)
-            g, gtop, gbot, mlo, mhi, _ = halo_ghost_rows(xa, a.axis(a.in_spec, row), dim_h, lh, rh, mesh=mesh,
-                                                         shapes=shapes, slab=slab, shape=vshape)
+            g, gtop, gbot, mlo, mhi, adjoint_rows = halo_ghost_rows(xa, a.axis(a.in_spec, row), dim_h, lh, rh,
+                                                                    mesh=mesh, shapes=shapes, slab=slab, shape=vshape)
         else:
             g, gtop, gbot = None, 0, 0
             mlo, mhi = kernel_pads[row]
         lead = xa.shape[:-3]
         flat = lambda t: t.reshape(-1, *t.shape[-3:]).contiguous()  # noqa: E731
-        wn = wa.permute([a.w_names.index(n) for n in [a.cout, a.kernel[0], a.kernel[1], a.cin]]).contiguous()
-        out = conv_impl.conv2d_ghost_2d(flat(xa), flat(g) if g is not None else None, gtop, gbot, flat(cols_g), gl,
-                                        gr, wn, ba, (mlo, mhi), (zl, zr))
+
+        def adjoint(dv):  # haloed-input gradient (flat NHWC) -> the shard's, through both exchanges
+            d = dv.reshape(*lead, *dv.shape[1:])
+            if adjoint_rows is not None:
+                d = adjoint_rows(d)
+            return flat(adjoint_cols(d))
+        wn = wa.permute([a.w_names.index(n) for n in [a.cout, a.kernel[0], a.kernel[1], a.cin]])
+        out = conv_impl.conv2d_ghost_2d_train(flat(xa), flat(g) if g is not None else None, gtop, gbot,
+                                              flat(cols_g), gl, gr, adjoint, wn, ba, (mlo, mhi), (zl, zr))
         out = out.reshape(*lead, *out.shape[1:])
         produced = list(a.in_names[:-3]) + [row, col, a.cout]
         return out.permute([produced.index(n) for n in a.out_names]).contiguous()

@@ -29,7 +29,8 @@ import torch
 
 from . import _native
 
-__all__ = ["conv2d_nhwc", "conv2d_native", "conv2d_ghost_rows", "conv2d_nhwc_ghost_rows", "pair_kernel_fits",
+__all__ = ["conv2d_nhwc", "conv2d_native", "conv2d_ghost_rows", "conv2d_nhwc_ghost_rows", "conv2d_ghost_2d",
+           "conv2d_ghost_2d_train", "pair_kernel_fits",
            "try_conv", "kernel_padding_ok"]
 
 _KERNEL = int(os.environ.get("EINSHARD_CONV_KERNEL", "0"))
@@ -72,6 +73,33 @@ def pair_kernel_fits(C, O, KH, KW):
                for ot in (128, 64, 32, 16))
 
 
+def _haloed_input_grad(grad, w, ph, pw, haloed):
+    """Gradient of a conv's (haloed) input: the conv of dY with the flipped,
+    channel-transposed kernel on the native kernels, else torch.  ``haloed()``
+    builds the input (only the torch path needs it)."""
+    O, KH, KW, C = w.shape
+    if O % 64 == 0 and KH - 1 >= max(ph) and KW - 1 >= max(pw):
+        wt = w.flip(1, 2).permute(3, 1, 2, 0).contiguous()  # [C][KH][KW][O]
+        return _run(_native.require(), grad, wt, None, (KH - 1 - ph[0], KH - 1 - ph[1]),
+                    (KW - 1 - pw[0], KW - 1 - pw[1]))
+    v = haloed()
+    xt = torch.nn.functional.pad(v.permute(0, 3, 1, 2), (pw[0], pw[1], ph[0], ph[1]))
+    dv = torch.nn.grad.conv2d_input(xt.shape, w.permute(0, 3, 1, 2), grad.permute(0, 3, 1, 2))
+    return dv[:, :, ph[0]:ph[0] + v.shape[1], pw[0]:pw[0] + v.shape[2]].permute(0, 2, 3, 1).contiguous()
+
+
+def _haloed_weight_grad(v, grad, w, ph, pw):
+    """Weight gradient of a conv over the haloed input ``v``."""
+    O, KH, KW, C = w.shape
+    if O % 64 == 0:
+        dw = torch.empty(O, KH, KW, C, dtype=torch.float32, device=v.device)
+        _native.require().conv2d_wgrad(v.contiguous(), grad, dw, ph[0], pw[0], ph[1], pw[1],
+                                       _native.error_word(v.device))
+        return dw.to(w.dtype)
+    xt = torch.nn.functional.pad(v.permute(0, 3, 1, 2), (pw[0], pw[1], ph[0], ph[1]))
+    return torch.nn.grad.conv2d_weight(xt, w.permute(0, 3, 1, 2).shape, grad.permute(0, 3, 1, 2)).permute(0, 2, 3, 1)
+
+
 class _Conv2dGhostRows(torch.autograd.Function):
     """NHWC conv2d of the rows [ghosts above; x; ghosts below] without
     assembling them: the pair kernel reads x and the ghost tensor in place.
@@ -94,35 +122,14 @@ class _Conv2dGhostRows(torch.autograd.Function):
         x, g, w = ctx.saved_tensors
         gtop, gbot, ph, pw, adjoint = ctx.meta
         grad = grad.contiguous()
-        O, KH, KW, C = w.shape
         gx = gw = gb = None
-        haloed = None
 
         def assembled():
             return torch.cat([g.narrow(1, 0, gtop), x, g.narrow(1, gtop, gbot)], 1)
-        native_dgrad = O % 64 == 0 and KH - 1 >= max(ph) and KW - 1 >= max(pw)
         if ctx.needs_input_grad[0]:
-            if native_dgrad:
-                wt = w.flip(1, 2).permute(3, 1, 2, 0).contiguous()  # [C][KH][KW][O]
-                dv = _run(_native.require(), grad, wt, None, (KH - 1 - ph[0], KH - 1 - ph[1]),
-                          (KW - 1 - pw[0], KW - 1 - pw[1]))
-            else:
-                haloed = assembled()
-                xt = torch.nn.functional.pad(haloed.permute(0, 3, 1, 2), (pw[0], pw[1], ph[0], ph[1]))
-                dv = torch.nn.grad.conv2d_input(xt.shape, w.permute(0, 3, 1, 2), grad.permute(0, 3, 1, 2))
-                dv = dv[:, :, ph[0]:ph[0] + haloed.shape[1], pw[0]:pw[0] + haloed.shape[2]].permute(0, 2, 3, 1)
-            gx = adjoint(dv.contiguous())
+            gx = adjoint(_haloed_input_grad(grad, w, ph, pw, assembled))
         if ctx.needs_input_grad[2]:
-            haloed = assembled() if haloed is None else haloed
-            if O % 64 == 0:
-                dw = torch.empty(O, KH, KW, C, dtype=torch.float32, device=x.device)
-                _native.require().conv2d_wgrad(haloed.contiguous(), grad, dw, ph[0], pw[0], ph[1], pw[1],
-                                               _native.error_word(x.device))
-                gw = dw.to(w.dtype)
-            else:
-                xt = torch.nn.functional.pad(haloed.permute(0, 3, 1, 2), (pw[0], pw[1], ph[0], ph[1]))
-                gw = torch.nn.grad.conv2d_weight(xt, w.permute(0, 3, 1, 2).shape,
-                                                 grad.permute(0, 3, 1, 2)).permute(0, 2, 3, 1)
+            gw = _haloed_weight_grad(assembled(), grad, w, ph, pw)
         if ctx.has_bias and ctx.needs_input_grad[3]:
             gb = grad.float().sum(dim=(0, 1, 2)).to(ctx.bias_dtype)
         return gx, None, gw, gb, None, None, None, None, None
@@ -263,6 +270,64 @@ def conv2d_ghost_2d(x, ghosts, gtop, gbot, cols, gl, gr, w, bias, ph, pw, run=No
         s = strip(W - KW + 1, W + gr).transpose(1, 2).contiguous()
         out[:, :, Wo - Q:] = run(s, wt, bias32, (0, pw[1]), ph).transpose(1, 2)
     return out
+
+
+def _assemble_2d(x, ghosts, gtop, gbot, cols, gl, gr):
+    """The haloed input [rows above; [cols left | x | cols right]; rows below]."""
+    mid = torch.cat([cols.narrow(2, 0, gl), x, cols.narrow(2, gl, gr)], 2)
+    if ghosts is None or gtop + gbot == 0:
+        return mid
+    return torch.cat([ghosts.narrow(1, 0, gtop), mid, ghosts.narrow(1, gtop, gbot)], 1)
+
+
+class _Conv2dGhost2D(torch.autograd.Function):
+    """Training form of ``conv2d_ghost_2d``: backward forms the gradient of the
+    whole haloed input (one flipped-kernel conv), hands it to ``adjoint`` (the
+    row exchange's adjoint, then the column exchange's, which return every
+    ghost's share to its owner) and takes the weight gradient over the haloed
+    input, assembled only in backward.  ``grads``: the input- and weight-
+    gradient functions (the native ones by default)."""
+
+    @staticmethod
+    def forward(ctx, x, ghosts, cols, w, bias, meta, adjoint):
+        gtop, gbot, gl, gr, ph, pw, run, grads = meta
+        ctx.save_for_backward(x, ghosts, cols, w)
+        ctx.meta, ctx.adjoint = meta, adjoint
+        ctx.has_bias = bias is not None
+        ctx.bias_dtype = bias.dtype if bias is not None else None
+        return conv2d_ghost_2d(x, ghosts, gtop, gbot, cols, gl, gr, w, bias, ph, pw, run=run)
+
+    @staticmethod
+    def backward(ctx, grad):
+        x, g, cols, w = ctx.saved_tensors
+        gtop, gbot, gl, gr, ph, pw, _, grads = ctx.meta
+        input_grad, weight_grad = grads or (_haloed_input_grad, _haloed_weight_grad)
+        grad = grad.contiguous()
+        gx = gw = gb = None
+        v = None
+
+        def assembled():
+            return _assemble_2d(x, g, gtop, gbot, cols, gl, gr)
+        if ctx.needs_input_grad[0]:
+            gx = ctx.adjoint(input_grad(grad, w, ph, pw, assembled))
+        if ctx.needs_input_grad[3]:
+            v = assembled() if v is None else v
+            gw = weight_grad(v, grad, w, ph, pw)
+        if ctx.has_bias and ctx.needs_input_grad[4]:
+            gb = grad.float().sum(dim=(0, 1, 2)).to(ctx.bias_dtype)
+        return gx, None, None, gw, gb, None, None
+
+
+def conv2d_ghost_2d_train(x, ghosts, gtop, gbot, cols, gl, gr, adjoint, w, bias=None, ph=0, pw=0, run=None,
+                          grads=None):
+    """``conv2d_ghost_2d`` with gradients: ``adjoint(dv)`` maps the gradient of
+    the haloed input to x's (the exchanges' adjoints).  ``run`` / ``grads``:
+    stand-ins for the native conv and its input / weight gradients."""
+    ph, pw = _lohi(ph), _lohi(pw)
+    ghosts = ghosts.detach().contiguous() if ghosts is not None else None
+    meta = (gtop, gbot, gl, gr, ph, pw, run, grads)
+    return _Conv2dGhost2D.apply(x.contiguous(), ghosts, cols.detach().contiguous(), w.contiguous(), bias, meta,
+                                adjoint)
 
 
 def conv2d_nhwc_ghost_rows(x, ghosts, gtop, gbot, adjoint, weight, bias, in_names, w_names, out_names, spatial,
