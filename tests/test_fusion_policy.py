@@ -101,3 +101,33 @@ def test_non_cuda_or_fp32_operands_are_never_fused(ranks, monkeypatch):
     ex = executor(output_steps=[AR])
     ex.x0 = SimpleNamespace(is_cuda=True, dtype=torch.float32)
     assert fn.provider(ex) is None
+
+
+def test_fused_nvls_kernel_reduces_in_the_gemm_epilogue_by_default(monkeypatch):
+    """Unless overridden, the fused GEMM + NVLS launch has no dedicated reducer
+    CTA pairs (overlap mode: the GEMM's epilogue warps reduce) and the kernel
+    picks its lag (two waves of CTA pairs); both reach the extension call."""
+    import importlib
+    monkeypatch.delenv("EINSHARD_NVLS_REDUCER_CLUSTERS", raising=False)
+    monkeypatch.delenv("EINSHARD_NVLS_LAG", raising=False)
+    mod = importlib.reload(fn)
+    try:
+        assert mod._NVLS_REDUCER_CLUSTERS == 0 and mod._NVLS_LAG == 0
+        calls = []
+
+        class Ext:
+            def gemm_allreduce_nvls(self, cid, a, b, out, reducers, lag, err):
+                calls.append((reducers, lag))
+
+        ws = SimpleNamespace(nvls=True, broken=False, cid=3, enter=lambda kind: None)
+        monkeypatch.setattr(mod._native, "require", lambda: Ext())
+        monkeypatch.setattr(mod._native, "error_word", lambda device: None)
+        monkeypatch.setattr(mod, "_prepare", lambda t: t)
+        from torch_einshard_b200.parallel import symmetric
+        monkeypatch.setattr(symmetric, "workspace_for", lambda group, nbytes: ws)
+        a = torch.zeros(1, 4, 8, dtype=torch.bfloat16)
+        b = torch.zeros(1, 8, 16, dtype=torch.bfloat16)
+        out = mod.gemm_allreduce_nvls(SimpleNamespace(group=None), a, b)
+        assert out is not None and out.shape == (1, 4, 16) and calls == [(0, 0)]
+    finally:
+        importlib.reload(fn)
