@@ -1017,6 +1017,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_allreduce", &gemm_allreduce, "fused tcgen05 GEMM + NVLink all-reduce (bf16)");
   m.def("conv2d_wgrad", &conv2d_wgrad, "weight gradient of the implicit-GEMM conv (split-K tcgen05, fp32 out)");
   m.def("conv2d_implicit", &conv2d_implicit, "implicit-GEMM NHWC conv2d on tcgen05 (stride 1)");
+  m.def("conv_pair_otile", [](int64_t C, int64_t O, int64_t KH, int64_t KW) {
+        return es::conv_pair_otile(static_cast<int>(C), static_cast<int>(O), static_cast<int>(KH), static_cast<int>(KW));
+      }, "output-channel tile of the CTA-pair conv for this shape (0: the kernel does not take it)");
   m.def("roll_copy", &roll_copy, "cyclic roll along several dims in one kernel");
   m.def("gemm_silu", &gemm_silu, "(silu(a @ b), a @ b), fused on the wide kernel when it runs the GEMM");
   m.def("silu_forward", &silu_forward, "elementwise silu");

@@ -49,6 +49,9 @@ const char* check_conv_args(const ConvArgs& a);
 int conv_launch(const ConvArgs& a, cudaStream_t stream);
 // The CTA-pair kernel with the weights resident in shared memory (conv_pair.cu).
 bool conv_pair_eligible(const ConvArgs& a);
+// Output-channel tile the pair kernel would use for this shape (0: it does not
+// take the shape: channel counts or a weight slice too large for shared memory).
+int conv_pair_otile(int C, int O, int KH, int KW);
 int conv_pair_launch(const ConvArgs& a, cudaStream_t stream);
 
 // Weight gradient of conv_launch's convolution: dw[o][kh][kw][c] (fp32, must be

@@ -472,6 +472,16 @@ int launch_pair(const ConvArgs& a, int otile, cudaStream_t stream) {
 
 }  // namespace
 
+int conv_pair_otile(int C, int O, int KH, int KW) {
+  if (C <= 0 || O <= 0 || KH <= 0 || KW < 1 || KW > 9 || C % kBK || O % 16) return 0;
+  ConvArgs a;
+  a.C = C;
+  a.O = O;
+  a.KH = KH;
+  a.KW = KW;
+  return pick_otile(a);
+}
+
 bool conv_pair_eligible(const ConvArgs& a) {
   if (a.gtop + a.gbot > 0 && (a.ghosts == nullptr || (reinterpret_cast<uintptr_t>(a.ghosts) & 15) != 0)) return false;
   if (a.out_wpitch > 0 && a.out_w0 + conv_wout(a) > a.out_wpitch) return false;

@@ -66,7 +66,12 @@ _PAIR_WEIGHT_BYTES = 232448 - 1024 - 4 * 136 * 128 - 256
 def pair_kernel_fits(C, O, KH, KW):
     """Whether the CTA-pair kernel (the only one that reads ghost rows) takes
     this shape: channels as its boxes need, and some output-channel tile whose
-    weight slice fits in shared memory (the kernel's own choice, csrc/conv_pair.cu)."""
+    weight slice fits in shared memory.  The extension answers when it is
+    loaded (``conv_pair_otile``, the kernel's own choice); the same rule is
+    restated here for hosts without it."""
+    mod = _native.module()
+    if mod is not None and hasattr(mod, "conv_pair_otile"):
+        return mod.conv_pair_otile(int(C), int(O), int(KH), int(KW)) > 0
     if C % 64 or O % 16 or KW > 9:
         return False
     return any(ot <= O and O % ot == 0 and KH * KW * (C // 64) * (ot // 2) * 128 <= _PAIR_WEIGHT_BYTES
