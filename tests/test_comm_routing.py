@@ -132,3 +132,27 @@ def test_protocol_switch_waits_for_the_other_kind(monkeypatch):
     comm.all_reduce_(torch.zeros(64, dtype=torch.float32))
     kinds = [c[0] for c in comm.mod.calls]
     assert kinds == ["nvls1", "quiesce", "acquire", "nvls1"]
+
+
+def test_automatic_set_up_is_opt_in_and_needs_cuda(monkeypatch):
+    """EINSHARD_AUTO_NATIVE_COMM lets the first lookup create a group's
+    communicator; off by default, never on CPU / gloo, and disable() blocks it."""
+    from torch_einshard_b200.parallel import symmetric
+    monkeypatch.setitem(symmetric._state, "enabled", False)
+    monkeypatch.setitem(symmetric._state, "auto_blocked", False)
+    assert symmetric._AUTO is False or "EINSHARD_AUTO_NATIVE_COMM" in __import__("os").environ
+    monkeypatch.setattr(symmetric, "_AUTO", False)
+    assert symmetric.communicator_for(object()) is None and not symmetric.enabled()
+    monkeypatch.setattr(symmetric, "_AUTO", True)
+    monkeypatch.setattr(symmetric.torch.cuda, "is_available", lambda: False)
+    assert symmetric.communicator_for(object()) is None and not symmetric.enabled()
+    monkeypatch.setattr(symmetric.torch.cuda, "is_available", lambda: True)
+    monkeypatch.setattr(symmetric.dist, "is_initialized", lambda: True)
+    monkeypatch.setattr(symmetric._native, "available", lambda: True)
+    made = []
+    monkeypatch.setattr(symmetric, "_group_key", lambda group: ("k",))
+    monkeypatch.setattr(symmetric, "communicator_for_group", lambda group: made.append(group) or "comm")
+    group = object()
+    assert symmetric.communicator_for(group) == "comm" and made == [group] and symmetric.enabled()
+    symmetric.disable()
+    assert symmetric.communicator_for(group) is None

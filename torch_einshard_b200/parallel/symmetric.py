@@ -734,12 +734,26 @@ def activate(mesh=None):
     for group in _mesh_groups(mesh):
         communicator_for_group(group)
     _state["enabled"] = True
+    _state["auto_blocked"] = False
     return True
 
 
 # ------------------------------------------------------------------ lookup used by the collective helpers
 
-_state = {"enabled": False}
+_state = {"enabled": False, "auto_blocked": False}
+# Opt-in lazy set-up for code that never calls setup_native_comm (drop-in users
+# of the reference's API): the first lookup on a CUDA / NCCL group creates that
+# group's communicator.  The lookup is collective like the helpers that make it
+# (every rank of the group reaches it in the same order).
+_AUTO = os.environ.get("EINSHARD_AUTO_NATIVE_COMM", "0") not in ("0", "")
+
+
+def _auto_activate():
+    if (not _AUTO or _state["auto_blocked"] or os.environ.get("EINSHARD_NATIVE_COMM", "1") in ("0", "")
+            or not torch.cuda.is_available() or not dist.is_initialized() or not _native.available()):
+        return False
+    _state["enabled"] = True
+    return True
 
 
 def enabled() -> bool:
@@ -750,19 +764,23 @@ def enabled() -> bool:
 def disable():
     """Route every collective to torch.distributed again (the heaps stay)."""
     _state["enabled"] = False
+    _state["auto_blocked"] = True
 
 
 def communicator_for(group):
     """The native communicator of ``group``, or None (not active, not eligible)."""
-    if not _state["enabled"] or group is None:
+    if group is None or (not _state["enabled"] and not _auto_activate()):
         return None
-    return _COMMS.get(_group_key(group))
+    comm = _COMMS.get(_group_key(group))
+    if comm is None and _AUTO and not _state["auto_blocked"]:
+        comm = communicator_for_group(group)
+    return comm
 
 
 def workspace_for(group, nbytes):
     """A communicator of ``group`` whose symmetric region holds ``nbytes``
     (collective: every member asks with the same size), or None."""
-    if not _state["enabled"] or group is None:
+    if group is None or communicator_for(group) is None:
         return None
     return workspace_for_group(group, nbytes)
 
