@@ -217,3 +217,28 @@ def test_conv_ghost_2d_native(gl, gr, gtop, gbot, ph, pw):
     assert got.shape == want.shape
     _close(got, want)
     _native.check_errors()
+
+
+def test_einconv_1d_runs_native_as_height_one(monkeypatch):
+    """A 1-D einconv runs on the native kernels as a 2-D conv of height 1
+    (forward and backward) and matches F.conv1d."""
+    import torch_einshard_b200 as es
+    from torch_einshard_b200.ops import conv_impl
+    calls = []
+    real = conv_impl._run
+    monkeypatch.setattr(conv_impl, "_run", lambda *a, **k: calls.append(1) or real(*a, **k))
+    torch.manual_seed(7)
+    x = torch.randn(3, 500, 64, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = (torch.randn(5, 64, 128, device="cuda") * 0.05).to(torch.bfloat16).requires_grad_(True)
+    y = es.einconv("b l c, k c o -> b l o", x, w, {"l": "k"}, checkpoint=None)
+    assert calls
+    xr = x.detach().float().requires_grad_(True)
+    wr = w.detach().float().requires_grad_(True)
+    yr = F.conv1d(xr.permute(0, 2, 1), wr.permute(2, 1, 0), padding=2).permute(0, 2, 1)
+    _close(y, yr)
+    g = torch.randn_like(y)
+    y.backward(g)
+    yr.backward(g.float())
+    _close(x.grad, xr.grad)
+    _close(w.grad, wr.grad)
+    _native.check_errors()

@@ -201,7 +201,8 @@ class _Conv2dNHWC(torch.autograd.Function):
 
 
 def supported(x, w_dtype, cin_size, ndim, dilation):
-    return (x.is_cuda and ndim == 2 and all(d == 1 for d in dilation) and x.dtype in (torch.bfloat16, torch.float16)
+    """1-D convs run as 2-D ones of height 1 (``conv2d_nhwc``)."""
+    return (x.is_cuda and ndim in (1, 2) and all(d == 1 for d in dilation) and x.dtype in (torch.bfloat16, torch.float16)
             and w_dtype == x.dtype and cin_size % 64 == 0)
 
 
@@ -226,7 +227,10 @@ def conv2d_nhwc(mod, x, weight, bias, in_names, w_names, out_names, spatial, ker
     lead = xn.shape[:len(batch)]
     xn = xn.reshape(-1, *xn.shape[len(batch):])
     wn = weight.permute([w_names.index(n) for n in [cout] + list(kernel) + [cin]])
-    out = conv2d_native(xn, wn, bias, pads.get(spatial[0], 0), pads.get(spatial[1], 0))
+    if len(spatial) == 1:  # a row of height 1: [B, L, C] -> [B, 1, L, C], [O, K, C] -> [O, 1, K, C]
+        out = conv2d_native(xn.unsqueeze(1), wn.unsqueeze(1), bias, 0, pads.get(spatial[0], 0)).squeeze(1)
+    else:
+        out = conv2d_native(xn, wn, bias, pads.get(spatial[0], 0), pads.get(spatial[1], 0))
     out = out.reshape(*lead, *out.shape[1:])
     produced = batch + list(spatial) + [cout]
     return out.permute([produced.index(n) for n in out_names]).contiguous()
